@@ -1,0 +1,206 @@
+/*
+ * ksd8.h — C ABI of the B200 (sm_100a) INT8 hot path of KSDraft.
+ *
+ * Every entry point takes raw device pointers, sizes and row strides (in
+ * elements), a `status` word in device memory (may be NULL) that kernels use
+ * to report device-side failures (timeouts), and a cudaStream_t passed as
+ * `void*` (NULL = legacy default stream).  Work is only enqueued on that
+ * stream: nothing synchronises, nothing allocates device memory.  The return
+ * value is a KSD8_* status: argument errors are detected on the host before
+ * any launch.
+ *
+ * Layout conventions follow the reference int8 tier (ksdraft/kernels/quant.py:1-14):
+ * row-major, the quantised dimension is the LAST one, weights are (N, K),
+ * scales are fp16, one per 128 consecutive elements, codes in [-127, 127].
+ *
+ * Reference interfaces replaced (paths within curvedinf/ksdraft):
+ *   ksd8_quantize_rows        ksdraft/kernels/quant.py:30 quantize_last_dim,
+ *                             ksdraft/train/stages.py:27 quantize_last_dim_dithered
+ *   ksd8_quantize_cols        quantize_last_dim(t.t().contiguous()) and
+ *                             quantize_last_dim(dequantize_last_dim(c, s).t()),
+ *                             ksdraft/kernels/ks3_int8.py:350,407-424
+ *   ksd8_w8a8_gemm            ksdraft/kernels/gemm.py:53 w8a8_gemm (+ the _w8a8_gemm_kernel at :18)
+ *   ksd8_w8a8_group_partials  per-group int32 dot products of gemm.py:34-45 (parity probe)
+ *   ksd8_ks3_pack             ksdraft/kernels/ks3_int8.py:262-277 _repack_masters (spine + warp part),
+ *                             :87 pack_spine, :158 _warp_scalars
+ *   ksd8_ks3_spine_quant      ksdraft/kernels/ks3_int8.py:169-234 _spine_features followed by
+ *                             quantize_last_dim(h) (:284, :331)
+ *   ksd8_ks3_vjp              ksdraft/kernels/ks3_int8.py:354-410 (geometry VJP, dc, its two quantisations)
+ *   ksd8_ks3_vjp_reduce       ksdraft/kernels/ks3_int8.py:381-395 (column reductions, STE factors)
+ *   ksd8_rosa_pack_bits       ksdraft/model/rosa.py:156-158 (bits = proj > 0) and the int8 bit inputs
+ *                             of rosa.py:40 _match_payload_sign
+ *   ksd8_rosa_match           ksdraft/model/rosa.py:40-98 _match_payload_sign (+ payload multiply of :164)
+ *   ksd8_rosa_timemix_quantize ksdraft/model/rosa.py:128-133 _shifted followed by the per-token
+ *                             quantisation of Int8Linear.forward (ksdraft/kernels/linear.py:69)
+ *   ksd8_adamw_step           torch.optim.AdamW.step over fp32 masters (ksdraft/train/__init__.py:166)
+ */
+#ifndef KSD8_H_
+#define KSD8_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define KSD8_OK 0
+#define KSD8_ERR_SHAPE 1          /* inconsistent sizes (reference: ValueError) */
+#define KSD8_ERR_ALIGN 2          /* pointer / stride not aligned as required */
+#define KSD8_ERR_DTYPE 3          /* unsupported dtype code (reference: TypeError) */
+#define KSD8_ERR_LAUNCH 4         /* CUDA launch / driver error */
+#define KSD8_ERR_DEVICE_TIMEOUT 5 /* a bounded device-side wait gave up */
+#define KSD8_ERR_UNSUPPORTED 6    /* valid request outside this build (e.g. group != 128 on the GEMM) */
+#define KSD8_ERR_ARG 7            /* bad scalar argument */
+#define KSD8_ERR_NONFINITE 8      /* status bit: an fp16 output overflowed (FP16 handoff) */
+
+/* ---- dtype codes ---- */
+#define KSD8_F32 0
+#define KSD8_F16 1
+#define KSD8_BF16 2
+#define KSD8_I8 3
+
+/* ---- quantiser flags ---- */
+#define KSD8_Q_ROUND_F16 1   /* round the input through fp16 first (x.float().to(float16)) */
+#define KSD8_Q_DITHER 2      /* add PTQR rounding dither from the Philox4x32-10 counter RNG */
+#define KSD8_Q_RELU 4        /* not used by the reference path; reserved */
+
+/* ---- GEMM epilogue flags ---- */
+#define KSD8_EPI_CLAMP_F16 1  /* fp16 output: saturate +-inf to +-65504 (ks3_int8.py:241-242) */
+#define KSD8_EPI_BIAS 2       /* add fp32 bias[n] after the group sum (linear.py:71) */
+#define KSD8_EPI_FLAG_NONFINITE 4 /* fp16 output: set KSD8_ERR_NONFINITE in *status on inf/nan */
+
+/* ---- nonlinear modes of the KS3 cell (ks3_int8.py:22-28) ---- */
+#define KSD8_NL_FP32 0
+#define KSD8_NL_FP16 1
+#define KSD8_NL_INT8 2
+
+int ksd8_version(void);
+const char* ksd8_status_string(int status);
+/* Last CUDA runtime error seen by a launch in this thread (cudaError_t as int). */
+int ksd8_last_cuda_error(void);
+int ksd8_sm_count(int device);
+
+/* Quantise `rows` rows of `k` elements (row stride ldx) in groups of `group`
+ * along the row.  codes: (rows, k) row stride ldc (padded lanes are not
+ * written); scales: (rows, ceil(k/group)) fp16, contiguous.  With
+ * KSD8_Q_DITHER, code = round(x/scale + (U - 0.5) * 2 * dither), U =
+ * (philox(seed, offset + flat_index) >> 8) * 2^-24, flat_index = row * Kp + col
+ * over the padded (rows, Kp) grid. */
+int ksd8_quantize_rows(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t ldx,
+                       int group, int flags, float dither, uint64_t seed, uint64_t offset,
+                       int8_t* codes, int64_t ldc, void* scales, int* status, void* stream);
+
+/* Transposed quantisation: x is (rows, cols) with row stride ldx.  The output
+ * is x^T (cols, rows) quantised along `rows` in groups of `group`:
+ * codes_t (cols, rows) row stride ldct, scales_t (cols, ceil(rows/group)).
+ * When x_dtype == KSD8_I8, x holds int8 codes whose real value is
+ * code * x_scales[r, c / x_group] (x_scales: (rows, ceil(cols/x_group)) fp16),
+ * i.e. dequantize -> transpose -> requantize in one pass. */
+int ksd8_quantize_cols(const void* x, int x_dtype, const void* x_scales, int x_group,
+                       int64_t rows, int64_t cols, int64_t ldx, int group, int flags,
+                       int8_t* codes_t, int64_t ldct, void* scales_t, int* status, void* stream);
+
+/* Y(M,N) = sum_g float(A_g . W_g^T) * (sa[m,g] * sw[n,g]), int32 dot per
+ * 128-wide K group on tcgen05 tensor cores, fp32 group sum in the canonical
+ * order acc = fmaf(float(dot_g), sa*sw, acc) for g = 0..G-1.
+ * a: (m, k) int8, row stride k; w: (n, k) int8, row stride k; k % 128 == 0,
+ * group must be 128; a_scales (m, k/128), w_scales (n, k/128) fp16.
+ * out_dtype: KSD8_F32 / KSD8_F16 / KSD8_BF16, row stride ldo. */
+int ksd8_w8a8_gemm(const int8_t* a, const void* a_scales, const int8_t* w, const void* w_scales,
+                   int64_t m, int64_t n, int64_t k, int group, void* out, int out_dtype,
+                   int64_t ldo, const float* bias, int epi_flags, int* status, void* stream);
+
+/* Parity probe: the per-group int32 partial dot products of the same
+ * tensor-core main loop, out (k/128, m, n) int32. */
+int ksd8_w8a8_group_partials(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
+                             int32_t* out, int* status, void* stream);
+
+/* KS3 pack of the small per-chart tensors from fp32 masters:
+ * coefficients (charts*6) -> spine_codes (charts, 6) int8 + spine_scale (charts) fp16
+ * (one GS group per 6-wide row, pack_spine); raw_scale/raw_shift (charts) ->
+ * softplus(.)+1e-4 and 0.5*tanh(.) quantised per element (one group each)
+ * into int8 codes + fp16 scales (the warp-scalar buffers of KS3Int8Cell). */
+int ksd8_ks3_pack(const float* coefficients, const float* raw_scale, const float* raw_shift,
+                  int64_t charts, int8_t* spine_codes, void* spine_scale,
+                  int8_t* warp_scale_codes, void* warp_scale_scales, int8_t* warp_shift_codes,
+                  void* warp_shift_scales, int* status, void* stream);
+
+/* Composed KS3 spine on fp16 coordinates (M, charts) followed by GS128
+ * requantisation of h along the charts: h_codes (M, charts), h_scales
+ * (M, ceil(charts/128)).  The warp scalars are given as their int8 codes and
+ * fp16 scales (one group per chart) and dequantised into the arithmetic
+ * domain of the mode (fp32 for KSD8_NL_FP32, fp16 otherwise).  With
+ * warp_*_codes == NULL the matching *_scales array holds the already
+ * dequantised fp16 scalars (the interface of ks3_triton.py:159 project_fused).
+ * lut: the 256-entry int8 tanh table (make_tanh_lut). */
+int ksd8_ks3_spine_quant(const void* coords, int64_t m, int64_t charts,
+                         const int8_t* spine_codes, const void* spine_scale,
+                         const int8_t* warp_scale_codes, const void* warp_scale_scales,
+                         const int8_t* warp_shift_codes, const void* warp_shift_scales,
+                         const int8_t* lut, int nonlinear, int8_t* h_codes, void* h_scales,
+                         int* status, void* stream);
+
+/* KS3 geometry VJP (fp16 arithmetic as the reference) on value = fp16(g @ up)
+ * and the saved fp16 coordinates, both (M, charts).  Writes dc quantised
+ * along charts (dc_codes (M, charts), dc_scales (M, charts/128)) and along
+ * tokens (dct_codes (charts, M), dct_scales (charts, ceil(M/128))), and
+ * per-128-token-tile column partial sums partials (ceil(M/128), 8, charts) fp32
+ * in the order d0..d5, dscale_t, dshift_t (dshift_t before its 0.5 factor).
+ * charts must be a multiple of 128. */
+int ksd8_ks3_vjp(const void* value, const void* coords, int64_t m, int64_t charts,
+                 const int8_t* spine_codes, const void* spine_scale,
+                 const int8_t* warp_scale_codes, const void* warp_scale_scales,
+                 const int8_t* warp_shift_codes, const void* warp_shift_scales,
+                 int8_t* dc_codes, void* dc_scales, int8_t* dct_codes, void* dct_scales,
+                 float* partials, int* status, void* stream);
+
+/* Reduce the VJP partials over token tiles (fixed order), round to fp16 and
+ * apply the STE factors of ks3_int8.py:391-395: dcoeff (charts, 6),
+ * dscale (charts), dshift (charts), all fp16.  Sets KSD8_ERR_NONFINITE in
+ * *status when one of them is not finite (FP16 handoff check). */
+int ksd8_ks3_vjp_reduce(const float* partials, int64_t n_tiles, int64_t charts,
+                        const float* raw_scale, const float* raw_shift, void* dcoeff16,
+                        void* dscale16, void* dshift16, int* status, void* stream);
+
+/* Pack Rosa symbol bits: bit(stream, t) = x[b*sb + t*st + s*ss] > 0 with
+ * stream = b*S + s, into words (streams, ceil(T/64)) uint64, bit t%64 of
+ * word t/64.  x_dtype: KSD8_F32 / KSD8_BF16 / KSD8_F16 / KSD8_I8. */
+int ksd8_rosa_pack_bits(const void* x, int x_dtype, int64_t batch, int64_t t_len,
+                        int64_t streams, int64_t sb, int64_t st, int64_t ss, uint64_t* words,
+                        int* status, void* stream);
+
+/* Longest-suffix match per stream (rosa.py:40-98): for each t, the longest
+ * L <= max_len with q[t-L+1..t] == k[j-L+1..j], L-1 <= j < t, latest such j;
+ * sign = +1 if v[j+1] else -1 (-1 without a match).  out[b*ob + t*ot + s*os]
+ * = payload[s] * sign (payload may be NULL = 1) as out_dtype; optional
+ * match_len / match_end (streams, T) int32 (0 / -1 without a match). */
+int ksd8_rosa_match(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw, int64_t batch,
+                    int64_t streams, int64_t t_len, int max_len, const float* payload,
+                    void* out, int out_dtype, int64_t ob, int64_t ot, int64_t os,
+                    int32_t* match_len, int32_t* match_end, int* status, void* stream);
+
+/* Rosa time-shift mix + per-token GS quantisation of the three projection
+ * inputs: x (B, T, d) bf16/f32; mix_q/k/v (d) fp32 = sigmoid(time_mix_*);
+ * in_X = prev + (x - prev) * mix_X with (x - prev) rounded to x's dtype.
+ * Outputs codes (B*T, d) and scales (B*T, ceil(d/128)) for q, k, v. */
+int ksd8_rosa_timemix_quantize(const void* x, int x_dtype, int64_t batch, int64_t t_len,
+                               int64_t d, const float* mix_q, const float* mix_k,
+                               const float* mix_v, int8_t* q_codes, void* q_scales,
+                               int8_t* k_codes, void* k_scales, int8_t* v_codes, void* v_scales,
+                               int* status, void* stream);
+
+/* Decoupled-weight-decay Adam over n fp32 parameters with fp16 or fp32
+ * gradients (grad_dtype), torch.optim.AdamW semantics (bias-corrected). */
+int ksd8_adamw_step(float* param, const void* grad, int grad_dtype, float* exp_avg,
+                    float* exp_avg_sq, int64_t n, float lr, float beta1, float beta2, float eps,
+                    float weight_decay, int step, int* status, void* stream);
+
+/* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
+int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KSD8_H_ */

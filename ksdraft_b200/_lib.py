@@ -1,0 +1,114 @@
+"""ctypes binding of libksd8.so (the C ABI declared in include/ksd8.h).
+
+The library is loaded lazily on first use.  There is no fallback: if the
+shared object is missing, or a tensor handed to an op is not a CUDA tensor,
+the op raises.  Status codes are mapped to the exceptions the reference
+raises for the same conditions (ValueError for shapes, TypeError for dtypes).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libksd8.so"
+
+OK, ERR_SHAPE, ERR_ALIGN, ERR_DTYPE, ERR_LAUNCH, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_ARG, \
+    ERR_NONFINITE = range(9)
+
+F32, F16, BF16, I8 = 0, 1, 2, 3
+Q_ROUND_F16, Q_DITHER = 1, 2
+EPI_CLAMP_F16, EPI_BIAS, EPI_FLAG_NONFINITE = 1, 2, 4
+NL = {"fp32": 0, "fp16": 1, "int8": 2}
+
+_DT = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.int8: I8}
+
+i64, i32, u64, f32, vp = C.c_int64, C.c_int, C.c_uint64, C.c_float, C.c_void_p
+
+# name -> argtypes (restype is always int)
+SIGNATURES: dict[str, list] = {
+    "ksd8_version": [],
+    "ksd8_status_string": [i32],
+    "ksd8_last_cuda_error": [],
+    "ksd8_sm_count": [i32],
+    "ksd8_quantize_rows": [vp, i32, i64, i64, i64, i32, i32, f32, u64, u64, vp, i64, vp, vp, vp],
+    "ksd8_quantize_cols": [vp, i32, vp, i32, i64, i64, i64, i32, i32, vp, i64, vp, vp, vp],
+    "ksd8_w8a8_gemm": [vp, vp, vp, vp, i64, i64, i64, i32, vp, i32, i64, vp, i32, vp, vp],
+    "ksd8_w8a8_group_partials": [vp, vp, i64, i64, i64, vp, vp, vp],
+    "ksd8_ks3_pack": [vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp],
+    "ksd8_ks3_spine_quant": [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, i32, vp, vp, vp, vp],
+    "ksd8_ks3_vjp": [vp, vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
+    "ksd8_ks3_vjp_reduce": [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp],
+    "ksd8_rosa_pack_bits": [vp, i32, i64, i64, i64, i64, i64, i64, vp, vp, vp],
+    "ksd8_rosa_match": [vp, vp, vp, i64, i64, i64, i32, vp, vp, i32, i64, i64, i64, vp, vp, vp,
+                        vp],
+    "ksd8_rosa_timemix_quantize": [vp, i32, i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                   vp, vp],
+    "ksd8_adamw_step": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp],
+    "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
+}
+
+_lib: C.CDLL | None = None
+
+
+def load() -> C.CDLL:
+    """Load libksd8.so and declare every entry point's signature."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m ksdraft_b200.build` "
+                "(ksdraft_b200 has no CPU fallback)")
+        lib = C.CDLL(str(LIB_PATH))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = C.c_char_p if name == "ksd8_status_string" else C.c_int
+        _lib = lib
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return load().ksd8_status_string(code).decode()
+
+
+def check(rc: int, what: str) -> None:
+    if rc == OK:
+        return
+    msg = f"{what}: {status_string(rc)}"
+    if rc == ERR_SHAPE:
+        raise ValueError(msg)
+    if rc == ERR_DTYPE:
+        raise TypeError(msg)
+    if rc == ERR_LAUNCH:
+        msg += f" (cudaError {load().ksd8_last_cuda_error()})"
+    raise RuntimeError(msg)
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "ksdraft_b200 ops run on CUDA tensors only (no CPU fallback); "
+                f"got a tensor on {t.device}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def lib() -> C.CDLL:
+    return load()

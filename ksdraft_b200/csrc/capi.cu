@@ -1,0 +1,263 @@
+// extern "C" boundary of libksd8: argument validation on the host, then the
+// launches of quant.cu / gemm_sm100.cu / ks3.cu / rosa.cu on the caller's stream.
+// Shape, dtype and alignment errors return a status before anything launches.
+#include <cstdio>
+
+#include "common.cuh"
+
+// launchers defined in the kernel translation units
+int ksd8_quantize_rows_launch(const void*, int, int64_t, int64_t, int64_t, int, int, float,
+                              uint64_t, uint64_t, int8_t*, int64_t, void*, cudaStream_t);
+int ksd8_quantize_cols_launch(const void*, int, const void*, int, int64_t, int64_t, int64_t, int,
+                              int8_t*, int64_t, void*, cudaStream_t);
+int ksd8_philox_launch(uint64_t, uint64_t, int64_t, float*, cudaStream_t);
+int ksd8_gemm_launch(const int8_t*, const void*, const int8_t*, const void*, int64_t, int64_t,
+                     int64_t, void*, int, int64_t, const float*, int, int*, cudaStream_t, bool);
+int ksd8_ks3_pack_launch(const float*, const float*, const float*, int64_t, int8_t*, void*,
+                         int8_t*, void*, int8_t*, void*, cudaStream_t);
+int ksd8_ks3_spine_quant_launch(const void*, int64_t, int64_t, const int8_t*, const void*,
+                                const int8_t*, const void*, const int8_t*, const void*,
+                                const int8_t*, int, int8_t*, void*, cudaStream_t);
+int ksd8_ks3_vjp_launch(const void*, const void*, int64_t, int64_t, const int8_t*, const void*,
+                        const int8_t*, const void*, const int8_t*, const void*, int8_t*, void*,
+                        int8_t*, void*, float*, cudaStream_t);
+int ksd8_ks3_vjp_reduce_launch(const float*, int64_t, int64_t, const float*, const float*, void*,
+                               void*, void*, int*, cudaStream_t);
+int ksd8_rosa_pack_bits_launch(const void*, int, int64_t, int64_t, int64_t, int64_t, int64_t,
+                               int64_t, uint64_t*, cudaStream_t);
+int ksd8_rosa_match_launch(const uint64_t*, const uint64_t*, const uint64_t*, int64_t, int64_t,
+                           int64_t, int, const float*, void*, int, int64_t, int64_t, int64_t,
+                           int32_t*, int32_t*, cudaStream_t);
+int ksd8_rosa_timemix_launch(const void*, int, int64_t, int64_t, int64_t, const float*,
+                             const float*, const float*, int8_t*, void*, int8_t*, void*, int8_t*,
+                             void*, cudaStream_t);
+int ksd8_adamw_launch(float*, const void*, int, float*, float*, int64_t, float, float, float,
+                      float, float, int, cudaStream_t);
+
+static thread_local int g_last_cuda_error = 0;
+
+static int finish(int rc) {
+  if (rc != KSD8_OK) return rc;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    g_last_cuda_error = (int)e;
+    return KSD8_ERR_LAUNCH;
+  }
+  return KSD8_OK;
+}
+
+static inline bool valid_float_dtype(int d) {
+  return d == KSD8_F32 || d == KSD8_F16 || d == KSD8_BF16;
+}
+
+static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+extern "C" {
+
+int ksd8_version(void) { return 1; }
+
+const char* ksd8_status_string(int status) {
+  switch (status) {
+    case KSD8_OK: return "ok";
+    case KSD8_ERR_SHAPE: return "shape mismatch";
+    case KSD8_ERR_ALIGN: return "misaligned pointer or stride";
+    case KSD8_ERR_DTYPE: return "unsupported dtype";
+    case KSD8_ERR_LAUNCH: return "CUDA launch failure";
+    case KSD8_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case KSD8_ERR_UNSUPPORTED: return "unsupported configuration";
+    case KSD8_ERR_ARG: return "invalid argument";
+    case KSD8_ERR_NONFINITE: return "non-finite fp16 output";
+    default: return "unknown status";
+  }
+}
+
+int ksd8_last_cuda_error(void) { return g_last_cuda_error; }
+
+int ksd8_sm_count(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return -1;
+  return n;
+}
+
+int ksd8_quantize_rows(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t ldx,
+                       int group, int flags, float dither, uint64_t seed, uint64_t offset,
+                       int8_t* codes, int64_t ldc, void* scales, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(x_dtype)) return KSD8_ERR_DTYPE;
+  if (group != 128) return KSD8_ERR_UNSUPPORTED;
+  if (rows < 0 || k < 0 || ldx < k || ldc < k) return KSD8_ERR_SHAPE;
+  if ((rows > 0 && k > 0) && (!x || !codes || !scales)) return KSD8_ERR_ARG;
+  if ((flags & KSD8_Q_DITHER) && !(dither >= 0.f)) return KSD8_ERR_ARG;
+  return finish(ksd8_quantize_rows_launch(x, x_dtype, rows, k, ldx, group, flags, dither, seed,
+                                          offset, codes, ldc, scales, S(stream)));
+}
+
+int ksd8_quantize_cols(const void* x, int x_dtype, const void* x_scales, int x_group,
+                       int64_t rows, int64_t cols, int64_t ldx, int group, int flags,
+                       int8_t* codes_t, int64_t ldct, void* scales_t, int* status, void* stream) {
+  (void)status;
+  if (!(valid_float_dtype(x_dtype) || x_dtype == KSD8_I8)) return KSD8_ERR_DTYPE;
+  if (group != 128) return KSD8_ERR_UNSUPPORTED;
+  if (x_dtype == KSD8_I8 && (!x_scales || x_group <= 0)) return KSD8_ERR_ARG;
+  if (rows < 0 || cols < 0 || ldx < cols || ldct < rows) return KSD8_ERR_SHAPE;
+  if ((rows > 0 && cols > 0) && (!x || !codes_t || !scales_t)) return KSD8_ERR_ARG;
+  return finish(ksd8_quantize_cols_launch(x, x_dtype, x_scales, x_group, rows, cols, ldx, flags,
+                                          codes_t, ldct, scales_t, S(stream)));
+}
+
+int ksd8_w8a8_gemm(const int8_t* a, const void* a_scales, const int8_t* w, const void* w_scales,
+                   int64_t m, int64_t n, int64_t k, int group, void* out, int out_dtype,
+                   int64_t ldo, const float* bias, int epi_flags, int* status, void* stream) {
+  if (group != 128) return KSD8_ERR_UNSUPPORTED;
+  if (!valid_float_dtype(out_dtype)) return KSD8_ERR_DTYPE;
+  if (m < 0 || n < 0 || k < 0 || (k % 128) != 0 || ldo < n) return KSD8_ERR_SHAPE;
+  if (m > INT32_MAX || n > INT32_MAX) return KSD8_ERR_SHAPE;
+  if (m == 0 || n == 0) return KSD8_OK;
+  if (!a || !w || !a_scales || !w_scales || !out) return KSD8_ERR_ARG;
+  if ((epi_flags & KSD8_EPI_BIAS) && !bias) return KSD8_ERR_ARG;
+  // TMA: 16-byte aligned base addresses (row pitch k is a multiple of 128).
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    return KSD8_ERR_ALIGN;
+  if (k == 0) return KSD8_ERR_SHAPE;
+  return finish(ksd8_gemm_launch(a, a_scales, w, w_scales, m, n, k, out, out_dtype, ldo, bias,
+                                 epi_flags, status, S(stream), false));
+}
+
+int ksd8_w8a8_group_partials(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
+                             int32_t* out, int* status, void* stream) {
+  if (m <= 0 || n <= 0 || k <= 0 || (k % 128) != 0) return KSD8_ERR_SHAPE;
+  if (!a || !w || !out) return KSD8_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    return KSD8_ERR_ALIGN;
+  // The scale operands are unused in this mode but the loader reads them:
+  // point them at the codes (any readable memory of sufficient size is fine).
+  return finish(ksd8_gemm_launch(a, nullptr, w, nullptr, m, n, k, out, KSD8_F32, n, nullptr, 0,
+                                 status, S(stream), true));
+}
+
+int ksd8_ks3_pack(const float* coefficients, const float* raw_scale, const float* raw_shift,
+                  int64_t charts, int8_t* spine_codes, void* spine_scale,
+                  int8_t* warp_scale_codes, void* warp_scale_scales, int8_t* warp_shift_codes,
+                  void* warp_shift_scales, int* status, void* stream) {
+  (void)status;
+  if (charts < 0) return KSD8_ERR_SHAPE;
+  if (charts > 0 && (!coefficients || !raw_scale || !raw_shift || !spine_codes || !spine_scale ||
+                     !warp_scale_codes || !warp_scale_scales || !warp_shift_codes ||
+                     !warp_shift_scales))
+    return KSD8_ERR_ARG;
+  return finish(ksd8_ks3_pack_launch(coefficients, raw_scale, raw_shift, charts, spine_codes,
+                                     spine_scale, warp_scale_codes, warp_scale_scales,
+                                     warp_shift_codes, warp_shift_scales, S(stream)));
+}
+
+int ksd8_ks3_spine_quant(const void* coords, int64_t m, int64_t charts,
+                         const int8_t* spine_codes, const void* spine_scale,
+                         const int8_t* warp_scale_codes, const void* warp_scale_scales,
+                         const int8_t* warp_shift_codes, const void* warp_shift_scales,
+                         const int8_t* lut, int nonlinear, int8_t* h_codes, void* h_scales,
+                         int* status, void* stream) {
+  (void)status;
+  if (nonlinear < KSD8_NL_FP32 || nonlinear > KSD8_NL_INT8) return KSD8_ERR_ARG;
+  if (m < 0 || charts < 0) return KSD8_ERR_SHAPE;
+  if (m > 0 && charts > 0 &&
+      (!coords || !spine_codes || !spine_scale || !warp_scale_scales || !warp_shift_scales ||
+       !lut || !h_codes || !h_scales))
+    return KSD8_ERR_ARG;
+  return finish(ksd8_ks3_spine_quant_launch(coords, m, charts, spine_codes, spine_scale,
+                                            warp_scale_codes, warp_scale_scales, warp_shift_codes,
+                                            warp_shift_scales, lut, nonlinear, h_codes, h_scales,
+                                            S(stream)));
+}
+
+int ksd8_ks3_vjp(const void* value, const void* coords, int64_t m, int64_t charts,
+                 const int8_t* spine_codes, const void* spine_scale,
+                 const int8_t* warp_scale_codes, const void* warp_scale_scales,
+                 const int8_t* warp_shift_codes, const void* warp_shift_scales,
+                 int8_t* dc_codes, void* dc_scales, int8_t* dct_codes, void* dct_scales,
+                 float* partials, int* status, void* stream) {
+  (void)status;
+  if (m < 0 || charts <= 0 || (charts % 128) != 0) return KSD8_ERR_SHAPE;
+  if (m > 0 && (!value || !coords || !spine_codes || !spine_scale || !warp_scale_codes ||
+                !warp_scale_scales || !warp_shift_codes || !warp_shift_scales || !dc_codes ||
+                !dc_scales || !dct_codes || !dct_scales || !partials))
+    return KSD8_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(value) & 7) || (reinterpret_cast<uintptr_t>(coords) & 7) ||
+      (reinterpret_cast<uintptr_t>(dc_codes) & 3))
+    return KSD8_ERR_ALIGN;
+  return finish(ksd8_ks3_vjp_launch(value, coords, m, charts, spine_codes, spine_scale,
+                                    warp_scale_codes, warp_scale_scales, warp_shift_codes,
+                                    warp_shift_scales, dc_codes, dc_scales, dct_codes, dct_scales,
+                                    partials, S(stream)));
+}
+
+int ksd8_ks3_vjp_reduce(const float* partials, int64_t n_tiles, int64_t charts,
+                        const float* raw_scale, const float* raw_shift, void* dcoeff16,
+                        void* dscale16, void* dshift16, int* status, void* stream) {
+  if (n_tiles < 0 || charts < 0) return KSD8_ERR_SHAPE;
+  if (charts > 0 && (!partials || !raw_scale || !raw_shift || !dcoeff16 || !dscale16 ||
+                     !dshift16))
+    return KSD8_ERR_ARG;
+  return finish(ksd8_ks3_vjp_reduce_launch(partials, n_tiles, charts, raw_scale, raw_shift,
+                                           dcoeff16, dscale16, dshift16, status, S(stream)));
+}
+
+int ksd8_rosa_pack_bits(const void* x, int x_dtype, int64_t batch, int64_t t_len,
+                        int64_t streams, int64_t sb, int64_t st, int64_t ss, uint64_t* words,
+                        int* status, void* stream) {
+  (void)status;
+  if (!(valid_float_dtype(x_dtype) || x_dtype == KSD8_I8)) return KSD8_ERR_DTYPE;
+  if (batch < 0 || t_len < 0 || streams < 0) return KSD8_ERR_SHAPE;
+  if (batch * streams * t_len > 0 && (!x || !words)) return KSD8_ERR_ARG;
+  return finish(
+      ksd8_rosa_pack_bits_launch(x, x_dtype, batch, t_len, streams, sb, st, ss, words, S(stream)));
+}
+
+int ksd8_rosa_match(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw, int64_t batch,
+                    int64_t streams, int64_t t_len, int max_len, const float* payload,
+                    void* out, int out_dtype, int64_t ob, int64_t ot, int64_t os,
+                    int32_t* match_len, int32_t* match_end, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(out_dtype)) return KSD8_ERR_DTYPE;
+  if (batch < 0 || streams < 0 || t_len < 0) return KSD8_ERR_SHAPE;
+  if (max_len < 0 || max_len > 64) return KSD8_ERR_ARG;
+  if (t_len > 25600) return KSD8_ERR_UNSUPPORTED;  // key windows must fit in shared memory
+  if (batch * streams * t_len > 0 && (!qw || !kw || !vw || !out)) return KSD8_ERR_ARG;
+  return finish(ksd8_rosa_match_launch(qw, kw, vw, batch, streams, t_len, max_len, payload, out,
+                                       out_dtype, ob, ot, os, match_len, match_end, S(stream)));
+}
+
+int ksd8_rosa_timemix_quantize(const void* x, int x_dtype, int64_t batch, int64_t t_len,
+                               int64_t d, const float* mix_q, const float* mix_k,
+                               const float* mix_v, int8_t* q_codes, void* q_scales,
+                               int8_t* k_codes, void* k_scales, int8_t* v_codes, void* v_scales,
+                               int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(x_dtype)) return KSD8_ERR_DTYPE;
+  if (batch < 0 || t_len < 0 || d < 0) return KSD8_ERR_SHAPE;
+  if (batch * t_len * d > 0 && (!x || !mix_q || !mix_k || !mix_v || !q_codes || !q_scales ||
+                                !k_codes || !k_scales || !v_codes || !v_scales))
+    return KSD8_ERR_ARG;
+  return finish(ksd8_rosa_timemix_launch(x, x_dtype, batch, t_len, d, mix_q, mix_k, mix_v,
+                                         q_codes, q_scales, k_codes, k_scales, v_codes, v_scales,
+                                         S(stream)));
+}
+
+int ksd8_adamw_step(float* param, const void* grad, int grad_dtype, float* exp_avg,
+                    float* exp_avg_sq, int64_t n, float lr, float beta1, float beta2, float eps,
+                    float weight_decay, int step, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(grad_dtype)) return KSD8_ERR_DTYPE;
+  if (n < 0) return KSD8_ERR_SHAPE;
+  if (step < 1) return KSD8_ERR_ARG;
+  if (n > 0 && (!param || !grad || !exp_avg || !exp_avg_sq)) return KSD8_ERR_ARG;
+  return finish(ksd8_adamw_launch(param, grad, grad_dtype, exp_avg, exp_avg_sq, n, lr, beta1,
+                                  beta2, eps, weight_decay, step, S(stream)));
+}
+
+int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream) {
+  if (n < 0) return KSD8_ERR_SHAPE;
+  if (n > 0 && !out) return KSD8_ERR_ARG;
+  return finish(ksd8_philox_launch(seed, offset, n, out, S(stream)));
+}
+
+}  // extern "C"

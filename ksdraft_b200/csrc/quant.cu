@@ -1,0 +1,239 @@
+// GS128 symmetric int8 quantisers (ksdraft/kernels/quant.py:30-52 and the
+// PTQR dither of ksdraft/train/stages.py:27-50).
+//
+// Per group of `group` consecutive elements along the quantised dimension
+// (zero padded to a whole group):
+//   amax  = max |x|
+//   scale = fp16( clamp(amax / 127, 2^-24, 65504) )      (fp32 IEEE division)
+//   code  = clamp( rint(x / scale [+ dither noise]), -127, 127 )
+// The dither noise is (U - 0.5) * (2 * dither) with U from Philox4x32-10 at
+// element index offset + row * Kp + col (Kp = padded row length).
+//
+// quantize_rows_kernel: one warp per (row, group), memory-bound, coalesced.
+// quantize_cols_kernel: x^T quantised along the rows of x; a 128 x 64 tile is
+//   staged in shared memory so both the reads of x and the writes of x^T are
+//   coalesced; also dequantises int8 codes on the fly (dequant -> transpose ->
+//   requant of ks3_int8.py:350, :407-424).
+#include "common.cuh"
+
+namespace ksd8 {
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+__device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
+
+// Load 4 consecutive elements starting at column c (masked to < k).
+template <typename T>
+__device__ __forceinline__ void load4(const T* row, int64_t c, int64_t k, float (&v)[4]) {
+  if (c + 4 <= k) {
+    if constexpr (sizeof(T) == 4) {
+      if ((reinterpret_cast<uintptr_t>(row + c) & 15) == 0) {
+        const float4 q = *reinterpret_cast<const float4*>(row + c);
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+        return;
+      }
+    } else {
+      if ((reinterpret_cast<uintptr_t>(row + c) & 7) == 0) {
+        const uint2 q = *reinterpret_cast<const uint2*>(row + c);
+        const T* e = reinterpret_cast<const T*>(&q);
+        v[0] = to_f32<T>(e[0]); v[1] = to_f32<T>(e[1]);
+        v[2] = to_f32<T>(e[2]); v[3] = to_f32<T>(e[3]);
+        return;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = (c + i < k) ? to_f32<T>(row[c + i]) : 0.f;
+}
+
+struct QRowArgs {
+  const void* x;
+  int64_t rows, k, ldx, ldc;
+  int group;  // 128
+  int flags;
+  float dither2;  // 2 * dither
+  uint64_t seed, offset;
+  int8_t* codes;
+  __half* scales;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(QRowArgs a) {
+  const int64_t groups = (a.k + 127) / 128;
+  const int64_t kp = groups * 128;
+  const int64_t total = a.rows * groups;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total;
+       w += warps) {
+    const int64_t r = w / groups;
+    const int64_t g = w - r * groups;
+    const int64_t c = g * 128 + lane * 4;
+    const T* row = reinterpret_cast<const T*>(a.x) + r * a.ldx;
+    float v[4];
+    load4<T>(row, c, a.k, v);
+    if (a.flags & KSD8_Q_ROUND_F16) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = round_f16(v[i]);
+    }
+    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    m = warp_max(m);
+    __half sh;
+    const float scale = gs_scale(m, &sh);
+    int q[4];
+    if (a.flags & KSD8_Q_DITHER) {
+      const uint64_t base = a.offset + (uint64_t)r * kp + c;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float u = philox_uniform(a.seed, base + i);
+        const float noise = __fmul_rn(__fsub_rn(u, 0.5f), a.dither2);
+        float t = __fadd_rn(__fdiv_rn(v[i], scale), noise);
+        t = fminf(fmaxf(rintf(t), -127.f), 127.f);
+        q[i] = (int)t;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q[i] = gs_code(v[i], scale);
+    }
+    int8_t* out = a.codes + r * a.ldc + c;
+    if (c + 4 <= a.k && (reinterpret_cast<uintptr_t>(out) & 3) == 0) {
+      char4 p = make_char4((char)q[0], (char)q[1], (char)q[2], (char)q[3]);
+      *reinterpret_cast<char4*>(out) = p;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (c + i < a.k) out[i] = (int8_t)q[i];
+    }
+    if (lane == 0) a.scales[r * groups + g] = sh;
+  }
+}
+
+struct QColArgs {
+  const void* x;
+  const __half* x_scales;
+  int x_group;
+  int64_t rows, cols, ldx, ldct;
+  int flags;
+  int8_t* codes_t;
+  __half* scales_t;
+};
+
+constexpr int QC_TR = 128;  // rows per tile (one output group)
+constexpr int QC_TC = 64;   // columns per tile
+
+template <typename T, bool DEQUANT>
+__global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
+  __shared__ float tile[QC_TR][QC_TC + 1];
+  const int64_t r0 = (int64_t)blockIdx.y * QC_TR;
+  const int64_t c0 = (int64_t)blockIdx.x * QC_TC;
+  const int tid = threadIdx.x;
+  const int64_t xs_groups = DEQUANT ? (a.cols + a.x_group - 1) / a.x_group : 0;
+  // Load: 4 rows per pass, 64 consecutive columns per row.
+  for (int rr = tid / QC_TC; rr < QC_TR; rr += 256 / QC_TC) {
+    const int cc = tid % QC_TC;
+    const int64_t r = r0 + rr, c = c0 + cc;
+    float v = 0.f;
+    if (r < a.rows && c < a.cols) {
+      const T* row = reinterpret_cast<const T*>(a.x) + r * a.ldx;
+      if constexpr (DEQUANT) {
+        const float code = (float)reinterpret_cast<const int8_t*>(row)[c];
+        v = code * __half2float(a.x_scales[r * xs_groups + c / a.x_group]);
+      } else {
+        v = to_f32<T>(row[c]);
+        if (a.flags & KSD8_Q_ROUND_F16) v = round_f16(v);
+      }
+    }
+    tile[rr][cc] = v;
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  const int64_t rgroups = (a.rows + 127) / 128;
+  for (int cc = warp; cc < QC_TC; cc += 8) {
+    const int64_t c = c0 + cc;
+    if (c >= a.cols) break;
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = tile[lane + 32 * i][cc];
+    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    m = warp_max(m);
+    __half sh;
+    const float scale = gs_scale(m, &sh);
+    int8_t* out = a.codes_t + c * a.ldct + r0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t r = r0 + lane + 32 * i;
+      if (r < a.rows) out[lane + 32 * i] = (int8_t)gs_code(v[i], scale);
+    }
+    if (lane == 0) a.scales_t[c * rgroups + blockIdx.y] = sh;
+  }
+}
+
+__global__ void philox_uniform_kernel(uint64_t seed, uint64_t offset, int64_t n, float* out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = philox_uniform(seed, offset + i);
+}
+
+}  // namespace ksd8
+
+using namespace ksd8;
+
+static int grid_for(int64_t work_items, int per_block, int max_blocks = 148 * 16) {
+  int64_t b = (work_items + per_block - 1) / per_block;
+  if (b < 1) b = 1;
+  if (b > max_blocks) b = max_blocks;
+  return (int)b;
+}
+
+int ksd8_quantize_rows_launch(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t ldx,
+                              int group, int flags, float dither, uint64_t seed, uint64_t offset,
+                              int8_t* codes, int64_t ldc, void* scales, cudaStream_t stream) {
+  QRowArgs a;
+  a.x = x; a.rows = rows; a.k = k; a.ldx = ldx; a.ldc = ldc; a.group = group; a.flags = flags;
+  a.dither2 = 2.0f * dither; a.seed = seed; a.offset = offset; a.codes = codes;
+  a.scales = reinterpret_cast<__half*>(scales);
+  const int64_t work = rows * ((k + 127) / 128);
+  if (work == 0) return KSD8_OK;
+  const int blocks = grid_for(work, 8);
+  switch (x_dtype) {
+    case KSD8_F32: quantize_rows_kernel<float><<<blocks, 256, 0, stream>>>(a); break;
+    case KSD8_F16: quantize_rows_kernel<__half><<<blocks, 256, 0, stream>>>(a); break;
+    case KSD8_BF16: quantize_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(a); break;
+    default: return KSD8_ERR_DTYPE;
+  }
+  return KSD8_OK;
+}
+
+int ksd8_quantize_cols_launch(const void* x, int x_dtype, const void* x_scales, int x_group,
+                              int64_t rows, int64_t cols, int64_t ldx, int flags, int8_t* codes_t,
+                              int64_t ldct, void* scales_t, cudaStream_t stream) {
+  QColArgs a;
+  a.x = x; a.x_scales = reinterpret_cast<const __half*>(x_scales); a.x_group = x_group;
+  a.rows = rows; a.cols = cols; a.ldx = ldx; a.ldct = ldct; a.flags = flags;
+  a.codes_t = codes_t; a.scales_t = reinterpret_cast<__half*>(scales_t);
+  if (rows == 0 || cols == 0) return KSD8_OK;
+  dim3 grid((unsigned)((cols + QC_TC - 1) / QC_TC), (unsigned)((rows + QC_TR - 1) / QC_TR));
+  switch (x_dtype) {
+    case KSD8_F32: quantize_cols_kernel<float, false><<<grid, 256, 0, stream>>>(a); break;
+    case KSD8_F16: quantize_cols_kernel<__half, false><<<grid, 256, 0, stream>>>(a); break;
+    case KSD8_BF16: quantize_cols_kernel<__nv_bfloat16, false><<<grid, 256, 0, stream>>>(a); break;
+    case KSD8_I8: quantize_cols_kernel<int8_t, true><<<grid, 256, 0, stream>>>(a); break;
+    default: return KSD8_ERR_DTYPE;
+  }
+  return KSD8_OK;
+}
+
+int ksd8_philox_launch(uint64_t seed, uint64_t offset, int64_t n, float* out, cudaStream_t stream) {
+  if (n == 0) return KSD8_OK;
+  philox_uniform_kernel<<<grid_for(n, 256), 256, 0, stream>>>(seed, offset, n, out);
+  return KSD8_OK;
+}

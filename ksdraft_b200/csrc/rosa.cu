@@ -1,0 +1,323 @@
+// Rosa 1-bit hard-retrieval mixer kernels (ksdraft/model/rosa.py).
+//
+//  rosa_pack_bits_kernel   bits = x > 0 packed 64 per word, per stream
+//                          (rosa.py:156-158 and the int8 inputs of :40).
+//  rosa_match_kernel       _match_payload_sign (rosa.py:40-98): for every t the
+//                          longest suffix match L <= max_len (the reference's
+//                          62-bit cap is part of the semantics) against key
+//                          suffixes ending at j in [L-1, t-1], the latest such j,
+//                          sign = v[j+1] ? +1 : -1, -1 without a match; the
+//                          payload multiply of :164 is fused into the store.
+//  rosa_timemix_quant_kernel _shifted (rosa.py:128-133) fused with the per-token
+//                          GS128 quantisation Int8Linear.forward applies to the
+//                          q/k/v projection inputs (linear.py:69).
+//
+// Match algorithm: the 64 most recent bits ending at t form a window word
+// W(t) with bit 63 = x[t], bit 62 = x[t-1], ...; the common-suffix length of
+// q at t and k at j is clz(Wq(t) ^ Wk(j)), capped at min(max_len, j+1).  One
+// CTA owns one stream: all key windows Wk(j) sit in shared memory, a warp
+// owns 32 consecutive positions t and walks j downwards in lockstep so the
+// Wk(j) reads are broadcasts.  The first j that reaches a length is the
+// latest one, so only strictly longer matches replace the current best;
+// a lane stops once best == min(max_len, t) and the warp stops when no lane
+// can still improve (remaining j are too short: length <= j+1).
+#include "common.cuh"
+
+namespace ksd8 {
+
+template <typename T>
+__device__ __forceinline__ bool positive(T v);
+template <>
+__device__ __forceinline__ bool positive<float>(float v) { return v > 0.f; }
+template <>
+__device__ __forceinline__ bool positive<__half>(__half v) { return __half2float(v) > 0.f; }
+template <>
+__device__ __forceinline__ bool positive<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v) > 0.f;
+}
+template <>
+__device__ __forceinline__ bool positive<int8_t>(int8_t v) { return v > 0; }
+
+// One thread per (word, stream); consecutive threads take consecutive streams
+// so that reads of a (B, T, S) layout are coalesced along S.
+template <typename T>
+__global__ void rosa_pack_bits_kernel(const T* x, int64_t batch, int64_t t_len, int64_t streams,
+                                      int64_t sb, int64_t st, int64_t ss, uint64_t* words) {
+  const int64_t nw = (t_len + 63) / 64;
+  const int64_t total = batch * streams * nw;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t s = i % streams;
+    const int64_t rest = i / streams;
+    const int64_t w = rest % nw;
+    const int64_t b = rest / nw;
+    const T* base = x + b * sb + s * ss;
+    uint64_t word = 0;
+    const int64_t t0 = w * 64;
+    const int n = (int)min((int64_t)64, t_len - t0);
+    for (int k = 0; k < n; ++k)
+      if (positive<T>(base[(t0 + k) * st])) word |= (1ull << k);
+    words[((b * streams + s) * nw) + w] = word;
+  }
+}
+
+// W(t): bits x[t-63 .. t], x[t] at bit 63; positions before 0 read as 0.
+__device__ __forceinline__ uint64_t window_at(const uint64_t* w, int64_t t) {
+  const int64_t wi = t >> 6;
+  const int sh = (int)(t & 63) + 1;  // 1..64
+  const uint64_t hi = w[wi];
+  const uint64_t lo = wi > 0 ? w[wi - 1] : 0ull;
+  return sh == 64 ? hi : ((lo >> sh) | (hi << (64 - sh)));
+}
+
+struct MatchArgs {
+  const uint64_t* qw;
+  const uint64_t* kw;
+  const uint64_t* vw;
+  int64_t batch, streams, t_len;
+  int max_len;
+  const float* payload;
+  void* out;
+  int out_dtype;
+  int64_t ob, ot, os;
+  int32_t* match_len;
+  int32_t* match_end;
+};
+
+__global__ void __launch_bounds__(512) rosa_match_kernel(MatchArgs a) {
+  extern __shared__ uint64_t sk[];  // Wk(j), j = 0 .. T-1
+  const int64_t stream = blockIdx.x;
+  const int64_t T = a.t_len;
+  const int64_t nw = (T + 63) / 64;
+  const uint64_t* qw = a.qw + stream * nw;
+  const uint64_t* kw = a.kw + stream * nw;
+  const uint64_t* vw = a.vw + stream * nw;
+  for (int64_t j = threadIdx.x; j < T; j += blockDim.x) sk[j] = window_at(kw, j);
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int64_t nblk = (T + 31) / 32;
+  const int64_t b = stream / a.streams, s = stream % a.streams;
+  const float pay = a.payload ? a.payload[s] : 1.f;
+  // Zig-zag assignment of 32-position blocks keeps the (t-proportional) work balanced.
+  for (int64_t round = 0; round * nwarps < nblk; ++round) {
+    const int64_t blk = (round & 1) ? ((round + 1) * nwarps - 1 - warp) : (round * nwarps + warp);
+    if (blk >= nblk) continue;
+    const int64_t t = blk * 32 + lane;
+    const bool valid = t < T;
+    const uint64_t wq = valid ? window_at(qw, t) : 0ull;
+    // longest achievable length at t: min(max_len, t) (j <= t-1 gives L <= t)
+    const int cap_t = valid ? (int)min((int64_t)a.max_len, t) : 0;
+    int best = 0;
+    int64_t bestj = -1;
+    // mask of the top (best+1) bits: a key window improves iff they all match
+    uint64_t mask = 1ull << 63;
+    int64_t j = min(blk * 32 + 31, T - 1) - 1;
+    for (; j >= 0; --j) {
+      const uint64_t x = wq ^ sk[j];
+      if (j < t && best < cap_t && (x & mask) == 0ull && j >= best) {
+        int l = x == 0ull ? 64 : __clzll((long long)x);
+        const int capj = (int)min((int64_t)cap_t, j + 1);
+        l = min(l, capj);
+        if (l > best) {
+          best = l;
+          bestj = j;
+          mask = best >= 63 ? ~0ull : ~((~0ull) >> (best + 1));
+        }
+      }
+      if ((j & 31) == 0) {
+        // stop when no lane can still find a longer match among j' < j
+        const bool can = valid && best < cap_t && (j - 1) >= best;
+        if (!__any_sync(0xffffffffu, can)) break;
+      }
+    }
+    if (valid) {
+      float sign = -1.f;
+      if (bestj >= 0) {
+        const int64_t succ = bestj + 1;
+        sign = ((vw[succ >> 6] >> (succ & 63)) & 1ull) ? 1.f : -1.f;
+      }
+      const float o = pay * sign;
+      const int64_t off = b * a.ob + t * a.ot + s * a.os;
+      if (a.out_dtype == KSD8_F32)
+        reinterpret_cast<float*>(a.out)[off] = o;
+      else if (a.out_dtype == KSD8_BF16)
+        reinterpret_cast<__nv_bfloat16*>(a.out)[off] = __float2bfloat16_rn(o);
+      else
+        reinterpret_cast<__half*>(a.out)[off] = __float2half_rn(o);
+      if (a.match_len) a.match_len[stream * T + t] = best;
+      if (a.match_end) a.match_end[stream * T + t] = (int32_t)bestj;
+    }
+  }
+}
+
+struct TimemixArgs {
+  const void* x;
+  int64_t batch, t_len, d;
+  const float* mix[3];
+  int8_t* codes[3];
+  __half* scales[3];
+};
+
+// One warp per (token, 128-wide group); lane owns 4 consecutive features.
+template <typename T>
+__global__ void __launch_bounds__(256) rosa_timemix_quant_kernel(TimemixArgs a) {
+  const int64_t groups = (a.d + 127) / 128;
+  const int64_t tokens = a.batch * a.t_len;
+  const int64_t total = tokens * groups;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const T* x = reinterpret_cast<const T*>(a.x);
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total;
+       w += nwarps) {
+    const int64_t tok = w / groups, g = w - tok * groups;
+    const int64_t t = tok % a.t_len;
+    const int64_t c = g * 128 + lane * 4;
+    float cur[4], prev[4], diff[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const bool in = c + i < a.d;
+      cur[i] = in ? (float)x[tok * a.d + c + i] : 0.f;
+      prev[i] = (in && t > 0) ? (float)x[(tok - 1) * a.d + c + i] : 0.f;
+      // (x - prev) is evaluated in x's dtype
+      if constexpr (sizeof(T) == 2) diff[i] = (float)(T)(cur[i] - prev[i]);
+      else diff[i] = cur[i] - prev[i];
+    }
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float mix = (c + i < a.d) ? a.mix[p][c + i] : 0.f;
+        v[i] = __fadd_rn(prev[i], __fmul_rn(diff[i], mix));
+      }
+      float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+      m = warp_max(m);
+      __half sh;
+      const float scale = gs_scale(m, &sh);
+      int8_t* out = a.codes[p] + tok * a.d + c;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (c + i < a.d) out[i] = (int8_t)gs_code(v[i], scale);
+      if (lane == 0) a.scales[p][tok * groups + g] = sh;
+    }
+  }
+}
+
+__global__ void adamw_kernel(float* p, const void* g, int gdt, float* m, float* v, int64_t n,
+                             float lr, float b1, float b2, float eps, float wd, float bc1,
+                             float bc2_sqrt) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float gr = gdt == KSD8_F16 ? __half2float(reinterpret_cast<const __half*>(g)[i])
+                     : gdt == KSD8_BF16
+                         ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[i])
+                         : reinterpret_cast<const float*>(g)[i];
+    float pi = p[i] * (1.f - lr * wd);
+    const float mi = b1 * m[i] + (1.f - b1) * gr;
+    const float vi = b2 * v[i] + (1.f - b2) * gr * gr;
+    m[i] = mi;
+    v[i] = vi;
+    const float denom = sqrtf(vi) / bc2_sqrt + eps;
+    pi -= (lr / bc1) * mi / denom;
+    p[i] = pi;
+  }
+}
+
+}  // namespace ksd8
+
+using namespace ksd8;
+
+int ksd8_rosa_pack_bits_launch(const void* x, int x_dtype, int64_t batch, int64_t t_len,
+                               int64_t streams, int64_t sb, int64_t st, int64_t ss,
+                               uint64_t* words, cudaStream_t stream) {
+  const int64_t total = batch * streams * ((t_len + 63) / 64);
+  if (total == 0) return KSD8_OK;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  switch (x_dtype) {
+    case KSD8_F32:
+      rosa_pack_bits_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(
+          reinterpret_cast<const float*>(x), batch, t_len, streams, sb, st, ss, words);
+      break;
+    case KSD8_F16:
+      rosa_pack_bits_kernel<__half><<<(unsigned)blocks, 256, 0, stream>>>(
+          reinterpret_cast<const __half*>(x), batch, t_len, streams, sb, st, ss, words);
+      break;
+    case KSD8_BF16:
+      rosa_pack_bits_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(
+          reinterpret_cast<const __nv_bfloat16*>(x), batch, t_len, streams, sb, st, ss, words);
+      break;
+    case KSD8_I8:
+      rosa_pack_bits_kernel<int8_t><<<(unsigned)blocks, 256, 0, stream>>>(
+          reinterpret_cast<const int8_t*>(x), batch, t_len, streams, sb, st, ss, words);
+      break;
+    default:
+      return KSD8_ERR_DTYPE;
+  }
+  return KSD8_OK;
+}
+
+int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
+                           int64_t batch, int64_t streams, int64_t t_len, int max_len,
+                           const float* payload, void* out, int out_dtype, int64_t ob, int64_t ot,
+                           int64_t os, int32_t* match_len, int32_t* match_end,
+                           cudaStream_t stream) {
+  if (batch * streams == 0 || t_len == 0) return KSD8_OK;
+  const size_t smem = (size_t)t_len * 8;
+  static int attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 48 * 1024 && !(attr_dev_mask & (1 << dev))) {
+    if (cudaFuncSetAttribute(rosa_match_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024) != cudaSuccess)
+      return KSD8_ERR_LAUNCH;
+    attr_dev_mask |= (1 << dev);
+  }
+  MatchArgs a;
+  a.qw = qw; a.kw = kw; a.vw = vw; a.batch = batch; a.streams = streams; a.t_len = t_len;
+  a.max_len = max_len; a.payload = payload; a.out = out; a.out_dtype = out_dtype;
+  a.ob = ob; a.ot = ot; a.os = os; a.match_len = match_len; a.match_end = match_end;
+  int threads = 512;
+  if (t_len <= 256) threads = 256;
+  rosa_match_kernel<<<(unsigned)(batch * streams), threads, smem, stream>>>(a);
+  return KSD8_OK;
+}
+
+int ksd8_rosa_timemix_launch(const void* x, int x_dtype, int64_t batch, int64_t t_len, int64_t d,
+                             const float* mq, const float* mk, const float* mv, int8_t* qc,
+                             void* qs, int8_t* kc, void* ks, int8_t* vc, void* vs,
+                             cudaStream_t stream) {
+  TimemixArgs a;
+  a.x = x; a.batch = batch; a.t_len = t_len; a.d = d;
+  a.mix[0] = mq; a.mix[1] = mk; a.mix[2] = mv;
+  a.codes[0] = qc; a.codes[1] = kc; a.codes[2] = vc;
+  a.scales[0] = reinterpret_cast<__half*>(qs);
+  a.scales[1] = reinterpret_cast<__half*>(ks);
+  a.scales[2] = reinterpret_cast<__half*>(vs);
+  const int64_t work = batch * t_len * ((d + 127) / 128);
+  if (work == 0) return KSD8_OK;
+  int64_t blocks = (work + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  switch (x_dtype) {
+    case KSD8_F32: rosa_timemix_quant_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(a); break;
+    case KSD8_BF16:
+      rosa_timemix_quant_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(a);
+      break;
+    case KSD8_F16: rosa_timemix_quant_kernel<__half><<<(unsigned)blocks, 256, 0, stream>>>(a); break;
+    default: return KSD8_ERR_DTYPE;
+  }
+  return KSD8_OK;
+}
+
+int ksd8_adamw_launch(float* p, const void* g, int gdt, float* m, float* v, int64_t n, float lr,
+                      float b1, float b2, float eps, float wd, int step, cudaStream_t stream) {
+  if (n == 0) return KSD8_OK;
+  const float bc1 = 1.f - powf(b1, (float)step);
+  const float bc2 = 1.f - powf(b2, (float)step);
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  adamw_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p, g, gdt, m, v, n, lr, b1, b2, eps, wd, bc1,
+                                                      sqrtf(bc2));
+  return KSD8_OK;
+}

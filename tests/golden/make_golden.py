@@ -1,0 +1,250 @@
+"""Generate the golden fixtures of tests/golden/ by running the REFERENCE itself.
+
+    python tests/golden/make_golden.py [--ref /path/to/ksdraft-checkout]
+
+Imports the reference package (curvedinf/ksdraft) read-only and runs its own
+CPU tier on seeded inputs; writes one compressed .npz per topic.  Only this
+container has the reference checkout, so the fixtures are committed and the
+GPU box never needs the reference at run time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def f16(t):
+    return t.detach().cpu().to(torch.float16).numpy()
+
+
+def f32(t):
+    return t.detach().cpu().float().numpy()
+
+
+def i8(t):
+    return t.detach().cpu().to(torch.int8).numpy()
+
+
+def save(name, **arrays):
+    np.savez_compressed(HERE / f"{name}.npz", **arrays)
+    print(f"wrote {name}.npz ({(HERE / f'{name}.npz').stat().st_size / 1e6:.2f} MB)")
+
+
+def gen_quant():
+    from ksdraft.kernels.quant import quantize_last_dim
+    g = torch.Generator().manual_seed(0)
+    cases = {
+        "randn3": torch.randn(64, 256, generator=g) * 3,
+        "partial": torch.randn(4, 100, generator=g),
+        "partial2": torch.randn(7, 300, generator=g) * 0.1,
+        "zeros": torch.zeros(2, 128),
+        "tiny": torch.randn(3, 256, generator=g) * 1e-9,
+        "huge": torch.randn(3, 256, generator=g) * 1e7,
+        "mixed": torch.cat([torch.randn(5, 128, generator=g) * 10 ** e for e in range(-4, 5)]),
+        "ties": (torch.randint(-254, 255, (16, 128), generator=g).float() * 0.5),
+    }
+    out = {}
+    for name, x in cases.items():
+        c, s = quantize_last_dim(x)
+        out[f"{name}_x"] = f32(x)
+        out[f"{name}_codes"] = i8(c)
+        out[f"{name}_scales"] = f16(s)
+    xb = (torch.randn(9, 384, generator=g) * 2).to(torch.bfloat16)
+    c, s = quantize_last_dim(xb)
+    out["bf16_x"] = f32(xb)
+    out["bf16_codes"], out["bf16_scales"] = i8(c), f16(s)
+    xh = (torch.randn(9, 384, generator=g) * 2).to(torch.float16)
+    c, s = quantize_last_dim(xh)
+    out["f16_x"] = f32(xh)
+    out["f16_codes"], out["f16_scales"] = i8(c), f16(s)
+    save("quant", **out)
+
+
+def gen_dither():
+    from ksdraft.train.stages import quantize_last_dim_dithered
+    out = {}
+    for i, (shape, dither) in enumerate((((8, 256), 0.5), ((5, 300), 0.25), ((4, 128), 1.0))):
+        x = torch.randn(*shape, generator=torch.Generator().manual_seed(10 + i)) * 3
+        Kp = (shape[1] + 127) // 128 * 128
+        u = torch.rand((shape[0], Kp // 128, 128), generator=torch.Generator().manual_seed(99 + i))
+        c, s = quantize_last_dim_dithered(x, 128, dither,
+                                          generator=torch.Generator().manual_seed(99 + i))
+        out[f"c{i}_x"], out[f"c{i}_u"] = f32(x), f32(u.reshape(shape[0], Kp))
+        out[f"c{i}_codes"], out[f"c{i}_scales"] = i8(c), f16(s)
+        out[f"c{i}_dither"] = np.float32(dither)
+    save("dither", **out)
+
+
+def gen_gemm():
+    from ksdraft.kernels.gemm import w8a8_gemm
+    from ksdraft.kernels.quant import quantize_last_dim
+    out = {}
+    # seed 0, A ~ N(0,1) [256,1536], W ~ N(0,0.02) [1536,1536]
+    torch.manual_seed(0)
+    A = torch.randn(256, 1536)
+    W = torch.randn(1536, 1536) * 0.02
+    ac, as_ = quantize_last_dim(A)
+    wc, ws = quantize_last_dim(W)
+    y = w8a8_gemm(ac, as_, wc, ws)
+    # inputs are regenerated from the seed by the tests (torch CPU RNG); the
+    # fixture keeps digests of the reference's codes/scales and 64 output rows
+    import hashlib
+    for name, t in (("ac", i8(ac)), ("as", f16(as_)), ("wc", i8(wc)), ("ws", f16(ws))):
+        out[f"cfg1_{name}_sha256"] = np.frombuffer(
+            hashlib.sha256(np.ascontiguousarray(t).tobytes()).digest(), np.uint8)
+    out.update(cfg1_y64=f32(y[:64]), cfg1_y_sum=np.float64(y.double().sum()),
+               cfg1_y_sqsum=np.float64(y.double().square().sum()))
+    # shapes of tests/test_int8.py:73 (incl. partial groups via padding)
+    g = torch.Generator().manual_seed(3)
+    for i, (M, K, N) in enumerate(((16, 256, 128), (64, 128, 96), (33, 384, 64), (128, 128, 128),
+                                   (5, 200, 24))):
+        a = torch.randn(M, K, generator=g)
+        w = torch.randn(N, K, generator=g) * 0.1
+        ac, as_ = quantize_last_dim(a)
+        wc, ws = quantize_last_dim(w)
+        y = w8a8_gemm(ac, as_, wc, ws)
+        out.update({f"s{i}_ac": i8(ac), f"s{i}_as": f16(as_), f"s{i}_wc": i8(wc),
+                    f"s{i}_ws": f16(ws), f"s{i}_y": f32(y)})
+    save("gemm", **out)
+
+
+def gen_ks3():
+    from ksdraft.kernels.ks3_int8 import KS3Int8Cell, make_tanh_lut, pack_spine
+    from ksdraft.kernels.quant import quantize_last_dim
+    from ksdraft.model.ks3 import KS3
+    out = {"lut": i8(make_tanh_lut("cpu"))}
+    torch.manual_seed(0)
+    cell = KS3(128, 256)
+    with torch.no_grad():
+        cell.coefficients.normal_(0, 0.3)
+        cell.raw_scale.uniform_(-2.0, 3.0)
+        cell.raw_shift.uniform_(-2.0, 2.0)
+        cell.raw_scale[:4] = torch.tensor([25.0, -30.0, 0.0, 20.0])
+    # pack: spine rows + warp scalars
+    sq, ss = pack_spine(cell.coefficients.detach().float())
+    out.update(coefficients=f32(cell.coefficients), raw_scale=f32(cell.raw_scale),
+               raw_shift=f32(cell.raw_shift), spine_codes=i8(sq), spine_scale=f16(ss))
+    for mode in ("int8", "fp16", "fp32"):
+        q = KS3Int8Cell(cell, group=128, nonlinear=mode)
+        if mode == "int8":
+            out.update(ws_codes=i8(q.warp_scale_codes), ws_scales=f16(q.warp_scale_scales),
+                       wh_codes=i8(q.warp_shift_codes), wh_scales=f16(q.warp_shift_scales))
+        # coordinates: random fp16 over the LUT range and beyond, plus edge values
+        gen = torch.Generator().manual_seed(5)
+        M = 96
+        coords = (torch.randn(M, 256, generator=gen) * 6).to(torch.float16)
+        edge = torch.tensor([0.0, -0.0, 3.2, -3.2, 12.8, -12.8, 12.796875, 65504.0, -65504.0,
+                             1e-5, -1e-5, 6e-8, 0.25, 0.5, 1.0, 127.0], dtype=torch.float16)
+        coords[:16, :16] = edge[None, :].expand(16, 16)
+        coords[16:32, :16] = edge[:, None].expand(16, 16)
+        x = coords.float().reshape(M, 256, 1)
+        c_all = q.spine_codes.reshape(256, 6)
+        cs = [c_all[:, i].reshape(256, 1) for i in range(6)]
+        ps = q.spine_scale.reshape(256)
+        arith = torch.float32 if mode == "fp32" else torch.float16
+        scale, shift = q._warp_scalars(arith)
+        h = q._spine_features(x, x, *cs, ps, scale, shift).reshape(M, 256)
+        hq, hs = quantize_last_dim(h)
+        out.update({f"{mode}_coords": f16(coords), f"{mode}_h": f32(h), f"{mode}_hq": i8(hq),
+                    f"{mode}_hs": f16(hs)})
+    save("ks3_spine", **out)
+
+
+def gen_ks3_layer():
+    """_KS3Int8Train fwd+bwd (the reference's composed CPU path), small shape."""
+    from ksdraft.kernels.gemm import w8a8_gemm
+    from ksdraft.kernels.ks3_int8 import KS3Int8Cell
+    from ksdraft.kernels.quant import dequantize_last_dim, quantize_last_dim
+    from ksdraft.model.ks3 import KS3
+    torch.manual_seed(1)
+    d, C, M = 256, 384, 256
+    cell = KS3(d, C)
+    with torch.no_grad():
+        cell.down.weight.normal_(0, 0.02)
+        cell.up.weight.normal_(0, 0.02)
+    q = KS3Int8Cell(cell, group=128, nonlinear="int8", trainable=True)
+    x = torch.randn(M, d).to(torch.bfloat16).requires_grad_(True)
+    gout = (torch.randn(M, d) * 1e-2).to(torch.bfloat16)
+    y = q(x)
+    y.backward(gout)
+    out = dict(x=f32(x), grad=f32(gout), down=f32(q.master_down), up=f32(q.master_up),
+               coefficients=f32(q.master_coefficients), raw_scale=f32(q.master_raw_scale),
+               raw_shift=f32(q.master_raw_shift), y=f32(y), dx=f32(x.grad),
+               ddown=f32(q.master_down.grad), dup=f32(q.master_up.grad),
+               dcoeff=f32(q.master_coefficients.grad), dscale=f32(q.master_raw_scale.grad),
+               dshift=f32(q.master_raw_shift.grad))
+    # intermediates, recomputed with the reference's own functions (ks3_int8.py:326-424)
+    with torch.no_grad():
+        xq, xs = quantize_last_dim(x.detach().float())
+        coords = w8a8_gemm(xq, xs, q.down_codes, q.down_scales).to(torch.float16) \
+            .clamp(-65504.0, 65504.0)
+        hfeat, _ = q._project(xq, xq, xs, q.down_codes, q.down_scales)
+        hq, hs = quantize_last_dim(hfeat)
+        g16 = gout.float().to(torch.float16)
+        gq, gs = quantize_last_dim(g16.float())
+        upT = quantize_last_dim(dequantize_last_dim(q.up_codes, q.up_scales).t().contiguous())
+        value = w8a8_gemm(gq, gs, *upT).to(torch.float16)
+    out.update(xq=i8(xq), xs=f16(xs), coords=f16(coords), hq=i8(hq), hs=f16(hs), gq=i8(gq),
+               gs=f16(gs), upT_q=i8(upT[0]), upT_s=f16(upT[1]), value=f16(value),
+               down_q=i8(q.down_codes), down_s=f16(q.down_scales), up_q=i8(q.up_codes),
+               up_s=f16(q.up_scales))
+    save("ks3_layer", **out)
+
+
+def gen_rosa():
+    from ksdraft.model.rosa import _match_payload_sign
+    out = {}
+    g = torch.Generator().manual_seed(7)
+    # random short streams (tests/test_rosa.py:39-49 regime) batched by length
+    for T in (1, 2, 3, 5, 9, 16):
+        q = torch.randint(0, 2, (24, T), generator=g, dtype=torch.int8)
+        k = torch.randint(0, 2, (24, T), generator=g, dtype=torch.int8)
+        v = torch.randint(0, 2, (24, T), generator=g, dtype=torch.int8)
+        s = _match_payload_sign(q, k, v)
+        out.update({f"T{T}_q": i8(q), f"T{T}_k": i8(k), f"T{T}_v": i8(v), f"T{T}_sign": f32(s)})
+    # long streams with repeated spans: matches longer than the 62-bit cap
+    T, S = 160, 6
+    q = torch.randint(0, 2, (S, T), generator=g, dtype=torch.int8)
+    k = q.clone()
+    k[:, 100:] = torch.randint(0, 2, (S, 60), generator=g, dtype=torch.int8)
+    k[1] = torch.randint(0, 2, (T,), generator=g, dtype=torch.int8)
+    k[2, :80] = q[2, 80:]
+    q[3] = 0
+    k[3] = 0
+    v = torch.randint(0, 2, (S, T), generator=g, dtype=torch.int8)
+    chunks = [_match_payload_sign(q[i:i + 1], k[i:i + 1], v[i:i + 1]) for i in range(S)]
+    out.update(long_q=i8(q), long_k=i8(k), long_v=i8(v), long_sign=f32(torch.cat(chunks)))
+    # explicit max_match_len
+    s5 = torch.cat([_match_payload_sign(q[i:i + 1], k[i:i + 1], v[i:i + 1], max_match_len=5)
+                    for i in range(S)])
+    out.update(long_sign_ml5=f32(s5))
+    # hand case of tests/test_rosa.py:25-36
+    out.update(hand_q=np.array([[0, 1, 1, 1]], np.int8), hand_k=np.array([[1, 0, 1, 1]], np.int8),
+               hand_v=np.array([[1, 0, 0, 1]], np.int8),
+               hand_sign=np.array([[-1.0, -1.0, -1.0, 1.0]], np.float32))
+    save("rosa", **out)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, args.ref)
+    torch.set_num_threads(8)
+    gen_quant()
+    gen_dither()
+    gen_gemm()
+    gen_ks3()
+    gen_ks3_layer()
+    gen_rosa()
+
+
+if __name__ == "__main__":
+    main()
