@@ -1,0 +1,351 @@
+"""Benchmark: KSDraft INT8 training step of one KS3 decoder layer.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+
+Workload (per GPU, weak scaling): one KS3 decoder layer at d_model=1536 with
+5888 charts, 4096 tokens (batch 8 x seq 512), INT8-native forward + backward
+(W8A8 GS128 forward, dgrad and wgrad GEMMs, fused spine / VJP cell), PTQR
+dither 0.5 LSB on the weight quantisation from a counter RNG, then the
+data-parallel gradient all-reduce (NCCL, N > 1) and an AdamW step on the fp32
+masters.  Inputs are synthetic: hidden states bf16 N(0,1), upstream gradient
+bf16 N(0,1e-2), weights N(0,0.02) (canonical KS3 init for the spine).
+
+`value`  tokens/s of the whole job with inputs resident in HBM, device-timed
+         with CUDA events per step (L2 flushed between steps), max over ranks.
+`e2e`    the same step through the public API with pinned host inputs copied
+         in and the layer output copied out inside the timed region.
+`roofline` the W8A8 GEMM (the dominant kernel): algorithmic ops per launch /
+         its CUDA-event duration inside the timed steps, against 2x the
+         measured dense bf16 peak of MEASURED_PEAKS.json (int8 = 2x bf16 rate).
+`cpu_baseline` / `--impl reference`: the CPU oracle port of the same layer
+         step (oracle/, numpy + C with OpenMP) on a bounded token sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+D_MODEL, CHARTS, TOKENS, BATCH, SEQ = 1536, 5888, 4096, 8, 512
+METRIC = "W8A8 GS128 GEMM TOPS; KSDraft INT8 train tokens/sec at 1/2/4/8 B200"
+DITHER = 0.5
+CPU_SAMPLE_TOKENS = 128
+
+
+def config(n: int) -> dict:
+    return {"workload": "BASELINE config 2: one KS3 decoder layer INT8 fwd+bwd (+DP all-reduce "
+                        "+ AdamW), d_model=1536, charts=5888, 4096 tokens/GPU",
+            "model": "KSDraft KS3 decoder layer (d_model=1536, charts=5888)",
+            "global_batch": BATCH * n, "seq_len": SEQ, "tokens_per_gpu": TOKENS,
+            "parallelism": f"dp{n}", "ptqr_dither": DITHER,
+            "l2": "flushed between timed steps (256 MiB write); step working set > L2"}
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16": float(d["bf16_tflops"]), "hbm": float(d["hbm_gbs"]), "src": "measured"}
+    return {"bf16": 1590.0, "hbm": 6650.0, "src": "fallback"}
+
+
+def gemm_traffic() -> float | None:
+    p = ROOT / "profiles" / "gemm_traffic.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bytes_per_launch"])
+    return None
+
+
+# ---------------------------------------------------------------- CPU side
+
+def cpu_layer_inputs(tokens: int, seed: int = 0):
+    rng = np.random.default_rng(seed)
+    import torch
+    x = torch.from_numpy(rng.standard_normal((tokens, D_MODEL)).astype(np.float32)) \
+        .to(torch.bfloat16).float().numpy()
+    g = torch.from_numpy((rng.standard_normal((tokens, D_MODEL)) * 1e-2).astype(np.float32)) \
+        .to(torch.bfloat16).float().numpy()
+    down = (rng.standard_normal((CHARTS, D_MODEL)) * 0.02).astype(np.float32)
+    up = (rng.standard_normal((D_MODEL, CHARTS)) * 0.02).astype(np.float32)
+    coeffs = (rng.standard_normal((CHARTS, 6)) * 0.05).astype(np.float32)
+    rs = np.full(CHARTS, 0.75, np.float32)
+    rh = np.zeros(CHARTS, np.float32)
+    return x, down, up, coeffs, rs, rh, g
+
+
+def cpu_baseline(steps: int = 2, warmup: int = 1, tokens: int = CPU_SAMPLE_TOKENS) -> dict:
+    """Time the oracle port of the layer step on the host cores (bounded sample)."""
+    from oracle import oracle
+    args = cpu_layer_inputs(tokens)
+    for _ in range(warmup):
+        oracle.ks3_layer(*args)
+    t = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        oracle.ks3_layer(*args)
+        t.append(time.perf_counter() - t0)
+    sec = statistics.median(t)
+    return {"value": tokens / sec, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{tokens} tokens of the config-2 layer step (fwd+bwd, 6 W8A8 GEMMs + "
+                      f"quantisers + spine/VJP), median of {steps}, oracle C+numpy, OpenMP",
+            "sec_per_sample": sec}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps = max(1, args.steps)
+    cb = cpu_baseline(steps=steps, warmup=max(1, min(args.warmup, 2)))
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": cb["sec_per_sample"] * 1e3 * TOKENS / CPU_SAMPLE_TOKENS,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": config(args.gpus),
+            "cpu_baseline": {k: cb[k] for k in ("kind", "cores", "sample", "value", "unit")},
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU side
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        loaded = [s for s in sm if s > 500] or sm
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit()
+                else None, "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from ksdraft_b200 import _lib
+    from ksdraft_b200.kernels.gemm import GemmTimer
+    from ksdraft_b200.kernels.ks3_int8 import KS3Int8Cell
+    from ksdraft_b200.model.ks3 import KS3
+    from ksdraft_b200.train.dp import KS3DataParallelStep, init_distributed
+
+    rank, world, local = init_distributed(timeout_s=300)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    torch.manual_seed(1234)                         # same weights on every rank
+    cell = KS3(D_MODEL, CHARTS)
+    with torch.no_grad():
+        cell.down.weight.normal_(0, 0.02)
+        cell.up.weight.normal_(0, 0.02)
+    q = KS3Int8Cell(cell.to(dev), nonlinear="int8", trainable=True)
+    q._dither = DITHER
+    q._dither_seed = 20260101
+    step = KS3DataParallelStep(q)
+
+    gen = torch.Generator().manual_seed(1000 + rank)  # each rank its own tokens
+    x_host = torch.randn(TOKENS, D_MODEL, generator=gen).to(torch.bfloat16).pin_memory()
+    g_host = (torch.randn(TOKENS, D_MODEL, generator=gen) * 1e-2).to(torch.bfloat16) \
+        .pin_memory()
+    y_host = torch.empty(TOKENS, D_MODEL, dtype=torch.bfloat16).pin_memory()
+    x_dev, g_dev = x_host.to(dev), g_host.to(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(x_dev, g_dev)
+    barrier()
+
+    # ---- device-resident timing (value) + per-GEMM events (roofline)
+    times = []
+    launches0 = _lib.LAUNCHES
+    with ClockSampler(local) as clocks, GemmTimer() as gt:
+        for _ in range(args.steps):
+            flush.zero_()
+            barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            step(x_dev, g_dev)
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+    launches = _lib.LAUNCHES - launches0
+    gemm = gt.durations_ms()
+    total_ms = torch.tensor([sum(times)], device=dev)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    total_ms = float(total_ms.item())
+
+    # ---- end to end through the public API with host buffers
+    e2e_times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        x_dev.copy_(x_host, non_blocking=True)
+        g_dev.copy_(g_host, non_blocking=True)
+        y = step(x_dev, g_dev)
+        y_host.copy_(y.detach(), non_blocking=True)
+        e.record()
+        torch.cuda.synchronize()
+        e2e_times.append(s.elapsed_time(e))
+    e2e_ms = torch.tensor([sum(e2e_times)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    if rank == 0:
+        tokens_total = TOKENS * world * args.steps
+        value = tokens_total / (total_ms / 1e3)
+        peaks = load_peaks()
+        gemm_ms = [d for d, _ in gemm]
+        ops = gemm[0][1] if gemm else 0
+        avg_gemm_ms = statistics.mean(gemm_ms) if gemm_ms else float("nan")
+        achieved = ops / (avg_gemm_ms / 1e3) / 1e12 if gemm_ms else None
+        peak_int8 = 2.0 * peaks["bf16"]
+        traffic = gemm_traffic()
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": config(world),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_int8,
+                         "unit": "TFLOP/s", "frac": achieved / peak_int8 if achieved else None,
+                         "traffic": traffic,
+                         "kernel": "w8a8_gemm_kernel (tcgen05 kind::i8), 6 launches/step of "
+                                   "2*4096*5888*1536 = 74.09 GOP each",
+                         "peak_note": f"2 x {peaks['src']} dense bf16 TF/s (int8 rate = 2x bf16)"
+                         },
+            "gemm": {"launches": len(gemm_ms), "avg_ms": avg_gemm_ms,
+                     "tops": achieved, "ops_per_launch": ops,
+                     "share_of_step": sum(gemm_ms) / sum(times) if times else None},
+            "e2e": {"value": TOKENS * world * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": x_host.numel() * 2 + g_host.numel() * 2,
+                    "d2h_bytes_per_step": y_host.numel() * 2},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = {k: v for k, v in cpu_baseline().items()
+                                    if k != "sec_per_sample"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_profile_case(case: str, iters: int) -> None:
+    """One kernel of the layer step at its config-2 shape, `iters` launches after
+    one warm-up (for ncu captures: small, single-kernel, ends by itself)."""
+    import torch
+
+    from ksdraft_b200.kernels.gemm import gemm_out
+    from ksdraft_b200.kernels.quant import quantize_cols, quantize_last_dim
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    if case == "gemm":
+        a = torch.randint(-127, 128, (TOKENS, D_MODEL), dtype=torch.int8, device=dev, generator=g)
+        w = torch.randint(-127, 128, (CHARTS, D_MODEL), dtype=torch.int8, device=dev, generator=g)
+        sa = (torch.rand(TOKENS, D_MODEL // 128, device=dev, generator=g) * 0.01).half()
+        sw = (torch.rand(CHARTS, D_MODEL // 128, device=dev, generator=g) * 0.01).half()
+        out = torch.empty(TOKENS, CHARTS, dtype=torch.float16, device=dev)
+        fn = lambda: gemm_out(a, sa, w, sw, out=out, clamp_f16=True)  # noqa: E731
+    elif case == "quant":
+        x = torch.randn(TOKENS, CHARTS, device=dev, generator=g)
+        fn = lambda: quantize_last_dim(x)  # noqa: E731
+    elif case == "quant_cols":
+        x = torch.randn(TOKENS, CHARTS, device=dev, generator=g).to(torch.bfloat16)
+        fn = lambda: quantize_cols(x)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown profile case {case}")
+    for _ in range(iters + 1):
+        fn()
+    torch.cuda.synchronize()
+    print(f"profile case {case}: {iters + 1} launches done")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", default=None,
+                    help="run one kernel (gemm | quant | quant_cols) a few times, for ncu")
+    ap.add_argument("--iters", type=int, default=3)
+    args = ap.parse_args()
+    if args.profile_case:
+        run_profile_case(args.profile_case, args.iters)
+        return
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -74,7 +74,14 @@ def status_string(code: int) -> str:
     return load().ksd8_status_string(code).decode()
 
 
+# Number of kernel-launching C-ABI calls made by this process (each compute
+# entry point enqueues exactly one kernel); read by bench.py for gpu_launches.
+LAUNCHES = 0
+
+
 def check(rc: int, what: str) -> None:
+    global LAUNCHES
+    LAUNCHES += 1
     if rc == OK:
         return
     msg = f"{what}: {status_string(rc)}"

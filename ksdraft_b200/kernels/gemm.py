@@ -19,6 +19,27 @@ from .. import _lib
 from .quant import GROUP_SIZE, _check_group
 
 
+class GemmTimer:
+    """Records a CUDA event pair around every GEMM launch while active
+    (on the launching stream); used by bench.py for the roofline figures."""
+
+    active: "GemmTimer | None" = None
+
+    def __init__(self):
+        self.pairs: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
+
+    def __enter__(self):
+        GemmTimer.active = self
+        return self
+
+    def __exit__(self, *exc):
+        GemmTimer.active = None
+
+    def durations_ms(self) -> list[tuple[float, int]]:
+        torch.cuda.synchronize()
+        return [(s.elapsed_time(e), ops) for s, e, ops in self.pairs]
+
+
 def _aligned(t: torch.Tensor) -> torch.Tensor:
     """Contiguous and 16-byte aligned (TMA base-address rule)."""
     if not t.is_contiguous() or t.data_ptr() % 16:
@@ -46,10 +67,17 @@ def gemm_out(a_codes: torch.Tensor, a_scales: torch.Tensor, w_codes: torch.Tenso
         flags |= _lib.EPI_CLAMP_F16
     if status is not None:
         flags |= _lib.EPI_FLAG_NONFINITE
+    timer = GemmTimer.active
+    if timer is not None:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
     rc = _lib.lib().ksd8_w8a8_gemm(
         a_codes.data_ptr(), a_scales.data_ptr(), w_codes.data_ptr(), w_scales.data_ptr(), M, N, K,
         GROUP_SIZE, out.data_ptr(), _lib.dtype_code(out), out.stride(0) if M > 1 else N,
         _lib.ptr(bias), flags, _lib.ptr(status), _lib.stream_ptr(a_codes.device))
+    if timer is not None:
+        ev1.record()
+        timer.pairs.append((ev0, ev1, 2 * M * N * K))
     _lib.check(rc, "w8a8_gemm")
     return out
 

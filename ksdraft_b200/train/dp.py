@@ -1,0 +1,126 @@
+"""Data-parallel training step for INT8 KS3 layers (one process per GPU).
+
+Every rank runs the same INT8 layer forward/backward on its own tokens; the
+gradients of the fp32 masters land in one flat, bucket-aligned buffer (the
+`.grad` of every master is a view into it), which is averaged across ranks
+with a single NCCL all-reduce, then the ksd8 AdamW kernel updates the masters.
+There is no other exchange: the path shards by tokens (weak scaling).
+
+The host-side pieces (flat views, averaging, the failure check before the
+collective) are plain torch and run on CPU `gloo` ranks in the tests.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+
+from .. import _lib
+
+
+class FlatGrads:
+    """Points each parameter's .grad at a slice of one contiguous fp32 buffer."""
+
+    def __init__(self, params: list[torch.nn.Parameter], align: int = 64):
+        self.params = list(params)
+        self.offsets = []
+        off = 0
+        for p in self.params:
+            self.offsets.append(off)
+            off += (p.numel() + align - 1) // align * align
+        self.numel = off
+        dev = self.params[0].device
+        self.buffer = torch.zeros(off, dtype=torch.float32, device=dev)
+        self.attach()
+
+    def attach(self) -> None:
+        for p, off in zip(self.params, self.offsets):
+            p.grad = self.buffer[off:off + p.numel()].view_as(p)
+
+    def zero_(self) -> None:
+        self.buffer.zero_()
+        self.attach()
+
+    def views(self):
+        for p, off in zip(self.params, self.offsets):
+            yield p, self.buffer[off:off + p.numel()]
+
+
+def allreduce_mean_(buffer: torch.Tensor, group=None) -> None:
+    """Average a flat gradient buffer over the ranks of `group` (no-op alone)."""
+    if not dist.is_available() or not dist.is_initialized():
+        return
+    world = dist.get_world_size(group)
+    if world == 1:
+        return
+    dist.all_reduce(buffer, op=dist.ReduceOp.SUM, group=group)
+    buffer.div_(world)
+
+
+def check_finite_across_ranks(buffer: torch.Tensor, group=None) -> bool:
+    """True when every rank's gradients are finite (one small all-reduce of a flag)."""
+    ok = torch.isfinite(buffer).all().to(torch.int32).reshape(1)
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+    return bool(ok.item())
+
+
+class AdamW:
+    """torch.optim.AdamW semantics over fp32 params, one ksd8 kernel launch per tensor."""
+
+    def __init__(self, params, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01):
+        self.params = list(params)
+        self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
+        self.state = [(torch.zeros_like(p), torch.zeros_like(p)) for p in self.params]
+        self.step_count = 0
+
+    @torch.no_grad()
+    def step(self) -> None:
+        self.step_count += 1
+        lib = _lib.lib()
+        for p, (m, v) in zip(self.params, self.state):
+            g = p.grad
+            if g is None:
+                continue
+            g = g.contiguous()
+            rc = lib.ksd8_adamw_step(p.data_ptr(), g.data_ptr(), _lib.dtype_code(g), m.data_ptr(),
+                                     v.data_ptr(), p.numel(), self.lr, self.betas[0],
+                                     self.betas[1], self.eps, self.wd, self.step_count, None,
+                                     _lib.stream_ptr(p.device))
+            _lib.check(rc, "adamw_step")
+
+
+def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
+    """(rank, world, local_rank) from the torchrun environment; NCCL on GPUs."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
+    return rank, world, local
+
+
+class KS3DataParallelStep:
+    """fwd + bwd + gradient all-reduce + AdamW for one trainable KS3Int8Cell."""
+
+    def __init__(self, cell, lr: float = 3e-4):
+        self.cell = cell
+        self.params = [cell.master_down, cell.master_up, cell.master_coefficients,
+                       cell.master_raw_scale, cell.master_raw_shift]
+        self.grads = FlatGrads(self.params)
+        self.opt = AdamW(self.params, lr=lr)
+
+    def __call__(self, x: torch.Tensor, grad_out: torch.Tensor) -> torch.Tensor:
+        self.grads.zero_()
+        x = x.detach().requires_grad_(True)
+        y = self.cell(x)
+        y.backward(grad_out)
+        allreduce_mean_(self.grads.buffer)
+        self.opt.step()
+        return y

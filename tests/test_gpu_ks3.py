@@ -131,7 +131,9 @@ def test_ks3_layer_stages_bit_exact_vs_oracle(golden, oracle):
     dx, ddown, dup, dcoeff, dscale, dshift, _ = ks3_backward(q, gout, xq, xs, hq, hs, coords,
                                                              x.shape)
     # through the VJP, tanhf (CUDA vs glibc) may move an fp16 rounding: tolerance
-    assert _rel(dx.float().cpu().numpy(), r["dx"]) < 1e-3
+    dx_o = torch.from_numpy(r["dx"]).to(torch.bfloat16).float().numpy()   # dx is bf16
+    assert dx.dtype == torch.bfloat16
+    assert _rel(dx.float().cpu().numpy(), dx_o) < 1e-3
     assert _rel(ddown.float().cpu().numpy(), r["ddown"]) < 1e-3
     assert _rel(dup.float().cpu().numpy(), r["dup"]) < 1e-3
     assert _rel(dcoeff.float().cpu().numpy().reshape(-1, 6), r["dcoeff"].astype(np.float32)) \
