@@ -25,6 +25,7 @@
  *                             :87 pack_spine, :158 _warp_scalars
  *   ksd8_ks3_spine_quant      ksdraft/kernels/ks3_int8.py:169-234 _spine_features followed by
  *                             quantize_last_dim(h) (:284, :331)
+ *   ksd8_ks3_spine_table      the (chart, LUT index)-only part of ks3_int8.py:206-227
  *   ksd8_ks3_vjp              ksdraft/kernels/ks3_int8.py:354-410 (geometry VJP, dc, its two quantisations)
  *   ksd8_ks3_vjp_reduce       ksdraft/kernels/ks3_int8.py:381-395 (column reductions, STE factors)
  *   ksd8_rosa_pack_bits       ksdraft/model/rosa.py:156-158 (bits = proj > 0) and the int8 bit inputs
@@ -138,8 +139,18 @@ int ksd8_ks3_spine_quant(const void* coords, int64_t m, int64_t charts,
                          const int8_t* spine_codes, const void* spine_scale,
                          const int8_t* warp_scale_codes, const void* warp_scale_scales,
                          const int8_t* warp_shift_codes, const void* warp_shift_scales,
-                         const int8_t* lut, int nonlinear, int8_t* h_codes, void* h_scales,
-                         int* status, void* stream);
+                         const int8_t* lut, int nonlinear, const void* table, int8_t* h_codes,
+                         void* h_scales, int* status, void* stream);
+
+/* Per-chart table of the 'int8' spine term for the 256 LUT indices
+ * (table (charts, 256) fp16, 16-byte aligned): everything of
+ * ks3_int8.py:206-227 that depends only on (chart, index).  Passing it to
+ * ksd8_ks3_spine_quant (KSD8_NL_INT8) selects the table-driven kernel, which
+ * gives the same codes and scales. */
+int ksd8_ks3_spine_table(int64_t charts, const int8_t* spine_codes, const void* spine_scale,
+                         const int8_t* warp_scale_codes, const void* warp_scale_scales,
+                         const int8_t* warp_shift_codes, const void* warp_shift_scales,
+                         const int8_t* lut, void* table, int* status, void* stream);
 
 /* KS3 geometry VJP (fp16 arithmetic as the reference) on value = fp16(g @ up)
  * and the saved fp16 coordinates, both (M, charts).  Writes dc quantised

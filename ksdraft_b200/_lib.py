@@ -38,7 +38,9 @@ SIGNATURES: dict[str, list] = {
     "ksd8_w8a8_gemm": [vp, vp, vp, vp, i64, i64, i64, i32, vp, i32, i64, vp, i32, vp, vp],
     "ksd8_w8a8_group_partials": [vp, vp, i64, i64, i64, vp, vp, vp],
     "ksd8_ks3_pack": [vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp],
-    "ksd8_ks3_spine_quant": [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, i32, vp, vp, vp, vp],
+    "ksd8_ks3_spine_quant": [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, i32, vp, vp, vp, vp,
+                             vp],
+    "ksd8_ks3_spine_table": [i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
     "ksd8_ks3_vjp": [vp, vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp],
     "ksd8_ks3_vjp_reduce": [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp],
     "ksd8_rosa_pack_bits": [vp, i32, i64, i64, i64, i64, i64, i64, vp, vp, vp],

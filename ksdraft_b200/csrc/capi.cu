@@ -15,9 +15,11 @@ int ksd8_gemm_launch(const int8_t*, const void*, const int8_t*, const void*, int
                      int64_t, void*, int, int64_t, const float*, int, int*, cudaStream_t, bool);
 int ksd8_ks3_pack_launch(const float*, const float*, const float*, int64_t, int8_t*, void*,
                          int8_t*, void*, int8_t*, void*, cudaStream_t);
+int ksd8_ks3_spine_table_launch(int64_t, const int8_t*, const void*, const int8_t*, const void*,
+                                const int8_t*, const void*, const int8_t*, void*, cudaStream_t);
 int ksd8_ks3_spine_quant_launch(const void*, int64_t, int64_t, const int8_t*, const void*,
                                 const int8_t*, const void*, const int8_t*, const void*,
-                                const int8_t*, int, int8_t*, void*, cudaStream_t);
+                                const int8_t*, int, const void*, int8_t*, void*, cudaStream_t);
 int ksd8_ks3_vjp_launch(const void*, const void*, int64_t, int64_t, const int8_t*, const void*,
                         const int8_t*, const void*, const int8_t*, const void*, int8_t*, void*,
                         int8_t*, void*, float*, cudaStream_t);
@@ -150,23 +152,40 @@ int ksd8_ks3_pack(const float* coefficients, const float* raw_scale, const float
                                      warp_shift_codes, warp_shift_scales, S(stream)));
 }
 
+int ksd8_ks3_spine_table(int64_t charts, const int8_t* spine_codes, const void* spine_scale,
+                         const int8_t* warp_scale_codes, const void* warp_scale_scales,
+                         const int8_t* warp_shift_codes, const void* warp_shift_scales,
+                         const int8_t* lut, void* table, int* status, void* stream) {
+  (void)status;
+  if (charts < 0) return KSD8_ERR_SHAPE;
+  if (charts > 0 && (!spine_codes || !spine_scale || !warp_scale_scales || !warp_shift_scales ||
+                     !lut || !table))
+    return KSD8_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(table) & 15) return KSD8_ERR_ALIGN;
+  return finish(ksd8_ks3_spine_table_launch(charts, spine_codes, spine_scale, warp_scale_codes,
+                                            warp_scale_scales, warp_shift_codes,
+                                            warp_shift_scales, lut, table, S(stream)));
+}
+
 int ksd8_ks3_spine_quant(const void* coords, int64_t m, int64_t charts,
                          const int8_t* spine_codes, const void* spine_scale,
                          const int8_t* warp_scale_codes, const void* warp_scale_scales,
                          const int8_t* warp_shift_codes, const void* warp_shift_scales,
-                         const int8_t* lut, int nonlinear, int8_t* h_codes, void* h_scales,
-                         int* status, void* stream) {
+                         const int8_t* lut, int nonlinear, const void* table, int8_t* h_codes,
+                         void* h_scales, int* status, void* stream) {
   (void)status;
   if (nonlinear < KSD8_NL_FP32 || nonlinear > KSD8_NL_INT8) return KSD8_ERR_ARG;
   if (m < 0 || charts < 0) return KSD8_ERR_SHAPE;
-  if (m > 0 && charts > 0 &&
+  if (m > 0 && charts > 0 && !table &&
       (!coords || !spine_codes || !spine_scale || !warp_scale_scales || !warp_shift_scales ||
        !lut || !h_codes || !h_scales))
     return KSD8_ERR_ARG;
+  if (m > 0 && charts > 0 && (!coords || !h_codes || !h_scales)) return KSD8_ERR_ARG;
+  if (table && (reinterpret_cast<uintptr_t>(table) & 15)) return KSD8_ERR_ALIGN;
   return finish(ksd8_ks3_spine_quant_launch(coords, m, charts, spine_codes, spine_scale,
                                             warp_scale_codes, warp_scale_scales, warp_shift_codes,
-                                            warp_shift_scales, lut, nonlinear, h_codes, h_scales,
-                                            S(stream)));
+                                            warp_shift_scales, lut, nonlinear, table, h_codes,
+                                            h_scales, S(stream)));
 }
 
 int ksd8_ks3_vjp(const void* value, const void* coords, int64_t m, int64_t charts,

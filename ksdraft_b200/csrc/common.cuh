@@ -250,6 +250,18 @@ __device__ __forceinline__ int gs_code(float x, float scale) {
   return (int)q;
 }
 
+// Same result as gs_code without a division on the common path.  y = x * rcp
+// (rcp = RN(1/scale)) is within 2^-16 of RN(x/scale) for |x/scale| < 256, so
+// rint(y) == rint(RN(x/scale)) unless y lies within 2^-14 of a half-integer;
+// those (and out-of-range quotients) take the IEEE division.
+__device__ __forceinline__ int gs_code_fast(float x, float scale, float rcp) {
+  const float y = x * rcp;
+  const float r = rintf(y);
+  if (fabsf(y) < 200.f && fabsf(y - r) < 0.49993896484375f)  // 0.5 - 2^-14
+    return (int)fminf(fmaxf(r, -127.f), 127.f);
+  return gs_code(x, scale);
+}
+
 // ---------------------------------------------------------------- Philox4x32-10
 // Counter-based RNG of Salmon, Moraes, Dror and Shaw, "Parallel random
 // numbers: as easy as 1, 2, 3" (SC'11): 10 rounds of the 4x32 Philox S-box

@@ -218,6 +218,158 @@ __global__ void __launch_bounds__(256) ks3_spine_quant_kernel(SpineArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- fast int8 spine
+//
+// In the 'int8' mode everything between the LUT index of the coordinate and
+// the fp16 spine term depends only on (chart, index): tq, the fp16 warp
+// chain, zq, the integer Horner sums and hmul(fp16(tsum), ps).  That term is
+// tabulated per chart for the 256 index values (ks3_spine_table_kernel) and
+// the per-element work reduces to index -> table -> requant:
+//   h   = relu(x + T[c][idx])                      (fp32)
+//   pre = fp16(h / 127)                            (per-element pre-scale)
+//   out = fp16(127*127) * (pre * pre) = 16128 * pre^2
+// The code is 127 whenever pre is a normal fp16 (|pre - h/127| <= 2^-11
+// relative, so h/pre lies in [126.94, 127.07] and rounds to 127); h/127 is
+// taken as h * RN(1/127) unless that product sits within 4 ulp of an fp16
+// rounding midpoint; zero, tiny or huge h take the exact generic path.
+
+constexpr int SPINE_TAB = 256;  // LUT index + 128
+
+__global__ void ks3_spine_table_kernel(int64_t charts, const int8_t* spine_codes,
+                                       const __half* spine_scale, const int8_t* ws_codes,
+                                       const __half* ws_scales, const int8_t* wh_codes,
+                                       const __half* wh_scales, const int8_t* lut,
+                                       __half* table) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= charts * SPINE_TAB) return;
+  const int64_t c = i / SPINE_TAB;
+  const int ti = (int)(i % SPINE_TAB) - 128;
+  const int tq = lut_at(lut, ti);
+  const float scale = dequant_scalar(ws_codes, ws_scales, c, true);
+  const float shift = dequant_scalar(wh_codes, wh_scales, c, true);
+  const float w1 = hmul((float)tq, 0.031496062874794006f);
+  const float w2 = hadd(w1, shift);
+  const float warp = hmul(scale, w2);
+  const int zq = lut_at(lut, lut_index(warp));
+  const int8_t* cc = spine_codes + c * 6;
+  const int c0 = cc[0], c1 = cc[1], c2 = cc[2], c3 = cc[3], c4 = cc[4], c5 = cc[5];
+  const int a = 2 * c0 - 2 * c1 + c2 + c3;
+  const int b = -3 * c0 + 3 * c1 - 2 * c2 - c3;
+  int poly = a * 64;
+  poly = round_div127(poly * tq * 4) + b * 64;
+  poly = round_div127(poly * tq * 4) + c2 * 64;
+  poly = round_div127(poly * tq * 4) + c0 * 64;
+  int warped = 4 * c5 * 64;
+  warped = round_div127(warped * zq) + 2 * c4 * 64;
+  warped = round_div127(warped * zq) - 3 * c5 * 64;
+  warped = round_div127(warped * zq) - c4 * 64;
+  const int tsum = (poly + warped) / 64;
+  table[i] = __float2half_rn(hmul(hr((float)tsum), __half2float(spine_scale[c])));
+}
+
+__device__ __forceinline__ float spine_out_int8(float h) {
+  h = fmaxf(h, 0.f);
+  const float y = h * 0.007874015718698502f;  // RN(1/127)
+  const int low13 = (int)(__float_as_uint(y) & 0x1FFFu);
+  if (y >= 6.103515625e-05f && y < 65504.f && abs(low13 - 0x1000) > 4) {
+    const float pre = hr(y);
+    return __fmul_rn(16128.f, __fmul_rn(pre, pre));
+  }
+  float pre = __fdiv_rn(h, 127.0f);
+  pre = hr(fminf(fmaxf(pre, 5.9604644775390625e-08f), 65504.0f));
+  float q = fminf(fmaxf(rintf(__fdiv_rn(h, pre)), -127.f), 127.f);
+  q = fmaxf(q, 0.f);
+  return __fmul_rn(hmul(q, q), __fmul_rn(pre, pre));
+}
+
+struct SpineFastArgs {
+  const __half* coords;
+  int64_t m, charts;
+  const __half* table;  // (charts, 256)
+  int8_t* h_codes;
+  __half* h_scales;
+};
+
+constexpr int SPF_LD = SPINE_TAB + 8;  // padded table row (halves)
+constexpr int SPF_SMEM = 128 * SPF_LD * 2;
+
+__global__ void __launch_bounds__(256) ks3_spine_int8_fast_kernel(SpineFastArgs a) {
+  extern __shared__ __half stab[];  // [128 charts][SPF_LD]
+  const int64_t g = blockIdx.x;
+  const int64_t groups = (a.charts + 127) / 128;
+  const int64_t cg0 = g * 128;
+  for (int i = threadIdx.x; i < 128 * (SPINE_TAB / 8); i += blockDim.x) {
+    const int ch = i / (SPINE_TAB / 8), v = i % (SPINE_TAB / 8);
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (cg0 + ch < a.charts)
+      val = *reinterpret_cast<const uint4*>(a.table + (cg0 + ch) * SPINE_TAB + v * 8);
+    *reinterpret_cast<uint4*>(stab + ch * SPF_LD + v * 8) = val;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t cbase = cg0 + lane * 4;
+  const bool full = cbase + 4 <= a.charts;
+  const __half2 quarter = __float2half2_rn(0.25f);
+  const __half2 lim = __float2half2_rn(3.19921875f);
+  const __half2 nlim = __float2half2_rn(-3.19921875f);
+  const __half2 k127 = __float2half2_rn(39.6875f);
+  const int64_t rows_per_block = (a.m + gridDim.y - 1) / gridDim.y;
+  const int64_t r_begin = blockIdx.y * rows_per_block;
+  const int64_t r_end = min(a.m, r_begin + rows_per_block);
+  for (int64_t r = r_begin + warp; r < r_end; r += 8) {
+    const __half* crow = a.coords + r * a.charts;
+    __half2 x2[2];
+    if (full) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(crow + cbase);
+      x2[0] = *reinterpret_cast<const __half2*>(&raw.x);
+      x2[1] = *reinterpret_cast<const __half2*>(&raw.y);
+    } else {
+      __half e[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) e[i] = cbase + i < a.charts ? crow[cbase + i] : __half(0.f);
+      x2[0] = __halves2half2(e[0], e[1]);
+      x2[1] = __halves2half2(e[2], e[3]);
+    }
+    float h[4];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      __half2 m2 = __hmul2_rn(x2[p], quarter);
+      m2 = __hmax2(__hmin2(m2, lim), nlim);
+      const __half2 s2 = __hmul2_rn(m2, k127);
+      const int i0 = __half2int_rn(__low2half(s2)) + 128;
+      const int i1 = __half2int_rn(__high2half(s2)) + 128;
+      const int ch = lane * 4 + 2 * p;
+      const float t0 = __half2float(stab[ch * SPF_LD + i0]);
+      const float t1 = __half2float(stab[(ch + 1) * SPF_LD + i1]);
+      const float2 xf = __half22float2(x2[p]);
+      h[2 * p] = spine_out_int8(__fadd_rn(xf.x, t0));
+      h[2 * p + 1] = spine_out_int8(__fadd_rn(xf.y, t1));
+    }
+    if (!full) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (cbase + i >= a.charts) h[i] = 0.f;
+    }
+    float mx = fmaxf(fmaxf(h[0], h[1]), fmaxf(h[2], h[3]));  // h >= 0
+    mx = warp_max(mx);
+    __half sh;
+    const float scale = gs_scale(mx, &sh);
+    const float rcp = __frcp_rn(scale);
+    int8_t* out = a.h_codes + r * a.charts + cbase;
+    const int q0 = gs_code_fast(h[0], scale, rcp), q1 = gs_code_fast(h[1], scale, rcp);
+    const int q2 = gs_code_fast(h[2], scale, rcp), q3 = gs_code_fast(h[3], scale, rcp);
+    if (full && ((reinterpret_cast<uintptr_t>(out) & 3) == 0)) {
+      *reinterpret_cast<char4*>(out) = make_char4((char)q0, (char)q1, (char)q2, (char)q3);
+    } else {
+      const int q[4] = {q0, q1, q2, q3};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (cbase + i < a.charts) out[i] = (int8_t)q[i];
+    }
+    if (lane == 0) a.h_scales[r * groups + g] = sh;
+  }
+}
+
 // ---------------------------------------------------------------- pack
 
 __device__ __forceinline__ float softplus_f32(float x) {
@@ -272,10 +424,9 @@ struct VjpArgs {
   float* partials;
 };
 
-struct VjpChart {
-  float c0, c1, c2, c4, c5;
-  float cubic, quad, cubic3, quad2, c5x4, c4x2, c5x12, c4x4, c5x3;
-  float scale, shift;
+// Per-chart constants of the VJP, as fp16 pairs (charts 2p and 2p+1 of a lane).
+struct VjpPair {
+  __half2 c0, c2, c4, cubic, quad, cubic3, quad2, c5x4, c4x2, c5x12, c4x4, c5x3, scale, shift;
 };
 
 constexpr int VJP_TM = 128;  // token rows per CTA (= one token-quantisation group)
@@ -283,6 +434,17 @@ constexpr int VJP_TC = 128;  // charts per CTA (= one chart-quantisation group)
 constexpr int VJP_LD = VJP_TC + 1;
 constexpr int VJP_SMEM = (VJP_TM * VJP_LD + 8 * 8 * VJP_TC) * 4;
 
+// fp16(tanh(x)) for an fp16 pair, tanh evaluated in fp32 (torch's Half tanh).
+__device__ __forceinline__ __half2 tanh16x2(__half2 x) {
+  const float2 f = __half22float2(x);
+  return __floats2half2_rn(tanhf(f.x), tanhf(f.y));
+}
+
+// The fp16 VJP of ks3_int8.py:354-402 with native fp16 pair arithmetic.  Each
+// op of the reference (torch CPU Half: fp32 compute, round to fp16) equals the
+// correctly rounded fp16 op because double rounding through fp32 is
+// innocuous for fp16 operands (24 >= 2*11 + 2); the _rn intrinsics keep
+// multiplies and adds from being fused.
 __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
   extern __shared__ float vsm[];
   float* tile = vsm;                       // [VJP_TM][VJP_LD] dc values
@@ -292,101 +454,133 @@ __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
   const int64_t cg = blockIdx.x;           // chart group
   const int64_t cbase = cg * VJP_TC + lane * 4;
 
-  VjpChart ch[4];
+  VjpPair pr[2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t c = cbase + i;
-    const float ps = __half2float(a.spine_scale[c]);
-    float cc[6];
+  for (int p = 0; p < 2; ++p) {
+    __half cc[2][6], sc[2], sh[2];
 #pragma unroll
-    for (int k = 0; k < 6; ++k) cc[k] = hr((float)a.spine_codes[c * 6 + k] * ps);
-    VjpChart& q = ch[i];
-    q.c0 = cc[0]; q.c1 = cc[1]; q.c2 = cc[2]; q.c4 = cc[4]; q.c5 = cc[5];
-    // cubic = 2*c0 - 2*c1 + c2 + c3 ; quad = -3*c0 + 3*c1 - 2*c2 - c3 (fp16 ops, left to right)
-    q.cubic = hadd(hadd(hsub(hmul(2.f, cc[0]), hmul(2.f, cc[1])), cc[2]), cc[3]);
-    q.quad = hsub(hsub(hadd(hmul(-3.f, cc[0]), hmul(3.f, cc[1])), hmul(2.f, cc[2])), cc[3]);
-    q.cubic3 = hmul(3.f, q.cubic);
-    q.quad2 = hmul(2.f, q.quad);
-    q.c5x4 = hmul(4.f, cc[5]);
-    q.c4x2 = hmul(2.f, cc[4]);
-    q.c5x12 = hmul(12.f, cc[5]);
-    q.c4x4 = hmul(4.f, cc[4]);
-    q.c5x3 = hmul(3.f, cc[5]);
-    q.scale = dequant_scalar(a.ws_codes, a.ws_scales, c, true);
-    q.shift = dequant_scalar(a.wh_codes, a.wh_scales, c, true);
+    for (int j = 0; j < 2; ++j) {
+      const int64_t c = cbase + 2 * p + j;
+      const float ps = __half2float(a.spine_scale[c]);
+#pragma unroll
+      for (int k = 0; k < 6; ++k)
+        cc[j][k] = __float2half_rn((float)a.spine_codes[c * 6 + k] * ps);
+      sc[j] = __float2half_rn(dequant_scalar(a.ws_codes, a.ws_scales, c, true));
+      sh[j] = __float2half_rn(dequant_scalar(a.wh_codes, a.wh_scales, c, true));
+    }
+    __half2 c[6];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) c[k] = __halves2half2(cc[0][k], cc[1][k]);
+    const __half2 two = __float2half2_rn(2.f), three = __float2half2_rn(3.f);
+    VjpPair& q = pr[p];
+    q.c0 = c[0]; q.c2 = c[2]; q.c4 = c[4];
+    // cubic = 2*c0 - 2*c1 + c2 + c3 ; quad = -3*c0 + 3*c1 - 2*c2 - c3
+    q.cubic = __hadd2_rn(__hadd2_rn(__hsub2_rn(__hmul2_rn(two, c[0]), __hmul2_rn(two, c[1])),
+                                    c[2]), c[3]);
+    q.quad = __hsub2_rn(__hsub2_rn(__hadd2_rn(__hmul2_rn(__float2half2_rn(-3.f), c[0]),
+                                              __hmul2_rn(three, c[1])),
+                                   __hmul2_rn(two, c[2])), c[3]);
+    q.cubic3 = __hmul2_rn(three, q.cubic);
+    q.quad2 = __hmul2_rn(two, q.quad);
+    q.c5x4 = __hmul2_rn(__float2half2_rn(4.f), c[5]);
+    q.c4x2 = __hmul2_rn(two, c[4]);
+    q.c5x12 = __hmul2_rn(__float2half2_rn(12.f), c[5]);
+    q.c4x4 = __hmul2_rn(__float2half2_rn(4.f), c[4]);
+    q.c5x3 = __hmul2_rn(three, c[5]);
+    q.scale = __halves2half2(sc[0], sc[1]);
+    q.shift = __halves2half2(sh[0], sh[1]);
   }
 
-  float acc[4][8];
+  float2 acc[2][8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int p = 0; p < 2; ++p)
 #pragma unroll
-    for (int k = 0; k < 8; ++k) acc[i][k] = 0.f;
+    for (int k = 0; k < 8; ++k) acc[p][k] = make_float2(0.f, 0.f);
 
+  const __half2 one = __float2half2_rn(1.f), two = __float2half2_rn(2.f);
+  const __half2 three = __float2half2_rn(3.f), four = __float2half2_rn(4.f);
+  const __half2 ntwo = __float2half2_rn(-2.f), quarter = __float2half2_rn(0.25f);
+  const __half2 sixteenth = __float2half2_rn(0.0625f), zero = __float2half2_rn(0.f);
   const int64_t gcharts = a.charts / 128;
   for (int rr = warp; rr < VJP_TM; rr += 8) {
     const int64_t r = m0 + rr;
-    float dc[4] = {0.f, 0.f, 0.f, 0.f};
+    float dcf[4] = {0.f, 0.f, 0.f, 0.f};
     if (r < a.m) {
       const uint2 vv = *reinterpret_cast<const uint2*>(a.value + r * a.charts + cbase);
       const uint2 xv = *reinterpret_cast<const uint2*>(a.coords + r * a.charts + cbase);
-      const __half* ve = reinterpret_cast<const __half*>(&vv);
-      const __half* xe = reinterpret_cast<const __half*>(&xv);
+      const __half2 v2[2] = {*reinterpret_cast<const __half2*>(&vv.x),
+                             *reinterpret_cast<const __half2*>(&vv.y)};
+      const __half2 x2[2] = {*reinterpret_cast<const __half2*>(&xv.x),
+                             *reinterpret_cast<const __half2*>(&xv.y)};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const VjpChart& q = ch[i];
-        const float value = __half2float(ve[i]);
-        const float x16 = __half2float(xe[i]);
-        const float th = hr(tanhf(hmul(x16, 0.25f)));
-        const float t = hmul(4.f, th);
-        const float u = hadd(t, q.shift);
-        const float z = hr(tanhf(hmul(q.scale, u)));
-        float sp = hadd(hmul(q.cubic, t), q.quad);
-        sp = hadd(hmul(sp, t), q.c2);
-        sp = hadd(hmul(sp, t), q.c0);
-        float wp = hadd(hmul(q.c5x4, z), q.c4x2);
-        wp = hsub(hmul(wp, z), q.c5x3);
-        wp = hsub(hmul(wp, z), q.c4);
-        const float rl = fmaxf(hadd(hadd(x16, sp), wp), 0.f);
-        const float dpre = hmul(hmul(value, 2.f), rl);
-        float dpoly = hadd(hmul(q.cubic3, t), q.quad2);
-        dpoly = hadd(hmul(dpoly, t), q.c2);
-        float dwarp = hadd(hmul(q.c5x12, z), q.c4x4);
-        dwarp = hsub(hmul(dwarp, z), q.c5x3);
-        const float zz = hmul(z, z);
-        const float dz = hmul(dwarp, hsub(1.f, zz));
-        const float tt = hmul(t, t);
-        const float dmean = hmul(hmul(dpre, hadd(dpoly, hmul(dz, q.scale))),
-                                 hsub(1.f, hmul(tt, 0.0625f)));
-        dc[i] = hadd(value, dmean);
-        const float t3 = hmul(tt, t);
-        const float z3 = hmul(zz, z);
-        acc[i][0] += hmul(dpre, hadd(hsub(hmul(2.f, t3), hmul(3.f, tt)), 1.f));
-        acc[i][1] += hmul(dpre, hadd(hmul(-2.f, t3), hmul(3.f, tt)));
-        acc[i][2] += hmul(dpre, hadd(hsub(t3, hmul(2.f, tt)), t));
-        acc[i][3] += hmul(dpre, hsub(t3, tt));
-        acc[i][4] += hmul(dpre, hsub(hmul(2.f, zz), 1.f));
-        acc[i][5] += hmul(dpre, hsub(hmul(4.f, z3), hmul(3.f, z)));
-        const float dd = hmul(dpre, dz);
-        acc[i][6] += hmul(dd, u);
-        acc[i][7] += hmul(dd, q.scale);
+      for (int p = 0; p < 2; ++p) {
+        const VjpPair& q = pr[p];
+        const __half2 x16 = x2[p], value = v2[p];
+        const __half2 t = __hmul2_rn(four, tanh16x2(__hmul2_rn(x16, quarter)));
+        const __half2 u = __hadd2_rn(t, q.shift);
+        const __half2 z = tanh16x2(__hmul2_rn(q.scale, u));
+        __half2 sp = __hadd2_rn(__hmul2_rn(q.cubic, t), q.quad);
+        sp = __hadd2_rn(__hmul2_rn(sp, t), q.c2);
+        sp = __hadd2_rn(__hmul2_rn(sp, t), q.c0);
+        __half2 wp = __hadd2_rn(__hmul2_rn(q.c5x4, z), q.c4x2);
+        wp = __hsub2_rn(__hmul2_rn(wp, z), q.c5x3);
+        wp = __hsub2_rn(__hmul2_rn(wp, z), q.c4);
+        const __half2 rl = __hmax2(__hadd2_rn(__hadd2_rn(x16, sp), wp), zero);
+        const __half2 dpre = __hmul2_rn(__hmul2_rn(value, two), rl);
+        __half2 dpoly = __hadd2_rn(__hmul2_rn(q.cubic3, t), q.quad2);
+        dpoly = __hadd2_rn(__hmul2_rn(dpoly, t), q.c2);
+        __half2 dwarp = __hadd2_rn(__hmul2_rn(q.c5x12, z), q.c4x4);
+        dwarp = __hsub2_rn(__hmul2_rn(dwarp, z), q.c5x3);
+        const __half2 zz = __hmul2_rn(z, z);
+        const __half2 dz = __hmul2_rn(dwarp, __hsub2_rn(one, zz));
+        const __half2 tt = __hmul2_rn(t, t);
+        const __half2 dmean =
+            __hmul2_rn(__hmul2_rn(dpre, __hadd2_rn(dpoly, __hmul2_rn(dz, q.scale))),
+                       __hsub2_rn(one, __hmul2_rn(tt, sixteenth)));
+        const float2 dc = __half22float2(__hadd2_rn(value, dmean));
+        dcf[2 * p] = dc.x;
+        dcf[2 * p + 1] = dc.y;
+        const __half2 t3 = __hmul2_rn(tt, t);
+        const __half2 z3 = __hmul2_rn(zz, z);
+        const __half2 dd = __hmul2_rn(dpre, dz);
+        const __half2 terms[8] = {
+            __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(__hmul2_rn(two, t3), __hmul2_rn(three, tt)),
+                                        one)),
+            __hmul2_rn(dpre, __hadd2_rn(__hmul2_rn(ntwo, t3), __hmul2_rn(three, tt))),
+            __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(t3, __hmul2_rn(two, tt)), t)),
+            __hmul2_rn(dpre, __hsub2_rn(t3, tt)),
+            __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(two, zz), one)),
+            __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(four, z3), __hmul2_rn(three, z))),
+            __hmul2_rn(dd, u),
+            __hmul2_rn(dd, q.scale)};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float2 f = __half22float2(terms[k]);
+          acc[p][k].x += f.x;
+          acc[p][k].y += f.y;
+        }
       }
       // dc quantised along charts: this row's 128 charts are one group.
-      float mx = fmaxf(fmaxf(fabsf(dc[0]), fabsf(dc[1])), fmaxf(fabsf(dc[2]), fabsf(dc[3])));
+      float mx = fmaxf(fmaxf(fabsf(dcf[0]), fabsf(dcf[1])), fmaxf(fabsf(dcf[2]), fabsf(dcf[3])));
       mx = warp_max(mx);
-      __half sh;
-      const float s = gs_scale(mx, &sh);
+      __half shq;
+      const float s = gs_scale(mx, &shq);
+      const float rcp = __frcp_rn(s);
       *reinterpret_cast<char4*>(a.dc_codes + r * a.charts + cbase) =
-          make_char4((char)gs_code(dc[0], s), (char)gs_code(dc[1], s), (char)gs_code(dc[2], s),
-                     (char)gs_code(dc[3], s));
-      if (lane == 0) a.dc_scales[r * gcharts + cg] = sh;
+          make_char4((char)gs_code_fast(dcf[0], s, rcp), (char)gs_code_fast(dcf[1], s, rcp),
+                     (char)gs_code_fast(dcf[2], s, rcp), (char)gs_code_fast(dcf[3], s, rcp));
+      if (lane == 0) a.dc_scales[r * gcharts + cg] = shq;
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) tile[rr * VJP_LD + lane * 4 + i] = dc[i];
+    for (int i = 0; i < 4; ++i) tile[rr * VJP_LD + lane * 4 + i] = dcf[i];
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int p = 0; p < 2; ++p)
 #pragma unroll
-    for (int k = 0; k < 8; ++k) red[(warp * 8 + k) * VJP_TC + lane * 4 + i] = acc[i][k];
+    for (int k = 0; k < 8; ++k) {
+      red[(warp * 8 + k) * VJP_TC + lane * 4 + 2 * p] = acc[p][k].x;
+      red[(warp * 8 + k) * VJP_TC + lane * 4 + 2 * p + 1] = acc[p][k].y;
+    }
   __syncthreads();
 
   // dc^T quantised along tokens: column c of the tile is one group of 128 tokens.
@@ -397,22 +591,23 @@ __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
     for (int i = 0; i < 4; ++i) v[i] = tile[(lane + 32 * i) * VJP_LD + cc];
     float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     mx = warp_max(mx);
-    __half sh;
-    const float s = gs_scale(mx, &sh);
+    __half shq;
+    const float s = gs_scale(mx, &shq);
+    const float rcp = __frcp_rn(s);
     const int64_t c = cg * VJP_TC + cc;
     int8_t* out = a.dct_codes + c * a.m + m0;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      if (m0 + lane + 32 * i < a.m) out[lane + 32 * i] = (int8_t)gs_code(v[i], s);
-    if (lane == 0) a.dct_scales[c * mgroups + blockIdx.y] = sh;
+      if (m0 + lane + 32 * i < a.m) out[lane + 32 * i] = (int8_t)gs_code_fast(v[i], s, rcp);
+    if (lane == 0) a.dct_scales[c * mgroups + blockIdx.y] = shq;
   }
   // Column partials: fixed-order sum over the 8 warps.
   for (int idx = threadIdx.x; idx < 8 * VJP_TC; idx += blockDim.x) {
     const int k = idx / VJP_TC, cc = idx % VJP_TC;
-    float s = 0.f;
+    float sum = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += red[(w * 8 + k) * VJP_TC + cc];
-    a.partials[((int64_t)blockIdx.y * 8 + k) * a.charts + cg * VJP_TC + cc] = s;
+    for (int w = 0; w < 8; ++w) sum += red[(w * 8 + k) * VJP_TC + cc];
+    a.partials[((int64_t)blockIdx.y * 8 + k) * a.charts + cg * VJP_TC + cc] = sum;
   }
 }
 
@@ -462,12 +657,51 @@ int ksd8_ks3_pack_launch(const float* coeffs, const float* raw_scale, const floa
   return KSD8_OK;
 }
 
+int ksd8_ks3_spine_table_launch(int64_t charts, const int8_t* spine_codes,
+                                const void* spine_scale, const int8_t* ws_codes,
+                                const void* ws_scales, const int8_t* wh_codes,
+                                const void* wh_scales, const int8_t* lut, void* table,
+                                cudaStream_t stream) {
+  if (charts == 0) return KSD8_OK;
+  const int64_t n = charts * SPINE_TAB;
+  ks3_spine_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+      charts, spine_codes, reinterpret_cast<const __half*>(spine_scale), ws_codes,
+      reinterpret_cast<const __half*>(ws_scales), wh_codes,
+      reinterpret_cast<const __half*>(wh_scales), lut, reinterpret_cast<__half*>(table));
+  return KSD8_OK;
+}
+
 int ksd8_ks3_spine_quant_launch(const void* coords, int64_t m, int64_t charts,
                                 const int8_t* spine_codes, const void* spine_scale,
                                 const int8_t* ws_codes, const void* ws_scales,
                                 const int8_t* wh_codes, const void* wh_scales, const int8_t* lut,
-                                int nl, int8_t* h_codes, void* h_scales, cudaStream_t stream) {
+                                int nl, const void* table, int8_t* h_codes, void* h_scales,
+                                cudaStream_t stream) {
   if (m == 0 || charts == 0) return KSD8_OK;
+  const int64_t groups = (charts + 127) / 128;
+  if (table && nl == KSD8_NL_INT8) {
+    static unsigned attr_dev_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_dev_mask & (1u << dev))) {
+      if (cudaFuncSetAttribute(ks3_spine_int8_fast_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, SPF_SMEM) !=
+          cudaSuccess)
+        return KSD8_ERR_LAUNCH;
+      attr_dev_mask |= (1u << dev);
+    }
+    SpineFastArgs f;
+    f.coords = reinterpret_cast<const __half*>(coords);
+    f.m = m; f.charts = charts; f.table = reinterpret_cast<const __half*>(table);
+    f.h_codes = h_codes; f.h_scales = reinterpret_cast<__half*>(h_scales);
+    int64_t yb = (148 * 3 + groups - 1) / groups;  // ~3 resident CTAs per SM
+    const int64_t max_yb = (m + 7) / 8;
+    if (yb > max_yb) yb = max_yb;
+    if (yb < 1) yb = 1;
+    ks3_spine_int8_fast_kernel<<<dim3((unsigned)groups, (unsigned)yb), 256, SPF_SMEM, stream>>>(
+        f);
+    return KSD8_OK;
+  }
   SpineArgs a;
   a.coords = reinterpret_cast<const __half*>(coords);
   a.m = m; a.charts = charts; a.spine_codes = spine_codes;
@@ -475,7 +709,6 @@ int ksd8_ks3_spine_quant_launch(const void* coords, int64_t m, int64_t charts,
   a.ws_codes = ws_codes; a.ws_scales = reinterpret_cast<const __half*>(ws_scales);
   a.wh_codes = wh_codes; a.wh_scales = reinterpret_cast<const __half*>(wh_scales);
   a.lut = lut; a.nl = nl; a.h_codes = h_codes; a.h_scales = reinterpret_cast<__half*>(h_scales);
-  const int64_t groups = (charts + 127) / 128;
   int64_t yb = (148 * 8 + groups - 1) / groups;  // ~8 CTAs per SM in total
   const int64_t max_yb = (m + 7) / 8;
   if (yb > max_yb) yb = max_yb;

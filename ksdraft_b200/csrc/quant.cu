@@ -10,10 +10,12 @@
 // element index offset + row * Kp + col (Kp = padded row length).
 //
 // quantize_rows_kernel: one warp per (row, group), memory-bound, coalesced.
-// quantize_cols_kernel: x^T quantised along the rows of x; a 128 x 64 tile is
-//   staged in shared memory so both the reads of x and the writes of x^T are
-//   coalesced; also dequantises int8 codes on the fly (dequant -> transpose ->
-//   requant of ks3_int8.py:350, :407-424).
+// quantize_cols_kernel: x^T quantised along the rows of x; a 128 x 128 tile
+//   is staged in shared memory so both the reads of x (16-byte vectors) and the
+//   writes of x^T are coalesced; also dequantises int8 codes on the fly
+//   (dequant -> transpose -> requant of ks3_int8.py:350, :407-424).
+// Codes use gs_code_fast: a reciprocal multiply with an exact fallback near
+// rounding ties, bit-identical to rint(x / scale).
 #include "common.cuh"
 
 namespace ksd8 {
@@ -91,18 +93,29 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(QRowArgs a) {
     const float scale = gs_scale(m, &sh);
     int q[4];
     if (a.flags & KSD8_Q_DITHER) {
+      // one Philox block serves the 4 consecutive elements when they share it
       const uint64_t base = a.offset + (uint64_t)r * kp + c;
+      float u[4];
+      if ((base & 3) == 0) {
+        uint32_t ctr[4] = {(uint32_t)(base >> 2), (uint32_t)(base >> 34), 0u, 0u};
+        philox4x32_10(ctr, (uint32_t)a.seed, (uint32_t)(a.seed >> 32));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) u[i] = (float)(ctr[i] >> 8) * 5.9604644775390625e-08f;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) u[i] = philox_uniform(a.seed, base + i);
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float u = philox_uniform(a.seed, base + i);
-        const float noise = __fmul_rn(__fsub_rn(u, 0.5f), a.dither2);
+        const float noise = __fmul_rn(__fsub_rn(u[i], 0.5f), a.dither2);
         float t = __fadd_rn(__fdiv_rn(v[i], scale), noise);
         t = fminf(fmaxf(rintf(t), -127.f), 127.f);
         q[i] = (int)t;
       }
     } else {
+      const float rcp = __frcp_rn(scale);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) q[i] = gs_code(v[i], scale);
+      for (int i = 0; i < 4; ++i) q[i] = gs_code_fast(v[i], scale, rcp);
     }
     int8_t* out = a.codes + r * a.ldc + c;
     if (c + 4 <= a.k && (reinterpret_cast<uintptr_t>(out) & 3) == 0) {
@@ -127,32 +140,77 @@ struct QColArgs {
   __half* scales_t;
 };
 
-constexpr int QC_TR = 128;  // rows per tile (one output group)
-constexpr int QC_TC = 64;   // columns per tile
+constexpr int QC_TR = 128;  // rows per tile (one output group along the rows)
+constexpr int QC_TC = 128;  // columns per tile
+constexpr int QC_LD = QC_TC + 1;
+constexpr int QC_SMEM = QC_TR * QC_LD * 4;
 
+// 16-byte vector of input elements -> floats (dequantised for int8 codes).
+template <typename T>
+struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+// One CTA per 128 x 128 tile: coalesced 16-byte row loads into shared memory
+// (as fp32), then each warp quantises columns: lane l owns rows l, l+32, l+64,
+// l+96 of the column (conflict-free with the odd row pitch), amax by shuffle,
+// one code byte per row written to x^T.
 template <typename T, bool DEQUANT>
 __global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
-  __shared__ float tile[QC_TR][QC_TC + 1];
+  extern __shared__ float tile[];  // [QC_TR][QC_LD]
   const int64_t r0 = (int64_t)blockIdx.y * QC_TR;
   const int64_t c0 = (int64_t)blockIdx.x * QC_TC;
   const int tid = threadIdx.x;
+  constexpr int VN = Vec16<T>::N;           // elements per 16-byte vector
+  constexpr int VPR = QC_TC / VN;           // vectors per tile row
   const int64_t xs_groups = DEQUANT ? (a.cols + a.x_group - 1) / a.x_group : 0;
-  // Load: 4 rows per pass, 64 consecutive columns per row.
-  for (int rr = tid / QC_TC; rr < QC_TR; rr += 256 / QC_TC) {
-    const int cc = tid % QC_TC;
-    const int64_t r = r0 + rr, c = c0 + cc;
-    float v = 0.f;
-    if (r < a.rows && c < a.cols) {
+  const bool vec_ok = (a.ldx * (int64_t)sizeof(T)) % 16 == 0 &&
+                      (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && c0 + QC_TC <= a.cols;
+  for (int idx = tid; idx < QC_TR * VPR; idx += 256) {
+    const int rr = idx / VPR, vv = idx % VPR;
+    const int64_t r = r0 + rr;
+    const int64_t c = c0 + vv * VN;
+    float v[VN];
+    if (r < a.rows) {
       const T* row = reinterpret_cast<const T*>(a.x) + r * a.ldx;
-      if constexpr (DEQUANT) {
-        const float code = (float)reinterpret_cast<const int8_t*>(row)[c];
-        v = code * __half2float(a.x_scales[r * xs_groups + c / a.x_group]);
+      float sc = 1.f;
+      if constexpr (DEQUANT) sc = __half2float(a.x_scales[r * xs_groups + c / a.x_group]);
+      if (vec_ok) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(row + c);
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int i = 0; i < VN; ++i) {
+          if constexpr (DEQUANT) v[i] = (float)e[i] * sc;
+          else v[i] = to_f32<T>(e[i]);
+        }
       } else {
-        v = to_f32<T>(row[c]);
-        if (a.flags & KSD8_Q_ROUND_F16) v = round_f16(v);
+#pragma unroll
+        for (int i = 0; i < VN; ++i) {
+          const int64_t ci = c + i;
+          if (ci < a.cols) {
+            if constexpr (DEQUANT) {
+              const float s2 = __half2float(a.x_scales[r * xs_groups + ci / a.x_group]);
+              v[i] = (float)row[ci] * s2;
+            } else {
+              v[i] = to_f32<T>(row[ci]);
+            }
+          } else {
+            v[i] = 0.f;
+          }
+        }
       }
+      if constexpr (!DEQUANT) {
+        if (a.flags & KSD8_Q_ROUND_F16) {
+#pragma unroll
+          for (int i = 0; i < VN; ++i) v[i] = round_f16(v[i]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VN; ++i) v[i] = 0.f;
     }
-    tile[rr][cc] = v;
+#pragma unroll
+    for (int i = 0; i < VN; ++i) tile[rr * QC_LD + vv * VN + i] = v[i];
   }
   __syncthreads();
   const int warp = tid >> 5, lane = tid & 31;
@@ -162,16 +220,17 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
     if (c >= a.cols) break;
     float v[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = tile[lane + 32 * i][cc];
+    for (int i = 0; i < 4; ++i) v[i] = tile[(lane + 32 * i) * QC_LD + cc];
     float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     m = warp_max(m);
     __half sh;
     const float scale = gs_scale(m, &sh);
+    const float rcp = __frcp_rn(scale);
     int8_t* out = a.codes_t + c * a.ldct + r0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int64_t r = r0 + lane + 32 * i;
-      if (r < a.rows) out[lane + 32 * i] = (int8_t)gs_code(v[i], scale);
+      if (r < a.rows) out[lane + 32 * i] = (int8_t)gs_code_fast(v[i], scale, rcp);
     }
     if (lane == 0) a.scales_t[c * rgroups + blockIdx.y] = sh;
   }
@@ -222,11 +281,27 @@ int ksd8_quantize_cols_launch(const void* x, int x_dtype, const void* x_scales, 
   a.codes_t = codes_t; a.scales_t = reinterpret_cast<__half*>(scales_t);
   if (rows == 0 || cols == 0) return KSD8_OK;
   dim3 grid((unsigned)((cols + QC_TC - 1) / QC_TC), (unsigned)((rows + QC_TR - 1) / QC_TR));
+  static unsigned attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1u << dev))) {
+    cudaFuncSetAttribute(quantize_cols_kernel<float, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QC_SMEM);
+    cudaFuncSetAttribute(quantize_cols_kernel<__half, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QC_SMEM);
+    cudaFuncSetAttribute(quantize_cols_kernel<__nv_bfloat16, false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QC_SMEM);
+    cudaFuncSetAttribute(quantize_cols_kernel<int8_t, true>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QC_SMEM);
+    attr_dev_mask |= (1u << dev);
+  }
   switch (x_dtype) {
-    case KSD8_F32: quantize_cols_kernel<float, false><<<grid, 256, 0, stream>>>(a); break;
-    case KSD8_F16: quantize_cols_kernel<__half, false><<<grid, 256, 0, stream>>>(a); break;
-    case KSD8_BF16: quantize_cols_kernel<__nv_bfloat16, false><<<grid, 256, 0, stream>>>(a); break;
-    case KSD8_I8: quantize_cols_kernel<int8_t, true><<<grid, 256, 0, stream>>>(a); break;
+    case KSD8_F32: quantize_cols_kernel<float, false><<<grid, 256, QC_SMEM, stream>>>(a); break;
+    case KSD8_F16: quantize_cols_kernel<__half, false><<<grid, 256, QC_SMEM, stream>>>(a); break;
+    case KSD8_BF16:
+      quantize_cols_kernel<__nv_bfloat16, false><<<grid, 256, QC_SMEM, stream>>>(a);
+      break;
+    case KSD8_I8: quantize_cols_kernel<int8_t, true><<<grid, 256, QC_SMEM, stream>>>(a); break;
     default: return KSD8_ERR_DTYPE;
   }
   return KSD8_OK;

@@ -83,9 +83,45 @@ def pack_spine(coefficients: torch.Tensor, group: int = GROUP_SIZE):
     return codes, scales.flatten().to(FP16)
 
 
+def spine_table(spine_codes, spine_scale, ws_codes, ws_scales, wh_codes, wh_scales,
+                lut) -> torch.Tensor:
+    """(charts, 256) fp16 table of the 'int8' spine term per (chart, LUT index)."""
+    C = spine_scale.numel()
+    table = torch.empty(C, 256, dtype=FP16, device=spine_codes.device)
+    rc = _lib.lib().ksd8_ks3_spine_table(
+        C, spine_codes.data_ptr(), spine_scale.data_ptr(), _lib.ptr(ws_codes),
+        ws_scales.data_ptr(), _lib.ptr(wh_codes), wh_scales.data_ptr(), lut.data_ptr(),
+        table.data_ptr(), None, _lib.stream_ptr(spine_codes.device))
+    _lib.check(rc, "ks3_spine_table")
+    return table
+
+
 def spine_quant(coords: torch.Tensor, spine_codes, spine_scale, ws_codes, ws_scales, wh_codes,
-                wh_scales, lut, nonlinear: str) -> tuple[torch.Tensor, torch.Tensor]:
-    """Composed spine (_spine_features) on fp16 coords + GS128 requant of h."""
+                wh_scales, lut, nonlinear: str, table: torch.Tensor | None = None
+                ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Composed spine (_spine_features) on fp16 coords + GS128 requant of h.
+
+    In 'int8' mode the per-(chart, index) table is built (or taken from
+    `table`) and the table-driven kernel runs; the results are identical."""
+    M, C = coords.shape
+    G = (C + GROUP_SIZE - 1) // GROUP_SIZE
+    hq = torch.empty(M, C, dtype=torch.int8, device=coords.device)
+    hs = torch.empty(M, G, dtype=FP16, device=coords.device)
+    if nonlinear == "int8" and table is None:
+        table = spine_table(spine_codes, spine_scale, ws_codes, ws_scales, wh_codes, wh_scales,
+                            lut)
+    rc = _lib.lib().ksd8_ks3_spine_quant(
+        coords.data_ptr(), M, C, spine_codes.data_ptr(), spine_scale.data_ptr(),
+        _lib.ptr(ws_codes), ws_scales.data_ptr(), _lib.ptr(wh_codes), wh_scales.data_ptr(),
+        lut.data_ptr(), _lib.NL[nonlinear], _lib.ptr(table if nonlinear == "int8" else None),
+        hq.data_ptr(), hs.data_ptr(), None, _lib.stream_ptr(coords.device))
+    _lib.check(rc, "ks3_spine_quant")
+    return hq, hs
+
+
+def spine_quant_generic(coords, spine_codes, spine_scale, ws_codes, ws_scales, wh_codes,
+                        wh_scales, lut, nonlinear: str):
+    """The per-element (table-free) kernel for every mode; parity cross-check."""
     M, C = coords.shape
     G = (C + GROUP_SIZE - 1) // GROUP_SIZE
     hq = torch.empty(M, C, dtype=torch.int8, device=coords.device)
@@ -93,7 +129,7 @@ def spine_quant(coords: torch.Tensor, spine_codes, spine_scale, ws_codes, ws_sca
     rc = _lib.lib().ksd8_ks3_spine_quant(
         coords.data_ptr(), M, C, spine_codes.data_ptr(), spine_scale.data_ptr(),
         _lib.ptr(ws_codes), ws_scales.data_ptr(), _lib.ptr(wh_codes), wh_scales.data_ptr(),
-        lut.data_ptr(), _lib.NL[nonlinear], hq.data_ptr(), hs.data_ptr(), None,
+        lut.data_ptr(), _lib.NL[nonlinear], None, hq.data_ptr(), hs.data_ptr(), None,
         _lib.stream_ptr(coords.device))
     _lib.check(rc, "ks3_spine_quant")
     return hq, hs

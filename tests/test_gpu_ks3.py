@@ -74,6 +74,31 @@ def test_spine_quant_random_vs_oracle(oracle):
     np.testing.assert_array_equal(_bits(hs.cpu().numpy()), _bits(hs_o))
 
 
+def test_spine_table_path_equals_generic_path():
+    """Table-driven int8 kernel == per-element kernel, incl. zero/tiny/huge h."""
+    from ksdraft_b200.kernels.ks3_int8 import (make_tanh_lut, pack_small, spine_quant,
+                                               spine_quant_generic)
+    rng = np.random.default_rng(7)
+    C, M = 1024, 700
+    coeffs = (rng.standard_normal((C, 6)) * rng.choice([0.01, 0.3, 3.0], (C, 1))).astype(
+        np.float32)
+    rs = rng.uniform(-3, 4, C).astype(np.float32)
+    rh = rng.uniform(-3, 3, C).astype(np.float32)
+    p = pack_small(*(torch.from_numpy(t).cuda() for t in (coeffs, rs, rh)))
+    scale = rng.choice([1e-4, 1e-2, 1.0, 30.0, 3000.0], (M, 1))
+    coords = (rng.standard_normal((M, C)) * scale).astype(np.float16)
+    coords[:8] = 0
+    coords[8:16, :64] = np.float16(65504)
+    coords[16:24, :64] = np.float16(-65504)
+    coords[24:32] = np.float16(6e-8)
+    cd = torch.from_numpy(coords).cuda()
+    lut = make_tanh_lut("cuda")
+    hq_f, hs_f = spine_quant(cd, *p, lut, "int8")
+    hq_g, hs_g = spine_quant_generic(cd, *p, lut, "int8")
+    assert torch.equal(hq_f, hq_g)
+    assert torch.equal(hs_f.view(torch.int16), hs_g.view(torch.int16))
+
+
 def _layer_inputs(golden):
     g = golden("ks3_layer")
     from ksdraft_b200.kernels.ks3_int8 import KS3Int8Cell
