@@ -318,6 +318,37 @@ def run_profile_case(case: str, iters: int) -> None:
     elif case == "quant_cols":
         x = torch.randn(TOKENS, CHARTS, device=dev, generator=g).to(torch.bfloat16)
         fn = lambda: quantize_cols(x)  # noqa: E731
+    elif case == "requant_t":
+        hq = torch.randint(-127, 128, (TOKENS, CHARTS), dtype=torch.int8, device=dev,
+                           generator=g)
+        hs = (torch.rand(TOKENS, CHARTS // 128, device=dev, generator=g) * 0.01).half()
+        fn = lambda: quantize_cols(hq, x_scales=hs)  # noqa: E731
+    elif case in ("spine", "vjp"):
+        from ksdraft_b200 import _lib
+        from ksdraft_b200.kernels.ks3_int8 import make_tanh_lut, pack_small, spine_quant
+        coeffs = torch.randn(CHARTS, 6, device=dev, generator=g) * 0.05
+        rs = torch.full((CHARTS,), 0.75, device=dev)
+        rh = torch.zeros(CHARTS, device=dev)
+        p = pack_small(coeffs, rs, rh)
+        coords = (torch.randn(TOKENS, CHARTS, device=dev, generator=g) * 0.5).half()
+        if case == "spine":
+            lut = make_tanh_lut(dev)
+            fn = lambda: spine_quant(coords, *p, lut, "int8")  # noqa: E731
+        else:
+            value = (torch.randn(TOKENS, CHARTS, device=dev, generator=g) * 1e-3).half()
+            nt = TOKENS // 128
+            outs = [torch.empty(TOKENS, CHARTS, dtype=torch.int8, device=dev),
+                    torch.empty(TOKENS, CHARTS // 128, dtype=torch.float16, device=dev),
+                    torch.empty(CHARTS, TOKENS, dtype=torch.int8, device=dev),
+                    torch.empty(CHARTS, nt, dtype=torch.float16, device=dev),
+                    torch.empty(nt, 8, CHARTS, device=dev)]
+
+            def fn():
+                rc = _lib.lib().ksd8_ks3_vjp(value.data_ptr(), coords.data_ptr(), TOKENS, CHARTS,
+                                             *(t.data_ptr() for t in p),
+                                             *(o.data_ptr() for o in outs), None,
+                                             _lib.stream_ptr(dev))
+                _lib.check(rc, "vjp")
     else:
         raise SystemExit(f"unknown profile case {case}")
     for _ in range(iters + 1):

@@ -268,7 +268,7 @@ __global__ void ks3_spine_table_kernel(int64_t charts, const int8_t* spine_codes
 }
 
 __device__ __forceinline__ float spine_out_int8(float h) {
-  h = fmaxf(h, 0.f);
+  if (!(h > 0.f)) return 0.f;  // ReLU zero: pre = 2^-24, code 0, out 0
   const float y = h * 0.007874015718698502f;  // RN(1/127)
   const int low13 = (int)(__float_as_uint(y) & 0x1FFFu);
   if (y >= 6.103515625e-05f && y < 65504.f && abs(low13 - 0x1000) > 4) {
@@ -429,185 +429,204 @@ struct VjpPair {
   __half2 c0, c2, c4, cubic, quad, cubic3, quad2, c5x4, c4x2, c5x12, c4x4, c5x3, scale, shift;
 };
 
-constexpr int VJP_TM = 128;  // token rows per CTA (= one token-quantisation group)
-constexpr int VJP_TC = 128;  // charts per CTA (= one chart-quantisation group)
-constexpr int VJP_LD = VJP_TC + 1;
-constexpr int VJP_SMEM = (VJP_TM * VJP_LD + 8 * 8 * VJP_TC) * 4;
+constexpr int VJP_TM = 128;  // token rows per tile (= one token-quantisation group)
+constexpr int VJP_TC = 128;  // charts per tile (= one chart-quantisation group)
+constexpr int VJP_LDH = VJP_TC + 2;    // dc tile row pitch in halves (260 bytes)
+constexpr int TANH_N = 0x4600;         // fp16 bit patterns of |a| < 6.0 are tabulated
+constexpr int VJP_SMEM = TANH_N * 2 + VJP_TM * VJP_LDH * 2 + 8 * 8 * VJP_TC * 4;
 
-// fp16(tanh(x)) for an fp16 pair, tanh evaluated in fp32 (torch's Half tanh).
-__device__ __forceinline__ __half2 tanh16x2(__half2 x) {
-  const float2 f = __half22float2(x);
-  return __floats2half2_rn(tanhf(f.x), tanhf(f.y));
+// fp16(tanh(a)) of an fp16 value through the shared-memory table: entry i
+// holds fp16(tanhf(fp16 with bits i)) for |a| < 6 (above it the fp16 result is
+// 1.0); tanh is odd, so the sign bit is carried over.
+__device__ __forceinline__ __half2 tanh16x2(const uint16_t* tab, __half2 x) {
+  const uint32_t b = *reinterpret_cast<const uint32_t*>(&x);
+  const uint32_t m0 = b & 0x7FFFu, m1 = (b >> 16) & 0x7FFFu;
+  const uint32_t r0 = m0 < (uint32_t)TANH_N ? tab[m0] : (m0 > 0x7C00u ? m0 : 0x3C00u);
+  const uint32_t r1 = m1 < (uint32_t)TANH_N ? tab[m1] : (m1 > 0x7C00u ? m1 : 0x3C00u);
+  const uint32_t o = (r0 | (b & 0x8000u)) | ((r1 << 16) | (b & 0x80000000u));
+  return *reinterpret_cast<const __half2*>(&o);
 }
 
 // The fp16 VJP of ks3_int8.py:354-402 with native fp16 pair arithmetic.  Each
 // op of the reference (torch CPU Half: fp32 compute, round to fp16) equals the
 // correctly rounded fp16 op because double rounding through fp32 is
 // innocuous for fp16 operands (24 >= 2*11 + 2); the _rn intrinsics keep
-// multiplies and adds from being fused.
+// multiplies and adds from being fused.  CTAs loop over 128 x 128 tiles so the
+// tanh table built at the start is reused.
 __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
-  extern __shared__ float vsm[];
-  float* tile = vsm;                       // [VJP_TM][VJP_LD] dc values
-  float* red = vsm + VJP_TM * VJP_LD;      // [8 warps][8 sums][VJP_TC]
+  extern __shared__ __align__(16) uint8_t vsm_raw[];
+  uint16_t* ttab = reinterpret_cast<uint16_t*>(vsm_raw);                      // [TANH_N]
+  __half* tile = reinterpret_cast<__half*>(vsm_raw + TANH_N * 2);              // [TM][LDH]
+  float* red = reinterpret_cast<float*>(vsm_raw + TANH_N * 2 + VJP_TM * VJP_LDH * 2);
+  for (int i = threadIdx.x; i < TANH_N; i += blockDim.x)
+    ttab[i] = __half_as_ushort(__float2half_rn(tanhf(__half2float(__ushort_as_half(
+        (unsigned short)i)))));
+  __syncthreads();
+
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t m0 = (int64_t)blockIdx.y * VJP_TM;
-  const int64_t cg = blockIdx.x;           // chart group
-  const int64_t cbase = cg * VJP_TC + lane * 4;
-
-  VjpPair pr[2];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    __half cc[2][6], sc[2], sh[2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int64_t c = cbase + 2 * p + j;
-      const float ps = __half2float(a.spine_scale[c]);
-#pragma unroll
-      for (int k = 0; k < 6; ++k)
-        cc[j][k] = __float2half_rn((float)a.spine_codes[c * 6 + k] * ps);
-      sc[j] = __float2half_rn(dequant_scalar(a.ws_codes, a.ws_scales, c, true));
-      sh[j] = __float2half_rn(dequant_scalar(a.wh_codes, a.wh_scales, c, true));
-    }
-    __half2 c[6];
-#pragma unroll
-    for (int k = 0; k < 6; ++k) c[k] = __halves2half2(cc[0][k], cc[1][k]);
-    const __half2 two = __float2half2_rn(2.f), three = __float2half2_rn(3.f);
-    VjpPair& q = pr[p];
-    q.c0 = c[0]; q.c2 = c[2]; q.c4 = c[4];
-    // cubic = 2*c0 - 2*c1 + c2 + c3 ; quad = -3*c0 + 3*c1 - 2*c2 - c3
-    q.cubic = __hadd2_rn(__hadd2_rn(__hsub2_rn(__hmul2_rn(two, c[0]), __hmul2_rn(two, c[1])),
-                                    c[2]), c[3]);
-    q.quad = __hsub2_rn(__hsub2_rn(__hadd2_rn(__hmul2_rn(__float2half2_rn(-3.f), c[0]),
-                                              __hmul2_rn(three, c[1])),
-                                   __hmul2_rn(two, c[2])), c[3]);
-    q.cubic3 = __hmul2_rn(three, q.cubic);
-    q.quad2 = __hmul2_rn(two, q.quad);
-    q.c5x4 = __hmul2_rn(__float2half2_rn(4.f), c[5]);
-    q.c4x2 = __hmul2_rn(two, c[4]);
-    q.c5x12 = __hmul2_rn(__float2half2_rn(12.f), c[5]);
-    q.c4x4 = __hmul2_rn(__float2half2_rn(4.f), c[4]);
-    q.c5x3 = __hmul2_rn(three, c[5]);
-    q.scale = __halves2half2(sc[0], sc[1]);
-    q.shift = __halves2half2(sh[0], sh[1]);
-  }
-
-  float2 acc[2][8];
-#pragma unroll
-  for (int p = 0; p < 2; ++p)
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc[p][k] = make_float2(0.f, 0.f);
-
+  const int64_t n_cg = a.charts / VJP_TC;
+  const int64_t n_mt = (a.m + VJP_TM - 1) / VJP_TM;
+  const int64_t gcharts = a.charts / 128;
+  const int64_t mgroups = n_mt;
   const __half2 one = __float2half2_rn(1.f), two = __float2half2_rn(2.f);
   const __half2 three = __float2half2_rn(3.f), four = __float2half2_rn(4.f);
   const __half2 ntwo = __float2half2_rn(-2.f), quarter = __float2half2_rn(0.25f);
   const __half2 sixteenth = __float2half2_rn(0.0625f), zero = __float2half2_rn(0.f);
-  const int64_t gcharts = a.charts / 128;
-  for (int rr = warp; rr < VJP_TM; rr += 8) {
-    const int64_t r = m0 + rr;
-    float dcf[4] = {0.f, 0.f, 0.f, 0.f};
-    if (r < a.m) {
-      const uint2 vv = *reinterpret_cast<const uint2*>(a.value + r * a.charts + cbase);
-      const uint2 xv = *reinterpret_cast<const uint2*>(a.coords + r * a.charts + cbase);
-      const __half2 v2[2] = {*reinterpret_cast<const __half2*>(&vv.x),
-                             *reinterpret_cast<const __half2*>(&vv.y)};
-      const __half2 x2[2] = {*reinterpret_cast<const __half2*>(&xv.x),
-                             *reinterpret_cast<const __half2*>(&xv.y)};
+
+  for (int64_t tile_id = blockIdx.x; tile_id < n_cg * n_mt; tile_id += gridDim.x) {
+    const int64_t cg = tile_id % n_cg;
+    const int64_t mt = tile_id / n_cg;
+    const int64_t m0 = mt * VJP_TM;
+    const int64_t cbase = cg * VJP_TC + lane * 4;
+
+    VjpPair pr[2];
 #pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const VjpPair& q = pr[p];
-        const __half2 x16 = x2[p], value = v2[p];
-        const __half2 t = __hmul2_rn(four, tanh16x2(__hmul2_rn(x16, quarter)));
-        const __half2 u = __hadd2_rn(t, q.shift);
-        const __half2 z = tanh16x2(__hmul2_rn(q.scale, u));
-        __half2 sp = __hadd2_rn(__hmul2_rn(q.cubic, t), q.quad);
-        sp = __hadd2_rn(__hmul2_rn(sp, t), q.c2);
-        sp = __hadd2_rn(__hmul2_rn(sp, t), q.c0);
-        __half2 wp = __hadd2_rn(__hmul2_rn(q.c5x4, z), q.c4x2);
-        wp = __hsub2_rn(__hmul2_rn(wp, z), q.c5x3);
-        wp = __hsub2_rn(__hmul2_rn(wp, z), q.c4);
-        const __half2 rl = __hmax2(__hadd2_rn(__hadd2_rn(x16, sp), wp), zero);
-        const __half2 dpre = __hmul2_rn(__hmul2_rn(value, two), rl);
-        __half2 dpoly = __hadd2_rn(__hmul2_rn(q.cubic3, t), q.quad2);
-        dpoly = __hadd2_rn(__hmul2_rn(dpoly, t), q.c2);
-        __half2 dwarp = __hadd2_rn(__hmul2_rn(q.c5x12, z), q.c4x4);
-        dwarp = __hsub2_rn(__hmul2_rn(dwarp, z), q.c5x3);
-        const __half2 zz = __hmul2_rn(z, z);
-        const __half2 dz = __hmul2_rn(dwarp, __hsub2_rn(one, zz));
-        const __half2 tt = __hmul2_rn(t, t);
-        const __half2 dmean =
-            __hmul2_rn(__hmul2_rn(dpre, __hadd2_rn(dpoly, __hmul2_rn(dz, q.scale))),
-                       __hsub2_rn(one, __hmul2_rn(tt, sixteenth)));
-        const float2 dc = __half22float2(__hadd2_rn(value, dmean));
-        dcf[2 * p] = dc.x;
-        dcf[2 * p + 1] = dc.y;
-        const __half2 t3 = __hmul2_rn(tt, t);
-        const __half2 z3 = __hmul2_rn(zz, z);
-        const __half2 dd = __hmul2_rn(dpre, dz);
-        const __half2 terms[8] = {
-            __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(__hmul2_rn(two, t3), __hmul2_rn(three, tt)),
-                                        one)),
-            __hmul2_rn(dpre, __hadd2_rn(__hmul2_rn(ntwo, t3), __hmul2_rn(three, tt))),
-            __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(t3, __hmul2_rn(two, tt)), t)),
-            __hmul2_rn(dpre, __hsub2_rn(t3, tt)),
-            __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(two, zz), one)),
-            __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(four, z3), __hmul2_rn(three, z))),
-            __hmul2_rn(dd, u),
-            __hmul2_rn(dd, q.scale)};
+    for (int p = 0; p < 2; ++p) {
+      __half cc[2][6], sc[2], sh[2];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float2 f = __half22float2(terms[k]);
-          acc[p][k].x += f.x;
-          acc[p][k].y += f.y;
-        }
+      for (int j = 0; j < 2; ++j) {
+        const int64_t c = cbase + 2 * p + j;
+        const float ps = __half2float(a.spine_scale[c]);
+#pragma unroll
+        for (int k = 0; k < 6; ++k)
+          cc[j][k] = __float2half_rn((float)a.spine_codes[c * 6 + k] * ps);
+        sc[j] = __float2half_rn(dequant_scalar(a.ws_codes, a.ws_scales, c, true));
+        sh[j] = __float2half_rn(dequant_scalar(a.wh_codes, a.wh_scales, c, true));
       }
-      // dc quantised along charts: this row's 128 charts are one group.
-      float mx = fmaxf(fmaxf(fabsf(dcf[0]), fabsf(dcf[1])), fmaxf(fabsf(dcf[2]), fabsf(dcf[3])));
+      __half2 c[6];
+#pragma unroll
+      for (int k = 0; k < 6; ++k) c[k] = __halves2half2(cc[0][k], cc[1][k]);
+      VjpPair& q = pr[p];
+      q.c0 = c[0]; q.c2 = c[2]; q.c4 = c[4];
+      // cubic = 2*c0 - 2*c1 + c2 + c3 ; quad = -3*c0 + 3*c1 - 2*c2 - c3
+      q.cubic = __hadd2_rn(__hadd2_rn(__hsub2_rn(__hmul2_rn(two, c[0]), __hmul2_rn(two, c[1])),
+                                      c[2]), c[3]);
+      q.quad = __hsub2_rn(__hsub2_rn(__hadd2_rn(__hmul2_rn(__float2half2_rn(-3.f), c[0]),
+                                                __hmul2_rn(three, c[1])),
+                                     __hmul2_rn(two, c[2])), c[3]);
+      q.cubic3 = __hmul2_rn(three, q.cubic);
+      q.quad2 = __hmul2_rn(two, q.quad);
+      q.c5x4 = __hmul2_rn(four, c[5]);
+      q.c4x2 = __hmul2_rn(two, c[4]);
+      q.c5x12 = __hmul2_rn(__float2half2_rn(12.f), c[5]);
+      q.c4x4 = __hmul2_rn(four, c[4]);
+      q.c5x3 = __hmul2_rn(three, c[5]);
+      q.scale = __halves2half2(sc[0], sc[1]);
+      q.shift = __halves2half2(sh[0], sh[1]);
+    }
+
+    float2 acc[2][8];
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[p][k] = make_float2(0.f, 0.f);
+
+    for (int rr = warp; rr < VJP_TM; rr += 8) {
+      const int64_t r = m0 + rr;
+      __half2 dch[2] = {zero, zero};
+      if (r < a.m) {
+        const uint2 vv = *reinterpret_cast<const uint2*>(a.value + r * a.charts + cbase);
+        const uint2 xv = *reinterpret_cast<const uint2*>(a.coords + r * a.charts + cbase);
+        const __half2 v2[2] = {*reinterpret_cast<const __half2*>(&vv.x),
+                               *reinterpret_cast<const __half2*>(&vv.y)};
+        const __half2 x2[2] = {*reinterpret_cast<const __half2*>(&xv.x),
+                               *reinterpret_cast<const __half2*>(&xv.y)};
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const VjpPair& q = pr[p];
+          const __half2 x16 = x2[p], value = v2[p];
+          const __half2 t = __hmul2_rn(four, tanh16x2(ttab, __hmul2_rn(x16, quarter)));
+          const __half2 u = __hadd2_rn(t, q.shift);
+          const __half2 z = tanh16x2(ttab, __hmul2_rn(q.scale, u));
+          __half2 sp = __hadd2_rn(__hmul2_rn(q.cubic, t), q.quad);
+          sp = __hadd2_rn(__hmul2_rn(sp, t), q.c2);
+          sp = __hadd2_rn(__hmul2_rn(sp, t), q.c0);
+          __half2 wp = __hadd2_rn(__hmul2_rn(q.c5x4, z), q.c4x2);
+          wp = __hsub2_rn(__hmul2_rn(wp, z), q.c5x3);
+          wp = __hsub2_rn(__hmul2_rn(wp, z), q.c4);
+          const __half2 rl = __hmax2(__hadd2_rn(__hadd2_rn(x16, sp), wp), zero);
+          const __half2 dpre = __hmul2_rn(__hmul2_rn(value, two), rl);
+          __half2 dpoly = __hadd2_rn(__hmul2_rn(q.cubic3, t), q.quad2);
+          dpoly = __hadd2_rn(__hmul2_rn(dpoly, t), q.c2);
+          __half2 dwarp = __hadd2_rn(__hmul2_rn(q.c5x12, z), q.c4x4);
+          dwarp = __hsub2_rn(__hmul2_rn(dwarp, z), q.c5x3);
+          const __half2 zz = __hmul2_rn(z, z);
+          const __half2 dz = __hmul2_rn(dwarp, __hsub2_rn(one, zz));
+          const __half2 tt = __hmul2_rn(t, t);
+          const __half2 dmean =
+              __hmul2_rn(__hmul2_rn(dpre, __hadd2_rn(dpoly, __hmul2_rn(dz, q.scale))),
+                         __hsub2_rn(one, __hmul2_rn(tt, sixteenth)));
+          dch[p] = __hadd2_rn(value, dmean);
+          const __half2 t3 = __hmul2_rn(tt, t);
+          const __half2 z3 = __hmul2_rn(zz, z);
+          const __half2 dd = __hmul2_rn(dpre, dz);
+          const __half2 terms[8] = {
+              __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(__hmul2_rn(two, t3), __hmul2_rn(three, tt)),
+                                          one)),
+              __hmul2_rn(dpre, __hadd2_rn(__hmul2_rn(ntwo, t3), __hmul2_rn(three, tt))),
+              __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(t3, __hmul2_rn(two, tt)), t)),
+              __hmul2_rn(dpre, __hsub2_rn(t3, tt)),
+              __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(two, zz), one)),
+              __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(four, z3), __hmul2_rn(three, z))),
+              __hmul2_rn(dd, u),
+              __hmul2_rn(dd, q.scale)};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float2 f = __half22float2(terms[k]);
+            acc[p][k].x += f.x;
+            acc[p][k].y += f.y;
+          }
+        }
+        // dc quantised along charts: this row's 128 charts are one group.
+        const float2 d01 = __half22float2(dch[0]), d23 = __half22float2(dch[1]);
+        float mx = fmaxf(fmaxf(fabsf(d01.x), fabsf(d01.y)), fmaxf(fabsf(d23.x), fabsf(d23.y)));
+        mx = warp_max(mx);
+        __half shq;
+        const float s = gs_scale(mx, &shq);
+        const float rcp = __frcp_rn(s);
+        *reinterpret_cast<char4*>(a.dc_codes + r * a.charts + cbase) =
+            make_char4((char)gs_code_fast(d01.x, s, rcp), (char)gs_code_fast(d01.y, s, rcp),
+                       (char)gs_code_fast(d23.x, s, rcp), (char)gs_code_fast(d23.y, s, rcp));
+        if (lane == 0) a.dc_scales[r * gcharts + cg] = shq;
+      }
+      __half2* trow = reinterpret_cast<__half2*>(tile + rr * VJP_LDH + lane * 4);
+      trow[0] = dch[0];
+      trow[1] = dch[1];
+    }
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        *reinterpret_cast<float2*>(&red[(warp * 8 + k) * VJP_TC + lane * 4 + 2 * p]) =
+            acc[p][k];
+    __syncthreads();
+
+    // dc^T quantised along tokens: column c of the tile is one group of 128 tokens.
+    for (int cc = warp; cc < VJP_TC; cc += 8) {
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __half2float(tile[(lane + 32 * i) * VJP_LDH + cc]);
+      float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
       mx = warp_max(mx);
       __half shq;
       const float s = gs_scale(mx, &shq);
       const float rcp = __frcp_rn(s);
-      *reinterpret_cast<char4*>(a.dc_codes + r * a.charts + cbase) =
-          make_char4((char)gs_code_fast(dcf[0], s, rcp), (char)gs_code_fast(dcf[1], s, rcp),
-                     (char)gs_code_fast(dcf[2], s, rcp), (char)gs_code_fast(dcf[3], s, rcp));
-      if (lane == 0) a.dc_scales[r * gcharts + cg] = shq;
+      const int64_t c = cg * VJP_TC + cc;
+      int8_t* out = a.dct_codes + c * a.m + m0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (m0 + lane + 32 * i < a.m) out[lane + 32 * i] = (int8_t)gs_code_fast(v[i], s, rcp);
+      if (lane == 0) a.dct_scales[c * mgroups + mt] = shq;
     }
+    // Column partials: fixed-order sum over the 8 warps.
+    for (int idx = threadIdx.x; idx < 8 * VJP_TC; idx += blockDim.x) {
+      const int k = idx / VJP_TC, cc = idx % VJP_TC;
+      float sum = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) tile[rr * VJP_LD + lane * 4 + i] = dcf[i];
-  }
-#pragma unroll
-  for (int p = 0; p < 2; ++p)
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      red[(warp * 8 + k) * VJP_TC + lane * 4 + 2 * p] = acc[p][k].x;
-      red[(warp * 8 + k) * VJP_TC + lane * 4 + 2 * p + 1] = acc[p][k].y;
+      for (int w = 0; w < 8; ++w) sum += red[(w * 8 + k) * VJP_TC + cc];
+      a.partials[(mt * 8 + k) * a.charts + cg * VJP_TC + cc] = sum;
     }
-  __syncthreads();
-
-  // dc^T quantised along tokens: column c of the tile is one group of 128 tokens.
-  const int64_t mgroups = (a.m + 127) / 128;
-  for (int cc = warp; cc < VJP_TC; cc += 8) {
-    float v[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = tile[(lane + 32 * i) * VJP_LD + cc];
-    float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    mx = warp_max(mx);
-    __half shq;
-    const float s = gs_scale(mx, &shq);
-    const float rcp = __frcp_rn(s);
-    const int64_t c = cg * VJP_TC + cc;
-    int8_t* out = a.dct_codes + c * a.m + m0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (m0 + lane + 32 * i < a.m) out[lane + 32 * i] = (int8_t)gs_code_fast(v[i], s, rcp);
-    if (lane == 0) a.dct_scales[c * mgroups + blockIdx.y] = shq;
-  }
-  // Column partials: fixed-order sum over the 8 warps.
-  for (int idx = threadIdx.x; idx < 8 * VJP_TC; idx += blockDim.x) {
-    const int k = idx / VJP_TC, cc = idx % VJP_TC;
-    float sum = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) sum += red[(w * 8 + k) * VJP_TC + cc];
-    a.partials[((int64_t)blockIdx.y * 8 + k) * a.charts + cg * VJP_TC + cc] = sum;
+    __syncthreads();
   }
 }
 
@@ -743,8 +762,9 @@ int ksd8_ks3_vjp_launch(const void* value, const void* coords, int64_t m, int64_
   a.dc_codes = dc_codes; a.dc_scales = reinterpret_cast<__half*>(dc_scales);
   a.dct_codes = dct_codes; a.dct_scales = reinterpret_cast<__half*>(dct_scales);
   a.partials = partials;
-  dim3 grid((unsigned)(charts / VJP_TC), (unsigned)((m + VJP_TM - 1) / VJP_TM));
-  ks3_vjp_kernel<<<grid, 256, VJP_SMEM, stream>>>(a);
+  const int64_t tiles = (charts / VJP_TC) * ((m + VJP_TM - 1) / VJP_TM);
+  const int64_t grid = tiles < 2 * 148 ? tiles : 2 * 148;  // 2 resident CTAs per SM
+  ks3_vjp_kernel<<<(unsigned)grid, 256, VJP_SMEM, stream>>>(a);
   return KSD8_OK;
 }
 
