@@ -254,12 +254,41 @@ __device__ __forceinline__ int gs_code(float x, float scale) {
 // (rcp = RN(1/scale)) is within 2^-16 of RN(x/scale) for |x/scale| < 256, so
 // rint(y) == rint(RN(x/scale)) unless y lies within 2^-14 of a half-integer;
 // those (and out-of-range quotients) take the IEEE division.
+// rcp may be the 1-ulp approximation of rcp_approx: |y - RN(x/scale)| then
+// stays below 2^-14 for |y| < 200, and the margin used is 2^-13.  The integer
+// is formed with the 1.5 * 2^23 shifter (round half to even, exact for
+// |y| < 2^22) on the FMA/ALU pipes instead of the conversion unit.
 __device__ __forceinline__ int gs_code_fast(float x, float scale, float rcp) {
-  const float y = x * rcp;
-  const float r = rintf(y);
-  if (fabsf(y) < 200.f && fabsf(y - r) < 0.49993896484375f)  // 0.5 - 2^-14
-    return (int)fminf(fmaxf(r, -127.f), 127.f);
+  const float y = __fmul_rn(x, rcp);
+  const float t = __fadd_rn(y, 12582912.f);
+  const float r = __fsub_rn(t, 12582912.f);
+  if (fabsf(y) < 200.f && fabsf(__fsub_rn(y, r)) < 0.4998779296875f) {  // 0.5 - 2^-13
+    const int q = __float_as_int(t) - 0x4B400000;
+    return min(max(q, -127), 127);
+  }
   return gs_code(x, scale);
+}
+
+// 1/s to within 1 ulp (s a normal fp32; GS scales are >= 2^-24).
+__device__ __forceinline__ float rcp_approx(float s) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+  return r;
+}
+
+// gs_scale without the division on the common path: y = amax * RN(1/127) is
+// within 2.5 ulp of RN(amax/127); unless y sits within 4 ulp of an fp16
+// rounding midpoint (or outside the normal fp16 range) fp16(y) is the exact
+// answer, otherwise the IEEE path decides.
+__device__ __forceinline__ float gs_scale_fast(float amax, __half* out_h) {
+  const float y = __fmul_rn(amax, 0.007874015718698502f);
+  const int low13 = (int)(__float_as_uint(y) & 0x1FFFu);
+  if (y >= 6.103515625e-05f && y < 65504.f && abs(low13 - 0x1000) > 4) {
+    const __half h = __float2half_rn(y);
+    if (out_h) *out_h = h;
+    return __half2float(h);
+  }
+  return gs_scale(amax, out_h);
 }
 
 // ---------------------------------------------------------------- Philox4x32-10

@@ -353,8 +353,8 @@ __global__ void __launch_bounds__(256) ks3_spine_int8_fast_kernel(SpineFastArgs 
     float mx = fmaxf(fmaxf(h[0], h[1]), fmaxf(h[2], h[3]));  // h >= 0
     mx = warp_max(mx);
     __half sh;
-    const float scale = gs_scale(mx, &sh);
-    const float rcp = __frcp_rn(scale);
+    const float scale = gs_scale_fast(mx, &sh);
+    const float rcp = rcp_approx(scale);
     int8_t* out = a.h_codes + r * a.charts + cbase;
     const int q0 = gs_code_fast(h[0], scale, rcp), q1 = gs_code_fast(h[1], scale, rcp);
     const int q2 = gs_code_fast(h[2], scale, rcp), q3 = gs_code_fast(h[3], scale, rcp);
@@ -582,8 +582,8 @@ __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
         float mx = fmaxf(fmaxf(fabsf(d01.x), fabsf(d01.y)), fmaxf(fabsf(d23.x), fabsf(d23.y)));
         mx = warp_max(mx);
         __half shq;
-        const float s = gs_scale(mx, &shq);
-        const float rcp = __frcp_rn(s);
+        const float s = gs_scale_fast(mx, &shq);
+        const float rcp = rcp_approx(s);
         *reinterpret_cast<char4*>(a.dc_codes + r * a.charts + cbase) =
             make_char4((char)gs_code_fast(d01.x, s, rcp), (char)gs_code_fast(d01.y, s, rcp),
                        (char)gs_code_fast(d23.x, s, rcp), (char)gs_code_fast(d23.y, s, rcp));
@@ -601,32 +601,59 @@ __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
             acc[p][k];
     __syncthreads();
 
-    // dc^T quantised along tokens: column c of the tile is one group of 128 tokens.
-    for (int cc = warp; cc < VJP_TC; cc += 8) {
-      float v[4];
+    // dc^T quantised along tokens: column c of the tile is one group of 128
+    // tokens.  Thread t owns column t % 128 and rows (t / 128) * 64 .. +64.
+    {
+      float* s_amax = red;  // reuse: [2][VJP_TC] after the partials are consumed below
+      const int cc = threadIdx.x & (VJP_TC - 1), half = threadIdx.x >> 7;
+      float mx = 0.f;
+#pragma unroll 16
+      for (int i = 0; i < 64; ++i)
+        mx = fmaxf(mx, fabsf(__half2float(tile[(half * 64 + i) * VJP_LDH + cc])));
+      // column partials first (they read `red`), then the amax exchange
+      for (int idx = threadIdx.x; idx < 8 * VJP_TC; idx += blockDim.x) {
+        const int k = idx / VJP_TC, c2 = idx % VJP_TC;
+        float sum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = __half2float(tile[(lane + 32 * i) * VJP_LDH + cc]);
-      float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-      mx = warp_max(mx);
+        for (int w = 0; w < 8; ++w) sum += red[(w * 8 + k) * VJP_TC + c2];
+        a.partials[(mt * 8 + k) * a.charts + cg * VJP_TC + c2] = sum;
+      }
+      __syncthreads();
+      s_amax[half * VJP_TC + cc] = mx;
+      __syncthreads();
+      mx = fmaxf(s_amax[cc], s_amax[VJP_TC + cc]);
       __half shq;
-      const float s = gs_scale(mx, &shq);
-      const float rcp = __frcp_rn(s);
+      const float s = gs_scale_fast(mx, &shq);
+      const float rcp = rcp_approx(s);
       const int64_t c = cg * VJP_TC + cc;
-      int8_t* out = a.dct_codes + c * a.m + m0;
+      const int64_t rb = m0 + half * 64;
+      int8_t* out = a.dct_codes + c * a.m + rb;
+      if (rb + 64 <= a.m && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (m0 + lane + 32 * i < a.m) out[lane + 32 * i] = (int8_t)gs_code_fast(v[i], s, rcp);
-      if (lane == 0) a.dct_scales[c * mgroups + mt] = shq;
-    }
-    // Column partials: fixed-order sum over the 8 warps.
-    for (int idx = threadIdx.x; idx < 8 * VJP_TC; idx += blockDim.x) {
-      const int k = idx / VJP_TC, cc = idx % VJP_TC;
-      float sum = 0.f;
+        for (int v = 0; v < 4; ++v) {
+          uint32_t w4[4];
 #pragma unroll
-      for (int w = 0; w < 8; ++w) sum += red[(w * 8 + k) * VJP_TC + cc];
-      a.partials[(mt * 8 + k) * a.charts + cg * VJP_TC + cc] = sum;
+          for (int j = 0; j < 4; ++j) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const int rr = half * 64 + v * 16 + j * 4 + b;
+              const int q = gs_code_fast(__half2float(tile[rr * VJP_LDH + cc]), s, rcp);
+              word |= (uint32_t)(q & 0xFF) << (8 * b);
+            }
+            w4[j] = word;
+          }
+          *reinterpret_cast<uint4*>(out + v * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      } else {
+        for (int i = 0; i < 64; ++i)
+          if (rb + i < a.m)
+            out[i] = (int8_t)gs_code_fast(__half2float(tile[(half * 64 + i) * VJP_LDH + cc]), s,
+                                          rcp);
+      }
+      if (half == 0) a.dct_scales[c * mgroups + mt] = shq;
     }
-    __syncthreads();
+    __syncthreads();  // tile / red are rewritten by the next tile
   }
 }
 

@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(QRowArgs a) {
     float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     m = warp_max(m);
     __half sh;
-    const float scale = gs_scale(m, &sh);
+    const float scale = gs_scale_fast(m, &sh);
     int q[4];
     if (a.flags & KSD8_Q_DITHER) {
       // one Philox block serves the 4 consecutive elements when they share it
@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(QRowArgs a) {
         q[i] = (int)t;
       }
     } else {
-      const float rcp = __frcp_rn(scale);
+      const float rcp = rcp_approx(scale);
 #pragma unroll
       for (int i = 0; i < 4; ++i) q[i] = gs_code_fast(v[i], scale, rcp);
     }
@@ -212,28 +212,49 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
 #pragma unroll
     for (int i = 0; i < VN; ++i) tile[rr * QC_LD + vv * VN + i] = v[i];
   }
+  // Thread t owns column t % 128, rows (t / 128) * 64 .. +64: a per-thread
+  // amax (conflict-free: consecutive lanes read consecutive columns), one
+  // exchange for the other half, then 64 codes written as 16-byte vectors of
+  // the x^T row.
+  __shared__ float s_amax[2][QC_TC];
+  const int cc = tid & (QC_TC - 1), half = tid >> 7;
+  const int64_t c = c0 + cc;
+  float m = 0.f;
+#pragma unroll 16
+  for (int i = 0; i < 64; ++i) m = fmaxf(m, fabsf(tile[(half * 64 + i) * QC_LD + cc]));
+  s_amax[half][cc] = m;
   __syncthreads();
-  const int warp = tid >> 5, lane = tid & 31;
+  if (c >= a.cols) return;
+  m = fmaxf(s_amax[0][cc], s_amax[1][cc]);
   const int64_t rgroups = (a.rows + 127) / 128;
-  for (int cc = warp; cc < QC_TC; cc += 8) {
-    const int64_t c = c0 + cc;
-    if (c >= a.cols) break;
-    float v[4];
+  __half sh;
+  const float scale = gs_scale_fast(m, &sh);
+  const float rcp = rcp_approx(scale);
+  const int64_t rb = r0 + half * 64;
+  int8_t* out = a.codes_t + c * a.ldct + rb;
+  if (rb + 64 <= a.rows && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = tile[(lane + 32 * i) * QC_LD + cc];
-    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    m = warp_max(m);
-    __half sh;
-    const float scale = gs_scale(m, &sh);
-    const float rcp = __frcp_rn(scale);
-    int8_t* out = a.codes_t + c * a.ldct + r0;
+    for (int v = 0; v < 4; ++v) {
+      uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t r = r0 + lane + 32 * i;
-      if (r < a.rows) out[lane + 32 * i] = (int8_t)gs_code_fast(v[i], scale, rcp);
+      for (int j = 0; j < 4; ++j) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int rr = half * 64 + v * 16 + j * 4 + b;
+          const int q = gs_code_fast(tile[rr * QC_LD + cc], scale, rcp);
+          word |= (uint32_t)(q & 0xFF) << (8 * b);
+        }
+        w[j] = word;
+      }
+      *reinterpret_cast<uint4*>(out + v * 16) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    if (lane == 0) a.scales_t[c * rgroups + blockIdx.y] = sh;
+  } else {
+    for (int i = 0; i < 64; ++i)
+      if (rb + i < a.rows) out[i] = (int8_t)gs_code_fast(tile[(half * 64 + i) * QC_LD + cc],
+                                                         scale, rcp);
   }
+  if (half == 0) a.scales_t[c * rgroups + blockIdx.y] = sh;
 }
 
 __global__ void philox_uniform_kernel(uint64_t seed, uint64_t offset, int64_t n, float* out) {
