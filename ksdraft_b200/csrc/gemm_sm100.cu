@@ -9,21 +9,30 @@
 //     s   = sa[m,g] * sw[n,g]                (fp32, round to nearest)
 //     acc = fmaf(float(dot_g[m,n]), s, acc)  for g = 0 .. G-1, acc0 = 0
 //
-// Structure (one 128 x BN output tile per CTA, warp-specialised):
+// Persistent, warp-specialised kernel; each CTA walks output tiles of
+// 128 x BN (static round robin) and, inside a tile, the K groups:
 //   warp 0       TMA producer: A tile (128 rows x 128 B) and W tile (BN rows x
-//                128 B) of K group g into an smem ring of STAGES slots,
+//                128 B) of a K group into an smem ring of STAGES slots,
 //                128-byte swizzle, no multicast.
 //   warp 1       TMEM allocation + single-thread MMA issue: 4 x
 //                tcgen05.mma.kind::i8 (K = 32 each) per group into one of two
-//                int32 accumulators in TMEM (ping-pong), commits to the smem
-//                slot's "empty" barrier and to the accumulator's "full" barrier.
+//                int32 accumulators in TMEM (ping-pong across groups and
+//                tiles); commits to the smem slot's "empty" barrier and to the
+//                accumulator's "full" barrier.
 //   warp 2       scale loader: fp16 sa[m0.., g] and sw[n0.., g] -> fp32 ring.
-//   warps 3..    epilogue: tcgen05.ld of the group's int32 accumulator, the
-//                fp32 fma above into registers (each thread owns one row and
-//                CPT consecutive columns), release of the accumulator; after
-//                the last group the bias/convert/store epilogue.
-// The int32 accumulator of group g+1 is produced by the tensor cores while
-// the epilogue warps scale group g.
+//   warp 3       idle (completes the role warpgroup)
+//   warps 4..    epilogue: each thread owns one row and CPT consecutive
+//                columns of the tile.  Per group it loads the int32
+//                accumulator from TMEM (one chunk ahead), adds it into its fp32
+//                registers with packed f32x2 ops, re-arms the TMEM chunk and
+//                releases it; after the tile's last group it converts and
+//                stores the row segment while the tensor cores already work
+//                on the next tile.
+// Conversion trick: every accumulator is pre-set (tcgen05.st) to the bit
+// pattern of 1.5 * 2^23, so after the group's MMAs it holds that pattern
+// plus the int32 dot product, i.e. the fp32 number 12582912 + dot (exact for
+// |dot| < 2^22; here |dot| <= 128 * 128 * 128 = 2^21).  One packed fp32
+// subtraction gives float(dot) with no int->float conversion.
 #include "common.cuh"
 
 namespace ksd8 {
@@ -41,9 +50,11 @@ struct GemmArgs {
 };
 
 constexpr int BM = 128;
-constexpr int BK = 128;  // one GS128 group of int8 = one 128-byte swizzled row
-constexpr int SRING = 8; // scale ring slots
-constexpr int SBATCH = 4; // groups of scales fetched per round by the scale warp
+constexpr int BK = 128;    // one GS128 group of int8 = one 128-byte swizzled row
+constexpr int SRING = 8;   // scale ring slots
+constexpr int SBATCH = 2;  // groups of scales fetched per round by the scale warp
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 1.5 * 2^23
+constexpr float MAGIC_F = 12582912.0f;
 
 template <int BN, int EPI_WARPS, int STAGES>
 struct GemmSmem {
@@ -61,15 +72,56 @@ struct GemmSmem {
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
 };
 
+__device__ __forceinline__ void tmem_st_magic_x8(uint32_t taddr) {
+  const uint32_t m = MAGIC_BITS;
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(
+          taddr),
+      "r"(m)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+}
+
+template <int W>
+__device__ __forceinline__ void tmem_ld_w(uint32_t taddr, uint32_t (&r)[W]) {
+  if constexpr (W == 8) tmem_ld_32x32b_x8(taddr, r);
+  else tmem_ld_32x32b_x16(taddr, r);
+}
+
+template <int W>
+__device__ __forceinline__ void tmem_st_magic_w(uint32_t taddr) {
+#pragma unroll
+  for (int i = 0; i < W; i += 8) tmem_st_magic_x8(taddr + i);
+}
+
+// Register split for the 12-warp (384-thread) variant: the block launches at
+// 168 registers per thread (64512 in total); the role warpgroup drops to 88
+// and the two epilogue warpgroups rise to 208: 128 * 88 + 256 * 208 = 64512.
+constexpr int REG_LAUNCH = 168, REG_ROLE = 88, REG_EPI = 208;
+static_assert(128 * REG_ROLE + 256 * REG_EPI <= 384 * REG_LAUNCH, "register split");
+
 template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS>
-__global__ void __launch_bounds__((3 + EPI_WARPS) * 32, 1)
+__global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   using L = GemmSmem<BN, EPI_WARPS, STAGES>;
+  constexpr bool REGSPLIT = (4 + EPI_WARPS) * 32 == 384;
   constexpr int CPT = BN * 4 / EPI_WARPS;  // columns per epilogue thread
-  constexpr int LDW = CPT >= 128 && EPI_WARPS > 4 ? 16 : 32;  // TMEM load width (registers)
+  constexpr int LDW = 16;  // TMEM load width (registers per chunk)
+  constexpr int NCH = CPT / LDW;
   constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
-  static_assert(CPT % 32 == 0, "epilogue chunking");
+  static_assert(CPT % LDW == 0 && LDW % 4 == 0, "epilogue chunking");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
 
   extern __shared__ uint8_t smem_raw[];
@@ -90,9 +142,10 @@ __global__ void __launch_bounds__((3 + EPI_WARPS) * 32, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * BM;
   const int G = args.G;
+  const int tiles_m = (args.M + BM - 1) / BM;
+  const int tiles_n = (args.N + BN - 1) / BN;
+  const int n_tiles = tiles_m * tiles_n;
   constexpr int EPI_THREADS = EPI_WARPS * 32;
 
   if (threadIdx.x == 0) {
@@ -124,207 +177,280 @@ __global__ void __launch_bounds__((3 + EPI_WARPS) * 32, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Role warpgroup (warps 0-3) and epilogue warpgroups each change their
+  // register allotment first, then dispatch on the warp index.
+  if (warp < 4) {
+    if constexpr (REGSPLIT) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_ROLE));
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    for (int g = 0; g < G; ++g) {
-      const int s = g % STAGES;
-      const uint32_t ph = (g / STAGES) & 1;
-      if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, args.status)) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
-        tma_load_2d(sA + s * L::A_BYTES, &tmA, &full[s], g * BK, m0);
-        tma_load_2d(sB + s * L::B_BYTES, &tmB, &full[s], g * BK, n0);
+    int gg = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+      for (int g = 0; g < G; ++g, ++gg) {
+        const int s = gg % STAGES;
+        const uint32_t ph = (gg / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, args.status)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+          tma_load_2d(sA + s * L::A_BYTES, &tmA, &full[s], g * BK, m0);
+          tma_load_2d(sB + s * L::B_BYTES, &tmB, &full[s], g * BK, n0);
+        }
+        __syncwarp();
       }
-      __syncwarp();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t IDESC = idesc_i8(BM, BN);
-    for (int g = 0; g < G; ++g) {
-      const int s = g % STAGES;
-      const uint32_t ph = (g / STAGES) & 1;
-      const int buf = g & 1;
-      const uint32_t aph = (g >> 1) & 1;
-      if (!mbar_wait(&full[s], ph, abort_flag, args.status)) break;
-      if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort_flag, args.status)) break;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t a_addr = smem_u32(sA + s * L::A_BYTES);
-        const uint32_t b_addr = smem_u32(sB + s * L::B_BYTES);
-        const uint32_t d_tmem = tmem_base + buf * BN;
+    int gg = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      for (int g = 0; g < G; ++g, ++gg) {
+        const int s = gg % STAGES;
+        const uint32_t ph = (gg / STAGES) & 1;
+        const int buf = gg & 1;
+        const uint32_t aph = (gg >> 1) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag, args.status)) { ok = false; break; }
+        if (!mbar_wait(&acc_empty[buf], aph, abort_flag, args.status)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(sA + s * L::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * L::B_BYTES);
+          const uint32_t d_tmem = tmem_base + buf * BN;
 #pragma unroll
-        for (int kk = 0; kk < BK / 32; ++kk) {
-          mma_i8(d_tmem, smem_desc_k128_sw128(a_addr + kk * 32),
-                 smem_desc_k128_sw128(b_addr + kk * 32), IDESC, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            mma_i8(d_tmem, smem_desc_k128_sw128(a_addr + kk * 32),
+                   smem_desc_k128_sw128(b_addr + kk * 32), IDESC, 1u);
+          }
+          mma_commit(&empty[s]);
+          mma_commit(&acc_full[buf]);
         }
-        mma_commit(&empty[s]);
-        mma_commit(&acc_full[buf]);
+        __syncwarp();
       }
-      __syncwarp();
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------ scale loader
-    for (int g0 = 0; g0 < G; g0 += SBATCH) {
-      float va[SBATCH][BM / 32];
-      float vw[SBATCH][BN / 32];
+    int gg0 = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+      for (int g0 = 0; ok && g0 < G; g0 += SBATCH) {
+        float va[SBATCH][BM / 32];
+        float vw[SBATCH][BN / 32];
 #pragma unroll
-      for (int j = 0; j < SBATCH; ++j) {
-        const int g = g0 + j;
+        for (int j = 0; j < SBATCH; ++j) {
+          const int g = g0 + j;
 #pragma unroll
-        for (int i = 0; i < BM / 32; ++i) {
-          const int r = m0 + lane + 32 * i;
-          va[j][i] = (PARTIALS || g >= G || r >= args.M)
-                         ? 0.f
-                         : __half2float(args.a_scales[(size_t)r * G + g]);
+          for (int i = 0; i < BM / 32; ++i) {
+            const int r = m0 + lane + 32 * i;
+            va[j][i] = (PARTIALS || g >= G || r >= args.M)
+                           ? 0.f
+                           : __half2float(args.a_scales[(size_t)r * G + g]);
+          }
+#pragma unroll
+          for (int i = 0; i < BN / 32; ++i) {
+            const int c = n0 + lane + 32 * i;
+            vw[j][i] = (PARTIALS || g >= G || c >= args.N)
+                           ? 0.f
+                           : __half2float(args.w_scales[(size_t)c * G + g]);
+          }
         }
 #pragma unroll
-        for (int i = 0; i < BN / 32; ++i) {
-          const int c = n0 + lane + 32 * i;
-          vw[j][i] = (PARTIALS || g >= G || c >= args.N)
-                         ? 0.f
-                         : __half2float(args.w_scales[(size_t)c * G + g]);
+        for (int j = 0; j < SBATCH; ++j) {
+          const int g = g0 + j;
+          // no early exit inside this unrolled loop: va/vw must stay in registers
+          if (ok && g < G) {
+            const int gg = gg0 + g;
+            const int slot = gg % SRING;
+            const uint32_t ph = (gg / SRING) & 1;
+            if (mbar_wait(&s_empty[slot], ph ^ 1, abort_flag, args.status)) {
+              float* dst = sScale + slot * L::SCALE_FLOATS;
+#pragma unroll
+              for (int i = 0; i < BM / 32; ++i) dst[lane + 32 * i] = va[j][i];
+#pragma unroll
+              for (int i = 0; i < BN / 32; ++i) dst[BM + lane + 32 * i] = vw[j][i];
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&s_full[slot]);
+            } else {
+              ok = false;
+            }
+          }
         }
       }
-      bool ok = true;
-#pragma unroll
-      for (int j = 0; j < SBATCH; ++j) {
-        const int g = g0 + j;
-        if (g >= G) break;
-        const int slot = g % SRING;
-        const uint32_t ph = (g / SRING) & 1;
-        if (!mbar_wait(&s_empty[slot], ph ^ 1, abort_flag, args.status)) { ok = false; break; }
-        float* dst = sScale + slot * L::SCALE_FLOATS;
-#pragma unroll
-        for (int i = 0; i < BM / 32; ++i) dst[lane + 32 * i] = va[j][i];
-#pragma unroll
-        for (int i = 0; i < BN / 32; ++i) dst[BM + lane + 32 * i] = vw[j][i];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_full[slot]);
-      }
-      if (!ok) break;
+      gg0 += G;
     }
+  }  // warp 3: idle
   } else {
+    if constexpr (REGSPLIT) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_EPI));
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 3;               // 0 .. EPI_WARPS-1
+    const int ew = warp - 4;               // 0 .. EPI_WARPS-1
     const int quad = warp & 3;             // TMEM lane quadrant this warp may access
     const int chalf = ew >> 2;             // which CPT-wide column slice
     const int row = quad * 32 + lane;      // row within the tile
     const int col0 = chalf * CPT;          // first column within the tile
     const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16);
 
-    float acc[CPT];
+    // Arm both accumulator buffers with the conversion offset.
 #pragma unroll
-    for (int i = 0; i < CPT; ++i) acc[i] = 0.f;
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) tmem_st_magic_w<LDW>(t_row + b * BN + col0 + c * LDW);
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(&acc_empty[0]);
+    mbar_arrive(&acc_empty[1]);
+
+    const float2 neg_magic = make_float2(-MAGIC_F, -MAGIC_F);
+    float2 acc[CPT / 2];
     bool ok = true;
-
-    for (int g = 0; g < G; ++g) {
-      const int buf = g & 1;
-      const uint32_t aph = (g >> 1) & 1;
-      const int slot = g % SRING;
-      const uint32_t sph = (g / SRING) & 1;
-      if (!mbar_wait(&acc_full[buf], aph, abort_flag, args.status)) { ok = false; break; }
-      if (!mbar_wait(&s_full[slot], sph, abort_flag, args.status)) { ok = false; break; }
-      tc_fence_after();
-      const float* sc = sScale + slot * L::SCALE_FLOATS;
-      const float sa = sc[row];
-      const float* sw = sc + BM + col0;
+    int gg = 0;
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
 #pragma unroll
-      for (int c = 0; c < CPT / LDW; ++c) {
-        uint32_t r[LDW];
-        tmem_ld_cols<LDW>(t_row + buf * BN + col0 + c * LDW, r);
+      for (int i = 0; i < CPT / 2; ++i) acc[i] = make_float2(0.f, 0.f);
+      for (int g = 0; g < G; ++g, ++gg) {
+        const int buf = gg & 1;
+        const uint32_t aph = (gg >> 1) & 1;
+        const int slot = gg % SRING;
+        const uint32_t sph = (gg / SRING) & 1;
+        if (!mbar_wait(&acc_full[buf], aph, abort_flag, args.status)) { ok = false; break; }
+        if (!mbar_wait(&s_full[slot], sph, abort_flag, args.status)) { ok = false; break; }
+        tc_fence_after();
+        const float* sc = sScale + slot * L::SCALE_FLOATS;
+        const float sa = sc[row];
+        const float2 sa2 = make_float2(sa, sa);
+        const float* sw = sc + BM + col0;
+        const uint32_t tb = t_row + buf * BN + col0;
+        uint32_t r[2][LDW];
+        tmem_ld_w<LDW>(tb, r[0]);
         tmem_wait_ld();
-        if constexpr (PARTIALS) {
-          const int m = m0 + row;
-          if (m < args.M) {
-            int32_t* o = reinterpret_cast<int32_t*>(args.out) +
-                         ((size_t)g * args.M + m) * args.N;
 #pragma unroll
-            for (int j = 0; j < LDW; ++j) {
-              const int n = n0 + col0 + c * LDW + j;
-              if (n < args.N) o[n] = (int32_t)r[j];
+        for (int c = 0; c < NCH; ++c) {
+          if (c + 1 < NCH) tmem_ld_w<LDW>(tb + (c + 1) * LDW, r[(c + 1) & 1]);
+          const uint32_t* rc = r[c & 1];
+          if constexpr (PARTIALS) {
+            const int m = m0 + row;
+            if (m < args.M) {
+              int32_t* o = reinterpret_cast<int32_t*>(args.out) +
+                           ((size_t)g * args.M + m) * args.N;
+#pragma unroll
+              for (int j = 0; j < LDW; ++j) {
+                const int n = n0 + col0 + c * LDW + j;
+                if (n < args.N) o[n] = (int32_t)(rc[j] - MAGIC_BITS);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < LDW; j += 4) {
+              const float4 w4 = *reinterpret_cast<const float4*>(sw + c * LDW + j);
+              const int o = (c * LDW + j) / 2;
+              const float2 d0 = __fadd2_rn(
+                  make_float2(__uint_as_float(rc[j]), __uint_as_float(rc[j + 1])), neg_magic);
+              const float2 d1 = __fadd2_rn(
+                  make_float2(__uint_as_float(rc[j + 2]), __uint_as_float(rc[j + 3])),
+                  neg_magic);
+              acc[o] = __ffma2_rn(d0, __fmul2_rn(sa2, make_float2(w4.x, w4.y)), acc[o]);
+              acc[o + 1] = __ffma2_rn(d1, __fmul2_rn(sa2, make_float2(w4.z, w4.w)), acc[o + 1]);
             }
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < LDW; j += 4) {
-            const int o = c * LDW + j;
-            const float4 w4 = *reinterpret_cast<const float4*>(sw + o);
-            acc[o + 0] = fmaf(i2f_exact22((int32_t)r[j + 0]), sa * w4.x, acc[o + 0]);
-            acc[o + 1] = fmaf(i2f_exact22((int32_t)r[j + 1]), sa * w4.y, acc[o + 1]);
-            acc[o + 2] = fmaf(i2f_exact22((int32_t)r[j + 2]), sa * w4.z, acc[o + 2]);
-            acc[o + 3] = fmaf(i2f_exact22((int32_t)r[j + 3]), sa * w4.w, acc[o + 3]);
-          }
+          tmem_st_magic_w<LDW>(tb + c * LDW);
+          if (c + 1 < NCH) tmem_wait_ld();
         }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        mbar_arrive(&s_empty[slot]);
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
-      mbar_arrive(&s_empty[slot]);
-    }
 
-    if constexpr (!PARTIALS) {
-      const int m = m0 + row;
-      if (ok && m < args.M) {
-        const int nb = n0 + col0;
-        const bool has_bias = (args.epi_flags & KSD8_EPI_BIAS) && args.bias;
-        if (has_bias) {
+      if constexpr (!PARTIALS) {
+        const int m = m0 + row;
+        if (ok && m < args.M) {
+          const int nb = n0 + col0;
+          if ((args.epi_flags & KSD8_EPI_BIAS) && args.bias) {
 #pragma unroll
-          for (int i = 0; i < CPT; ++i) {
-            const int n = nb + i;
-            acc[i] = __fadd_rn(acc[i], n < args.N ? args.bias[n] : 0.f);
-          }
-        }
-        const bool full_cols = (nb + CPT) <= args.N;
-        if (args.out_dtype == KSD8_F32) {
-          float* o = reinterpret_cast<float*>(args.out) + (size_t)m * args.ldo + nb;
-          if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
-#pragma unroll
-            for (int i = 0; i < CPT; i += 4)
-              *reinterpret_cast<float4*>(o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-          } else {
-            for (int i = 0; i < CPT; ++i)
-              if (nb + i < args.N) o[i] = acc[i];
-          }
-        } else if (args.out_dtype == KSD8_BF16) {
-          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)m * args.ldo + nb;
-          if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
-#pragma unroll
-            for (int i = 0; i < CPT; i += 8) {
-              uint4 v;
-              __nv_bfloat162 p0 = __floats2bfloat162_rn(acc[i + 0], acc[i + 1]);
-              __nv_bfloat162 p1 = __floats2bfloat162_rn(acc[i + 2], acc[i + 3]);
-              __nv_bfloat162 p2 = __floats2bfloat162_rn(acc[i + 4], acc[i + 5]);
-              __nv_bfloat162 p3 = __floats2bfloat162_rn(acc[i + 6], acc[i + 7]);
-              v.x = *reinterpret_cast<uint32_t*>(&p0);
-              v.y = *reinterpret_cast<uint32_t*>(&p1);
-              v.z = *reinterpret_cast<uint32_t*>(&p2);
-              v.w = *reinterpret_cast<uint32_t*>(&p3);
-              *reinterpret_cast<uint4*>(o + i) = v;
+            for (int i = 0; i < CPT / 2; ++i) {  // (already unrolled)
+              const int n = nb + 2 * i;
+              acc[i].x = __fadd_rn(acc[i].x, n < args.N ? args.bias[n] : 0.f);
+              acc[i].y = __fadd_rn(acc[i].y, n + 1 < args.N ? args.bias[n + 1] : 0.f);
             }
-          } else {
-            for (int i = 0; i < CPT; ++i)
-              if (nb + i < args.N) o[i] = __float2bfloat16_rn(acc[i]);
           }
-        } else {  // KSD8_F16
-          __half* o = reinterpret_cast<__half*>(args.out) + (size_t)m * args.ldo + nb;
-          const bool clamp = args.epi_flags & KSD8_EPI_CLAMP_F16;
-          bool bad = false;
-          __half hv[CPT];
+          const bool full_cols = (nb + CPT) <= args.N;
+          if (args.out_dtype == KSD8_F32) {
+            float* o = reinterpret_cast<float*>(args.out) + (size_t)m * args.ldo + nb;
+            if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
 #pragma unroll
-          for (int i = 0; i < CPT; ++i) {
-            __half h = __float2half_rn(acc[i]);
-            if (clamp && __hisinf(h)) h = __float2half_rn(acc[i] > 0.f ? 65504.f : -65504.f);
-            bad |= (__hisinf(h) || __hisnan(h)) && (nb + i < args.N);
-            hv[i] = h;
-          }
-          if (bad && (args.epi_flags & KSD8_EPI_FLAG_NONFINITE))
-            record_error(args.status, KSD8_ERR_NONFINITE);
-          if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+              for (int i = 0; i < CPT / 2; i += 2)
+                *reinterpret_cast<float4*>(o + 2 * i) =
+                    make_float4(acc[i].x, acc[i].y, acc[i + 1].x, acc[i + 1].y);
+            } else {
 #pragma unroll
-            for (int i = 0; i < CPT; i += 8)
-              *reinterpret_cast<uint4*>(o + i) = *reinterpret_cast<const uint4*>(&hv[i]);
-          } else {
-            for (int i = 0; i < CPT; ++i)
-              if (nb + i < args.N) o[i] = hv[i];
+              for (int i = 0; i < CPT / 2; ++i) {
+                if (nb + 2 * i < args.N) o[2 * i] = acc[i].x;
+                if (nb + 2 * i + 1 < args.N) o[2 * i + 1] = acc[i].y;
+              }
+            }
+          } else if (args.out_dtype == KSD8_BF16) {
+            __nv_bfloat16* o =
+                reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)m * args.ldo + nb;
+            if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+              for (int i = 0; i < CPT / 2; i += 4) {
+                uint4 v;
+                __nv_bfloat162 p0 = __float22bfloat162_rn(acc[i]);
+                __nv_bfloat162 p1 = __float22bfloat162_rn(acc[i + 1]);
+                __nv_bfloat162 p2 = __float22bfloat162_rn(acc[i + 2]);
+                __nv_bfloat162 p3 = __float22bfloat162_rn(acc[i + 3]);
+                v.x = *reinterpret_cast<uint32_t*>(&p0);
+                v.y = *reinterpret_cast<uint32_t*>(&p1);
+                v.z = *reinterpret_cast<uint32_t*>(&p2);
+                v.w = *reinterpret_cast<uint32_t*>(&p3);
+                *reinterpret_cast<uint4*>(o + 2 * i) = v;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < CPT / 2; ++i) {
+                if (nb + 2 * i < args.N) o[2 * i] = __float2bfloat16_rn(acc[i].x);
+                if (nb + 2 * i + 1 < args.N) o[2 * i + 1] = __float2bfloat16_rn(acc[i].y);
+              }
+            }
+          } else {  // KSD8_F16
+            __half* o = reinterpret_cast<__half*>(args.out) + (size_t)m * args.ldo + nb;
+            const bool clamp = args.epi_flags & KSD8_EPI_CLAMP_F16;
+            bool bad = false;
+            const bool vec = full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
+#pragma unroll
+            for (int i = 0; i < CPT / 2; i += 4) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                __half2 h = __float22half2_rn(acc[i + u]);
+                if (clamp) {
+                  if (__hisinf(__low2half(h)))
+                    h = __halves2half2(__float2half_rn(acc[i + u].x > 0.f ? 65504.f : -65504.f),
+                                       __high2half(h));
+                  if (__hisinf(__high2half(h)))
+                    h = __halves2half2(__low2half(h),
+                                       __float2half_rn(acc[i + u].y > 0.f ? 65504.f : -65504.f));
+                }
+                const int n = nb + 2 * (i + u);
+                bad |= (n < args.N) && (__hisinf(__low2half(h)) || __hisnan(__low2half(h)));
+                bad |= (n + 1 < args.N) && (__hisinf(__high2half(h)) || __hisnan(__high2half(h)));
+                pk[u] = *reinterpret_cast<uint32_t*>(&h);
+              }
+              if (vec) {
+                *reinterpret_cast<uint4*>(o + 2 * i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              } else {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const int n = nb + 2 * (i + u);
+                  const __half2 h = *reinterpret_cast<const __half2*>(&pk[u]);
+                  if (n < args.N) o[2 * (i + u)] = __low2half(h);
+                  if (n + 1 < args.N) o[2 * (i + u) + 1] = __high2half(h);
+                }
+              }
+            }
+            if (bad && (args.epi_flags & KSD8_EPI_FLAG_NONFINITE))
+              record_error(args.status, KSD8_ERR_NONFINITE);
           }
         }
       }
@@ -372,6 +498,20 @@ static bool make_tmap_i8(CUtensorMap* map, const void* ptr, int64_t rows, int64_
   return r == CUDA_SUCCESS;
 }
 
+static int sm_count_cached() {
+  static int n[32] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 32) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    n[dev] = v;
+  }
+  return n[dev];
+}
+
 template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS>
 static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t k,
                        cudaStream_t stream) {
@@ -389,8 +529,20 @@ static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t 
   CUtensorMap ta, tb;
   if (!make_tmap_i8(&ta, a, args.M, k, BM)) return KSD8_ERR_LAUNCH;
   if (!make_tmap_i8(&tb, w, args.N, k, BN)) return KSD8_ERR_LAUNCH;
-  dim3 grid((args.N + BN - 1) / BN, (args.M + BM - 1) / BM);
-  kern<<<grid, (3 + EPI_WARPS) * 32, L::ALLOC, stream>>>(ta, tb, args);
+  const int tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN);
+  const int sms = sm_count_cached();
+  const int grid = tiles < sms ? tiles : sms;
+  if ((4 + EPI_WARPS) * 32 == 384) {
+    // the register split is only valid for the launch register count it was sized for
+    static int regs_checked[32] = {0};
+    if (dev >= 0 && dev < 32 && !regs_checked[dev]) {
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != REG_LAUNCH)
+        return KSD8_ERR_UNSUPPORTED;
+      regs_checked[dev] = 1;
+    }
+  }
+  kern<<<grid, (4 + EPI_WARPS) * 32, L::ALLOC, stream>>>(ta, tb, args);
   return KSD8_OK;
 }
 
@@ -416,9 +568,9 @@ int ksd8_gemm_launch(const int8_t* a, const void* a_scales, const int8_t* w, con
   args.epi_flags = epi_flags;
   if (partials) return launch_gemm<128, 4, 4, true>(a, w, args, k, stream);
   // Tile width: cost model = waves x per-tile time, a tile costing its width
-  // plus a fixed prologue/epilogue share (in 128-column units: 2.5 vs 1.5).
+  // plus a fixed share (in 128-column units: 2.5 for 256-wide vs 1.5).
   const int64_t tiles_m = (m + 127) / 128;
-  const int64_t sms = 148;
+  const int64_t sms = sm_count_cached();
   const int64_t w256 = (tiles_m * ((n + 255) / 256) + sms - 1) / sms;
   const int64_t w128 = (tiles_m * ((n + 127) / 128) + sms - 1) / sms;
   if (n > 128 && w256 * 5 <= w128 * 3)

@@ -152,9 +152,7 @@ struct Vec16 {
 };
 
 // One CTA per 128 x 128 tile: coalesced 16-byte row loads into shared memory
-// (as fp32), then each warp quantises columns: lane l owns rows l, l+32, l+64,
-// l+96 of the column (conflict-free with the odd row pitch), amax by shuffle,
-// one code byte per row written to x^T.
+// (as fp32), then each thread quantises half a column (see below).
 template <typename T, bool DEQUANT>
 __global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
   extern __shared__ float tile[];  // [QC_TR][QC_LD]
@@ -217,6 +215,7 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
   // exchange for the other half, then 64 codes written as 16-byte vectors of
   // the x^T row.
   __shared__ float s_amax[2][QC_TC];
+  __syncthreads();
   const int cc = tid & (QC_TC - 1), half = tid >> 7;
   const int64_t c = c0 + cc;
   float m = 0.f;
