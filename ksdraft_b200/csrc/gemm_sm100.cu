@@ -56,10 +56,10 @@ constexpr int SBATCH = 2;  // groups of scales fetched per round by the scale wa
 constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
 
-template <int BN, int EPI_WARPS, int STAGES>
+template <int BN, int EPI_WARPS, int STAGES, int CG>
 struct GemmSmem {
   static constexpr int A_BYTES = BM * BK;
-  static constexpr int B_BYTES = BN * BK;
+  static constexpr int B_BYTES = (BN / CG) * BK;  // a CTA pair splits W's rows
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SCALE_FLOATS = BM + BN;
   static constexpr int OFF_A = 0;
@@ -111,11 +111,12 @@ __device__ __forceinline__ void tmem_st_magic_w(uint32_t taddr) {
 constexpr int REG_LAUNCH = 168, REG_ROLE = 88, REG_EPI = 208;
 static_assert(128 * REG_ROLE + 256 * REG_EPI <= 384 * REG_LAUNCH, "register split");
 
-template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS>
+template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS, int CG>
 __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
-  using L = GemmSmem<BN, EPI_WARPS, STAGES>;
+  using L = GemmSmem<BN, EPI_WARPS, STAGES, CG>;
+  static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per MMA");
   constexpr bool REGSPLIT = (4 + EPI_WARPS) * 32 == 384;
   constexpr int CPT = BN * 4 / EPI_WARPS;  // columns per epilogue thread
   constexpr int LDW = 16;  // TMEM load width (registers per chunk)
@@ -143,10 +144,14 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int G = args.G;
-  const int tiles_m = (args.M + BM - 1) / BM;
+  // A work unit is one CTA (CG = 1) or one CTA pair (CG = 2) computing a
+  // (128 * CG) x BN tile; this CTA owns rows [rank * 128, rank * 128 + 128).
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int unit = blockIdx.x / CG;
+  const int n_units = gridDim.x / CG;
+  const int tiles_m = (args.M + BM * CG - 1) / (BM * CG);
   const int tiles_n = (args.N + BN - 1) / BN;
   const int n_tiles = tiles_m * tiles_n;
-  constexpr int EPI_THREADS = EPI_WARPS * 32;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -155,11 +160,11 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], EPI_THREADS);
+      mbar_init(&acc_empty[b], EPI_WARPS * CG);
     }
     for (int s = 0; s < SRING; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], EPI_THREADS);
+      mbar_init(&s_empty[s], EPI_WARPS);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -169,11 +174,17 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // peer barriers initialised before any remote arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -185,26 +196,34 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     // ------------------------------------------------------------ TMA producer
     int gg = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+    for (int tile = unit; ok && tile < n_tiles; tile += n_units) {
+      const int m0 = (tile % tiles_m) * BM * CG + rank * BM;
+      const int nb = (tile / tiles_m) * BN + rank * (BN / CG);
       for (int g = 0; g < G; ++g, ++gg) {
         const int s = gg % STAGES;
         const uint32_t ph = (gg / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, args.status)) { ok = false; break; }
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
-          tma_load_2d(sA + s * L::A_BYTES, &tmA, &full[s], g * BK, m0);
-          tma_load_2d(sB + s * L::B_BYTES, &tmB, &full[s], g * BK, n0);
+          if constexpr (CG == 2) {
+            // both CTAs' bytes are counted on the leader's barrier
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * L::STAGE_BYTES);
+            tma_load_2d_pair(sA + s * L::A_BYTES, &tmA, &full[s], g * BK, m0);
+            tma_load_2d_pair(sB + s * L::B_BYTES, &tmB, &full[s], g * BK, nb);
+          } else {
+            mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+            tma_load_2d(sA + s * L::A_BYTES, &tmA, &full[s], g * BK, m0);
+            tma_load_2d(sB + s * L::B_BYTES, &tmB, &full[s], g * BK, nb);
+          }
         }
         __syncwarp();
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 && rank == 0) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t IDESC = idesc_i8(BM, BN);
+    constexpr uint32_t IDESC = idesc_i8(BM * CG, BN);
     int gg = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+    for (int tile = unit; ok && tile < n_tiles; tile += n_units) {
       for (int g = 0; g < G; ++g, ++gg) {
         const int s = gg % STAGES;
         const uint32_t ph = (gg / STAGES) & 1;
@@ -217,13 +236,21 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
           const uint32_t a_addr = smem_u32(sA + s * L::A_BYTES);
           const uint32_t b_addr = smem_u32(sB + s * L::B_BYTES);
           const uint32_t d_tmem = tmem_base + buf * BN;
+          if constexpr (CG == 2) {
 #pragma unroll
-          for (int kk = 0; kk < BK / 32; ++kk) {
-            mma_i8(d_tmem, smem_desc_k128_sw128(a_addr + kk * 32),
-                   smem_desc_k128_sw128(b_addr + kk * 32), IDESC, 1u);
+            for (int kk = 0; kk < BK / 32; ++kk)
+              mma_i8_pair(d_tmem, smem_desc_k128_sw128(a_addr + kk * 32),
+                          smem_desc_k128_sw128(b_addr + kk * 32), IDESC, 1u);
+            mma_commit_pair(&empty[s], 0x3);
+            mma_commit_pair(&acc_full[buf], 0x3);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < BK / 32; ++kk)
+              mma_i8(d_tmem, smem_desc_k128_sw128(a_addr + kk * 32),
+                     smem_desc_k128_sw128(b_addr + kk * 32), IDESC, 1u);
+            mma_commit(&empty[s]);
+            mma_commit(&acc_full[buf]);
           }
-          mma_commit(&empty[s]);
-          mma_commit(&acc_full[buf]);
         }
         __syncwarp();
       }
@@ -232,8 +259,8 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     // ------------------------------------------------------------ scale loader
     int gg0 = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+    for (int tile = unit; ok && tile < n_tiles; tile += n_units) {
+      const int m0 = (tile % tiles_m) * BM * CG + rank * BM, n0 = (tile / tiles_m) * BN;
       for (int g0 = 0; ok && g0 < G; g0 += SBATCH) {
         float va[SBATCH][BM / 32];
         float vw[SBATCH][BN / 32];
@@ -297,15 +324,23 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
       for (int c = 0; c < NCH; ++c) tmem_st_magic_w<LDW>(t_row + b * BN + col0 + c * LDW);
     tmem_wait_st();
     tc_fence_before();
-    mbar_arrive(&acc_empty[0]);
-    mbar_arrive(&acc_empty[1]);
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (CG == 2) {
+        mbar_arrive_cluster(&acc_empty[0], 0);
+        mbar_arrive_cluster(&acc_empty[1], 0);
+      } else {
+        mbar_arrive(&acc_empty[0]);
+        mbar_arrive(&acc_empty[1]);
+      }
+    }
 
     const float2 neg_magic = make_float2(-MAGIC_F, -MAGIC_F);
     float2 acc[CPT / 2];
     bool ok = true;
     int gg = 0;
-    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+    for (int tile = unit; ok && tile < n_tiles; tile += n_units) {
+      const int m0 = (tile % tiles_m) * BM * CG + rank * BM, n0 = (tile / tiles_m) * BN;
 #pragma unroll
       for (int i = 0; i < CPT / 2; ++i) acc[i] = make_float2(0.f, 0.f);
       for (int g = 0; g < G; ++g, ++gg) {
@@ -358,8 +393,12 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&acc_empty[buf]);
-        mbar_arrive(&s_empty[slot]);
+        __syncwarp();  // one arrival per warp once all its lanes are done
+        if (lane == 0) {
+          if constexpr (CG == 2) mbar_arrive_cluster(&acc_empty[buf], 0);
+          else mbar_arrive(&acc_empty[buf]);
+          mbar_arrive(&s_empty[slot]);
+        }
       }
 
       if constexpr (!PARTIALS) {
@@ -458,9 +497,13 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // the leader's MMAs read the peer's shared memory
+  else __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -512,11 +555,11 @@ static int sm_count_cached() {
   return n[dev];
 }
 
-template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS>
+template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS, int CG>
 static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t k,
                        cudaStream_t stream) {
-  using L = GemmSmem<BN, EPI_WARPS, STAGES>;
-  auto kern = w8a8_gemm_kernel<BN, EPI_WARPS, STAGES, PARTIALS>;
+  using L = GemmSmem<BN, EPI_WARPS, STAGES, CG>;
+  auto kern = w8a8_gemm_kernel<BN, EPI_WARPS, STAGES, PARTIALS, CG>;
   static unsigned attr_dev_mask = 0;  // per-device opt-in to > 48 KB of shared memory
   int dev = 0;
   cudaGetDevice(&dev);
@@ -528,10 +571,11 @@ static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t 
   }
   CUtensorMap ta, tb;
   if (!make_tmap_i8(&ta, a, args.M, k, BM)) return KSD8_ERR_LAUNCH;
-  if (!make_tmap_i8(&tb, w, args.N, k, BN)) return KSD8_ERR_LAUNCH;
-  const int tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN);
+  if (!make_tmap_i8(&tb, w, args.N, k, BN / CG)) return KSD8_ERR_LAUNCH;
+  const int tiles = ((args.M + BM * CG - 1) / (BM * CG)) * ((args.N + BN - 1) / BN);
   const int sms = sm_count_cached();
-  const int grid = tiles < sms ? tiles : sms;
+  const int units = sms / CG;
+  const int grid = (tiles < units ? tiles : units) * CG;
   if ((4 + EPI_WARPS) * 32 == 384) {
     // the register split is only valid for the launch register count it was sized for
     static int regs_checked[32] = {0};
@@ -542,7 +586,23 @@ static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t 
       regs_checked[dev] = 1;
     }
   }
-  kern<<<grid, (4 + EPI_WARPS) * 32, L::ALLOC, stream>>>(ta, tb, args);
+  if constexpr (CG == 2) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3((4 + EPI_WARPS) * 32);
+    cfg.dynamicSmemBytes = L::ALLOC;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, ta, tb, args) != cudaSuccess) return KSD8_ERR_LAUNCH;
+  } else {
+    kern<<<grid, (4 + EPI_WARPS) * 32, L::ALLOC, stream>>>(ta, tb, args);
+  }
   return KSD8_OK;
 }
 
@@ -566,7 +626,13 @@ int ksd8_gemm_launch(const int8_t* a, const void* a_scales, const int8_t* w, con
   args.ldo = ldo;
   args.out_dtype = out_dtype;
   args.epi_flags = epi_flags;
-  if (partials) return launch_gemm<128, 4, 4, true>(a, w, args, k, stream);
+  if (partials) {
+    if (m >= 256 && n >= 256) return launch_gemm<256, 8, 6, true, 2>(a, w, args, k, stream);
+    return launch_gemm<128, 4, 4, true, 1>(a, w, args, k, stream);
+  }
+  // CTA pairs (cta_group::2, 256 x 256 tiles, half of the operands staged per
+  // CTA) whenever both dimensions fill a pair tile.
+  if (m >= 256 && n >= 256) return launch_gemm<256, 8, 6, false, 2>(a, w, args, k, stream);
   // Tile width: cost model = waves x per-tile time, a tile costing its width
   // plus a fixed share (in 128-column units: 2.5 for 256-wide vs 1.5).
   const int64_t tiles_m = (m + 127) / 128;
@@ -574,6 +640,6 @@ int ksd8_gemm_launch(const int8_t* a, const void* a_scales, const int8_t* w, con
   const int64_t w256 = (tiles_m * ((n + 255) / 256) + sms - 1) / sms;
   const int64_t w128 = (tiles_m * ((n + 127) / 128) + sms - 1) / sms;
   if (n > 128 && w256 * 5 <= w128 * 3)
-    return launch_gemm<256, 8, 4, false>(a, w, args, k, stream);
-  return launch_gemm<128, 4, 4, false>(a, w, args, k, stream);
+    return launch_gemm<256, 8, 4, false, 1>(a, w, args, k, stream);
+  return launch_gemm<128, 4, 4, false, 1>(a, w, args, k, stream);
 }
