@@ -66,7 +66,8 @@ struct GemmSmem {
   static constexpr int OFF_B = STAGES * A_BYTES;
   static constexpr int OFF_SCALE = STAGES * STAGE_BYTES;
   static constexpr int OFF_BAR = OFF_SCALE + SRING * SCALE_FLOATS * 4;
-  static constexpr int N_BARS = 2 * STAGES + 4 + 2 * SRING;
+  static constexpr int NBUF = 512 / BN < 4 ? 512 / BN : 4;  // TMEM accumulator buffers
+  static constexpr int N_BARS = 2 * STAGES + 2 * NBUF + 2 * SRING;
   static constexpr int OFF_MISC = OFF_BAR + N_BARS * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
@@ -96,7 +97,8 @@ __device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[
 template <int W>
 __device__ __forceinline__ void tmem_ld_w(uint32_t taddr, uint32_t (&r)[W]) {
   if constexpr (W == 8) tmem_ld_32x32b_x8(taddr, r);
-  else tmem_ld_32x32b_x16(taddr, r);
+  else if constexpr (W == 16) tmem_ld_32x32b_x16(taddr, r);
+  else tmem_ld_32x32b_x32(taddr, r);
 }
 
 template <int W>
@@ -119,9 +121,13 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per MMA");
   constexpr bool REGSPLIT = (4 + EPI_WARPS) * 32 == 384;
   constexpr int CPT = BN * 4 / EPI_WARPS;  // columns per epilogue thread
-  constexpr int LDW = 16;  // TMEM load width (registers per chunk)
+  // TMEM load width (registers per chunk): 32 columns per tcgen05.ld halves
+  // the exposed load round trips of 16-column chunks.
+  constexpr int LDW = 32;
   constexpr int NCH = CPT / LDW;
-  constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
+  constexpr int NBUF = L::NBUF;
+  constexpr int TMEM_COLS = NBUF * BN <= 256 ? 256 : 512;
+  static_assert(NBUF * BN <= 512, "TMEM capacity");
   static_assert(CPT % LDW == 0 && LDW % 4 == 0, "epilogue chunking");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
 
@@ -135,9 +141,9 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;
-  uint64_t* acc_empty = bars + 2 * STAGES + 2;
-  uint64_t* s_full = bars + 2 * STAGES + 4;
-  uint64_t* s_empty = bars + 2 * STAGES + 4 + SRING;
+  uint64_t* acc_empty = bars + 2 * STAGES + NBUF;
+  uint64_t* s_full = bars + 2 * STAGES + 2 * NBUF;
+  uint64_t* s_empty = bars + 2 * STAGES + 2 * NBUF + SRING;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -158,7 +164,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], EPI_WARPS * CG);
     }
@@ -227,8 +233,8 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
       for (int g = 0; g < G; ++g, ++gg) {
         const int s = gg % STAGES;
         const uint32_t ph = (gg / STAGES) & 1;
-        const int buf = gg & 1;
-        const uint32_t aph = (gg >> 1) & 1;
+        const int buf = gg % NBUF;
+        const uint32_t aph = (gg / NBUF) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag, args.status)) { ok = false; break; }
         if (!mbar_wait(&acc_empty[buf], aph, abort_flag, args.status)) { ok = false; break; }
         tc_fence_after();
@@ -317,21 +323,19 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     const int col0 = chalf * CPT;          // first column within the tile
     const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16);
 
-    // Arm both accumulator buffers with the conversion offset.
+    // Arm every accumulator buffer with the conversion offset.
 #pragma unroll
-    for (int b = 0; b < 2; ++b)
+    for (int b = 0; b < NBUF; ++b)
 #pragma unroll
       for (int c = 0; c < NCH; ++c) tmem_st_magic_w<LDW>(t_row + b * BN + col0 + c * LDW);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
-      if constexpr (CG == 2) {
-        mbar_arrive_cluster(&acc_empty[0], 0);
-        mbar_arrive_cluster(&acc_empty[1], 0);
-      } else {
-        mbar_arrive(&acc_empty[0]);
-        mbar_arrive(&acc_empty[1]);
+#pragma unroll
+      for (int b = 0; b < NBUF; ++b) {
+        if constexpr (CG == 2) mbar_arrive_cluster(&acc_empty[b], 0);
+        else mbar_arrive(&acc_empty[b]);
       }
     }
 
@@ -344,8 +348,8 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
 #pragma unroll
       for (int i = 0; i < CPT / 2; ++i) acc[i] = make_float2(0.f, 0.f);
       for (int g = 0; g < G; ++g, ++gg) {
-        const int buf = gg & 1;
-        const uint32_t aph = (gg >> 1) & 1;
+        const int buf = gg % NBUF;
+        const uint32_t aph = (gg / NBUF) & 1;
         const int slot = gg % SRING;
         const uint32_t sph = (gg / SRING) & 1;
         if (!mbar_wait(&acc_full[buf], aph, abort_flag, args.status)) { ok = false; break; }
@@ -630,9 +634,6 @@ int ksd8_gemm_launch(const int8_t* a, const void* a_scales, const int8_t* w, con
     if (m >= 256 && n >= 256) return launch_gemm<256, 8, 6, true, 2>(a, w, args, k, stream);
     return launch_gemm<128, 4, 4, true, 1>(a, w, args, k, stream);
   }
-  // CTA pairs (cta_group::2, 256 x 256 tiles, half of the operands staged per
-  // CTA) whenever both dimensions fill a pair tile.
-  if (m >= 256 && n >= 256) return launch_gemm<256, 8, 6, false, 2>(a, w, args, k, stream);
   // Tile width: cost model = waves x per-tile time, a tile costing its width
   // plus a fixed share (in 128-column units: 2.5 for 256-wide vs 1.5).
   const int64_t tiles_m = (m + 127) / 128;
