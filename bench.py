@@ -62,7 +62,7 @@ def load_peaks() -> dict:
 
 
 def gemm_traffic() -> float | None:
-    p = ROOT / "profiles" / "gemm_traffic.json"
+    p = ROOT / "profiles" / "w8a8_gemm_traffic.json"
     if p.exists():
         return float(json.loads(p.read_text())["bytes_per_launch"])
     return None

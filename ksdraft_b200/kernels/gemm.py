@@ -16,7 +16,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
-from .quant import GROUP_SIZE, _check_group
+from .quant import GROUP_SIZE, SCALE_DTYPE, _check_group  # noqa: F401 (reference names)
 
 
 class GemmTimer:

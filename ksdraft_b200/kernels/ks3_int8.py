@@ -26,7 +26,7 @@ import torch
 from torch import nn
 
 from .. import _lib
-from .gemm import gemm_out
+from .gemm import gemm_out, w8a8_gemm  # noqa: F401 (reference names)
 from .quant import GROUP_SIZE, _check_group, dequantize_last_dim, quantize_cols, \
     quantize_last_dim
 

@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 
 from .gemm import _validate_and_pad, gemm_out
-from .ks3_int8 import spine_quant
+from .ks3_int8 import TANH_DOMAIN, spine_quant  # noqa: F401 (reference names)
 from .quant import _check_group
 
 FP16 = torch.float16

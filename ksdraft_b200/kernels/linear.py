@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from .gemm import gemm_out, _validate_and_pad
+from .gemm import gemm_out, _validate_and_pad, w8a8_gemm  # noqa: F401 (reference names)
 from .quant import GROUP_SIZE, dequantize_last_dim, quantize_last_dim
 
 
