@@ -210,6 +210,37 @@ int ksd8_adamw_step(float* param, const void* grad, int grad_dtype, float* exp_a
 /* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);
 
+/* ---- allocation-free variant (no counterpart in the reference) ----
+ *
+ * ksd8_ks3_vjp_static: ksd8_ks3_vjp followed by ksd8_ks3_vjp_reduce, with the
+ * (n_tiles, 8, charts) fp32 partials held in a file-scope static device array
+ * of KSD8_VJP_STATIC_MAX_PARTIALS floats (8 MiB) instead of caller scratch.
+ * The reference has no such entry point: its backward (ks3_int8.py:354-395)
+ * lets torch allocate the intermediate.  This one allocates nothing (no
+ * cudaMalloc / cudaFree, no library allocator) and writes the same outputs,
+ * bit for bit, as the two-call path.
+ *   - Limit: ceil(m / 128) * 8 * charts <= KSD8_VJP_STATIC_MAX_PARTIALS, e.g.
+ *     m = 4096 tokens with up to 8192 charts; larger requests return
+ *     KSD8_ERR_SCRATCH_LIMIT before anything launches.
+ *   - Set-up: the first call on each device (with that device current) looks
+ *     up the array's device address once with cudaGetSymbolAddress and caches
+ *     it; make that first call before any stream capture on the device.
+ *   - Nothing in the scratch needs clearing: the VJP writes every partial the
+ *     reduction then reads.
+ *   - Calls that overlap on one device (other streams, other host threads)
+ *     share the one array and race; serialise them.
+ * Arguments are those of ksd8_ks3_vjp (minus partials) and of
+ * ksd8_ks3_vjp_reduce (minus partials, n_tiles); status may be NULL. */
+#define KSD8_VJP_STATIC_MAX_PARTIALS (1 << 21)
+#define KSD8_ERR_SCRATCH_LIMIT 9 /* request exceeds a static scratch array */
+int ksd8_ks3_vjp_static(const void* value, const void* coords, int64_t m, int64_t charts,
+                        const int8_t* spine_codes, const void* spine_scale,
+                        const int8_t* warp_scale_codes, const void* warp_scale_scales,
+                        const int8_t* warp_shift_codes, const void* warp_shift_scales,
+                        int8_t* dc_codes, void* dc_scales, int8_t* dct_codes, void* dct_scales,
+                        const float* raw_scale, const float* raw_shift, void* dcoeff16,
+                        void* dscale16, void* dshift16, int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

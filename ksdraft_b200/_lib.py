@@ -17,6 +17,8 @@ LIB_PATH = Path(__file__).resolve().parent / "libksd8.so"
 
 OK, ERR_SHAPE, ERR_ALIGN, ERR_DTYPE, ERR_LAUNCH, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_ARG, \
     ERR_NONFINITE = range(9)
+ERR_SCRATCH_LIMIT = 9
+VJP_STATIC_MAX_PARTIALS = 1 << 21
 
 F32, F16, BF16, I8 = 0, 1, 2, 3
 Q_ROUND_F16, Q_DITHER = 1, 2
@@ -50,6 +52,8 @@ SIGNATURES: dict[str, list] = {
                                    vp, vp],
     "ksd8_adamw_step": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp],
     "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
+    "ksd8_ks3_vjp_static": [vp, vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                            vp, vp, vp, vp],
 }
 
 _lib: C.CDLL | None = None

@@ -69,6 +69,7 @@ const char* ksd8_status_string(int status) {
     case KSD8_ERR_UNSUPPORTED: return "unsupported configuration";
     case KSD8_ERR_ARG: return "invalid argument";
     case KSD8_ERR_NONFINITE: return "non-finite fp16 output";
+    case KSD8_ERR_SCRATCH_LIMIT: return "request exceeds the static scratch capacity";
     default: return "unknown status";
   }
 }
@@ -280,3 +281,80 @@ int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, v
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free VJP
+//
+// ksd8_ks3_vjp_static: the VJP and its reduction with the partials in a
+// file-scope static device array (8 MiB, resident in every device context
+// that loads this library).  Its device address is looked up once per device
+// with cudaGetSymbolAddress, with that device current, and cached.  The VJP
+// writes every (tile, k, chart) partial that the reduction reads, so nothing
+// is cleared.  Calls that overlap on one device share the array and race.
+
+#include <mutex>
+
+static __device__ __align__(256) float g_vjp_scratch[KSD8_VJP_STATIC_MAX_PARTIALS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_vjp_scratch_mu;
+float* g_vjp_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_vjp_scratch on the current device (set-up on first use).
+int vjp_scratch_for_current_device(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    g_last_cuda_error = (int)e;
+    return KSD8_ERR_LAUNCH;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return KSD8_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_vjp_scratch_mu);
+  if (!g_vjp_scratch_ptr[dev]) {
+    float* ptr = nullptr;
+    e = cudaGetSymbolAddress((void**)&ptr, g_vjp_scratch);
+    if (e != cudaSuccess || !ptr) {
+      g_last_cuda_error = (int)e;
+      return KSD8_ERR_LAUNCH;
+    }
+    g_vjp_scratch_ptr[dev] = ptr;
+  }
+  *out = g_vjp_scratch_ptr[dev];
+  return KSD8_OK;
+}
+}  // namespace
+
+extern "C" int ksd8_ks3_vjp_static(const void* value, const void* coords, int64_t m,
+                                   int64_t charts, const int8_t* spine_codes,
+                                   const void* spine_scale, const int8_t* warp_scale_codes,
+                                   const void* warp_scale_scales, const int8_t* warp_shift_codes,
+                                   const void* warp_shift_scales, int8_t* dc_codes,
+                                   void* dc_scales, int8_t* dct_codes, void* dct_scales,
+                                   const float* raw_scale, const float* raw_shift,
+                                   void* dcoeff16, void* dscale16, void* dshift16, int* status,
+                                   void* stream) {
+  if (m < 0 || charts <= 0 || (charts % 128) != 0) return KSD8_ERR_SHAPE;
+  const int64_t n_tiles = (m + 127) / 128;
+  const int64_t per_tile = 8 * charts;
+  if (per_tile > KSD8_VJP_STATIC_MAX_PARTIALS ||
+      n_tiles > KSD8_VJP_STATIC_MAX_PARTIALS / per_tile)
+    return KSD8_ERR_SCRATCH_LIMIT;
+  if (!raw_scale || !raw_shift || !dcoeff16 || !dscale16 || !dshift16) return KSD8_ERR_ARG;
+  if (m > 0 && (!value || !coords || !spine_codes || !spine_scale || !warp_scale_codes ||
+                !warp_scale_scales || !warp_shift_codes || !warp_shift_scales || !dc_codes ||
+                !dc_scales || !dct_codes || !dct_scales))
+    return KSD8_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(value) & 7) || (reinterpret_cast<uintptr_t>(coords) & 7) ||
+      (reinterpret_cast<uintptr_t>(dc_codes) & 3))
+    return KSD8_ERR_ALIGN;
+  float* partials = nullptr;
+  int rc = vjp_scratch_for_current_device(&partials);
+  if (rc != KSD8_OK) return rc;
+  rc = finish(ksd8_ks3_vjp_launch(value, coords, m, charts, spine_codes, spine_scale,
+                                  warp_scale_codes, warp_scale_scales, warp_shift_codes,
+                                  warp_shift_scales, dc_codes, dc_scales, dct_codes, dct_scales,
+                                  partials, S(stream)));
+  if (rc != KSD8_OK) return rc;
+  return finish(ksd8_ks3_vjp_reduce_launch(partials, n_tiles, charts, raw_scale, raw_shift,
+                                           dcoeff16, dscale16, dshift16, status, S(stream)));
+}
