@@ -69,7 +69,12 @@ extern "C" {
 /* ---- GEMM epilogue flags ---- */
 #define KSD8_EPI_CLAMP_F16 1  /* fp16 output: saturate +-inf to +-65504 (ks3_int8.py:241-242) */
 #define KSD8_EPI_BIAS 2       /* add fp32 bias[n] after the group sum (linear.py:71) */
-#define KSD8_EPI_FLAG_NONFINITE 4 /* fp16 output: set KSD8_ERR_NONFINITE in *status on inf/nan */
+#define KSD8_EPI_FLAG_NONFINITE 4 /* fp16 output or ROUND_F16: set KSD8_ERR_NONFINITE in *status on inf/nan */
+#define KSD8_EPI_ROUND_F16 8  /* fp32 output holds float(fp16(y)): the FP16 grad handoff of
+                                 ks3_int8.py:75-84 written straight into an fp32 grad buffer */
+#define KSD8_EPI_IF_STATUS 16 /* predicated launch: the kernel returns at once unless *status
+                                 is non-zero (the handoff's fp32 overflow fallback, decided on
+                                 the device without a host round trip) */
 
 /* ---- nonlinear modes of the KS3 cell (ks3_int8.py:22-28) ---- */
 #define KSD8_NL_FP32 0
@@ -158,7 +163,9 @@ int ksd8_ks3_spine_table(int64_t charts, const int8_t* spine_codes, const void* 
  * tokens (dct_codes (charts, M), dct_scales (charts, ceil(M/128))), and
  * per-128-token-tile column partial sums partials (ceil(M/128), 8, charts) fp32
  * in the order d0..d5, dscale_t, dshift_t (dshift_t before its 0.5 factor).
- * charts must be a multiple of 128. */
+ * charts must be a multiple of 128; value and coords 16-byte aligned (they
+ * are read as TMA tiles).  A device-side wait that gives up sets
+ * KSD8_ERR_DEVICE_TIMEOUT in *status (status may be NULL). */
 int ksd8_ks3_vjp(const void* value, const void* coords, int64_t m, int64_t charts,
                  const int8_t* spine_codes, const void* spine_scale,
                  const int8_t* warp_scale_codes, const void* warp_scale_scales,

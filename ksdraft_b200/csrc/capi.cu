@@ -22,7 +22,7 @@ int ksd8_ks3_spine_quant_launch(const void*, int64_t, int64_t, const int8_t*, co
                                 const int8_t*, int, const void*, int8_t*, void*, cudaStream_t);
 int ksd8_ks3_vjp_launch(const void*, const void*, int64_t, int64_t, const int8_t*, const void*,
                         const int8_t*, const void*, const int8_t*, const void*, int8_t*, void*,
-                        int8_t*, void*, float*, cudaStream_t);
+                        int8_t*, void*, float*, int*, cudaStream_t);
 int ksd8_ks3_vjp_reduce_launch(const float*, int64_t, int64_t, const float*, const float*, void*,
                                void*, void*, int*, cudaStream_t);
 int ksd8_rosa_pack_bits_launch(const void*, int, int64_t, int64_t, int64_t, int64_t, int64_t,
@@ -118,6 +118,8 @@ int ksd8_w8a8_gemm(const int8_t* a, const void* a_scales, const int8_t* w, const
   if (m == 0 || n == 0) return KSD8_OK;
   if (!a || !w || !a_scales || !w_scales || !out) return KSD8_ERR_ARG;
   if ((epi_flags & KSD8_EPI_BIAS) && !bias) return KSD8_ERR_ARG;
+  if ((epi_flags & KSD8_EPI_IF_STATUS) && !status) return KSD8_ERR_ARG;
+  if ((epi_flags & KSD8_EPI_ROUND_F16) && out_dtype != KSD8_F32) return KSD8_ERR_ARG;
   // TMA: 16-byte aligned base addresses (row pitch k is a multiple of 128).
   if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
     return KSD8_ERR_ALIGN;
@@ -195,19 +197,18 @@ int ksd8_ks3_vjp(const void* value, const void* coords, int64_t m, int64_t chart
                  const int8_t* warp_shift_codes, const void* warp_shift_scales,
                  int8_t* dc_codes, void* dc_scales, int8_t* dct_codes, void* dct_scales,
                  float* partials, int* status, void* stream) {
-  (void)status;
   if (m < 0 || charts <= 0 || (charts % 128) != 0) return KSD8_ERR_SHAPE;
   if (m > 0 && (!value || !coords || !spine_codes || !spine_scale || !warp_scale_codes ||
                 !warp_scale_scales || !warp_shift_codes || !warp_shift_scales || !dc_codes ||
                 !dc_scales || !dct_codes || !dct_scales || !partials))
     return KSD8_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(value) & 7) || (reinterpret_cast<uintptr_t>(coords) & 7) ||
+  if ((reinterpret_cast<uintptr_t>(value) & 15) || (reinterpret_cast<uintptr_t>(coords) & 15) ||
       (reinterpret_cast<uintptr_t>(dc_codes) & 3))
     return KSD8_ERR_ALIGN;
   return finish(ksd8_ks3_vjp_launch(value, coords, m, charts, spine_codes, spine_scale,
                                     warp_scale_codes, warp_scale_scales, warp_shift_codes,
                                     warp_shift_scales, dc_codes, dc_scales, dct_codes, dct_scales,
-                                    partials, S(stream)));
+                                    partials, status, S(stream)));
 }
 
 int ksd8_ks3_vjp_reduce(const float* partials, int64_t n_tiles, int64_t charts,
@@ -344,7 +345,7 @@ extern "C" int ksd8_ks3_vjp_static(const void* value, const void* coords, int64_
                 !warp_scale_scales || !warp_shift_codes || !warp_shift_scales || !dc_codes ||
                 !dc_scales || !dct_codes || !dct_scales))
     return KSD8_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(value) & 7) || (reinterpret_cast<uintptr_t>(coords) & 7) ||
+  if ((reinterpret_cast<uintptr_t>(value) & 15) || (reinterpret_cast<uintptr_t>(coords) & 15) ||
       (reinterpret_cast<uintptr_t>(dc_codes) & 3))
     return KSD8_ERR_ALIGN;
   float* partials = nullptr;
@@ -353,7 +354,7 @@ extern "C" int ksd8_ks3_vjp_static(const void* value, const void* coords, int64_
   rc = finish(ksd8_ks3_vjp_launch(value, coords, m, charts, spine_codes, spine_scale,
                                   warp_scale_codes, warp_scale_scales, warp_shift_codes,
                                   warp_shift_scales, dc_codes, dc_scales, dct_codes, dct_scales,
-                                  partials, S(stream)));
+                                  partials, status, S(stream)));
   if (rc != KSD8_OK) return rc;
   return finish(ksd8_ks3_vjp_reduce_launch(partials, n_tiles, charts, raw_scale, raw_shift,
                                            dcoeff16, dscale16, dshift16, status, S(stream)));

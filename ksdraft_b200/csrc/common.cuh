@@ -113,6 +113,34 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Orders this thread's generic-proxy accesses of shared memory before later
+// async-proxy (TMA) accesses of the same bytes (a buffer refilled by TMA
+// after threads read or wrote it).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Host: cuTensorMapEncodeTiled through the runtime's driver entry point
+// (no link-time dependency on libcuda).
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static inline PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_slot, uint32_t ncols) {
@@ -260,6 +288,15 @@ __device__ __forceinline__ int gs_code(float x, float scale) {
 // stays below 2^-14 for |y| < 200, and the margin used is 2^-13.  The integer
 // is formed with the 1.5 * 2^23 shifter (round half to even, exact for
 // |y| < 2^22) on the FMA/ALU pipes instead of the conversion unit.
+// Out-of-line IEEE paths of the fast quantisers: rarely taken, kept out of the
+// callers' hot loops so that those stay small in the instruction cache.
+static __device__ __noinline__ int gs_code_slow(float x, float scale) { return gs_code(x, scale); }
+static __device__ __noinline__ uint32_t gs_scale_slow_bits(float amax) {
+  __half h;
+  gs_scale(amax, &h);
+  return __half_as_ushort(h);
+}
+
 __device__ __forceinline__ int gs_code_fast(float x, float scale, float rcp) {
   const float y = __fmul_rn(x, rcp);
   const float t = __fadd_rn(y, 12582912.f);
@@ -268,7 +305,7 @@ __device__ __forceinline__ int gs_code_fast(float x, float scale, float rcp) {
     const int q = __float_as_int(t) - 0x4B400000;
     return min(max(q, -127), 127);
   }
-  return gs_code(x, scale);
+  return gs_code_slow(x, scale);
 }
 
 // 1/s to within 1 ulp (s a normal fp32; GS scales are >= 2^-24).
@@ -290,7 +327,9 @@ __device__ __forceinline__ float gs_scale_fast(float amax, __half* out_h) {
     if (out_h) *out_h = h;
     return __half2float(h);
   }
-  return gs_scale(amax, out_h);
+  const __half h = __ushort_as_half((unsigned short)gs_scale_slow_bits(amax));
+  if (out_h) *out_h = h;
+  return __half2float(h);
 }
 
 // ---------------------------------------------------------------- Philox4x32-10

@@ -159,6 +159,10 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   const int tiles_n = (args.N + BN - 1) / BN;
   const int n_tiles = tiles_m * tiles_n;
 
+  // Predicated launch: nothing to do unless an earlier kernel flagged *status
+  // (every CTA reads the same word, written before this launch in stream order).
+  if ((args.epi_flags & KSD8_EPI_IF_STATUS) && (!args.status || *args.status == 0)) return;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -418,6 +422,20 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
             }
           }
           const bool full_cols = (nb + CPT) <= args.N;
+          if (args.out_dtype == KSD8_F32 && (args.epi_flags & KSD8_EPI_ROUND_F16)) {
+            // FP16 gradient handoff into an fp32 buffer: store float(fp16(acc))
+            bool bad = false;
+#pragma unroll
+            for (int i = 0; i < CPT / 2; ++i) {
+              const __half2 h = __float22half2_rn(acc[i]);
+              const int n = nb + 2 * i;
+              bad |= (n < args.N) && (__hisinf(__low2half(h)) || __hisnan(__low2half(h)));
+              bad |= (n + 1 < args.N) && (__hisinf(__high2half(h)) || __hisnan(__high2half(h)));
+              acc[i] = __half22float2(h);
+            }
+            if (bad && (args.epi_flags & KSD8_EPI_FLAG_NONFINITE))
+              record_error(args.status, KSD8_ERR_NONFINITE);
+          }
           if (args.out_dtype == KSD8_F32) {
             float* o = reinterpret_cast<float*>(args.out) + (size_t)m * args.ldo + nb;
             if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
@@ -511,24 +529,6 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
 }
 
 // ------------------------------------------------------------------ host side
-
-typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static PFN_encodeTiled get_encode_fn() {
-  static PFN_encodeTiled fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_encodeTiled>(p);
-  }
-  return fn;
-}
 
 // int8 (rows, k) row-major, box = box_rows x 128 bytes, 128-byte swizzle.
 static bool make_tmap_i8(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k,

@@ -267,6 +267,15 @@ __global__ void ks3_spine_table_kernel(int64_t charts, const int8_t* spine_codes
   table[i] = __float2half_rn(hmul(hr((float)tsum), __half2float(spine_scale[c])));
 }
 
+// IEEE path of spine_out_int8 (out of line: rarely taken).
+static __device__ __noinline__ float spine_out_int8_slow(float h) {
+  float pre = __fdiv_rn(h, 127.0f);
+  pre = hr(fminf(fmaxf(pre, 5.9604644775390625e-08f), 65504.0f));
+  float q = fminf(fmaxf(rintf(__fdiv_rn(h, pre)), -127.f), 127.f);
+  q = fmaxf(q, 0.f);
+  return __fmul_rn(hmul(q, q), __fmul_rn(pre, pre));
+}
+
 __device__ __forceinline__ float spine_out_int8(float h) {
   if (!(h > 0.f)) return 0.f;  // ReLU zero: pre = 2^-24, code 0, out 0
   const float y = h * 0.007874015718698502f;  // RN(1/127)
@@ -275,11 +284,7 @@ __device__ __forceinline__ float spine_out_int8(float h) {
     const float pre = hr(y);
     return __fmul_rn(16128.f, __fmul_rn(pre, pre));
   }
-  float pre = __fdiv_rn(h, 127.0f);
-  pre = hr(fminf(fmaxf(pre, 5.9604644775390625e-08f), 65504.0f));
-  float q = fminf(fmaxf(rintf(__fdiv_rn(h, pre)), -127.f), 127.f);
-  q = fmaxf(q, 0.f);
-  return __fmul_rn(hmul(q, q), __fmul_rn(pre, pre));
+  return spine_out_int8_slow(h);
 }
 
 struct SpineFastArgs {
@@ -292,6 +297,7 @@ struct SpineFastArgs {
 
 constexpr int SPF_LD = SPINE_TAB + 8;  // padded table row (halves)
 constexpr int SPF_SMEM = 128 * SPF_LD * 2;
+constexpr int SPF_R = 4;  // rows per warp iteration
 
 __global__ void __launch_bounds__(256) ks3_spine_int8_fast_kernel(SpineFastArgs a) {
   extern __shared__ __half stab[];  // [128 charts][SPF_LD]
@@ -313,60 +319,85 @@ __global__ void __launch_bounds__(256) ks3_spine_int8_fast_kernel(SpineFastArgs 
   const __half2 lim = __float2half2_rn(3.19921875f);
   const __half2 nlim = __float2half2_rn(-3.19921875f);
   const __half2 k127 = __float2half2_rn(39.6875f);
+  // s in [-127, 127] -> fp16(s + 1664) lies in [1537, 1791] (ulp 1), so its
+  // low 10 bits are rint_even(s) + 640: the LUT index is (bits & 0x3FF) - 512.
+  const __half2 idx_magic = __float2half2_rn(1664.f);
   const int64_t rows_per_block = (a.m + gridDim.y - 1) / gridDim.y;
   const int64_t r_begin = blockIdx.y * rows_per_block;
   const int64_t r_end = min(a.m, r_begin + rows_per_block);
-  for (int64_t r = r_begin + warp; r < r_end; r += 8) {
-    const __half* crow = a.coords + r * a.charts;
-    __half2 x2[2];
-    if (full) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(crow + cbase);
-      x2[0] = *reinterpret_cast<const __half2*>(&raw.x);
-      x2[1] = *reinterpret_cast<const __half2*>(&raw.y);
-    } else {
-      __half e[4];
+  const __half* tab0 = stab + (lane * 4) * SPF_LD;
+  // Each warp takes SPF_R consecutive rows per iteration: their loads are all
+  // in flight together and their group reductions interleave.
+  for (int64_t r0 = r_begin + warp * SPF_R; r0 < r_end; r0 += 8 * SPF_R) {
+    uint2 raw[SPF_R];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) e[i] = cbase + i < a.charts ? crow[cbase + i] : __half(0.f);
-      x2[0] = __halves2half2(e[0], e[1]);
-      x2[1] = __halves2half2(e[2], e[3]);
-    }
-    float h[4];
+    for (int k = 0; k < SPF_R; ++k) {
+      const int64_t r = r0 + k;
+      raw[k] = make_uint2(0u, 0u);
+      if (r < r_end) {
+        const __half* crow = a.coords + r * a.charts;
+        if (full) {
+          raw[k] = __ldcs(reinterpret_cast<const uint2*>(crow + cbase));
+        } else {
+          __half e[4];
 #pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      __half2 m2 = __hmul2_rn(x2[p], quarter);
-      m2 = __hmax2(__hmin2(m2, lim), nlim);
-      const __half2 s2 = __hmul2_rn(m2, k127);
-      const int i0 = __half2int_rn(__low2half(s2)) + 128;
-      const int i1 = __half2int_rn(__high2half(s2)) + 128;
-      const int ch = lane * 4 + 2 * p;
-      const float t0 = __half2float(stab[ch * SPF_LD + i0]);
-      const float t1 = __half2float(stab[(ch + 1) * SPF_LD + i1]);
-      const float2 xf = __half22float2(x2[p]);
-      h[2 * p] = spine_out_int8(__fadd_rn(xf.x, t0));
-      h[2 * p + 1] = spine_out_int8(__fadd_rn(xf.y, t1));
+          for (int i = 0; i < 4; ++i) e[i] = cbase + i < a.charts ? crow[cbase + i] : __half(0.f);
+          const __half2 lo = __halves2half2(e[0], e[1]), hi = __halves2half2(e[2], e[3]);
+          raw[k].x = *reinterpret_cast<const uint32_t*>(&lo);
+          raw[k].y = *reinterpret_cast<const uint32_t*>(&hi);
+        }
+      }
     }
-    if (!full) {
+    float h[SPF_R][4], mx[SPF_R];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (cbase + i >= a.charts) h[i] = 0.f;
-    }
-    float mx = fmaxf(fmaxf(h[0], h[1]), fmaxf(h[2], h[3]));  // h >= 0
-    mx = warp_max(mx);
-    __half sh;
-    const float scale = gs_scale_fast(mx, &sh);
-    const float rcp = rcp_approx(scale);
-    int8_t* out = a.h_codes + r * a.charts + cbase;
-    const int q0 = gs_code_fast(h[0], scale, rcp), q1 = gs_code_fast(h[1], scale, rcp);
-    const int q2 = gs_code_fast(h[2], scale, rcp), q3 = gs_code_fast(h[3], scale, rcp);
-    if (full && ((reinterpret_cast<uintptr_t>(out) & 3) == 0)) {
-      *reinterpret_cast<char4*>(out) = make_char4((char)q0, (char)q1, (char)q2, (char)q3);
-    } else {
-      const int q[4] = {q0, q1, q2, q3};
+    for (int k = 0; k < SPF_R; ++k) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (cbase + i < a.charts) out[i] = (int8_t)q[i];
+      for (int p = 0; p < 2; ++p) {
+        const uint32_t word = p ? raw[k].y : raw[k].x;
+        const __half2 x2 = *reinterpret_cast<const __half2*>(&word);
+        __half2 m2 = __hmul2_rn(x2, quarter);
+        m2 = __hmax2(__hmin2(m2, lim), nlim);
+        const __half2 y2 = __hadd2_rn(__hmul2_rn(m2, k127), idx_magic);
+        const uint32_t yb = *reinterpret_cast<const uint32_t*>(&y2);
+        const int i0 = (int)(yb & 0x3FFu) - 512;
+        const int i1 = (int)((yb >> 16) & 0x3FFu) - 512;
+        const float t0 = __half2float(tab0[(2 * p) * SPF_LD + i0]);
+        const float t1 = __half2float(tab0[(2 * p + 1) * SPF_LD + i1]);
+        const float2 xf = __half22float2(x2);
+        h[k][2 * p] = spine_out_int8(__fadd_rn(xf.x, t0));
+        h[k][2 * p + 1] = spine_out_int8(__fadd_rn(xf.y, t1));
+      }
+      if (!full) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (cbase + i >= a.charts) h[k][i] = 0.f;
+      }
+      mx[k] = fmaxf(fmaxf(h[k][0], h[k][1]), fmaxf(h[k][2], h[k][3]));  // h >= 0
     }
-    if (lane == 0) a.h_scales[r * groups + g] = sh;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int k = 0; k < SPF_R; ++k) mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], o));
+#pragma unroll
+    for (int k = 0; k < SPF_R; ++k) {
+      const int64_t r = r0 + k;
+      if (r >= r_end) break;
+      __half sh;
+      const float scale = gs_scale_fast(mx[k], &sh);
+      const float rcp = rcp_approx(scale);
+      int8_t* out = a.h_codes + r * a.charts + cbase;
+      const int q0 = gs_code_fast(h[k][0], scale, rcp), q1 = gs_code_fast(h[k][1], scale, rcp);
+      const int q2 = gs_code_fast(h[k][2], scale, rcp), q3 = gs_code_fast(h[k][3], scale, rcp);
+      if (full && ((reinterpret_cast<uintptr_t>(out) & 3) == 0)) {
+        *reinterpret_cast<char4*>(out) = make_char4((char)q0, (char)q1, (char)q2, (char)q3);
+      } else {
+        const int q[4] = {q0, q1, q2, q3};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (cbase + i < a.charts) out[i] = (int8_t)q[i];
+      }
+      if (lane == 0) a.h_scales[r * groups + g] = sh;
+    }
   }
 }
 
@@ -431,9 +462,14 @@ struct VjpPair {
 
 constexpr int VJP_TM = 128;  // token rows per tile (= one token-quantisation group)
 constexpr int VJP_TC = 128;  // charts per tile (= one chart-quantisation group)
-constexpr int VJP_LDH = VJP_TC + 2;    // dc tile row pitch in halves (260 bytes)
 constexpr int TANH_N = 0x4600;         // fp16 bit patterns of |a| < 6.0 are tabulated
-constexpr int VJP_SMEM = TANH_N * 2 + VJP_TM * VJP_LDH * 2 + 8 * 8 * VJP_TC * 4;
+constexpr int VJP_TILE_BYTES = VJP_TM * VJP_TC * 2;           // one fp16 tile (32 KB)
+constexpr int VJP_OFF_TANH = 4 * VJP_TILE_BYTES;              // 2 stages x (value, coords)
+constexpr int VJP_OFF_BAR = VJP_OFF_TANH + TANH_N * 2;
+constexpr int VJP_SMEM = VJP_OFF_BAR + 32 + 1024;             // + slack for 1 KB alignment
+constexpr int VJP_THREADS = 512;                              // 16 warps, 8 rows each per tile
+constexpr int VJP_WARPS = VJP_THREADS / 32;
+constexpr int VJP_ROWS_PER_WARP = VJP_TM / VJP_WARPS;
 
 // fp16(tanh(a)) of an fp16 value through the shared-memory table: entry i
 // holds fp16(tanhf(fp16 with bits i)) for |a| < 6 (above it the fp16 result is
@@ -447,73 +483,169 @@ __device__ __forceinline__ __half2 tanh16x2(const uint16_t* tab, __half2 x) {
   return *reinterpret_cast<const __half2*>(&o);
 }
 
-// The fp16 VJP of ks3_int8.py:354-402 with native fp16 pair arithmetic.  Each
+// Per-chart VJP constants of one lane's 4 charts (two fp16 pairs).
+__device__ __forceinline__ void vjp_constants(const VjpArgs& a, int64_t cbase, VjpPair (&pr)[2]) {
+  const __half2 two = __float2half2_rn(2.f), three = __float2half2_rn(3.f);
+  const __half2 four = __float2half2_rn(4.f);
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    __half cc[2][6], sc[2], sh[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int64_t c = cbase + 2 * p + j;
+      const float ps = __half2float(a.spine_scale[c]);
+#pragma unroll
+      for (int k = 0; k < 6; ++k)
+        cc[j][k] = __float2half_rn((float)a.spine_codes[c * 6 + k] * ps);
+      sc[j] = __float2half_rn(dequant_scalar(a.ws_codes, a.ws_scales, c, true));
+      sh[j] = __float2half_rn(dequant_scalar(a.wh_codes, a.wh_scales, c, true));
+    }
+    __half2 c[6];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) c[k] = __halves2half2(cc[0][k], cc[1][k]);
+    VjpPair& q = pr[p];
+    q.c0 = c[0]; q.c2 = c[2]; q.c4 = c[4];
+    // cubic = 2*c0 - 2*c1 + c2 + c3 ; quad = -3*c0 + 3*c1 - 2*c2 - c3
+    q.cubic = __hadd2_rn(__hadd2_rn(__hsub2_rn(__hmul2_rn(two, c[0]), __hmul2_rn(two, c[1])),
+                                    c[2]), c[3]);
+    q.quad = __hsub2_rn(__hsub2_rn(__hadd2_rn(__hmul2_rn(__float2half2_rn(-3.f), c[0]),
+                                              __hmul2_rn(three, c[1])),
+                                   __hmul2_rn(two, c[2])), c[3]);
+    q.cubic3 = __hmul2_rn(three, q.cubic);
+    q.quad2 = __hmul2_rn(two, q.quad);
+    q.c5x4 = __hmul2_rn(four, c[5]);
+    q.c4x2 = __hmul2_rn(two, c[4]);
+    q.c5x12 = __hmul2_rn(__float2half2_rn(12.f), c[5]);
+    q.c4x4 = __hmul2_rn(four, c[4]);
+    q.c5x3 = __hmul2_rn(three, c[5]);
+    q.scale = __halves2half2(sc[0], sc[1]);
+    q.shift = __halves2half2(sh[0], sh[1]);
+  }
+}
+
+// One fp16 pair of the VJP of ks3_int8.py:354-402: returns dc = value + dmean
+// and adds the 8 column-reduction terms (ks3_int8.py:381-388) into acc.
+__device__ __forceinline__ __half2 vjp_pair(const uint16_t* ttab, const VjpPair& q,
+                                            __half2 x16, __half2 value, float2 (&acc)[8]) {
+  const __half2 one = __float2half2_rn(1.f), two = __float2half2_rn(2.f);
+  const __half2 three = __float2half2_rn(3.f), four = __float2half2_rn(4.f);
+  const __half2 ntwo = __float2half2_rn(-2.f), quarter = __float2half2_rn(0.25f);
+  const __half2 sixteenth = __float2half2_rn(0.0625f), zero = __float2half2_rn(0.f);
+  const __half2 t = __hmul2_rn(four, tanh16x2(ttab, __hmul2_rn(x16, quarter)));
+  const __half2 u = __hadd2_rn(t, q.shift);
+  const __half2 z = tanh16x2(ttab, __hmul2_rn(q.scale, u));
+  __half2 sp = __hadd2_rn(__hmul2_rn(q.cubic, t), q.quad);
+  sp = __hadd2_rn(__hmul2_rn(sp, t), q.c2);
+  sp = __hadd2_rn(__hmul2_rn(sp, t), q.c0);
+  __half2 wp = __hadd2_rn(__hmul2_rn(q.c5x4, z), q.c4x2);
+  wp = __hsub2_rn(__hmul2_rn(wp, z), q.c5x3);
+  wp = __hsub2_rn(__hmul2_rn(wp, z), q.c4);
+  const __half2 rl = __hmax2(__hadd2_rn(__hadd2_rn(x16, sp), wp), zero);
+  const __half2 dpre = __hmul2_rn(__hmul2_rn(value, two), rl);
+  __half2 dpoly = __hadd2_rn(__hmul2_rn(q.cubic3, t), q.quad2);
+  dpoly = __hadd2_rn(__hmul2_rn(dpoly, t), q.c2);
+  __half2 dwarp = __hadd2_rn(__hmul2_rn(q.c5x12, z), q.c4x4);
+  dwarp = __hsub2_rn(__hmul2_rn(dwarp, z), q.c5x3);
+  const __half2 zz = __hmul2_rn(z, z);
+  const __half2 dz = __hmul2_rn(dwarp, __hsub2_rn(one, zz));
+  const __half2 tt = __hmul2_rn(t, t);
+  const __half2 dmean =
+      __hmul2_rn(__hmul2_rn(dpre, __hadd2_rn(dpoly, __hmul2_rn(dz, q.scale))),
+                 __hsub2_rn(one, __hmul2_rn(tt, sixteenth)));
+  const __half2 t3 = __hmul2_rn(tt, t);
+  const __half2 z3 = __hmul2_rn(zz, z);
+  const __half2 dd = __hmul2_rn(dpre, dz);
+  const __half2 terms[8] = {
+      __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(__hmul2_rn(two, t3), __hmul2_rn(three, tt)), one)),
+      __hmul2_rn(dpre, __hadd2_rn(__hmul2_rn(ntwo, t3), __hmul2_rn(three, tt))),
+      __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(t3, __hmul2_rn(two, tt)), t)),
+      __hmul2_rn(dpre, __hsub2_rn(t3, tt)),
+      __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(two, zz), one)),
+      __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(four, z3), __hmul2_rn(three, z))),
+      __hmul2_rn(dd, u),
+      __hmul2_rn(dd, q.scale)};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float2 f = __half22float2(terms[k]);
+    acc[k].x += f.x;
+    acc[k].y += f.y;
+  }
+  return __hadd2_rn(value, dmean);
+}
+
+// The fp16 VJP of ks3_int8.py:354-418 with native fp16 pair arithmetic.  Each
 // op of the reference (torch CPU Half: fp32 compute, round to fp16) equals the
 // correctly rounded fp16 op because double rounding through fp32 is
 // innocuous for fp16 operands (24 >= 2*11 + 2); the _rn intrinsics keep
-// multiplies and adds from being fused.  CTAs loop over 128 x 128 tiles so the
-// tanh table built at the start is reused.
-__global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
-  extern __shared__ __align__(16) uint8_t vsm_raw[];
-  uint16_t* ttab = reinterpret_cast<uint16_t*>(vsm_raw);                      // [TANH_N]
-  __half* tile = reinterpret_cast<__half*>(vsm_raw + TANH_N * 2);              // [TM][LDH]
-  float* red = reinterpret_cast<float*>(vsm_raw + TANH_N * 2 + VJP_TM * VJP_LDH * 2);
+// multiplies and adds from being fused.
+//
+// Persistent, one CTA of 16 warps per SM over 128 x 128 (token, chart) tiles,
+// a contiguous chart-major range of tiles per CTA.  The value and coords tiles
+// arrive by TMA (2D tensor maps, no swizzle) into two stages; tile i + 2 is
+// requested as soon as tile i's stage is released, so the HBM reads of the
+// next tile overlap this tile's arithmetic.  Per tile: each warp computes 8
+// rows, writes dc in place over the value tile and quantises each row along
+// charts; the 8 column partials are then reduced across warps (in the spent
+// coords tile) and dc^T is quantised along tokens (thread t: column t % 128,
+// 32 rows).
+__global__ void __launch_bounds__(VJP_THREADS, 1)
+    ks3_vjp_kernel(const __grid_constant__ CUtensorMap tm_value,
+                   const __grid_constant__ CUtensorMap tm_coords, VjpArgs a, int* status) {
+  extern __shared__ uint8_t vsm_raw[];
+  uint8_t* vsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(vsm_raw) + 1023) &
+                                            ~uintptr_t(1023));
+  uint16_t* ttab = reinterpret_cast<uint16_t*>(vsm + VJP_OFF_TANH);
+  uint64_t* full = reinterpret_cast<uint64_t*>(vsm + VJP_OFF_BAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(vsm + VJP_OFF_BAR + 16);
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t n_cg = a.charts / VJP_TC;
+  const int64_t n_mt = (a.m + VJP_TM - 1) / VJP_TM;
+  const int64_t n_tiles = n_cg * n_mt;
+  const int64_t t_begin = n_tiles * blockIdx.x / gridDim.x;
+  const int64_t t_end = n_tiles * (blockIdx.x + 1) / gridDim.x;
+  const int64_t gcharts = a.charts / 128;
+  const int64_t mgroups = n_mt;
+
+  auto issue = [&](int64_t i) {  // TMA of tile t_begin + i into stage i & 1
+    const int64_t tile = t_begin + i;
+    const int32_t x = (int32_t)((tile / n_mt) * VJP_TC), y = (int32_t)((tile % n_mt) * VJP_TM);
+    uint8_t* st = vsm + (i & 1) * 2 * VJP_TILE_BYTES;
+    mbar_arrive_expect_tx(&full[i & 1], 2 * VJP_TILE_BYTES);
+    tma_load_2d(st, &tm_value, &full[i & 1], x, y);
+    tma_load_2d(st + VJP_TILE_BYTES, &tm_coords, &full[i & 1], x, y);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_value);
+    tma_prefetch_desc(&tm_coords);
+    for (int64_t i = 0; i < 2 && t_begin + i < t_end; ++i) issue(i);
+  }
   for (int i = threadIdx.x; i < TANH_N; i += blockDim.x)
     ttab[i] = __half_as_ushort(__float2half_rn(tanhf(__half2float(__ushort_as_half(
         (unsigned short)i)))));
   __syncthreads();
 
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t n_cg = a.charts / VJP_TC;
-  const int64_t n_mt = (a.m + VJP_TM - 1) / VJP_TM;
-  const int64_t gcharts = a.charts / 128;
-  const int64_t mgroups = n_mt;
-  const __half2 one = __float2half2_rn(1.f), two = __float2half2_rn(2.f);
-  const __half2 three = __float2half2_rn(3.f), four = __float2half2_rn(4.f);
-  const __half2 ntwo = __float2half2_rn(-2.f), quarter = __float2half2_rn(0.25f);
-  const __half2 sixteenth = __float2half2_rn(0.0625f), zero = __float2half2_rn(0.f);
-
-  for (int64_t tile_id = blockIdx.x; tile_id < n_cg * n_mt; tile_id += gridDim.x) {
-    const int64_t cg = tile_id % n_cg;
-    const int64_t mt = tile_id / n_cg;
+  int64_t cur_cg = -1;
+  VjpPair pr[2];
+  int64_t consumed = 0;
+  for (int64_t i = 0; t_begin + i < t_end; ++i) {
+    const int64_t tile = t_begin + i;
+    const int64_t cg = tile / n_mt, mt = tile % n_mt;
     const int64_t m0 = mt * VJP_TM;
     const int64_t cbase = cg * VJP_TC + lane * 4;
-
-    VjpPair pr[2];
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      __half cc[2][6], sc[2], sh[2];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int64_t c = cbase + 2 * p + j;
-        const float ps = __half2float(a.spine_scale[c]);
-#pragma unroll
-        for (int k = 0; k < 6; ++k)
-          cc[j][k] = __float2half_rn((float)a.spine_codes[c * 6 + k] * ps);
-        sc[j] = __float2half_rn(dequant_scalar(a.ws_codes, a.ws_scales, c, true));
-        sh[j] = __float2half_rn(dequant_scalar(a.wh_codes, a.wh_scales, c, true));
-      }
-      __half2 c[6];
-#pragma unroll
-      for (int k = 0; k < 6; ++k) c[k] = __halves2half2(cc[0][k], cc[1][k]);
-      VjpPair& q = pr[p];
-      q.c0 = c[0]; q.c2 = c[2]; q.c4 = c[4];
-      // cubic = 2*c0 - 2*c1 + c2 + c3 ; quad = -3*c0 + 3*c1 - 2*c2 - c3
-      q.cubic = __hadd2_rn(__hadd2_rn(__hsub2_rn(__hmul2_rn(two, c[0]), __hmul2_rn(two, c[1])),
-                                      c[2]), c[3]);
-      q.quad = __hsub2_rn(__hsub2_rn(__hadd2_rn(__hmul2_rn(__float2half2_rn(-3.f), c[0]),
-                                                __hmul2_rn(three, c[1])),
-                                     __hmul2_rn(two, c[2])), c[3]);
-      q.cubic3 = __hmul2_rn(three, q.cubic);
-      q.quad2 = __hmul2_rn(two, q.quad);
-      q.c5x4 = __hmul2_rn(four, c[5]);
-      q.c4x2 = __hmul2_rn(two, c[4]);
-      q.c5x12 = __hmul2_rn(__float2half2_rn(12.f), c[5]);
-      q.c4x4 = __hmul2_rn(four, c[4]);
-      q.c5x3 = __hmul2_rn(three, c[5]);
-      q.scale = __halves2half2(sc[0], sc[1]);
-      q.shift = __halves2half2(sh[0], sh[1]);
+    if (cg != cur_cg) {  // global loads of the chart constants overlap the TMA wait
+      vjp_constants(a, cbase, pr);
+      cur_cg = cg;
     }
+    const bool got = mbar_wait(&full[i & 1], (uint32_t)((i >> 1) & 1), abort_flag, status);
+    if (!__syncthreads_and(got && !*abort_flag)) break;  // every thread leaves together
+    consumed = i + 1;
+    __half* vtile = reinterpret_cast<__half*>(vsm + (i & 1) * 2 * VJP_TILE_BYTES);
+    const __half* xtile = vtile + VJP_TM * VJP_TC;
 
     float2 acc[2][8];
 #pragma unroll
@@ -521,66 +653,26 @@ __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[p][k] = make_float2(0.f, 0.f);
 
-    for (int rr = warp; rr < VJP_TM; rr += 8) {
+    for (int j = 0; j < VJP_ROWS_PER_WARP; ++j) {
+      const int rr = warp * VJP_ROWS_PER_WARP + j;
       const int64_t r = m0 + rr;
-      __half2 dch[2] = {zero, zero};
+      __half2* trow = reinterpret_cast<__half2*>(vtile + rr * VJP_TC + lane * 4);
+      const uint2 vv = *reinterpret_cast<const uint2*>(trow);
+      const uint2 xv = *reinterpret_cast<const uint2*>(xtile + rr * VJP_TC + lane * 4);
+      __half2 dch0 = __float2half2_rn(0.f), dch1 = dch0;
       if (r < a.m) {
-        const uint2 vv = *reinterpret_cast<const uint2*>(a.value + r * a.charts + cbase);
-        const uint2 xv = *reinterpret_cast<const uint2*>(a.coords + r * a.charts + cbase);
-        const __half2 v2[2] = {*reinterpret_cast<const __half2*>(&vv.x),
-                               *reinterpret_cast<const __half2*>(&vv.y)};
-        const __half2 x2[2] = {*reinterpret_cast<const __half2*>(&xv.x),
-                               *reinterpret_cast<const __half2*>(&xv.y)};
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const VjpPair& q = pr[p];
-          const __half2 x16 = x2[p], value = v2[p];
-          const __half2 t = __hmul2_rn(four, tanh16x2(ttab, __hmul2_rn(x16, quarter)));
-          const __half2 u = __hadd2_rn(t, q.shift);
-          const __half2 z = tanh16x2(ttab, __hmul2_rn(q.scale, u));
-          __half2 sp = __hadd2_rn(__hmul2_rn(q.cubic, t), q.quad);
-          sp = __hadd2_rn(__hmul2_rn(sp, t), q.c2);
-          sp = __hadd2_rn(__hmul2_rn(sp, t), q.c0);
-          __half2 wp = __hadd2_rn(__hmul2_rn(q.c5x4, z), q.c4x2);
-          wp = __hsub2_rn(__hmul2_rn(wp, z), q.c5x3);
-          wp = __hsub2_rn(__hmul2_rn(wp, z), q.c4);
-          const __half2 rl = __hmax2(__hadd2_rn(__hadd2_rn(x16, sp), wp), zero);
-          const __half2 dpre = __hmul2_rn(__hmul2_rn(value, two), rl);
-          __half2 dpoly = __hadd2_rn(__hmul2_rn(q.cubic3, t), q.quad2);
-          dpoly = __hadd2_rn(__hmul2_rn(dpoly, t), q.c2);
-          __half2 dwarp = __hadd2_rn(__hmul2_rn(q.c5x12, z), q.c4x4);
-          dwarp = __hsub2_rn(__hmul2_rn(dwarp, z), q.c5x3);
-          const __half2 zz = __hmul2_rn(z, z);
-          const __half2 dz = __hmul2_rn(dwarp, __hsub2_rn(one, zz));
-          const __half2 tt = __hmul2_rn(t, t);
-          const __half2 dmean =
-              __hmul2_rn(__hmul2_rn(dpre, __hadd2_rn(dpoly, __hmul2_rn(dz, q.scale))),
-                         __hsub2_rn(one, __hmul2_rn(tt, sixteenth)));
-          dch[p] = __hadd2_rn(value, dmean);
-          const __half2 t3 = __hmul2_rn(tt, t);
-          const __half2 z3 = __hmul2_rn(zz, z);
-          const __half2 dd = __hmul2_rn(dpre, dz);
-          const __half2 terms[8] = {
-              __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(__hmul2_rn(two, t3), __hmul2_rn(three, tt)),
-                                          one)),
-              __hmul2_rn(dpre, __hadd2_rn(__hmul2_rn(ntwo, t3), __hmul2_rn(three, tt))),
-              __hmul2_rn(dpre, __hadd2_rn(__hsub2_rn(t3, __hmul2_rn(two, tt)), t)),
-              __hmul2_rn(dpre, __hsub2_rn(t3, tt)),
-              __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(two, zz), one)),
-              __hmul2_rn(dpre, __hsub2_rn(__hmul2_rn(four, z3), __hmul2_rn(three, z))),
-              __hmul2_rn(dd, u),
-              __hmul2_rn(dd, q.scale)};
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float2 f = __half22float2(terms[k]);
-            acc[p][k].x += f.x;
-            acc[p][k].y += f.y;
-          }
-        }
+        dch0 = vjp_pair(ttab, pr[0], *reinterpret_cast<const __half2*>(&xv.x),
+                        *reinterpret_cast<const __half2*>(&vv.x), acc[0]);
+        dch1 = vjp_pair(ttab, pr[1], *reinterpret_cast<const __half2*>(&xv.y),
+                        *reinterpret_cast<const __half2*>(&vv.y), acc[1]);
+      }
+      trow[0] = dch0;  // dc replaces value in place (same thread, same bytes)
+      trow[1] = dch1;
+      const float2 d01 = __half22float2(dch0), d23 = __half22float2(dch1);
+      float mx = fmaxf(fmaxf(fabsf(d01.x), fabsf(d01.y)), fmaxf(fabsf(d23.x), fabsf(d23.y)));
+      mx = warp_max(mx);
+      if (r < a.m) {
         // dc quantised along charts: this row's 128 charts are one group.
-        const float2 d01 = __half22float2(dch[0]), d23 = __half22float2(dch[1]);
-        float mx = fmaxf(fmaxf(fabsf(d01.x), fabsf(d01.y)), fmaxf(fabsf(d23.x), fabsf(d23.y)));
-        mx = warp_max(mx);
         __half shq;
         const float s = gs_scale_fast(mx, &shq);
         const float rcp = rcp_approx(s);
@@ -589,27 +681,43 @@ __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
                        (char)gs_code_fast(d23.x, s, rcp), (char)gs_code_fast(d23.y, s, rcp));
         if (lane == 0) a.dc_scales[r * gcharts + cg] = shq;
       }
-      __half2* trow = reinterpret_cast<__half2*>(tile + rr * VJP_LDH + lane * 4);
-      trow[0] = dch[0];
-      trow[1] = dch[1];
     }
+    // Column partials across the 16 warps, in the coords tile (no longer
+    // needed): warps 8..15 park theirs, warps 0..7 add them to their own,
+    // then the 8 pair sums are added in warp order.
+    float* red = reinterpret_cast<float*>(vtile + VJP_TM * VJP_TC);  // [8][8][VJP_TC]
+    __syncthreads();  // every warp is done reading the coords tile
+    if (warp >= 8) {
 #pragma unroll
-    for (int p = 0; p < 2; ++p)
+      for (int p = 0; p < 2; ++p)
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        *reinterpret_cast<float2*>(&red[(warp * 8 + k) * VJP_TC + lane * 4 + 2 * p]) =
-            acc[p][k];
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float2*>(&red[((warp - 8) * 8 + k) * VJP_TC + lane * 4 + 2 * p]) =
+              acc[p][k];
+    }
+    __syncthreads();
+    if (warp < 8) {
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float2* slot =
+              reinterpret_cast<float2*>(&red[(warp * 8 + k) * VJP_TC + lane * 4 + 2 * p]);
+          const float2 o = *slot;
+          *slot = make_float2(acc[p][k].x + o.x, acc[p][k].y + o.y);
+        }
+    }
     __syncthreads();
 
     // dc^T quantised along tokens: column c of the tile is one group of 128
-    // tokens.  Thread t owns column t % 128 and rows (t / 128) * 64 .. +64.
+    // tokens.  Thread t owns column t % 128 and rows (t / 128) * 32 .. +32.
     {
-      float* s_amax = red;  // reuse: [2][VJP_TC] after the partials are consumed below
-      const int cc = threadIdx.x & (VJP_TC - 1), half = threadIdx.x >> 7;
+      float* s_amax = red;  // reuse: [4][VJP_TC] after the partials are consumed below
+      const int cc = threadIdx.x & (VJP_TC - 1), quarter = threadIdx.x >> 7;
       float mx = 0.f;
 #pragma unroll 16
-      for (int i = 0; i < 64; ++i)
-        mx = fmaxf(mx, fabsf(__half2float(tile[(half * 64 + i) * VJP_LDH + cc])));
+      for (int r = 0; r < 32; ++r)
+        mx = fmaxf(mx, fabsf(__half2float(vtile[(quarter * 32 + r) * VJP_TC + cc])));
       // column partials first (they read `red`), then the amax exchange
       for (int idx = threadIdx.x; idx < 8 * VJP_TC; idx += blockDim.x) {
         const int k = idx / VJP_TC, c2 = idx % VJP_TC;
@@ -619,41 +727,56 @@ __global__ void __launch_bounds__(256) ks3_vjp_kernel(VjpArgs a) {
         a.partials[(mt * 8 + k) * a.charts + cg * VJP_TC + c2] = sum;
       }
       __syncthreads();
-      s_amax[half * VJP_TC + cc] = mx;
+      s_amax[quarter * VJP_TC + cc] = mx;
       __syncthreads();
-      mx = fmaxf(s_amax[cc], s_amax[VJP_TC + cc]);
+      mx = fmaxf(fmaxf(s_amax[cc], s_amax[VJP_TC + cc]),
+                 fmaxf(s_amax[2 * VJP_TC + cc], s_amax[3 * VJP_TC + cc]));
       __half shq;
       const float s = gs_scale_fast(mx, &shq);
       const float rcp = rcp_approx(s);
       const int64_t c = cg * VJP_TC + cc;
-      const int64_t rb = m0 + half * 64;
+      const int64_t rb = m0 + quarter * 32;
       int8_t* out = a.dct_codes + c * a.m + rb;
-      if (rb + 64 <= a.m && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+      if (rb + 32 <= a.m && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
+        for (int v = 0; v < 2; ++v) {
           uint32_t w4[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int jj = 0; jj < 4; ++jj) {
             uint32_t word = 0;
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
-              const int rr = half * 64 + v * 16 + j * 4 + b;
-              const int q = gs_code_fast(__half2float(tile[rr * VJP_LDH + cc]), s, rcp);
+              const int rr = quarter * 32 + v * 16 + jj * 4 + b;
+              const int q = gs_code_fast(__half2float(vtile[rr * VJP_TC + cc]), s, rcp);
               word |= (uint32_t)(q & 0xFF) << (8 * b);
             }
-            w4[j] = word;
+            w4[jj] = word;
           }
           *reinterpret_cast<uint4*>(out + v * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       } else {
-        for (int i = 0; i < 64; ++i)
-          if (rb + i < a.m)
-            out[i] = (int8_t)gs_code_fast(__half2float(tile[(half * 64 + i) * VJP_LDH + cc]), s,
-                                          rcp);
+        for (int r = 0; r < 32; ++r)
+          if (rb + r < a.m)
+            out[r] = (int8_t)gs_code_fast(__half2float(vtile[(quarter * 32 + r) * VJP_TC + cc]),
+                                          s, rcp);
       }
-      if (half == 0) a.dct_scales[c * mgroups + mt] = shq;
+      if (quarter == 0) a.dct_scales[c * mgroups + mt] = shq;
     }
-    __syncthreads();  // tile / red are rewritten by the next tile
+    __syncthreads();  // stage i & 1 is free again
+    if (threadIdx.x == 0 && t_begin + i + 2 < t_end) {
+      fence_proxy_async_smem();  // generic reads/writes of the stage before the TMA refill
+      issue(i + 2);
+    }
+  }
+  // After a timeout: let the copies still in flight land (bounded) before the
+  // CTA's shared memory is released.
+  if (threadIdx.x == 0 && *abort_flag) {
+    for (int64_t i = consumed; i < consumed + 2 && t_begin + i < t_end; ++i) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full[i & 1], (uint32_t)((i >> 1) & 1)) &&
+             globaltimer_ns() - t0 < KSD8_WAIT_NS) {
+      }
+    }
   }
 }
 
@@ -764,21 +887,44 @@ int ksd8_ks3_spine_quant_launch(const void* coords, int64_t m, int64_t charts,
   return KSD8_OK;
 }
 
+// fp16 (rows, cols) row-major tensor read as 128 x 128 tiles, no swizzle.
+static bool make_tmap_f16_tile(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)VJP_TC, (cuuint32_t)VJP_TM};
+  cuuint32_t estr[2] = {1u, 1u};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 int ksd8_ks3_vjp_launch(const void* value, const void* coords, int64_t m, int64_t charts,
                         const int8_t* spine_codes, const void* spine_scale, const int8_t* ws_codes,
                         const void* ws_scales, const int8_t* wh_codes, const void* wh_scales,
                         int8_t* dc_codes, void* dc_scales, int8_t* dct_codes, void* dct_scales,
-                        float* partials, cudaStream_t stream) {
+                        float* partials, int* status, cudaStream_t stream) {
   if (m == 0) return KSD8_OK;
-  static int attr_dev_mask = 0;
+  static unsigned attr_dev_mask = 0;
+  static int sm_count[32] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_dev_mask & (1 << dev))) {
+  if (dev < 0 || dev >= 32) return KSD8_ERR_UNSUPPORTED;
+  if (!(attr_dev_mask & (1u << dev))) {
     if (cudaFuncSetAttribute(ks3_vjp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              VJP_SMEM) != cudaSuccess)
       return KSD8_ERR_LAUNCH;
-    attr_dev_mask |= (1 << dev);
+    if (cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) !=
+            cudaSuccess ||
+        sm_count[dev] <= 0)
+      return KSD8_ERR_LAUNCH;
+    attr_dev_mask |= (1u << dev);
   }
+  CUtensorMap tv, tx;
+  if (!make_tmap_f16_tile(&tv, value, m, charts) || !make_tmap_f16_tile(&tx, coords, m, charts))
+    return KSD8_ERR_LAUNCH;
   VjpArgs a;
   a.value = reinterpret_cast<const __half*>(value);
   a.coords = reinterpret_cast<const __half*>(coords);
@@ -790,8 +936,8 @@ int ksd8_ks3_vjp_launch(const void* value, const void* coords, int64_t m, int64_
   a.dct_codes = dct_codes; a.dct_scales = reinterpret_cast<__half*>(dct_scales);
   a.partials = partials;
   const int64_t tiles = (charts / VJP_TC) * ((m + VJP_TM - 1) / VJP_TM);
-  const int64_t grid = tiles < 2 * 148 ? tiles : 2 * 148;  // 2 resident CTAs per SM
-  ks3_vjp_kernel<<<(unsigned)grid, 256, VJP_SMEM, stream>>>(a);
+  const int64_t grid = tiles < sm_count[dev] ? tiles : sm_count[dev];  // one CTA per SM
+  ks3_vjp_kernel<<<(unsigned)grid, VJP_THREADS, VJP_SMEM, stream>>>(tv, tx, a, status);
   return KSD8_OK;
 }
 

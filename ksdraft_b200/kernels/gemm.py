@@ -50,8 +50,13 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
 def gemm_out(a_codes: torch.Tensor, a_scales: torch.Tensor, w_codes: torch.Tensor,
              w_scales: torch.Tensor, *, out: torch.Tensor | None = None,
              out_dtype: torch.dtype = torch.float32, bias: torch.Tensor | None = None,
-             clamp_f16: bool = False, status: torch.Tensor | None = None) -> torch.Tensor:
-    """Y = A W^T with GS128 scales; K must already be a multiple of 128."""
+             clamp_f16: bool = False, status: torch.Tensor | None = None,
+             round_f16: bool = False, if_status: bool = False) -> torch.Tensor:
+    """Y = A W^T with GS128 scales; K must already be a multiple of 128.
+
+    round_f16 (fp32 `out`): store float(fp16(Y)) and flag overflow in `status`
+    (the FP16 gradient handoff written into an fp32 buffer).  if_status: the
+    launch does nothing unless `status` is already non-zero on the device."""
     _lib.require_cuda(a_codes, a_scales, w_codes, w_scales)
     M, K = a_codes.shape
     N = w_codes.shape[0]
@@ -65,9 +70,15 @@ def gemm_out(a_codes: torch.Tensor, a_scales: torch.Tensor, w_codes: torch.Tenso
         flags |= _lib.EPI_BIAS
     if clamp_f16:
         flags |= _lib.EPI_CLAMP_F16
-    if status is not None:
+    if status is not None and not if_status:
         flags |= _lib.EPI_FLAG_NONFINITE
-    timer = GemmTimer.active
+    if round_f16:
+        flags |= _lib.EPI_ROUND_F16
+    if if_status:
+        if status is None:
+            raise ValueError("if_status needs a status tensor")
+        flags |= _lib.EPI_IF_STATUS
+    timer = GemmTimer.active if not if_status else None  # predicated launches are not timed
     if timer is not None:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()

@@ -255,16 +255,11 @@ class _KS3Int8Train(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, inputs, down, up, coefficients, raw_scale, raw_shift, cell):
-        _lib.require_cuda(inputs)
-        cell._repack_masters()
-        x = inputs.reshape(-1, inputs.shape[-1])
-        xq, xs = quantize_last_dim(x, cell.group)
-        hq, hs, coords = cell._project(xq, xs)
-        y = gemm_out(hq, hs, cell.up_codes, cell.up_scales, out_dtype=cell._out_dtype(inputs))
+        y, saved = ks3_train_forward(cell, inputs)
         ctx.cell = cell
         ctx.input_shape = inputs.shape
-        ctx.save_for_backward(xq, xs, hq, hs, coords)
-        return y.reshape(*inputs.shape[:-1], cell.out_features)
+        ctx.save_for_backward(*saved)
+        return y
 
     @staticmethod
     def backward(ctx, grad_out):
@@ -273,7 +268,35 @@ class _KS3Int8Train(torch.autograd.Function):
         return ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, ctx.input_shape)
 
 
-def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_handoff=True):
+def _pad_k(codes: torch.Tensor) -> torch.Tensor:
+    """Zero codes up to the next multiple of 128 along the last dim."""
+    pad = -codes.shape[-1] % GROUP_SIZE
+    return torch.nn.functional.pad(codes, (0, pad)) if pad else codes
+
+
+def ks3_train_forward(cell, inputs):
+    """Training forward of ks3_int8.py:326-338: re-pack the masters, quantise x,
+    project, spine, up-projection.  Returns (y, (xq, xs, hq, hs, coords))."""
+    _lib.require_cuda(inputs)
+    cell._repack_masters()
+    x = inputs.reshape(-1, inputs.shape[-1])
+    xq, xs = quantize_last_dim(x, cell.group)
+    hq, hs, coords = cell._project(xq, xs)
+    y = gemm_out(hq, hs, cell.up_codes, cell.up_scales, out_dtype=cell._out_dtype(inputs))
+    return y.reshape(*inputs.shape[:-1], cell.out_features), (xq, xs, hq, hs, coords)
+
+
+def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_handoff=True,
+                 grads_into=None):
+    """Backward of ks3_int8.py:341-429.
+
+    Returns (dx, ddown, dup, dcoeff, dscale, dshift, None) as the reference's
+    autograd Function.  With `grads_into` (a dict of fp32 tensors shaped like
+    the masters: down, up, coefficients, raw_scale, raw_shift) the parameter
+    gradients are instead written there, as the values the FP16 handoff
+    (ks3_int8.py:75-84) gives after the cast to the fp32 masters, and only dx
+    is returned.  That path decides the overflow fallback on the device (a
+    predicated fp32 re-run of the wgrad GEMM), so it never waits for the GPU."""
     M, C = coords.shape
     dev = coords.device
     g = grad_out.reshape(-1, cell.out_features)
@@ -322,9 +345,24 @@ def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_hand
                   else torch.float32)
     # wgrads, quantised along tokens (ks3_int8.py:417-424)
     xT_q, xT_s = quantize_cols(xq, x_scales=xs, x_group=cell.group)
-    ddown = gemm_out(dctq, dcts, xT_q, xT_s, out_dtype=FP16, status=flags[1:2])
     gT_q, gT_s = quantize_cols(g, round_f16=True)
     hT_q, hT_s = quantize_cols(hq, x_scales=hs, x_group=cell.group)
+    if M % GROUP_SIZE:  # the wgrads contract over tokens: zero-pad K (gemm.py:71-73)
+        dctq, xT_q, gT_q, hT_q = (_pad_k(t) for t in (dctq, xT_q, gT_q, hT_q))
+    if grads_into is not None:
+        dx = dx.reshape(input_shape).to(grad_out.dtype)
+        for name, (aq, as_, bq, bs), flag in (("down", (dctq, dcts, xT_q, xT_s), flags[1:2]),
+                                              ("up", (gT_q, gT_s, hT_q, hT_s), flags[2:3])):
+            out = grads_into[name]
+            gemm_out(aq, as_, bq, bs, out=out, round_f16=True, status=flag)
+            gemm_out(aq, as_, bq, bs, out=out, status=flag, if_status=True)  # fp32 fallback
+        # dcoeff / dscale / dshift are fp16 already in the reference (:387-394):
+        # the handoff hands them over unchanged, the masters see float(fp16)
+        grads_into["coefficients"].copy_(dcoeff.view_as(grads_into["coefficients"]))
+        grads_into["raw_scale"].copy_(dscale.view_as(grads_into["raw_scale"]))
+        grads_into["raw_shift"].copy_(dshift.view_as(grads_into["raw_shift"]))
+        return dx
+    ddown = gemm_out(dctq, dcts, xT_q, xT_s, out_dtype=FP16, status=flags[1:2])
     dup = gemm_out(gT_q, gT_s, hT_q, hT_s, out_dtype=FP16, status=flags[2:3])
 
     bad = [False, False, False]

@@ -114,13 +114,18 @@ class KS3DataParallelStep:
         self.params = [cell.master_down, cell.master_up, cell.master_coefficients,
                        cell.master_raw_scale, cell.master_raw_shift]
         self.grads = FlatGrads(self.params)
+        self.grad_views = {name: p.grad for name, p in zip(
+            ("down", "up", "coefficients", "raw_scale", "raw_shift"), self.params)}
         self.opt = AdamW(self.params, lr=lr)
 
     def __call__(self, x: torch.Tensor, grad_out: torch.Tensor) -> torch.Tensor:
-        self.grads.zero_()
-        x = x.detach().requires_grad_(True)
-        y = self.cell(x)
-        y.backward(grad_out)
+        """One step.  The backward writes every parameter gradient straight into
+        the flat fp32 buffer (as the reference's autograd would leave it after
+        the FP16 handoff and the cast to fp32), so no zeroing, casting or
+        accumulation pass runs and nothing waits for the GPU."""
+        from ..kernels.ks3_int8 import ks3_backward, ks3_train_forward
+        y, saved = ks3_train_forward(self.cell, x.detach())
+        ks3_backward(self.cell, grad_out, *saved, x.shape, grads_into=self.grad_views)
         allreduce_mean_(self.grads.buffer)
         self.opt.step()
         return y

@@ -1,0 +1,77 @@
+"""GPU: the data-parallel step's direct-to-buffer backward equals the
+reference-shaped autograd path (ks3_int8.py:326-429 + the FP16 handoff
+:75-84 + the cast into fp32 masters), including the fp32 overflow fallback."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _cell(d, C, seed):
+    from ksdraft_b200.kernels.ks3_int8 import KS3Int8Cell
+    from ksdraft_b200.model.ks3 import KS3
+    torch.manual_seed(seed)
+    cell = KS3(d, C)
+    with torch.no_grad():
+        cell.down.weight.normal_(0, 0.02)
+        cell.up.weight.normal_(0, 0.02)
+    return KS3Int8Cell(cell.cuda(), nonlinear="int8", trainable=True)
+
+
+def _autograd_grads(q, x, g):
+    for p in (q.master_down, q.master_up, q.master_coefficients, q.master_raw_scale,
+              q.master_raw_shift):
+        p.grad = None
+    xr = x.detach().requires_grad_(True)
+    y = q(xr)
+    y.backward(g)
+    return y.detach(), xr.grad, [p.grad.float().clone() for p in (
+        q.master_down, q.master_up, q.master_coefficients, q.master_raw_scale,
+        q.master_raw_shift)]
+
+
+def _direct_grads(q, x, g):
+    from ksdraft_b200.kernels.ks3_int8 import ks3_backward, ks3_train_forward
+    views = {n: torch.full_like(p, float("nan"), dtype=torch.float32) for n, p in zip(
+        ("down", "up", "coefficients", "raw_scale", "raw_shift"),
+        (q.master_down, q.master_up, q.master_coefficients, q.master_raw_scale,
+         q.master_raw_shift))}
+    y, saved = ks3_train_forward(q, x)
+    dx = ks3_backward(q, g, *saved, x.shape, grads_into=views)
+    torch.cuda.synchronize()
+    return y, dx, [views[n] for n in ("down", "up", "coefficients", "raw_scale", "raw_shift")]
+
+
+@pytest.mark.parametrize("g_scale", [1e-2, 3e3])   # 3e3 overflows fp16 in the wgrads
+def test_direct_backward_equals_autograd(g_scale):
+    q = _cell(256, 384, 5)
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(300, 256, device="cuda", generator=gen).to(torch.bfloat16)
+    g = (torch.randn(300, 256, device="cuda", generator=gen) * g_scale).to(torch.bfloat16)
+    y_a, dx_a, ga = _autograd_grads(q, x, g)
+    y_d, dx_d, gd = _direct_grads(q, x, g)
+    assert torch.equal(y_a, y_d)
+    assert torch.equal(dx_a, dx_d)
+    for name, a, b in zip(("down", "up", "coefficients", "raw_scale", "raw_shift"), ga, gd):
+        a = a.reshape(b.shape)
+        same = (a == b) | (torch.isnan(a) & torch.isnan(b))
+        assert bool(same.all()), name
+    if g_scale > 1:   # the fallback path ran: some wgrad is beyond fp16 range
+        assert max(float(ga[0].abs().max()), float(ga[1].abs().max())) > 65504
+
+
+def test_data_parallel_step_runs_and_updates():
+    from ksdraft_b200.train.dp import KS3DataParallelStep
+    q = _cell(256, 384, 6)
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    x = torch.randn(256, 256, device="cuda", generator=gen).to(torch.bfloat16)
+    g = (torch.randn(256, 256, device="cuda", generator=gen) * 1e-2).to(torch.bfloat16)
+    _, _, ga = _autograd_grads(q, x, g)      # reference-shaped grads, before any update
+    step = KS3DataParallelStep(q)            # attaches the flat fp32 grad buffer
+    before = q.master_down.detach().clone()
+    step(x, g)
+    torch.cuda.synchronize()
+    assert torch.equal(step.grad_views["down"].reshape(ga[0].shape), ga[0])
+    assert torch.equal(step.grad_views["up"].reshape(ga[1].shape), ga[1])
+    assert not torch.equal(before, q.master_down.detach())
