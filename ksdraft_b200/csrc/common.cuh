@@ -18,6 +18,9 @@
 
 #include "../../include/ksd8.h"
 
+#ifndef KSD8_SUSPEND_NS
+#define KSD8_SUSPEND_NS 20000u  // suspend-time hint of one try_wait (woken on completion)
+#endif
 #ifndef KSD8_WAIT_NS
 #define KSD8_WAIT_NS 2000000000ull  // 2 s of global-timer time per wait
 #endif
@@ -75,6 +78,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a warp whose phase is not complete is
+// parked (up to `ns` nanoseconds, woken when the phase completes) instead of
+// re-issuing the test, so waiting warps leave the issue slots of their SM
+// sub-partition to the warps that compute.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait. Returns false (and records a timeout) when the phase did not
 // complete within KSD8_WAIT_NS, or when another warp of the CTA already gave
 // up (abort flag in shared memory), so that every role drains promptly.
@@ -84,8 +103,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++n & 255u) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, KSD8_SUSPEND_NS)) return true;
+    if ((++n & 15u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > KSD8_WAIT_NS) {
         *abort_flag = 1;

@@ -19,8 +19,8 @@
 //                int32 accumulators in TMEM (ping-pong across groups and
 //                tiles); commits to the smem slot's "empty" barrier and to the
 //                accumulator's "full" barrier.
-//   warp 2       scale loader: fp16 sa[m0.., g] and sw[n0.., g] -> fp32 ring.
-//   warp 3       idle (completes the role warpgroup)
+//   warps 2, 3   scale loaders (alternate batches of groups): fp16 sa[m0.., g]
+//                and sw[n0.., g] -> fp32 ring.
 //   warps 4..    epilogue: each thread owns one row and CPT consecutive
 //                columns of the tile.  Per group it loads the int32
 //                accumulator from TMEM (one chunk ahead), adds it into its fp32
@@ -51,8 +51,8 @@ struct GemmArgs {
 
 constexpr int BM = 128;
 constexpr int BK = 128;    // one GS128 group of int8 = one 128-byte swizzled row
-constexpr int SRING = 8;   // scale ring slots
-constexpr int SBATCH = 2;  // groups of scales fetched per round by the scale warp
+constexpr int SRING = 16;  // scale ring slots
+constexpr int SBATCH = 4;  // groups of scales fetched per round by each scale warp
 constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
 
@@ -107,11 +107,29 @@ __device__ __forceinline__ void tmem_st_magic_w(uint32_t taddr) {
   for (int i = 0; i < W; i += 8) tmem_st_magic_x8(taddr + i);
 }
 
-// Register split for the 12-warp (384-thread) variant: the block launches at
-// 168 registers per thread (64512 in total); the role warpgroup drops to 88
-// and the two epilogue warpgroups rise to 208: 128 * 88 + 256 * 208 = 64512.
-constexpr int REG_LAUNCH = 168, REG_ROLE = 88, REG_EPI = 208;
-static_assert(128 * REG_ROLE + 256 * REG_EPI <= 384 * REG_LAUNCH, "register split");
+// Register splits (setmaxnreg) by block size.  12 warps (384 threads): launch
+// at 168 per thread, role warpgroup 88, the two epilogue warpgroups 208
+// (128 * 88 + 256 * 208 = 64512).  20 warps (640 threads): launch at 96, role
+// 56, the four epilogue warpgroups 104 (128 * 56 + 512 * 104 = 60416 <= 61440).
+template <int THREADS>
+struct RegSplit {
+  static constexpr bool on = false;
+  static constexpr int launch = 0, role = 0, epi = 0;
+};
+template <>
+struct RegSplit<384> {
+  static constexpr bool on = true;
+  static constexpr int launch = 168, role = 88, epi = 208;
+};
+template <>
+struct RegSplit<640> {
+  static constexpr bool on = true;
+  static constexpr int launch = 96, role = 56, epi = 104;
+};
+static_assert(128 * RegSplit<384>::role + 256 * RegSplit<384>::epi <= 384 * RegSplit<384>::launch,
+              "register split");
+static_assert(128 * RegSplit<640>::role + 512 * RegSplit<640>::epi <= 640 * RegSplit<640>::launch,
+              "register split");
 
 template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS, int CG>
 __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
@@ -119,12 +137,16 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
                      const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   using L = GemmSmem<BN, EPI_WARPS, STAGES, CG>;
   static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per MMA");
-  constexpr bool REGSPLIT = (4 + EPI_WARPS) * 32 == 384;
+  using RS = RegSplit<(4 + EPI_WARPS) * 32>;
+  constexpr bool REGSPLIT = RS::on;
   constexpr int CPT = BN * 4 / EPI_WARPS;  // columns per epilogue thread
   // TMEM load width (registers per chunk): 32 columns per tcgen05.ld halves
   // the exposed load round trips of 16-column chunks.
   constexpr int LDW = 32;
   constexpr int NCH = CPT / LDW;
+  // Slices of up to 64 columns per thread are read from TMEM in one round
+  // trip and the accumulator is released before the arithmetic.
+  constexpr bool EARLY = CPT <= 64;
   constexpr int NBUF = L::NBUF;
   constexpr int TMEM_COLS = NBUF * BN <= 256 ? 256 : 512;
   static_assert(NBUF * BN <= 512, "TMEM capacity");
@@ -201,7 +223,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   // Role warpgroup (warps 0-3) and epilogue warpgroups each change their
   // register allotment first, then dispatch on the warp index.
   if (warp < 4) {
-    if constexpr (REGSPLIT) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_ROLE));
+    if constexpr (REGSPLIT) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RS::role));
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     int gg = 0;
@@ -265,60 +287,63 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
         __syncwarp();
       }
     }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------ scale loader
-    int gg0 = 0;
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ scale loaders
+    // Two warps take alternate batches of SBATCH consecutive groups of this
+    // CTA's group sequence (gg), so that up to 2 * SBATCH groups of scale
+    // loads are in flight; each group's fp16 scales go to ring slot gg % SRING
+    // as fp32.
+    const int li = warp - 2;
+    const int my_tiles = unit < n_tiles ? (n_tiles - unit + n_units - 1) / n_units : 0;
+    const int total = my_tiles * G;
     bool ok = true;
-    for (int tile = unit; ok && tile < n_tiles; tile += n_units) {
-      const int m0 = (tile % tiles_m) * BM * CG + rank * BM, n0 = (tile / tiles_m) * BN;
-      for (int g0 = 0; ok && g0 < G; g0 += SBATCH) {
-        float va[SBATCH][BM / 32];
-        float vw[SBATCH][BN / 32];
+    for (int b0 = li * SBATCH; ok && b0 < total; b0 += 2 * SBATCH) {
+      float va[SBATCH][BM / 32];
+      float vw[SBATCH][BN / 32];
 #pragma unroll
-        for (int j = 0; j < SBATCH; ++j) {
-          const int g = g0 + j;
+      for (int j = 0; j < SBATCH; ++j) {
+        const int gg = b0 + j;
+        const int tile = unit + (gg / G) * n_units;
+        const int g = gg % G;
+        const int m0 = (tile % tiles_m) * BM * CG + rank * BM, n0 = (tile / tiles_m) * BN;
+        const bool live = !PARTIALS && gg < total;
 #pragma unroll
-          for (int i = 0; i < BM / 32; ++i) {
-            const int r = m0 + lane + 32 * i;
-            va[j][i] = (PARTIALS || g >= G || r >= args.M)
-                           ? 0.f
-                           : __half2float(args.a_scales[(size_t)r * G + g]);
-          }
-#pragma unroll
-          for (int i = 0; i < BN / 32; ++i) {
-            const int c = n0 + lane + 32 * i;
-            vw[j][i] = (PARTIALS || g >= G || c >= args.N)
-                           ? 0.f
-                           : __half2float(args.w_scales[(size_t)c * G + g]);
-          }
+        for (int i = 0; i < BM / 32; ++i) {
+          const int r = m0 + lane + 32 * i;
+          va[j][i] = (!live || r >= args.M) ? 0.f
+                                            : __half2float(args.a_scales[(size_t)r * G + g]);
         }
 #pragma unroll
-        for (int j = 0; j < SBATCH; ++j) {
-          const int g = g0 + j;
-          // no early exit inside this unrolled loop: va/vw must stay in registers
-          if (ok && g < G) {
-            const int gg = gg0 + g;
-            const int slot = gg % SRING;
-            const uint32_t ph = (gg / SRING) & 1;
-            if (mbar_wait(&s_empty[slot], ph ^ 1, abort_flag, args.status)) {
-              float* dst = sScale + slot * L::SCALE_FLOATS;
+        for (int i = 0; i < BN / 32; ++i) {
+          const int c = n0 + lane + 32 * i;
+          vw[j][i] = (!live || c >= args.N) ? 0.f
+                                            : __half2float(args.w_scales[(size_t)c * G + g]);
+        }
+      }
 #pragma unroll
-              for (int i = 0; i < BM / 32; ++i) dst[lane + 32 * i] = va[j][i];
+      for (int j = 0; j < SBATCH; ++j) {
+        const int gg = b0 + j;
+        // no early exit inside this unrolled loop: va/vw must stay in registers
+        if (ok && gg < total) {
+          const int slot = gg % SRING;
+          const uint32_t ph = (gg / SRING) & 1;
+          if (mbar_wait(&s_empty[slot], ph ^ 1, abort_flag, args.status)) {
+            float* dst = sScale + slot * L::SCALE_FLOATS;
 #pragma unroll
-              for (int i = 0; i < BN / 32; ++i) dst[BM + lane + 32 * i] = vw[j][i];
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&s_full[slot]);
-            } else {
-              ok = false;
-            }
+            for (int i = 0; i < BM / 32; ++i) dst[lane + 32 * i] = va[j][i];
+#pragma unroll
+            for (int i = 0; i < BN / 32; ++i) dst[BM + lane + 32 * i] = vw[j][i];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_full[slot]);
+          } else {
+            ok = false;
           }
         }
       }
-      gg0 += G;
     }
-  }  // warp 3: idle
+  }
   } else {
-    if constexpr (REGSPLIT) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_EPI));
+    if constexpr (REGSPLIT) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(RS::epi));
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 4;               // 0 .. EPI_WARPS-1
     const int quad = warp & 3;             // TMEM lane quadrant this warp may access
@@ -364,48 +389,94 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
         const float2 sa2 = make_float2(sa, sa);
         const float* sw = sc + BM + col0;
         const uint32_t tb = t_row + buf * BN + col0;
-        uint32_t r[2][LDW];
-        tmem_ld_w<LDW>(tb, r[0]);
-        tmem_wait_ld();
+        if constexpr (EARLY) {
+          // Whole slice in one round trip: CPT/32 loads, one wait, re-arm, and
+          // release the accumulator to the MMA before any arithmetic.
+          uint32_t r[CPT];
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          if (c + 1 < NCH) tmem_ld_w<LDW>(tb + (c + 1) * LDW, r[(c + 1) & 1]);
-          const uint32_t* rc = r[c & 1];
+          for (int c = 0; c < CPT / 32; ++c)
+            tmem_ld_32x32b_x32(tb + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < CPT / 8; ++c) tmem_st_magic_x8(tb + c * 8);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 2) mbar_arrive_cluster(&acc_empty[buf], 0);
+            else mbar_arrive(&acc_empty[buf]);
+          }
           if constexpr (PARTIALS) {
             const int m = m0 + row;
             if (m < args.M) {
               int32_t* o = reinterpret_cast<int32_t*>(args.out) +
                            ((size_t)g * args.M + m) * args.N;
 #pragma unroll
-              for (int j = 0; j < LDW; ++j) {
-                const int n = n0 + col0 + c * LDW + j;
-                if (n < args.N) o[n] = (int32_t)(rc[j] - MAGIC_BITS);
+              for (int j = 0; j < CPT; ++j) {
+                const int n = n0 + col0 + j;
+                if (n < args.N) o[n] = (int32_t)(r[j] - MAGIC_BITS);
               }
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < LDW; j += 4) {
-              const float4 w4 = *reinterpret_cast<const float4*>(sw + c * LDW + j);
-              const int o = (c * LDW + j) / 2;
+            for (int j = 0; j < CPT; j += 4) {
+              const float4 w4 = *reinterpret_cast<const float4*>(sw + j);
+              const int o = j / 2;
               const float2 d0 = __fadd2_rn(
-                  make_float2(__uint_as_float(rc[j]), __uint_as_float(rc[j + 1])), neg_magic);
+                  make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), neg_magic);
               const float2 d1 = __fadd2_rn(
-                  make_float2(__uint_as_float(rc[j + 2]), __uint_as_float(rc[j + 3])),
-                  neg_magic);
+                  make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])), neg_magic);
               acc[o] = __ffma2_rn(d0, __fmul2_rn(sa2, make_float2(w4.x, w4.y)), acc[o]);
               acc[o + 1] = __ffma2_rn(d1, __fmul2_rn(sa2, make_float2(w4.z, w4.w)), acc[o + 1]);
             }
           }
-          tmem_st_magic_w<LDW>(tb + c * LDW);
-          if (c + 1 < NCH) tmem_wait_ld();
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();  // one arrival per warp once all its lanes are done
-        if (lane == 0) {
-          if constexpr (CG == 2) mbar_arrive_cluster(&acc_empty[buf], 0);
-          else mbar_arrive(&acc_empty[buf]);
-          mbar_arrive(&s_empty[slot]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_empty[slot]);
+        } else {
+          uint32_t r[2][LDW];
+          tmem_ld_w<LDW>(tb, r[0]);
+          tmem_wait_ld();
+  #pragma unroll
+          for (int c = 0; c < NCH; ++c) {
+            if (c + 1 < NCH) tmem_ld_w<LDW>(tb + (c + 1) * LDW, r[(c + 1) & 1]);
+            const uint32_t* rc = r[c & 1];
+            if constexpr (PARTIALS) {
+              const int m = m0 + row;
+              if (m < args.M) {
+                int32_t* o = reinterpret_cast<int32_t*>(args.out) +
+                             ((size_t)g * args.M + m) * args.N;
+  #pragma unroll
+                for (int j = 0; j < LDW; ++j) {
+                  const int n = n0 + col0 + c * LDW + j;
+                  if (n < args.N) o[n] = (int32_t)(rc[j] - MAGIC_BITS);
+                }
+              }
+            } else {
+  #pragma unroll
+              for (int j = 0; j < LDW; j += 4) {
+                const float4 w4 = *reinterpret_cast<const float4*>(sw + c * LDW + j);
+                const int o = (c * LDW + j) / 2;
+                const float2 d0 = __fadd2_rn(
+                    make_float2(__uint_as_float(rc[j]), __uint_as_float(rc[j + 1])), neg_magic);
+                const float2 d1 = __fadd2_rn(
+                    make_float2(__uint_as_float(rc[j + 2]), __uint_as_float(rc[j + 3])),
+                    neg_magic);
+                acc[o] = __ffma2_rn(d0, __fmul2_rn(sa2, make_float2(w4.x, w4.y)), acc[o]);
+                acc[o + 1] = __ffma2_rn(d1, __fmul2_rn(sa2, make_float2(w4.z, w4.w)), acc[o + 1]);
+              }
+            }
+            tmem_st_magic_w<LDW>(tb + c * LDW);
+            if (c + 1 < NCH) tmem_wait_ld();
+          }
+
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();  // one arrival per warp once all its lanes are done
+          if (lane == 0) {
+            if constexpr (CG == 2) mbar_arrive_cluster(&acc_empty[buf], 0);
+            else mbar_arrive(&acc_empty[buf]);
+            mbar_arrive(&s_empty[slot]);
+          }
         }
       }
 
@@ -580,12 +651,13 @@ static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t 
   const int sms = sm_count_cached();
   const int units = sms / CG;
   const int grid = (tiles < units ? tiles : units) * CG;
-  if ((4 + EPI_WARPS) * 32 == 384) {
+  if constexpr (RegSplit<(4 + EPI_WARPS) * 32>::on) {
     // the register split is only valid for the launch register count it was sized for
     static int regs_checked[32] = {0};
     if (dev >= 0 && dev < 32 && !regs_checked[dev]) {
       cudaFuncAttributes fa;
-      if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != REG_LAUNCH)
+      if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess ||
+          fa.numRegs != RegSplit<(4 + EPI_WARPS) * 32>::launch)
         return KSD8_ERR_UNSUPPORTED;
       regs_checked[dev] = 1;
     }
@@ -634,10 +706,15 @@ int ksd8_gemm_launch(const int8_t* a, const void* a_scales, const int8_t* w, con
     if (m >= 256 && n >= 256) return launch_gemm<256, 8, 6, true, 2>(a, w, args, k, stream);
     return launch_gemm<128, 4, 4, true, 1>(a, w, args, k, stream);
   }
-  // Tile width: cost model = waves x per-tile time, a tile costing its width
-  // plus a fixed share (in 128-column units: 2.5 for 256-wide vs 1.5).
   const int64_t tiles_m = (m + 127) / 128;
   const int64_t sms = sm_count_cached();
+  // At least one full wave of 128 x 128 tiles: 8 epilogue warps of 64 columns
+  // each, 4 TMEM accumulator buffers, accumulator released before the math.
+  if (tiles_m * ((n + 127) / 128) >= sms)
+    return launch_gemm<128, 8, 4, false, 1>(a, w, args, k, stream);
+  // Smaller problems: tile width by cost model = waves x per-tile time, a tile
+  // costing its width plus a fixed share (in 128-column units: 2.5 for
+  // 256-wide vs 1.5).
   const int64_t w256 = (tiles_m * ((n + 255) / 256) + sms - 1) / sms;
   const int64_t w128 = (tiles_m * ((n + 127) / 128) + sms - 1) / sms;
   if (n > 128 && w256 * 5 <= w128 * 3)
