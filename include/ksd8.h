@@ -217,6 +217,37 @@ int ksd8_adamw_step(float* param, const void* grad, int grad_dtype, float* exp_a
 /* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);
 
+/* ---- LM head: vocab-parallel cross-entropy and top-k ----
+ *
+ * The reference head is the tied fp32 nn.Linear(d, V) + F.cross_entropy of
+ * ksdraft/model/draft.py:39,51,82 and ksdraft/train/__init__.py:77.  With the
+ * vocabulary split into contiguous shards (one per rank) the logits shard
+ * (M, V_local) comes from ksd8_w8a8_gemm; these entry points reduce it. */
+
+/* Per row of the shard: out_max = max_c l, out_sum = sum_c exp(l - out_max),
+ * out_tgt = l[targets[row] - vstart] when that column is in the shard, else 0.
+ * logits (M, V_local) row stride ld, dtype KSD8_F32 / KSD8_BF16 / KSD8_F16;
+ * targets (M) int64 global vocab ids; outputs (M) fp32. */
+int ksd8_ce_partials(const void* logits, int dtype, int64_t m, int64_t v_local, int64_t ld,
+                     const int64_t* targets, int64_t vstart, float* out_max, float* out_sum,
+                     float* out_tgt, int* status, void* stream);
+
+/* dlogits[row, c] = (exp(l - gmax[row]) / gsum[row] - [vstart + c == targets[row]]) * scale,
+ * the cross-entropy gradient of the shard given the global max and sum of
+ * exp over all shards (scale = 1 / total rows for the mean reduction).
+ * dlogits fp32 (M, V_local) row stride ldd. */
+int ksd8_ce_grad(const void* logits, int dtype, int64_t m, int64_t v_local, int64_t ld,
+                 const int64_t* targets, int64_t vstart, const float* gmax, const float* gsum,
+                 float scale, float* dlogits, int64_t ldd, int* status, void* stream);
+
+/* Per-row top-k (1 <= k <= 32) of vals (M, C) row stride ld: out_vals (M, k)
+ * fp32 descending, out_ids (M, k) int64; ids are offset + column, or idx[row,
+ * column] when idx (M, C, same stride) is given (merging gathered shard
+ * candidates).  Ties: the smaller id first. */
+int ksd8_topk_rows(const void* vals, int dtype, const int64_t* idx, int64_t m, int64_t c,
+                   int64_t ld, int k, int64_t offset, float* out_vals, int64_t* out_ids,
+                   int* status, void* stream);
+
 /* ---- allocation-free variant (no counterpart in the reference) ----
  *
  * ksd8_ks3_vjp_static: ksd8_ks3_vjp followed by ksd8_ks3_vjp_reduce, with the

@@ -52,6 +52,9 @@ SIGNATURES: dict[str, list] = {
                                    vp, vp],
     "ksd8_adamw_step": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp],
     "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
+    "ksd8_ce_partials": [vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp],
+    "ksd8_ce_grad": [vp, i32, i64, i64, i64, vp, i64, vp, vp, f32, vp, i64, vp, vp],
+    "ksd8_topk_rows": [vp, i32, vp, i64, i64, i64, i32, i64, vp, vp, vp, vp],
     "ksd8_ks3_vjp_static": [vp, vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                             vp, vp, vp, vp],
 }

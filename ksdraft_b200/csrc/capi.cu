@@ -33,6 +33,12 @@ int ksd8_rosa_match_launch(const uint64_t*, const uint64_t*, const uint64_t*, in
 int ksd8_rosa_timemix_launch(const void*, int, int64_t, int64_t, int64_t, const float*,
                              const float*, const float*, int8_t*, void*, int8_t*, void*, int8_t*,
                              void*, cudaStream_t);
+int ksd8_ce_partials_launch(const void*, int, int64_t, int64_t, int64_t, const int64_t*, int64_t,
+                            float*, float*, float*, cudaStream_t);
+int ksd8_ce_grad_launch(const void*, int, int64_t, int64_t, int64_t, const int64_t*, int64_t,
+                        const float*, const float*, float, float*, int64_t, cudaStream_t);
+int ksd8_topk_rows_launch(const void*, int, const int64_t*, int64_t, int64_t, int64_t, int, int64_t,
+                          float*, int64_t*, cudaStream_t);
 int ksd8_adamw_launch(float*, const void*, int, float*, float*, int64_t, float, float, float,
                       float, float, int, cudaStream_t);
 
@@ -273,6 +279,43 @@ int ksd8_adamw_step(float* param, const void* grad, int grad_dtype, float* exp_a
   if (n > 0 && (!param || !grad || !exp_avg || !exp_avg_sq)) return KSD8_ERR_ARG;
   return finish(ksd8_adamw_launch(param, grad, grad_dtype, exp_avg, exp_avg_sq, n, lr, beta1,
                                   beta2, eps, weight_decay, step, S(stream)));
+}
+
+int ksd8_ce_partials(const void* logits, int dtype, int64_t m, int64_t v_local, int64_t ld,
+                     const int64_t* targets, int64_t vstart, float* out_max, float* out_sum,
+                     float* out_tgt, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  if (m < 0 || v_local <= 0 || ld < v_local || vstart < 0) return KSD8_ERR_SHAPE;
+  if (m > 0 && (!logits || !targets || !out_max || !out_sum || !out_tgt)) return KSD8_ERR_ARG;
+  if (m > INT32_MAX) return KSD8_ERR_SHAPE;
+  return finish(ksd8_ce_partials_launch(logits, dtype, m, v_local, ld, targets, vstart, out_max,
+                                        out_sum, out_tgt, S(stream)));
+}
+
+int ksd8_ce_grad(const void* logits, int dtype, int64_t m, int64_t v_local, int64_t ld,
+                 const int64_t* targets, int64_t vstart, const float* gmax, const float* gsum,
+                 float scale, float* dlogits, int64_t ldd, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  if (m < 0 || v_local <= 0 || ld < v_local || ldd < v_local || vstart < 0) return KSD8_ERR_SHAPE;
+  if (m > 65535) return KSD8_ERR_UNSUPPORTED;  // rows map to grid.y
+  if (m > 0 && (!logits || !targets || !gmax || !gsum || !dlogits)) return KSD8_ERR_ARG;
+  return finish(ksd8_ce_grad_launch(logits, dtype, m, v_local, ld, targets, vstart, gmax, gsum,
+                                    scale, dlogits, ldd, S(stream)));
+}
+
+int ksd8_topk_rows(const void* vals, int dtype, const int64_t* idx, int64_t m, int64_t c,
+                   int64_t ld, int k, int64_t offset, float* out_vals, int64_t* out_ids,
+                   int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  if (k < 1 || k > 32) return KSD8_ERR_ARG;
+  if (m < 0 || c < k || ld < c) return KSD8_ERR_SHAPE;
+  if (m > INT32_MAX) return KSD8_ERR_SHAPE;
+  if (m > 0 && (!vals || !out_vals || !out_ids)) return KSD8_ERR_ARG;
+  return finish(ksd8_topk_rows_launch(vals, dtype, idx, m, c, ld, k, offset, out_vals, out_ids,
+                                      S(stream)));
 }
 
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream) {

@@ -1,0 +1,290 @@
+// LM head (vocab projection) kernels around the W8A8 GEMM: vocab-parallel
+// cross-entropy partials and gradient, and per-row top-k for drafting.
+//
+// The reference head is a tied fp32 nn.Linear(d, V) followed by
+// F.cross_entropy (ksdraft/model/draft.py:39,51,82; ksdraft/train/__init__.py:77).
+// Here each rank owns a contiguous vocab shard of the logits (M, V_local) and
+// reduces it to three floats per row: the shard max, the shard sum of
+// exp(logit - max) and the target logit when the target falls in the shard.
+// The host combines ranks with all-reduces of those (M) vectors
+// (max, then rescaled sum, then target), so no logits cross NVLink.
+//
+//   ce_partials_kernel   one CTA per row, online max / sum-of-exp over the shard
+//   ce_grad_kernel       dlogits = (exp(l - lse) - [col == target]) * scale
+//   topk_rows_kernel     per-row top-k (value desc, index asc on ties)
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace ksd8 {
+
+constexpr float LOG2E = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_val(const T* p) {
+  if constexpr (std::is_same<T, float>::value) return *p;
+  else if constexpr (std::is_same<T, __half>::value) return __half2float(*p);
+  else return __bfloat162float(*p);
+}
+
+// (m, s) <- online merge of a value v: s counts exp(v - m) for the running max m.
+__device__ __forceinline__ void online_add(float& m, float& s, float v) {
+  if (v > m) {
+    s = s * ex2_approx((m - v) * LOG2E) + 1.f;
+    m = v;
+  } else {
+    s += ex2_approx((v - m) * LOG2E);
+  }
+}
+
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  if (m2 > m) {
+    s = s * ex2_approx((m - m2) * LOG2E) + s2;
+    m = m2;
+  } else if (m2 != -INFINITY) {
+    s += s2 * ex2_approx((m2 - m) * LOG2E);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) ce_partials_kernel(const T* logits, int64_t V, int64_t ld,
+                                                          const int64_t* targets, int64_t vstart,
+                                                          float* out_max, float* out_sum,
+                                                          float* out_tgt) {
+  const int64_t row = blockIdx.x;
+  const T* lr = logits + row * ld;
+  float m = -INFINITY, s = 0.f;
+  constexpr int VEC = 16 / sizeof(T);
+  const bool vec = ((reinterpret_cast<uintptr_t>(lr) & 15) == 0);
+  int64_t c0 = 0;
+  if (vec) {
+    const int64_t nv = V / VEC;
+    for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) {
+      const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(lr) + i);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) online_add(m, s, ld_val(e + j));
+    }
+    c0 = nv * VEC;
+  }
+  for (int64_t c = c0 + threadIdx.x; c < V; c += blockDim.x) online_add(m, s, ld_val(lr + c));
+  // block reduction of (m, s)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  __shared__ float sm[8], ss[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = sm[0], S = ss[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) online_merge(M, S, sm[w], ss[w]);
+    out_max[row] = M;
+    out_sum[row] = S;
+    const int64_t t = targets[row] - vstart;
+    out_tgt[row] = (t >= 0 && t < V) ? ld_val(lr + t) : 0.f;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) ce_grad_kernel(const T* logits, int64_t V, int64_t ld,
+                                                      const int64_t* targets, int64_t vstart,
+                                                      const float* gmax, const float* gsum,
+                                                      float scale, float* dlogits,
+                                                      int64_t ldd) {
+  const int64_t row = blockIdx.y;
+  const T* lr = logits + row * ld;
+  float* dr = dlogits + row * ldd;
+  // exp(l - lse) = 2^((l - max) * log2e) / sum
+  const float mx = gmax[row];
+  const float inv = 1.f / gsum[row];
+  const int64_t t = targets[row] - vstart;
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < V;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    const float p = ex2_approx((ld_val(lr + c) - mx) * LOG2E) * inv;
+    dr[c] = (p - (c == t ? 1.f : 0.f)) * scale;
+  }
+}
+
+// ---------------------------------------------------------------- top-k
+
+constexpr int TOPK_MAX = 32;
+
+// a before b: larger value, then smaller index
+__device__ __forceinline__ bool topk_before(float va, int64_t ia, float vb, int64_t ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) topk_rows_kernel(const T* vals, const int64_t* idx,
+                                                        int64_t C, int64_t ld, int k,
+                                                        int64_t offset, float* out_v,
+                                                        int64_t* out_i) {
+  const int64_t row = blockIdx.x;
+  const T* vr = vals + row * ld;
+  const int64_t* ir = idx ? idx + row * ld : nullptr;
+  // per-thread sorted candidate list (insertion; most values fail the first test)
+  float lv[TOPK_MAX];
+  int64_t li[TOPK_MAX];
+#pragma unroll
+  for (int j = 0; j < TOPK_MAX; ++j) {
+    lv[j] = -INFINITY;
+    li[j] = INT64_MAX;
+  }
+  for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
+    const float v = ld_val(vr + c);
+    const int64_t id = ir ? ir[c] : offset + c;
+    if (!topk_before(v, id, lv[k - 1], li[k - 1])) continue;
+    // insert, keeping lv[0..k) sorted: shift the entries it beats one down
+    int p = k - 1;
+    bool moving = true;
+#pragma unroll
+    for (int q = TOPK_MAX - 1; q >= 1; --q) {
+      if (q < k && moving) {
+        if (topk_before(v, id, lv[q - 1], li[q - 1])) {
+          lv[q] = lv[q - 1];
+          li[q] = li[q - 1];
+          p = q - 1;
+        } else {
+          moving = false;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < TOPK_MAX; ++j)
+      if (j == p) {
+        lv[j] = v;
+        li[j] = id;
+      }
+  }
+  // k rounds of block arg-best over the threads' list heads
+  __shared__ float wv[8];
+  __shared__ int64_t wi[8];
+  __shared__ int wt[8];
+  __shared__ int winner;
+  int head = 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int64_t bi = INT64_MAX;
+#pragma unroll
+    for (int j = 0; j < TOPK_MAX; ++j)
+      if (j == head) {
+        bv = lv[j];
+        bi = li[j];
+      }
+    int bt = threadIdx.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int64_t i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      const int t2 = __shfl_xor_sync(0xffffffffu, bt, o);
+      if (topk_before(v2, i2, bv, bi)) {
+        bv = v2;
+        bi = i2;
+        bt = t2;
+      }
+    }
+    if (lane == 0) {
+      wv[warp] = bv;
+      wi[warp] = bi;
+      wt[warp] = bt;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float v = wv[0];
+      int64_t i = wi[0];
+      int t = wt[0];
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+        if (topk_before(wv[w], wi[w], v, i)) {
+          v = wv[w];
+          i = wi[w];
+          t = wt[w];
+        }
+      out_v[row * k + r] = v;
+      out_i[row * k + r] = i;
+      winner = t;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x == winner) ++head;
+    __syncthreads();
+  }
+}
+
+template <typename T>
+static int launch_partials(const void* logits, int64_t M, int64_t V, int64_t ld,
+                           const int64_t* targets, int64_t vstart, float* mx, float* sm,
+                           float* tg, cudaStream_t stream) {
+  ce_partials_kernel<T><<<(unsigned)M, 256, 0, stream>>>(reinterpret_cast<const T*>(logits), V,
+                                                         ld, targets, vstart, mx, sm, tg);
+  return KSD8_OK;
+}
+
+template <typename T>
+static int launch_grad(const void* logits, int64_t M, int64_t V, int64_t ld,
+                       const int64_t* targets, int64_t vstart, const float* gmax,
+                       const float* gsum, float scale, float* dl, int64_t ldd,
+                       cudaStream_t stream) {
+  const int64_t bx = (V + 1023) / 1024;
+  dim3 grid((unsigned)(bx < 64 ? bx : 64), (unsigned)M);
+  ce_grad_kernel<T><<<grid, 256, 0, stream>>>(reinterpret_cast<const T*>(logits), V, ld, targets,
+                                              vstart, gmax, gsum, scale, dl, ldd);
+  return KSD8_OK;
+}
+
+template <typename T>
+static int launch_topk(const void* vals, const int64_t* idx, int64_t M, int64_t C, int64_t ld,
+                       int k, int64_t offset, float* ov, int64_t* oi, cudaStream_t stream) {
+  topk_rows_kernel<T><<<(unsigned)M, 256, 0, stream>>>(reinterpret_cast<const T*>(vals), idx, C,
+                                                       ld, k, offset, ov, oi);
+  return KSD8_OK;
+}
+
+}  // namespace ksd8
+
+using namespace ksd8;
+
+int ksd8_ce_partials_launch(const void* logits, int dtype, int64_t M, int64_t V, int64_t ld,
+                            const int64_t* targets, int64_t vstart, float* mx, float* sm,
+                            float* tg, cudaStream_t stream) {
+  if (M == 0) return KSD8_OK;
+  if (dtype == KSD8_F32) return launch_partials<float>(logits, M, V, ld, targets, vstart, mx, sm, tg, stream);
+  if (dtype == KSD8_BF16)
+    return launch_partials<__nv_bfloat16>(logits, M, V, ld, targets, vstart, mx, sm, tg, stream);
+  return launch_partials<__half>(logits, M, V, ld, targets, vstart, mx, sm, tg, stream);
+}
+
+int ksd8_ce_grad_launch(const void* logits, int dtype, int64_t M, int64_t V, int64_t ld,
+                        const int64_t* targets, int64_t vstart, const float* gmax,
+                        const float* gsum, float scale, float* dl, int64_t ldd,
+                        cudaStream_t stream) {
+  if (M == 0 || V == 0) return KSD8_OK;
+  if (dtype == KSD8_F32)
+    return launch_grad<float>(logits, M, V, ld, targets, vstart, gmax, gsum, scale, dl, ldd, stream);
+  if (dtype == KSD8_BF16)
+    return launch_grad<__nv_bfloat16>(logits, M, V, ld, targets, vstart, gmax, gsum, scale, dl,
+                                      ldd, stream);
+  return launch_grad<__half>(logits, M, V, ld, targets, vstart, gmax, gsum, scale, dl, ldd, stream);
+}
+
+int ksd8_topk_rows_launch(const void* vals, int dtype, const int64_t* idx, int64_t M, int64_t C,
+                          int64_t ld, int k, int64_t offset, float* ov, int64_t* oi,
+                          cudaStream_t stream) {
+  if (M == 0) return KSD8_OK;
+  if (dtype == KSD8_F32) return launch_topk<float>(vals, idx, M, C, ld, k, offset, ov, oi, stream);
+  if (dtype == KSD8_BF16)
+    return launch_topk<__nv_bfloat16>(vals, idx, M, C, ld, k, offset, ov, oi, stream);
+  return launch_topk<__half>(vals, idx, M, C, ld, k, offset, ov, oi, stream);
+}

@@ -168,6 +168,47 @@ def group_partials_numpy(a_codes, w_codes):
     return np.einsum("mgk,ngk->gmn", a, w).astype(np.int32)
 
 
+# ------------------------------------------------------------------ LM head
+
+def _pad128(c):
+    pad = -c.shape[-1] % 128
+    return np.pad(c, [(0, 0)] * (c.ndim - 1) + [(0, pad)]) if pad else c
+
+
+def lm_head_ce(x, w, targets):
+    """INT8-tier LM head + mean cross-entropy and its backward.
+
+    Forward follows Int8Linear semantics (ksdraft/kernels/linear.py:67-73:
+    per-token and per-row GS128, w8a8_gemm) for the tied head of
+    ksdraft/model/draft.py:39,51,82, then F.cross_entropy (mean,
+    ksdraft/train/__init__.py:77) in float64.  Backward: dlogits = (softmax -
+    onehot) / M, then dx = q(dl) q(W^T)^T and dW = q(dl^T) q(x^T)^T, W8A8 as
+    the cell backward of ksdraft/kernels/ks3_int8.py:410-424.
+    Returns (loss, logits fp32, dx fp32, dW fp32)."""
+    x = np.asarray(x, np.float32)
+    w = np.asarray(w, np.float32)
+    t = np.asarray(targets, np.int64)
+    M = x.shape[0]
+    xq, xs = quantize_last_dim(x)
+    wq, ws = quantize_last_dim(w)
+    logits = w8a8_gemm_canonical(_pad128(xq), xs, _pad128(wq), ws)
+    l64 = logits.astype(np.float64)
+    mx = l64.max(1, keepdims=True)
+    se = np.exp(l64 - mx).sum(1, keepdims=True)
+    lse = (np.log(se) + mx)[:, 0]
+    loss = float(np.mean(lse - l64[np.arange(M), t]))
+    p = np.exp(l64 - lse[:, None])
+    p[np.arange(M), t] -= 1.0
+    dl = (p / M).astype(np.float32)
+    dq, ds = quantize_last_dim(dl)
+    wT_q, wT_s = quantize_last_dim(dequantize_last_dim(wq, ws).T.copy())
+    dx = w8a8_gemm_canonical(_pad128(dq), ds, _pad128(wT_q), wT_s)
+    dlT_q, dlT_s = quantize_last_dim(dl.T.copy())
+    xT_q, xT_s = quantize_last_dim(x.T.copy())
+    dw = w8a8_gemm_canonical(_pad128(dlT_q), dlT_s, _pad128(xT_q), xT_s)
+    return loss, logits, dx, dw
+
+
 # ------------------------------------------------------------------ KS3
 
 def make_tanh_lut() -> np.ndarray:

@@ -1,0 +1,173 @@
+"""Multi-rank host logic on CPU (gloo, world size 2, 127.0.0.1): data-parallel
+gradient averaging and finiteness agreement (ksdraft_b200/train/dp.py), the
+vocab-parallel cross-entropy combine and top-k merge of the LM head
+(ksdraft_b200/model/head.py), and failure detection when a rank dies before a
+collective.  Each rank is a spawned child process; results come back through
+files under tmp_path."""
+
+import json
+import os
+import socket
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout_s=30):
+    import datetime
+    sys.path.insert(0, str(ROOT))
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _run(fn, world, tmp_path, *args):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=fn, args=(r, world, port, str(tmp_path), *args))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    return [p.exitcode for p in procs]
+
+
+# ---------------------------------------------------------------- data parallel
+
+def _dp_worker(rank, world, port, out):
+    _init(rank, world, port)
+    from ksdraft_b200.train.dp import FlatGrads, allreduce_mean_, check_finite_across_ranks
+    torch.manual_seed(0)
+    params = [torch.nn.Parameter(torch.zeros(5, 3)), torch.nn.Parameter(torch.zeros(7))]
+    fg = FlatGrads(params)
+    for i, (p, view) in enumerate(fg.views()):
+        view.copy_(torch.arange(view.numel(), dtype=torch.float32) * (rank + 1) + i)
+    allreduce_mean_(fg.buffer)
+    res = {"grads": [p.grad.reshape(-1).tolist() for p in params]}
+    res["finite_all"] = check_finite_across_ranks(fg.buffer)
+    if rank == 1:
+        fg.buffer[3] = float("nan")
+    res["finite_one_bad"] = check_finite_across_ranks(fg.buffer)
+    Path(out, f"dp{rank}.json").write_text(json.dumps(res))
+    dist.destroy_process_group()
+
+
+def test_dp_allreduce_mean_and_finite_flags(tmp_path):
+    assert _run(_dp_worker, 2, tmp_path) == [0, 0]
+    for r in range(2):
+        res = json.loads(Path(tmp_path, f"dp{r}.json").read_text())
+        for i, g in enumerate(res["grads"]):
+            base = np.arange(len(g), dtype=np.float64)
+            np.testing.assert_allclose(g, (base * 1 + i + base * 2 + i) / 2, rtol=1e-6)
+        assert res["finite_all"] is True
+        assert res["finite_one_bad"] is False     # every rank sees rank 1's NaN
+
+
+# ---------------------------------------------------------------- vocab-parallel head
+
+def _logits(M, V, seed=3):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, V, generator=g) * 3
+    t = torch.randint(0, V, (M,), generator=g)
+    x[0, :] = 1.25             # a row of ties for the top-k
+    return x, t
+
+
+def _head_worker(rank, world, port, out, V, M, k):
+    _init(rank, world, port)
+    from ksdraft_b200.model.head import combine_ce_partials, gather_topk, vocab_shard
+    logits, t = _logits(M, V)
+    start, size = vocab_shard(V, rank, world)
+    shard = logits[:, start:start + size]
+    # this rank's partials, computed on the host as the kernel defines them
+    mx = shard.max(1).values
+    sm = torch.exp(shard - mx[:, None]).sum(1)
+    local = (t >= start) & (t < start + size)
+    tg = torch.where(local, shard[torch.arange(M), (t - start).clamp(0, size - 1)],
+                     torch.zeros(M))
+    _, _, loss_rows = combine_ce_partials(mx, sm, tg, group=dist.group.WORLD)
+
+    def select(vals, kk, offset=0, ids=None):   # host stand-in for the top-k kernel
+        order = np.lexsort((ids.numpy(), -vals.numpy()), axis=1)[:, :kk]
+        return (torch.from_numpy(np.take_along_axis(vals.numpy(), order, 1)),
+                torch.from_numpy(np.take_along_axis(ids.numpy(), order, 1)))
+
+    ids = torch.arange(start, start + size).expand(M, size)
+    lv, li = select(shard, k, ids=ids)
+    gv, gi = gather_topk(lv, li, k, group=dist.group.WORLD, select=select)
+    Path(out, f"head{rank}.json").write_text(json.dumps({
+        "loss_rows": loss_rows.tolist(), "topv": gv.tolist(), "topi": gi.tolist(),
+        "shard": [start, size]}))
+    dist.destroy_process_group()
+
+
+def test_vocab_parallel_ce_and_topk_merge(tmp_path):
+    V, M, k = 1000, 6, 5           # 8 groups of 128 (last partial): shards 512 + 488
+    assert _run(_head_worker, 2, tmp_path, V, M, k) == [0, 0]
+    logits, t = _logits(M, V)
+    l64 = logits.double()
+    full = torch.logsumexp(l64, 1) - l64[torch.arange(M), t]
+    order = np.lexsort((np.broadcast_to(np.arange(V), (M, V)), -logits.numpy()), axis=1)[:, :k]
+    shards = []
+    for r in range(2):
+        res = json.loads(Path(tmp_path, f"head{r}.json").read_text())
+        np.testing.assert_allclose(res["loss_rows"], full.numpy(), rtol=1e-5, atol=1e-5)
+        np.testing.assert_array_equal(np.array(res["topi"]), order)
+        np.testing.assert_allclose(res["topv"], np.take_along_axis(logits.numpy(), order, 1))
+        shards.append(res["shard"])
+    assert shards == [[0, 512], [512, 488]]
+
+
+def test_vocab_shard_boundaries():
+    from ksdraft_b200.model.head import vocab_shard
+    for V in (150144, 1000, 128, 300):
+        for world in (1, 2, 3, 4, 8):
+            parts = [vocab_shard(V, r, world) for r in range(world)]
+            assert parts[0][0] == 0
+            assert sum(s for _, s in parts) == V
+            for (a, s), (b, _) in zip(parts, parts[1:]):
+                assert a + s == b and a % 128 == 0 and b % 128 == 0
+    assert vocab_shard(150144, 1, 2) == (75008, 75136)   # 586 + 587 groups
+
+
+# ---------------------------------------------------------------- failure detection
+
+def _fail_worker(rank, world, port, out):
+    _init(rank, world, port, timeout_s=5)
+    if rank == 1:
+        os._exit(3)                  # dies between steps, before the collective
+    t0 = time.time()
+    err = None
+    try:
+        x = torch.ones(4)
+        dist.all_reduce(x)
+    except Exception as e:           # noqa: BLE001 - any error ends the wait
+        err = type(e).__name__
+    Path(out, "fail0.json").write_text(json.dumps({"error": err, "seconds": time.time() - t0}))
+    os._exit(0)
+
+
+def test_peer_death_ends_collective_with_error(tmp_path):
+    codes = _run(_fail_worker, 2, tmp_path)
+    assert codes[1] == 3
+    res = json.loads(Path(tmp_path, "fail0.json").read_text())
+    assert res["error"] is not None                 # detected, not hung
+    assert res["seconds"] < 60
