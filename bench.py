@@ -123,16 +123,56 @@ def run_reference(args) -> None:
 # ---------------------------------------------------------------- GPU side
 
 class ClockSampler:
+    """SM clock and clock-event reasons during the timed region, read every 5 ms
+    through NVML on a background thread (nvidia-smi -lms as the fallback).
+    Only reads: no clock, power or mode of the GPU is changed."""
+
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
+        self.samples = []       # (sm_mhz, reason bits)
+        self.max_mhz = None
+        self.stop = None
+        self.thread = None
         self.proc = None
         self.path = None
 
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.index)
+        try:
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:  # noqa: BLE001 - fall back to the visible index
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
     def __enter__(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.stop = threading.Event()
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                             int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                    except Exception:  # noqa: BLE001
+                        break
+                    self.stop.wait(0.005)
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # noqa: BLE001 - no NVML: nvidia-smi
+            pass
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -145,6 +185,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -153,13 +196,22 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        if self.thread is not None:
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+            sm = [s for s, _ in self.samples]
+            loaded = [s for s in sm if s > 500] or sm
+            reasons = sorted({name for _, bits in self.samples for name, bit in self.REASONS
+                              if bits & bit})
+            return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
         rows = []
         try:
             for line in open(self.path):
                 parts = [p.strip() for p in line.split(",")]
                 if len(parts) >= 9:
                     rows.append(parts)
-        except OSError:
+        except (OSError, TypeError):
             pass
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
@@ -173,7 +225,8 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(loaded) if loaded else None,
                 "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit()
-                else None, "reasons": sorted(reasons), "samples": len(rows)}
+                else None, "reasons": sorted(reasons), "samples": len(rows),
+                "source": "nvidia-smi"}
 
 
 def run_ours(args) -> None:

@@ -108,6 +108,7 @@ int ksd8_quantize_cols(const void* x, int x_dtype, const void* x_scales, int x_g
   if (!(valid_float_dtype(x_dtype) || x_dtype == KSD8_I8)) return KSD8_ERR_DTYPE;
   if (group != 128) return KSD8_ERR_UNSUPPORTED;
   if (x_dtype == KSD8_I8 && (!x_scales || x_group <= 0)) return KSD8_ERR_ARG;
+  if (x_dtype == KSD8_I8 && (x_group % 128) != 0) return KSD8_ERR_UNSUPPORTED;
   if (rows < 0 || cols < 0 || ldx < cols || ldct < rows) return KSD8_ERR_SHAPE;
   if ((rows > 0 && cols > 0) && (!x || !codes_t || !scales_t)) return KSD8_ERR_ARG;
   return finish(ksd8_quantize_cols_launch(x, x_dtype, x_scales, x_group, rows, cols, ldx, flags,

@@ -780,24 +780,44 @@ __global__ void __launch_bounds__(VJP_THREADS, 1)
   }
 }
 
-__global__ void ks3_vjp_reduce_kernel(const float* partials, int64_t n_tiles, int64_t charts,
-                                      const float* raw_scale, const float* raw_shift,
-                                      __half* dcoeff, __half* dscale, __half* dshift,
-                                      int* status) {
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= charts) return;
+// One thread per (chart, term): 32 charts x 8 terms per CTA.  Each sums its
+// term over the token tiles in tile order (loads unrolled so several are in
+// flight); the 8 sums of a chart then meet in shared memory for the fp16
+// rounding and the STE factors.
+constexpr int VRED_CHARTS = 32;
+__global__ void __launch_bounds__(VRED_CHARTS * 8)
+    ks3_vjp_reduce_kernel(const float* partials, int64_t n_tiles, int64_t charts,
+                          const float* raw_scale, const float* raw_shift, __half* dcoeff,
+                          __half* dscale, __half* dshift, int* status) {
+  __shared__ float sums[8][VRED_CHARTS];
+  const int lc = threadIdx.x % VRED_CHARTS, k = threadIdx.x / VRED_CHARTS;
+  const int64_t c = (int64_t)blockIdx.x * VRED_CHARTS + lc;
+  float sk = 0.f;
+  if (c < charts) {
+    const float* p = partials + (int64_t)k * charts + c;
+    const int64_t stride = 8 * charts;
+    int64_t t = 0;
+    for (; t + 8 <= n_tiles; t += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = p[(t + u) * stride];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sk += v[u];
+    }
+    for (; t < n_tiles; ++t) sk += p[t * stride];
+  }
+  sums[k][lc] = sk;
+  __syncthreads();
+  if (k != 0 || c >= charts) return;
   float s[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) s[k] = 0.f;
-  for (int64_t t = 0; t < n_tiles; ++t)
-#pragma unroll
-    for (int k = 0; k < 8; ++k) s[k] += partials[(t * 8 + k) * charts + c];
+  for (int q = 0; q < 8; ++q) s[q] = sums[q][lc];
   bool bad = false;
 #pragma unroll
-  for (int k = 0; k < 6; ++k) {
-    const __half h = __float2half_rn(s[k]);
+  for (int q = 0; q < 6; ++q) {
+    const __half h = __float2half_rn(s[q]);
     bad |= __hisinf(h) || __hisnan(h);
-    dcoeff[c * 6 + k] = h;
+    dcoeff[c * 6 + q] = h;
   }
   const float sig = 1.f / (1.f + expf(-raw_scale[c]));
   const float th = tanhf(raw_shift[c]);
@@ -945,7 +965,8 @@ int ksd8_ks3_vjp_reduce_launch(const float* partials, int64_t n_tiles, int64_t c
                                const float* raw_scale, const float* raw_shift, void* dcoeff16,
                                void* dscale16, void* dshift16, int* status, cudaStream_t stream) {
   if (charts == 0) return KSD8_OK;
-  ks3_vjp_reduce_kernel<<<(unsigned)((charts + 127) / 128), 128, 0, stream>>>(
+  ks3_vjp_reduce_kernel<<<(unsigned)((charts + VRED_CHARTS - 1) / VRED_CHARTS), VRED_CHARTS * 8,
+                          0, stream>>>(
       partials, n_tiles, charts, raw_scale, raw_shift, reinterpret_cast<__half*>(dcoeff16),
       reinterpret_cast<__half*>(dscale16), reinterpret_cast<__half*>(dshift16), status);
   return KSD8_OK;

@@ -30,6 +30,8 @@ template <>
 __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
   return __bfloat162float(v);
 }
+template <>
+__device__ __forceinline__ float to_f32<int8_t>(int8_t v) { return (float)v; }
 
 __device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
 
@@ -68,65 +70,108 @@ struct QRowArgs {
   __half* scales;
 };
 
+// Dithered code, the reference formula rint(RN(RN(x / scale) + noise))
+// clamped to +-127 (ksdraft/train/stages.py:42-48), IEEE division only near a
+// rounding boundary: y = x * rcp is within 2^-14 of RN(x / scale) for |y| <
+// 200 (see gs_code_fast), so t = RN(y + noise) is within 2^-13 of the
+// reference's t and rounds the same unless it lies within 2^-13 of a
+// half-integer.
+static __device__ __noinline__ int gs_code_dither_slow(float x, float scale, float noise) {
+  const float t = __fadd_rn(__fdiv_rn(x, scale), noise);
+  return (int)fminf(fmaxf(rintf(t), -127.f), 127.f);
+}
+
+__device__ __forceinline__ int gs_code_dither_fast(float x, float scale, float rcp, float noise) {
+  const float y = __fmul_rn(x, rcp);
+  const float t = __fadd_rn(y, noise);
+  const float r = rintf(t);
+  if (fabsf(y) < 200.f && fabsf(__fsub_rn(t, r)) < 0.4998779296875f)
+    return (int)fminf(fmaxf(r, -127.f), 127.f);
+  return gs_code_dither_slow(x, scale, noise);
+}
+
+constexpr int QR_U = 1;  // groups of one row per warp iteration (occupancy keeps loads in flight)
+
+// One warp per QR_U consecutive 128-wide groups of a row per iteration: the
+// QR_U loads are in flight together and the QR_U warp reductions interleave.
 template <typename T>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(QRowArgs a) {
   const int64_t groups = (a.k + 127) / 128;
   const int64_t kp = groups * 128;
-  const int64_t total = a.rows * groups;
+  const int64_t ublocks = (groups + QR_U - 1) / QR_U;
+  const int64_t total = a.rows * ublocks;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total;
        w += warps) {
-    const int64_t r = w / groups;
-    const int64_t g = w - r * groups;
-    const int64_t c = g * 128 + lane * 4;
+    const int64_t r = w / ublocks;
+    const int64_t g0 = (w - r * ublocks) * QR_U;
     const T* row = reinterpret_cast<const T*>(a.x) + r * a.ldx;
-    float v[4];
-    load4<T>(row, c, a.k, v);
-    if (a.flags & KSD8_Q_ROUND_F16) {
+    float v[QR_U][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = round_f16(v[i]);
-    }
-    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    m = warp_max(m);
-    __half sh;
-    const float scale = gs_scale_fast(m, &sh);
-    int q[4];
-    if (a.flags & KSD8_Q_DITHER) {
-      // one Philox block serves the 4 consecutive elements when they share it
-      const uint64_t base = a.offset + (uint64_t)r * kp + c;
-      float u[4];
-      if ((base & 3) == 0) {
-        uint32_t ctr[4] = {(uint32_t)(base >> 2), (uint32_t)(base >> 34), 0u, 0u};
-        philox4x32_10(ctr, (uint32_t)a.seed, (uint32_t)(a.seed >> 32));
-#pragma unroll
-        for (int i = 0; i < 4; ++i) u[i] = (float)(ctr[i] >> 8) * 5.9604644775390625e-08f;
+    for (int u = 0; u < QR_U; ++u) {
+      const int64_t c = (g0 + u) * 128 + lane * 4;
+      if (g0 + u < groups) {
+        load4<T>(row, c, a.k, v[u]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) u[i] = philox_uniform(a.seed, base + i);
+        for (int i = 0; i < 4; ++i) v[u][i] = 0.f;
       }
+    }
+    float m[QR_U];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float noise = __fmul_rn(__fsub_rn(u[i], 0.5f), a.dither2);
-        float t = __fadd_rn(__fdiv_rn(v[i], scale), noise);
-        t = fminf(fmaxf(rintf(t), -127.f), 127.f);
-        q[i] = (int)t;
+    for (int u = 0; u < QR_U; ++u) {
+      if (a.flags & KSD8_Q_ROUND_F16) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[u][i] = round_f16(v[u][i]);
       }
-    } else {
+      m[u] = fmaxf(fmaxf(fabsf(v[u][0]), fabsf(v[u][1])), fmaxf(fabsf(v[u][2]), fabsf(v[u][3])));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < QR_U; ++u) m[u] = fmaxf(m[u], __shfl_xor_sync(0xffffffffu, m[u], o));
+#pragma unroll
+    for (int u = 0; u < QR_U; ++u) {
+      const int64_t g = g0 + u;
+      if (g >= groups) break;
+      const int64_t c = g * 128 + lane * 4;
+      __half sh;
+      const float scale = gs_scale_fast(m[u], &sh);
       const float rcp = rcp_approx(scale);
+      int q[4];
+      if (a.flags & KSD8_Q_DITHER) {
+        // one Philox block serves the 4 consecutive elements when they share it
+        const uint64_t base = a.offset + (uint64_t)r * kp + c;
+        float uu[4];
+        if ((base & 3) == 0) {
+          uint32_t ctr[4] = {(uint32_t)(base >> 2), (uint32_t)(base >> 34), 0u, 0u};
+          philox4x32_10(ctr, (uint32_t)a.seed, (uint32_t)(a.seed >> 32));
 #pragma unroll
-      for (int i = 0; i < 4; ++i) q[i] = gs_code_fast(v[i], scale, rcp);
-    }
-    int8_t* out = a.codes + r * a.ldc + c;
-    if (c + 4 <= a.k && (reinterpret_cast<uintptr_t>(out) & 3) == 0) {
-      char4 p = make_char4((char)q[0], (char)q[1], (char)q[2], (char)q[3]);
-      *reinterpret_cast<char4*>(out) = p;
-    } else {
+          for (int i = 0; i < 4; ++i) uu[i] = (float)(ctr[i] >> 8) * 5.9604644775390625e-08f;
+        } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (c + i < a.k) out[i] = (int8_t)q[i];
+          for (int i = 0; i < 4; ++i) uu[i] = philox_uniform(a.seed, base + i);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float noise = __fmul_rn(__fsub_rn(uu[i], 0.5f), a.dither2);
+          q[i] = gs_code_dither_fast(v[u][i], scale, rcp, noise);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] = gs_code_fast(v[u][i], scale, rcp);
+      }
+      int8_t* out = a.codes + r * a.ldc + c;
+      if (c + 4 <= a.k && (reinterpret_cast<uintptr_t>(out) & 3) == 0) {
+        *reinterpret_cast<char4*>(out) = make_char4((char)q[0], (char)q[1], (char)q[2], (char)q[3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (c + i < a.k) out[i] = (int8_t)q[i];
+      }
+      if (lane == 0) a.scales[r * groups + g] = sh;
     }
-    if (lane == 0) a.scales[r * groups + g] = sh;
   }
 }
 
@@ -142,85 +187,78 @@ struct QColArgs {
 
 constexpr int QC_TR = 128;  // rows per tile (one output group along the rows)
 constexpr int QC_TC = 128;  // columns per tile
-constexpr int QC_LD = QC_TC + 1;
-constexpr int QC_SMEM = QC_TR * QC_LD * 4;
 
-// 16-byte vector of input elements -> floats (dequantised for int8 codes).
 template <typename T>
-struct Vec16 {
-  static constexpr int N = 16 / sizeof(T);
+struct QColTile {
+  static constexpr int ROW_BYTES = QC_TC * (int)sizeof(T) + 16;  // padded source row
+  static constexpr int SMEM = QC_TR * ROW_BYTES + QC_TR * 4;     // + per-row dequant scale
 };
 
-// One CTA per 128 x 128 tile: coalesced 16-byte row loads into shared memory
-// (as fp32), then each thread quantises half a column (see below).
+template <typename T>
+__device__ __forceinline__ float qcol_val(const uint8_t* tile, int rr, int cc) {
+  return to_f32<T>(*reinterpret_cast<const T*>(tile + rr * QColTile<T>::ROW_BYTES +
+                                               cc * (int)sizeof(T)));
+}
+
+// One CTA per 128 x 128 tile.  The tile is staged in shared memory in its
+// source type (int8 codes: 18 KB, so up to 8 CTAs per SM keep loads in
+// flight) by coalesced 16-byte row loads; int8 codes keep one dequantisation
+// scale per row (with GS128 input scales a 128-column tile lies in one input
+// group), applied when the values are read back.
 template <typename T, bool DEQUANT>
 __global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
-  extern __shared__ float tile[];  // [QC_TR][QC_LD]
+  extern __shared__ __align__(16) uint8_t qsm[];
+  using TL = QColTile<T>;
+  float* rscale = reinterpret_cast<float*>(qsm + QC_TR * TL::ROW_BYTES);
   const int64_t r0 = (int64_t)blockIdx.y * QC_TR;
   const int64_t c0 = (int64_t)blockIdx.x * QC_TC;
   const int tid = threadIdx.x;
-  constexpr int VN = Vec16<T>::N;           // elements per 16-byte vector
+  constexpr int VN = 16 / (int)sizeof(T);   // elements per 16-byte vector
   constexpr int VPR = QC_TC / VN;           // vectors per tile row
   const int64_t xs_groups = DEQUANT ? (a.cols + a.x_group - 1) / a.x_group : 0;
   const bool vec_ok = (a.ldx * (int64_t)sizeof(T)) % 16 == 0 &&
                       (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && c0 + QC_TC <= a.cols;
+  if constexpr (DEQUANT) {
+    for (int rr = tid; rr < QC_TR; rr += 256) {
+      const int64_t r = r0 + rr;
+      rscale[rr] = r < a.rows ? __half2float(a.x_scales[r * xs_groups + c0 / a.x_group]) : 0.f;
+    }
+  }
   for (int idx = tid; idx < QC_TR * VPR; idx += 256) {
     const int rr = idx / VPR, vv = idx % VPR;
     const int64_t r = r0 + rr;
     const int64_t c = c0 + vv * VN;
-    float v[VN];
+    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
     if (r < a.rows) {
       const T* row = reinterpret_cast<const T*>(a.x) + r * a.ldx;
-      float sc = 1.f;
-      if constexpr (DEQUANT) sc = __half2float(a.x_scales[r * xs_groups + c / a.x_group]);
       if (vec_ok) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(row + c);
-        const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-        for (int i = 0; i < VN; ++i) {
-          if constexpr (DEQUANT) v[i] = (float)e[i] * sc;
-          else v[i] = to_f32<T>(e[i]);
-        }
+        raw = __ldcs(reinterpret_cast<const uint4*>(row + c));
       } else {
+        T* e = reinterpret_cast<T*>(&raw);
 #pragma unroll
-        for (int i = 0; i < VN; ++i) {
-          const int64_t ci = c + i;
-          if (ci < a.cols) {
-            if constexpr (DEQUANT) {
-              const float s2 = __half2float(a.x_scales[r * xs_groups + ci / a.x_group]);
-              v[i] = (float)row[ci] * s2;
-            } else {
-              v[i] = to_f32<T>(row[ci]);
-            }
-          } else {
-            v[i] = 0.f;
-          }
-        }
+        for (int i = 0; i < VN; ++i) e[i] = (c + i < a.cols) ? row[c + i] : T(0);
       }
-      if constexpr (!DEQUANT) {
-        if (a.flags & KSD8_Q_ROUND_F16) {
-#pragma unroll
-          for (int i = 0; i < VN; ++i) v[i] = round_f16(v[i]);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < VN; ++i) v[i] = 0.f;
     }
-#pragma unroll
-    for (int i = 0; i < VN; ++i) tile[rr * QC_LD + vv * VN + i] = v[i];
+    *reinterpret_cast<uint4*>(qsm + rr * TL::ROW_BYTES + vv * 16) = raw;
   }
-  // Thread t owns column t % 128, rows (t / 128) * 64 .. +64: a per-thread
-  // amax (conflict-free: consecutive lanes read consecutive columns), one
-  // exchange for the other half, then 64 codes written as 16-byte vectors of
+  // Column phase: thread t owns column t % 128 and rows (t / 128) * 64 .. +64:
+  // per-thread amax (consecutive lanes read consecutive columns), one
+  // exchange for the other half, and 64 codes written as 16-byte vectors of
   // the x^T row.
   __shared__ float s_amax[2][QC_TC];
   __syncthreads();
   const int cc = tid & (QC_TC - 1), half = tid >> 7;
   const int64_t c = c0 + cc;
+  const bool rf16 = !DEQUANT && (a.flags & KSD8_Q_ROUND_F16);
+  auto val = [&](int rr) -> float {
+    float v = qcol_val<T>(qsm, rr, cc);
+    if constexpr (DEQUANT) v = v * rscale[rr];
+    else if (rf16) v = round_f16(v);
+    return v;
+  };
   float m = 0.f;
 #pragma unroll 16
-  for (int i = 0; i < 64; ++i) m = fmaxf(m, fabsf(tile[(half * 64 + i) * QC_LD + cc]));
+  for (int i = 0; i < 64; ++i) m = fmaxf(m, fabsf(val(half * 64 + i)));
   s_amax[half][cc] = m;
   __syncthreads();
   if (c >= a.cols) return;
@@ -240,8 +278,7 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
         uint32_t word = 0;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-          const int rr = half * 64 + v * 16 + j * 4 + b;
-          const int q = gs_code_fast(tile[rr * QC_LD + cc], scale, rcp);
+          const int q = gs_code_fast(val(half * 64 + v * 16 + j * 4 + b), scale, rcp);
           word |= (uint32_t)(q & 0xFF) << (8 * b);
         }
         w[j] = word;
@@ -250,8 +287,7 @@ __global__ void __launch_bounds__(256) quantize_cols_kernel(QColArgs a) {
     }
   } else {
     for (int i = 0; i < 64; ++i)
-      if (rb + i < a.rows) out[i] = (int8_t)gs_code_fast(tile[(half * 64 + i) * QC_LD + cc],
-                                                         scale, rcp);
+      if (rb + i < a.rows) out[i] = (int8_t)gs_code_fast(val(half * 64 + i), scale, rcp);
   }
   if (half == 0) a.scales_t[c * rgroups + blockIdx.y] = sh;
 }
@@ -280,7 +316,7 @@ int ksd8_quantize_rows_launch(const void* x, int x_dtype, int64_t rows, int64_t 
   a.x = x; a.rows = rows; a.k = k; a.ldx = ldx; a.ldc = ldc; a.group = group; a.flags = flags;
   a.dither2 = 2.0f * dither; a.seed = seed; a.offset = offset; a.codes = codes;
   a.scales = reinterpret_cast<__half*>(scales);
-  const int64_t work = rows * ((k + 127) / 128);
+  const int64_t work = rows * (((k + 127) / 128 + QR_U - 1) / QR_U);
   if (work == 0) return KSD8_OK;
   const int blocks = grid_for(work, 8);
   switch (x_dtype) {
@@ -306,22 +342,30 @@ int ksd8_quantize_cols_launch(const void* x, int x_dtype, const void* x_scales, 
   cudaGetDevice(&dev);
   if (!(attr_dev_mask & (1u << dev))) {
     cudaFuncSetAttribute(quantize_cols_kernel<float, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, QC_SMEM);
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QColTile<float>::SMEM);
     cudaFuncSetAttribute(quantize_cols_kernel<__half, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, QC_SMEM);
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QColTile<__half>::SMEM);
     cudaFuncSetAttribute(quantize_cols_kernel<__nv_bfloat16, false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, QC_SMEM);
+                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         QColTile<__nv_bfloat16>::SMEM);
     cudaFuncSetAttribute(quantize_cols_kernel<int8_t, true>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, QC_SMEM);
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, QColTile<int8_t>::SMEM);
     attr_dev_mask |= (1u << dev);
   }
   switch (x_dtype) {
-    case KSD8_F32: quantize_cols_kernel<float, false><<<grid, 256, QC_SMEM, stream>>>(a); break;
-    case KSD8_F16: quantize_cols_kernel<__half, false><<<grid, 256, QC_SMEM, stream>>>(a); break;
-    case KSD8_BF16:
-      quantize_cols_kernel<__nv_bfloat16, false><<<grid, 256, QC_SMEM, stream>>>(a);
+    case KSD8_F32:
+      quantize_cols_kernel<float, false><<<grid, 256, QColTile<float>::SMEM, stream>>>(a);
       break;
-    case KSD8_I8: quantize_cols_kernel<int8_t, true><<<grid, 256, QC_SMEM, stream>>>(a); break;
+    case KSD8_F16:
+      quantize_cols_kernel<__half, false><<<grid, 256, QColTile<__half>::SMEM, stream>>>(a);
+      break;
+    case KSD8_BF16:
+      quantize_cols_kernel<__nv_bfloat16, false>
+          <<<grid, 256, QColTile<__nv_bfloat16>::SMEM, stream>>>(a);
+      break;
+    case KSD8_I8:
+      quantize_cols_kernel<int8_t, true><<<grid, 256, QColTile<int8_t>::SMEM, stream>>>(a);
+      break;
     default: return KSD8_ERR_DTYPE;
   }
   return KSD8_OK;

@@ -286,8 +286,15 @@ def ks3_train_forward(cell, inputs):
     return y.reshape(*inputs.shape[:-1], cell.out_features), (xq, xs, hq, hs, coords)
 
 
+def _wgrad_into(out, aq, as_, bq, bs, flag):
+    """fp32 wgrad with the FP16 handoff rounding, and its predicated fp32
+    re-run when any element overflowed fp16 (decided on the device)."""
+    gemm_out(aq, as_, bq, bs, out=out, round_f16=True, status=flag)
+    gemm_out(aq, as_, bq, bs, out=out, status=flag, if_status=True)
+
+
 def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_handoff=True,
-                 grads_into=None):
+                 grads_into=None, on_grad=None):
     """Backward of ks3_int8.py:341-429.
 
     Returns (dx, ddown, dup, dcoeff, dscale, dshift, None) as the reference's
@@ -296,7 +303,11 @@ def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_hand
     gradients are instead written there, as the values the FP16 handoff
     (ks3_int8.py:75-84) gives after the cast to the fp32 masters, and only dx
     is returned.  That path decides the overflow fallback on the device (a
-    predicated fp32 re-run of the wgrad GEMM), so it never waits for the GPU."""
+    predicated fp32 re-run of the wgrad GEMM), so it never waits for the GPU.
+    There `on_grad(names)` is called as soon as those gradients are written
+    (the data-parallel step starts their all-reduce there); the up-projection
+    wgrad, which needs only g and h, comes first so that its reduction
+    overlaps the rest of the backward."""
     M, C = coords.shape
     dev = coords.device
     g = grad_out.reshape(-1, cell.out_features)
@@ -305,6 +316,17 @@ def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_hand
     lib = _lib.lib()
     stream = _lib.stream_ptr(dev)
     flags = torch.zeros(3, dtype=torch.int32, device=dev)
+    notify = on_grad if on_grad is not None else (lambda names: None)
+
+    gT_q = None
+    if grads_into is not None:
+        # dup = q(g^T) @ q(h^T)^T first (ks3_int8.py:421-424)
+        gT_q, gT_s = quantize_cols(g, round_f16=True)
+        hT_q, hT_s = quantize_cols(hq, x_scales=hs, x_group=cell.group)
+        if M % GROUP_SIZE:
+            gT_q, hT_q = _pad_k(gT_q), _pad_k(hT_q)
+        _wgrad_into(grads_into["up"], gT_q, gT_s, hT_q, hT_s, flags[2:3])
+        notify(("up",))
 
     # value = fp16(q(g16) @ q(dequant(up)^T)^T)   (ks3_int8.py:345-352)
     gq = torch.empty(M, cell.out_features, dtype=torch.int8, device=dev)
@@ -336,6 +358,21 @@ def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_hand
                                  raw_shift.data_ptr(), dcoeff.data_ptr(), dscale.data_ptr(),
                                  dshift.data_ptr(), flags[0:1].data_ptr(), stream)
     _lib.check(rc, "ks3_vjp_reduce")
+    if grads_into is not None:
+        # dcoeff / dscale / dshift are fp16 already in the reference (:387-394):
+        # the handoff hands them over unchanged, the masters see float(fp16)
+        grads_into["coefficients"].copy_(dcoeff.view_as(grads_into["coefficients"]))
+        grads_into["raw_scale"].copy_(dscale.view_as(grads_into["raw_scale"]))
+        grads_into["raw_shift"].copy_(dshift.view_as(grads_into["raw_shift"]))
+        notify(("coefficients", "raw_scale", "raw_shift"))
+
+    # ddown = q(dc^T) @ q(x^T)^T, quantised along tokens (ks3_int8.py:417-420)
+    xT_q, xT_s = quantize_cols(xq, x_scales=xs, x_group=cell.group)
+    if M % GROUP_SIZE:  # the wgrads contract over tokens: zero-pad K (gemm.py:71-73)
+        dctq, xT_q = _pad_k(dctq), _pad_k(xT_q)
+    if grads_into is not None:
+        _wgrad_into(grads_into["down"], dctq, dcts, xT_q, xT_s, flags[1:2])
+        notify(("down",))
 
     # dx = q(dc) @ q(dequant(down)^T)^T   (ks3_int8.py:410-412)
     downT_q, downT_s = quantize_cols(cell.down_codes, x_scales=cell.down_scales,
@@ -343,25 +380,12 @@ def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_hand
     dx = gemm_out(dcq, dcs, downT_q, downT_s, out_dtype=grad_out.dtype
                   if grad_out.dtype in (torch.float32, torch.bfloat16, torch.float16)
                   else torch.float32)
-    # wgrads, quantised along tokens (ks3_int8.py:417-424)
-    xT_q, xT_s = quantize_cols(xq, x_scales=xs, x_group=cell.group)
+    if grads_into is not None:
+        return dx.reshape(input_shape).to(grad_out.dtype)
     gT_q, gT_s = quantize_cols(g, round_f16=True)
     hT_q, hT_s = quantize_cols(hq, x_scales=hs, x_group=cell.group)
-    if M % GROUP_SIZE:  # the wgrads contract over tokens: zero-pad K (gemm.py:71-73)
-        dctq, xT_q, gT_q, hT_q = (_pad_k(t) for t in (dctq, xT_q, gT_q, hT_q))
-    if grads_into is not None:
-        dx = dx.reshape(input_shape).to(grad_out.dtype)
-        for name, (aq, as_, bq, bs), flag in (("down", (dctq, dcts, xT_q, xT_s), flags[1:2]),
-                                              ("up", (gT_q, gT_s, hT_q, hT_s), flags[2:3])):
-            out = grads_into[name]
-            gemm_out(aq, as_, bq, bs, out=out, round_f16=True, status=flag)
-            gemm_out(aq, as_, bq, bs, out=out, status=flag, if_status=True)  # fp32 fallback
-        # dcoeff / dscale / dshift are fp16 already in the reference (:387-394):
-        # the handoff hands them over unchanged, the masters see float(fp16)
-        grads_into["coefficients"].copy_(dcoeff.view_as(grads_into["coefficients"]))
-        grads_into["raw_scale"].copy_(dscale.view_as(grads_into["raw_scale"]))
-        grads_into["raw_shift"].copy_(dshift.view_as(grads_into["raw_shift"]))
-        return dx
+    if M % GROUP_SIZE:
+        gT_q, hT_q = _pad_k(gT_q), _pad_k(hT_q)
     ddown = gemm_out(dctq, dcts, xT_q, xT_s, out_dtype=FP16, status=flags[1:2])
     dup = gemm_out(gT_q, gT_s, hT_q, hT_s, out_dtype=FP16, status=flags[2:3])
 

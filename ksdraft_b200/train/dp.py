@@ -48,6 +48,14 @@ class FlatGrads:
         for p, off in zip(self.params, self.offsets):
             yield p, self.buffer[off:off + p.numel()]
 
+    def span(self, params) -> torch.Tensor:
+        """The contiguous slice of the buffer covering `params` (and the zero
+        padding between them)."""
+        idx = [i for i, p in enumerate(self.params) if any(p is q for q in params)]
+        lo = self.offsets[min(idx)]
+        hi = self.offsets[max(idx)] + self.params[max(idx)].numel()
+        return self.buffer[lo:hi]
+
 
 def allreduce_mean_(buffer: torch.Tensor, group=None) -> None:
     """Average a flat gradient buffer over the ranks of `group` (no-op alone)."""
@@ -58,6 +66,27 @@ def allreduce_mean_(buffer: torch.Tensor, group=None) -> None:
         return
     dist.all_reduce(buffer, op=dist.ReduceOp.SUM, group=group)
     buffer.div_(world)
+
+
+def allreduce_mean_async(t: torch.Tensor, group=None):
+    """Start averaging `t` over the ranks; returns a list of pending works whose
+    wait() completes the mean in place (NCCL averages in the collective, gloo
+    sums and the caller's wait_all divides).  Empty when running alone."""
+    if not dist.is_available() or not dist.is_initialized():
+        return []
+    world = dist.get_world_size(group)
+    if world == 1:
+        return []
+    if dist.get_backend(group) == "nccl":
+        return [(dist.all_reduce(t, op=dist.ReduceOp.AVG, group=group, async_op=True), None)]
+    return [(dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group, async_op=True), (t, world))]
+
+
+def wait_all(pending) -> None:
+    for work, post in pending:
+        work.wait()
+        if post is not None:
+            post[0].div_(post[1])
 
 
 def check_finite_across_ranks(buffer: torch.Tensor, group=None) -> bool:
@@ -109,13 +138,15 @@ def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
 class KS3DataParallelStep:
     """fwd + bwd + gradient all-reduce + AdamW for one trainable KS3Int8Cell."""
 
-    def __init__(self, cell, lr: float = 3e-4):
+    def __init__(self, cell, lr: float = 3e-4, group=None):
         self.cell = cell
         self.params = [cell.master_down, cell.master_up, cell.master_coefficients,
                        cell.master_raw_scale, cell.master_raw_shift]
         self.grads = FlatGrads(self.params)
-        self.grad_views = {name: p.grad for name, p in zip(
-            ("down", "up", "coefficients", "raw_scale", "raw_shift"), self.params)}
+        self.named = dict(zip(("down", "up", "coefficients", "raw_scale", "raw_shift"),
+                              self.params))
+        self.grad_views = {name: p.grad for name, p in self.named.items()}
+        self.group = group
         self.opt = AdamW(self.params, lr=lr)
 
     def __call__(self, x: torch.Tensor, grad_out: torch.Tensor) -> torch.Tensor:
@@ -125,7 +156,13 @@ class KS3DataParallelStep:
         accumulation pass runs and nothing waits for the GPU."""
         from ..kernels.ks3_int8 import ks3_backward, ks3_train_forward
         y, saved = ks3_train_forward(self.cell, x.detach())
-        ks3_backward(self.cell, grad_out, *saved, x.shape, grads_into=self.grad_views)
-        allreduce_mean_(self.grads.buffer)
+        pending = []
+
+        def on_grad(names):   # each gradient's mean over the ranks starts as soon as it exists
+            params = [self.named[n] for n in names]
+            pending.extend(allreduce_mean_async(self.grads.span(params), self.group))
+        ks3_backward(self.cell, grad_out, *saved, x.shape, grads_into=self.grad_views,
+                     on_grad=on_grad)
+        wait_all(pending)
         self.opt.step()
         return y

@@ -54,7 +54,8 @@ def _run(fn, world, tmp_path, *args):
 
 def _dp_worker(rank, world, port, out):
     _init(rank, world, port)
-    from ksdraft_b200.train.dp import FlatGrads, allreduce_mean_, check_finite_across_ranks
+    from ksdraft_b200.train.dp import (FlatGrads, allreduce_mean_, allreduce_mean_async,
+                                       check_finite_across_ranks, wait_all)
     torch.manual_seed(0)
     params = [torch.nn.Parameter(torch.zeros(5, 3)), torch.nn.Parameter(torch.zeros(7))]
     fg = FlatGrads(params)
@@ -62,6 +63,12 @@ def _dp_worker(rank, world, port, out):
         view.copy_(torch.arange(view.numel(), dtype=torch.float32) * (rank + 1) + i)
     allreduce_mean_(fg.buffer)
     res = {"grads": [p.grad.reshape(-1).tolist() for p in params]}
+    # the overlapped form: start the mean of one parameter's span, then wait
+    params[1].grad.fill_(10.0 * (rank + 1))
+    pending = allreduce_mean_async(fg.span([params[1]]), dist.group.WORLD)
+    wait_all(pending)
+    res["span_mean"] = params[1].grad.tolist()
+    res["span_len"] = fg.span(params).numel()
     res["finite_all"] = check_finite_across_ranks(fg.buffer)
     if rank == 1:
         fg.buffer[3] = float("nan")
@@ -77,6 +84,8 @@ def test_dp_allreduce_mean_and_finite_flags(tmp_path):
         for i, g in enumerate(res["grads"]):
             base = np.arange(len(g), dtype=np.float64)
             np.testing.assert_allclose(g, (base * 1 + i + base * 2 + i) / 2, rtol=1e-6)
+        assert res["span_mean"] == [15.0] * 7
+        assert res["span_len"] == 64 + 7          # first param padded to 64, then the second
         assert res["finite_all"] is True
         assert res["finite_one_bad"] is False     # every rank sees rank 1's NaN
 
