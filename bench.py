@@ -349,6 +349,25 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def rosa_ids(B: int, T: int, seed: int = 0, vocab: int = 150144):
+    """Config-3 token ids: Zipf(1.1) over the vocabulary, then repeated spans of
+    length 8-64 copied from earlier positions until 10% of positions are covered."""
+    rng = np.random.default_rng(seed)
+    ranks = np.arange(1, vocab + 1, dtype=np.float64)
+    p = ranks ** -1.1
+    p /= p.sum()
+    ids = rng.choice(vocab, size=(B, T), p=p).astype(np.int64)
+    for b in range(B):
+        covered = 0
+        while covered < T // 10:
+            L = int(rng.integers(8, 65))
+            dst = int(rng.integers(L, T - L))
+            src = int(rng.integers(0, dst - L + 1))
+            ids[b, dst:dst + L] = ids[b, src:src + L]
+            covered += L
+    return ids
+
+
 def run_profile_case(case: str, iters: int) -> None:
     """One kernel of the layer step at its config-2 shape, `iters` launches after
     one warm-up (for ncu captures: small, single-kernel, ends by itself)."""
@@ -402,12 +421,35 @@ def run_profile_case(case: str, iters: int) -> None:
                                              *(o.data_ptr() for o in outs), None,
                                              _lib.stream_ptr(dev))
                 _lib.check(rc, "vjp")
+    elif case == "rosa":
+        # config 3: batch 4 x seq 4096, 512 streams (2048 stream sequences); bits
+        # from Zipf(1.1) ids with repeated spans (length 8-64, 10% of positions)
+        from ksdraft_b200.model.rosa import match_words, pack_bits
+        B, T, S = 4, 4096, 512
+        ids = rosa_ids(B, T, seed=0)
+        idt = torch.from_numpy(ids).to(dev)
+        salt = torch.arange(S, device=dev, dtype=torch.int64)
+        bits = []
+        for tag in (1, 2, 3):  # q, k, v: stand-ins for sign(proj(E[ids])) per stream
+            h = (idt[:, :, None] * 0x9E3779B1 + salt[None, None, :] * 0x85EBCA77 + tag * 0xC2B2AE3D)
+            h = (h ^ (h >> 15)) * 0x2C1B3C6D
+            bits.append(((h >> 17) & 1).to(torch.int8).contiguous())   # (B, T, S)
+        words = [pack_bits(b, B, T, S, T * S, S, 1) for b in bits]
+        out = torch.empty(B, T, S, dtype=torch.float32, device=dev)
+        fn = lambda: match_words(*words, B, S, T, 62, out=out,  # noqa: E731
+                                 strides=(T * S, S, 1))
     else:
         raise SystemExit(f"unknown profile case {case}")
-    for _ in range(iters + 1):
-        fn()
+    fn()
     torch.cuda.synchronize()
-    print(f"profile case {case}: {iters + 1} launches done")
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(iters):
+        fn()
+    ev1.record()
+    torch.cuda.synchronize()
+    print(f"profile case {case}: {iters + 1} launches done, "
+          f"{ev0.elapsed_time(ev1) / max(iters, 1):.4f} ms per launch (CUDA events)")
 
 
 def main() -> None:

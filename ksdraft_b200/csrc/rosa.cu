@@ -151,6 +151,120 @@ __global__ void __launch_bounds__(512) rosa_match_kernel(MatchArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- prefix-table matcher
+//
+// Same result as rosa_match_kernel in O(1) expected work per position.  One
+// warp per stream walks t = 0 .. T-1; before the query at t it inserts key
+// position j = t - 1 into 12 tables: level L maps the top L bits of Wk(j) to
+// the latest j + 1 with j >= L - 1 (so the padding bits before position 0 never
+// count).  The query reads the 12 levels in parallel (lane L - 1 reads level
+// L); the highest level that hits is the match length and its entry the latest
+// endpoint: a key with a longer effective match would sit in the next level.
+// When level 12 hits, the keys sharing those 12 bits are walked newest first
+// through per-position links for the exact length (up to the cap); the walk
+// stops at the first key reaching min(max_len, t).
+constexpr int RP_LEVELS = 12;
+constexpr int RP_TBL = 1 << (RP_LEVELS + 1);   // levels 1..12 at offsets 2^L - 2 (8190 used)
+constexpr int RP_WARPS = 8;                    // streams per CTA (fewer when T is long)
+constexpr int RP_TMAX = 8192;                  // links are uint16 positions + 1
+
+__device__ __forceinline__ int rp_off(int L) { return (1 << L) - 2; }
+
+// W(t) from words held in shared memory.
+__device__ __forceinline__ uint64_t window_sm(const uint64_t* w, int64_t t) {
+  const int64_t wi = t >> 6;
+  const int sh = (int)(t & 63) + 1;
+  const uint64_t hi = w[wi];
+  const uint64_t lo = wi > 0 ? w[wi - 1] : 0ull;
+  return sh == 64 ? hi : ((lo >> sh) | (hi << (64 - sh)));
+}
+
+// Per-warp shared memory: level tables (RP_TBL uint16), chain links (T
+// uint16), then the stream's q, k and v bit words (3 x ceil(T/64) uint64).
+__global__ void __launch_bounds__(RP_WARPS * 32) rosa_match_prefix_kernel(MatchArgs a,
+                                                                           int stride) {
+  extern __shared__ __align__(16) uint8_t rsm_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t stream = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (stream >= a.batch * a.streams) return;  // the whole warp: no CTA barrier below
+  const int64_t T = a.t_len;
+  const int64_t nw = (T + 63) / 64;
+  uint8_t* base = rsm_raw + (size_t)warp * stride;
+  uint16_t* tbl = reinterpret_cast<uint16_t*>(base);
+  uint16_t* prev = tbl + RP_TBL;
+  uint64_t* sq = reinterpret_cast<uint64_t*>(base + (((size_t)RP_TBL + T) * 2 + 15) / 16 * 16);
+  uint64_t* sk = sq + nw;
+  uint64_t* sv = sk + nw;
+  for (int i = lane; i < RP_TBL / 8; i += 32) reinterpret_cast<uint4*>(tbl)[i] = make_uint4(0, 0, 0, 0);
+  for (int64_t i = lane; i < nw; i += 32) {
+    sq[i] = a.qw[stream * nw + i];
+    sk[i] = a.kw[stream * nw + i];
+    sv[i] = a.vw[stream * nw + i];
+  }
+  __syncwarp();
+  const int64_t b = stream / a.streams, s = stream % a.streams;
+  const float pay = a.payload ? a.payload[s] : 1.f;
+  const int L = lane + 1;               // this lane's level (lanes 0..11)
+  const int off = lane < RP_LEVELS ? rp_off(L) : 0;
+  for (int64_t t = 0; t < T; ++t) {
+    // insert key position j = t - 1 into this lane's level; the query below
+    // reads the same level from the same lane, so no barrier is needed
+    if (t >= 1 && lane < RP_LEVELS && t >= L) {
+      const int64_t j = t - 1;
+      const int idx = off + (int)(window_sm(sk, j) >> (64 - L));
+      if (L == RP_LEVELS) prev[j] = tbl[idx];
+      tbl[idx] = (uint16_t)t;             // j + 1
+    }
+    const uint64_t wq = window_sm(sq, t);
+    const int cap = (int)min((int64_t)a.max_len, t);
+    uint32_t hj = 0;
+    if (lane < RP_LEVELS && L <= cap) hj = tbl[off + (int)(wq >> (64 - L))];
+    const unsigned mask = __ballot_sync(0xffffffffu, hj != 0);
+    int best = 0;
+    int64_t bestj = -1;
+    if (mask) {
+      const int lh = 32 - __clz((int)mask);
+      const uint32_t head = __shfl_sync(0xffffffffu, hj, lh - 1);
+      best = lh;
+      bestj = (int64_t)head - 1;
+      if (lh == RP_LEVELS && cap > RP_LEVELS) {
+        __syncwarp();  // the chain links were written by the level-12 lane
+        best = 0;
+        bestj = -1;
+        for (uint32_t c = head; c != 0;) {
+          const int64_t j = (int64_t)c - 1;
+          const uint64_t x = wq ^ window_sm(sk, j);
+          int l = x == 0ull ? 64 : __clzll((long long)x);
+          l = min(l, (int)min((int64_t)cap, j + 1));
+          if (l > best) {
+            best = l;
+            bestj = j;
+            if (best == cap) break;
+          }
+          c = prev[j];
+        }
+      }
+    }
+    if (lane == (int)(t & 31)) {
+      float sign = -1.f;
+      if (bestj >= 0) {
+        const int64_t succ = bestj + 1;
+        sign = ((sv[succ >> 6] >> (succ & 63)) & 1ull) ? 1.f : -1.f;
+      }
+      const float o = pay * sign;
+      const int64_t oo = b * a.ob + t * a.ot + s * a.os;
+      if (a.out_dtype == KSD8_F32)
+        reinterpret_cast<float*>(a.out)[oo] = o;
+      else if (a.out_dtype == KSD8_BF16)
+        reinterpret_cast<__nv_bfloat16*>(a.out)[oo] = __float2bfloat16_rn(o);
+      else
+        reinterpret_cast<__half*>(a.out)[oo] = __float2half_rn(o);
+      if (a.match_len) a.match_len[stream * T + t] = best;
+      if (a.match_end) a.match_end[stream * T + t] = (int32_t)bestj;
+    }
+  }
+}
+
 struct TimemixArgs {
   const void* x;
   int64_t batch, t_len, d;
@@ -278,6 +392,28 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
   a.qw = qw; a.kw = kw; a.vw = vw; a.batch = batch; a.streams = streams; a.t_len = t_len;
   a.max_len = max_len; a.payload = payload; a.out = out; a.out_dtype = out_dtype;
   a.ob = ob; a.ot = ot; a.os = os; a.match_len = match_len; a.match_end = match_end;
+  if (t_len < RP_TMAX) {
+    static unsigned prefix_attr = 0;
+    // bytes per warp: tables + links (16-byte aligned), then 3 x ceil(T/64) words
+    // (a multiple of 16 bytes, so that every warp's region keeps the 16-byte
+    // alignment of its vector stores)
+    const int stride = (int)(((((size_t)RP_TBL + t_len) * 2 + 15) / 16 * 16 +
+                              3 * 8 * (size_t)((t_len + 63) / 64) + 15) / 16 * 16);
+    int nwarps = (int)((227 * 1024) / (size_t)stride);
+    if (nwarps > RP_WARPS) nwarps = RP_WARPS;
+    const size_t psmem = (size_t)nwarps * stride;
+    if (!(prefix_attr & (1u << dev))) {
+      if (cudaFuncSetAttribute(rosa_match_prefix_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+          cudaSuccess)
+        return KSD8_ERR_LAUNCH;
+      prefix_attr |= (1u << dev);
+    }
+    const int64_t n = batch * streams;
+    rosa_match_prefix_kernel<<<(unsigned)((n + nwarps - 1) / nwarps), nwarps * 32, psmem,
+                               stream>>>(a, stride);
+    return KSD8_OK;
+  }
   int threads = 512;
   if (t_len <= 256) threads = 256;
   rosa_match_kernel<<<(unsigned)(batch * streams), threads, smem, stream>>>(a);

@@ -38,7 +38,8 @@ def _streams(rng, S, T, repeat_frac=0.3):
 
 
 @pytest.mark.parametrize("S,T", [(8, 1), (8, 2), (16, 33), (16, 64), (16, 65), (12, 300),
-                                 (6, 1000), (3, 4096)])
+                                 (6, 1000), (3, 4096), (64, 2048),
+                                 (2, 8300)])   # T >= 8192: the brute-force kernel
 def test_match_indices_vs_oracle(oracle, S, T):
     from ksdraft_b200.model.rosa import match_payload_sign_with_indices
     rng = np.random.default_rng(S * 1000 + T)
