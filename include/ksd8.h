@@ -257,6 +257,11 @@ int ksd8_topk_rows(const void* vals, int dtype, const int64_t* idx, int64_t m, i
  * lets torch allocate the intermediate.  This one allocates nothing (no
  * cudaMalloc / cudaFree, no library allocator) and writes the same outputs,
  * bit for bit, as the two-call path.
+ * Who needs it: code that drives the backward through this C ABI from
+ * another runtime -- an FFI binding or plugin host that is handed its device
+ * buffers by an owner which reserved all device memory up front -- has no
+ * allocator to get the partials buffer from, and calling cudaMalloc in the
+ * middle of a training step would also stall the device for every stream.
  *   - Limit: ceil(m / 128) * 8 * charts <= KSD8_VJP_STATIC_MAX_PARTIALS, e.g.
  *     m = 4096 tokens with up to 8192 charts; larger requests return
  *     KSD8_ERR_SCRATCH_LIMIT before anything launches.

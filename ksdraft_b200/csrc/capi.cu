@@ -331,7 +331,10 @@ int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, v
 //
 // ksd8_ks3_vjp_static: the VJP and its reduction with the partials in a
 // file-scope static device array (8 MiB, resident in every device context
-// that loads this library).  Its device address is looked up once per device
+// that loads this library), for callers that cannot allocate: a binding or
+// plugin host given its device buffers by an owner that reserved the memory
+// up front has no allocator of its own, and a cudaMalloc mid-step would stall
+// the device.  Its device address is looked up once per device
 // with cudaGetSymbolAddress, with that device current, and cached.  The VJP
 // writes every (tile, k, chart) partial that the reduction reads, so nothing
 // is cleared.  Calls that overlap on one device share the array and race.

@@ -1,6 +1,9 @@
 """ksd8_ks3_vjp_static (partials in a static device array, no allocation)
 against the two-call path ksd8_ks3_vjp + ksd8_ks3_vjp_reduce with caller
-scratch.  Named to be collected last; every test builds its own inputs, so the
+scratch.  The static entry point serves callers that cannot allocate device
+memory (a binding or plugin host handed its buffers by an owner that reserved
+all memory up front); it must produce the same bits as the path whose
+partials buffer the caller provides.  Named to be collected last; every test builds its own inputs, so the
 file also passes alone in a fresh process."""
 
 import numpy as np
