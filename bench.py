@@ -421,6 +421,21 @@ def run_profile_case(case: str, iters: int) -> None:
                                              *(o.data_ptr() for o in outs), None,
                                              _lib.stream_ptr(dev))
                 _lib.check(rc, "vjp")
+    elif case == "head":
+        # LM head of one vocab shard: 4096 tokens x d 1536 x V 150144 (one GPU
+        # holds the whole vocabulary), W8A8 logits + CE partials + gradient +
+        # dgrad / wgrad, forward and backward
+        from ksdraft_b200.model.head import VocabParallelHead
+        V = 150144
+        w = torch.randn(V, D_MODEL, device=dev, generator=g) * 0.02
+        head = VocabParallelHead(w)
+        x = torch.randn(TOKENS, D_MODEL, device=dev, generator=g).to(torch.bfloat16)
+        tg = torch.randint(0, V, (TOKENS,), device=dev, generator=g)
+
+        def fn():
+            xd = x.detach().requires_grad_(True)
+            head.weight.grad = None
+            head.cross_entropy(xd, tg).backward()
     elif case == "rosa":
         # config 3: batch 4 x seq 4096, 512 streams (2048 stream sequences); bits
         # from Zipf(1.1) ids with repeated spans (length 8-64, 10% of positions)

@@ -240,6 +240,18 @@ int ksd8_ce_grad(const void* logits, int dtype, int64_t m, int64_t v_local, int6
                  const int64_t* targets, int64_t vstart, const float* gmax, const float* gsum,
                  float scale, float* dlogits, int64_t ldd, int* status, void* stream);
 
+/* ksd8_ce_grad's dlogits quantised straight into the two backward GEMM
+ * operands, without writing dlogits: dq (M, Vp) codes along the vocabulary
+ * (row stride ldq >= Vp = ceil(V_local/128)*128) with dq_scales (M, Vp/128)
+ * fp16, and dqt (V_local, Mp) codes along the tokens (row stride ldqt >= Mp =
+ * ceil(M/128)*128) with dqt_scales (V_local, Mp/128) fp16 -- the same codes as
+ * ksd8_quantize_rows / ksd8_quantize_cols of the fp32 dlogits; the padded
+ * tails are zero codes. */
+int ksd8_ce_grad_quant(const void* logits, int dtype, int64_t m, int64_t v_local, int64_t ld,
+                       const int64_t* targets, int64_t vstart, const float* gmax,
+                       const float* gsum, float scale, int8_t* dq, int64_t ldq, void* dq_scales,
+                       int8_t* dqt, int64_t ldqt, void* dqt_scales, int* status, void* stream);
+
 /* Per-row top-k (1 <= k <= 32) of vals (M, C) row stride ld: out_vals (M, k)
  * fp32 descending, out_ids (M, k) int64; ids are offset + column, or idx[row,
  * column] when idx (M, C, same stride) is given (merging gathered shard

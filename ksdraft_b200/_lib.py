@@ -54,6 +54,8 @@ SIGNATURES: dict[str, list] = {
     "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
     "ksd8_ce_partials": [vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp],
     "ksd8_ce_grad": [vp, i32, i64, i64, i64, vp, i64, vp, vp, f32, vp, i64, vp, vp],
+    "ksd8_ce_grad_quant": [vp, i32, i64, i64, i64, vp, i64, vp, vp, f32, vp, i64, vp, vp, i64, vp,
+                           vp, vp],
     "ksd8_topk_rows": [vp, i32, vp, i64, i64, i64, i32, i64, vp, vp, vp, vp],
     "ksd8_ks3_vjp_static": [vp, vp, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                             vp, vp, vp, vp],

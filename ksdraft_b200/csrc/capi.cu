@@ -39,6 +39,9 @@ int ksd8_ce_grad_launch(const void*, int, int64_t, int64_t, int64_t, const int64
                         const float*, const float*, float, float*, int64_t, cudaStream_t);
 int ksd8_topk_rows_launch(const void*, int, const int64_t*, int64_t, int64_t, int64_t, int, int64_t,
                           float*, int64_t*, cudaStream_t);
+int ksd8_ce_grad_quant_launch(const void*, int, int64_t, int64_t, int64_t, const int64_t*, int64_t,
+                              const float*, const float*, float, int8_t*, int64_t, void*, int8_t*,
+                              int64_t, void*, cudaStream_t);
 int ksd8_adamw_launch(float*, const void*, int, float*, float*, int64_t, float, float, float,
                       float, float, int, cudaStream_t);
 
@@ -304,6 +307,24 @@ int ksd8_ce_grad(const void* logits, int dtype, int64_t m, int64_t v_local, int6
   if (m > 0 && (!logits || !targets || !gmax || !gsum || !dlogits)) return KSD8_ERR_ARG;
   return finish(ksd8_ce_grad_launch(logits, dtype, m, v_local, ld, targets, vstart, gmax, gsum,
                                     scale, dlogits, ldd, S(stream)));
+}
+
+int ksd8_ce_grad_quant(const void* logits, int dtype, int64_t m, int64_t v_local, int64_t ld,
+                       const int64_t* targets, int64_t vstart, const float* gmax,
+                       const float* gsum, float scale, int8_t* dq, int64_t ldq, void* dq_scales,
+                       int8_t* dqt, int64_t ldqt, void* dqt_scales, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  const int64_t vp = (v_local + 127) / 128 * 128, mp = (m + 127) / 128 * 128;
+  if (m < 0 || v_local <= 0 || ld < v_local || vstart < 0 || ldq < vp || ldqt < mp)
+    return KSD8_ERR_SHAPE;
+  if (m > 65535 * 128 || v_local > 2147483647LL * 128) return KSD8_ERR_UNSUPPORTED;  // grid
+  if (m > 0 && (!logits || !targets || !gmax || !gsum || !dq || !dq_scales || !dqt ||
+                !dqt_scales))
+    return KSD8_ERR_ARG;
+  return finish(ksd8_ce_grad_quant_launch(logits, dtype, m, v_local, ld, targets, vstart, gmax,
+                                          gsum, scale, dq, ldq, dq_scales, dqt, ldqt, dqt_scales,
+                                          S(stream)));
 }
 
 int ksd8_topk_rows(const void* vals, int dtype, const int64_t* idx, int64_t m, int64_t c,

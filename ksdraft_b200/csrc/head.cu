@@ -118,6 +118,117 @@ __global__ void __launch_bounds__(256) ce_grad_kernel(const T* logits, int64_t V
   }
 }
 
+// ---------------------------------------------------------------- fused gradient + quantisation
+
+struct CeGQArgs {
+  const void* logits;
+  int64_t M, V, ld;
+  const int64_t* targets;
+  int64_t vstart;
+  const float* gmax;
+  const float* gsum;
+  float scale;
+  int8_t* dq;          // (M, Vp) codes along the vocabulary, row stride ldq
+  int64_t ldq;
+  __half* dq_scales;   // (M, Vp / 128)
+  int8_t* dqt;         // (V, Mp) codes along the tokens, row stride ldqt
+  int64_t ldqt;
+  __half* dqt_scales;  // (V, Mp / 128)
+};
+
+constexpr int CGQ_LD = 129;  // fp32 tile pitch
+
+// One CTA per 128-token x 128-vocab tile of the logits shard.  Warp w turns
+// rows 16w .. 16w + 15 into dlogits with ce_grad_kernel's expression (same
+// bits), quantises each row along the vocabulary (one 128-wide group) in
+// registers and parks the values in shared memory; then thread t quantises
+// column t % 128 along the tokens (rows (t / 128) * 64 .. + 64, 16-byte
+// stores).  Columns past V and rows past M hold zeros, so the padded tails of
+// both code tensors come out zero for the GEMMs that contract over them.
+template <typename T>
+__global__ void __launch_bounds__(256) ce_grad_quant_kernel(CeGQArgs a) {
+  extern __shared__ float gt[];  // [128][CGQ_LD]
+  const int64_t r0 = (int64_t)blockIdx.y * 128, c0 = (int64_t)blockIdx.x * 128;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t vgroups = (a.V + 127) / 128;
+  for (int i = 0; i < 16; ++i) {
+    const int rr = warp * 16 + i;
+    const int64_t r = r0 + rr;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (r < a.M) {
+      const T* lr = reinterpret_cast<const T*>(a.logits) + r * a.ld;
+      const float mx = a.gmax[r];
+      const float inv = 1.f / a.gsum[r];
+      const int64_t t = a.targets[r] - a.vstart;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t c = c0 + lane * 4 + j;
+        if (c < a.V) {
+          const float p = ex2_approx((ld_val(lr + c) - mx) * LOG2E) * inv;
+          v[j] = (p - (c == t ? 1.f : 0.f)) * a.scale;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) gt[rr * CGQ_LD + lane * 4 + j] = v[j];
+    if (r < a.M) {
+      float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+      m = warp_max(m);
+      __half sh;
+      const float sc = gs_scale_fast(m, &sh);
+      const float rcp = rcp_approx(sc);
+      int q[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q[j] = gs_code_fast(v[j], sc, rcp);
+      int8_t* out = a.dq + r * a.ldq + c0 + lane * 4;
+      if ((reinterpret_cast<uintptr_t>(out) & 3) == 0) {
+        *reinterpret_cast<char4*>(out) = make_char4((char)q[0], (char)q[1], (char)q[2], (char)q[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) out[j] = (int8_t)q[j];
+      }
+      if (lane == 0) a.dq_scales[r * vgroups + blockIdx.x] = sh;
+    }
+  }
+  __shared__ float s_amax[2][128];
+  __syncthreads();
+  const int cc = threadIdx.x & 127, half = threadIdx.x >> 7;
+  const int64_t c = c0 + cc;
+  float m = 0.f;
+#pragma unroll 16
+  for (int i = 0; i < 64; ++i) m = fmaxf(m, fabsf(gt[(half * 64 + i) * CGQ_LD + cc]));
+  s_amax[half][cc] = m;
+  __syncthreads();
+  if (c >= a.V) return;
+  m = fmaxf(s_amax[0][cc], s_amax[1][cc]);
+  const int64_t mgroups = (a.M + 127) / 128;
+  __half sh;
+  const float sc = gs_scale_fast(m, &sh);
+  const float rcp = rcp_approx(sc);
+  int8_t* out = a.dqt + c * a.ldqt + r0 + half * 64;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+#pragma unroll
+    for (int q16 = 0; q16 < 4; ++q16) {
+      uint32_t w[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int rr = half * 64 + q16 * 16 + jj * 4 + b;
+          word |= (uint32_t)(gs_code_fast(gt[rr * CGQ_LD + cc], sc, rcp) & 0xFF) << (8 * b);
+        }
+        w[jj] = word;
+      }
+      *reinterpret_cast<uint4*>(out + q16 * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+    for (int i = 0; i < 64; ++i)
+      out[i] = (int8_t)gs_code_fast(gt[(half * 64 + i) * CGQ_LD + cc], sc, rcp);
+  }
+  if (half == 0) a.dqt_scales[c * mgroups + blockIdx.y] = sh;
+}
+
 // ---------------------------------------------------------------- top-k
 
 constexpr int TOPK_MAX = 32;
@@ -277,6 +388,35 @@ int ksd8_ce_grad_launch(const void* logits, int dtype, int64_t M, int64_t V, int
     return launch_grad<__nv_bfloat16>(logits, M, V, ld, targets, vstart, gmax, gsum, scale, dl,
                                       ldd, stream);
   return launch_grad<__half>(logits, M, V, ld, targets, vstart, gmax, gsum, scale, dl, ldd, stream);
+}
+
+int ksd8_ce_grad_quant_launch(const void* logits, int dtype, int64_t M, int64_t V, int64_t ld,
+                              const int64_t* targets, int64_t vstart, const float* gmax,
+                              const float* gsum, float scale, int8_t* dq, int64_t ldq,
+                              void* dq_scales, int8_t* dqt, int64_t ldqt, void* dqt_scales,
+                              cudaStream_t stream) {
+  if (M == 0 || V == 0) return KSD8_OK;
+  CeGQArgs a;
+  a.logits = logits; a.M = M; a.V = V; a.ld = ld; a.targets = targets; a.vstart = vstart;
+  a.gmax = gmax; a.gsum = gsum; a.scale = scale; a.dq = dq; a.ldq = ldq;
+  a.dq_scales = reinterpret_cast<__half*>(dq_scales); a.dqt = dqt; a.ldqt = ldqt;
+  a.dqt_scales = reinterpret_cast<__half*>(dqt_scales);
+  const int smem = 128 * CGQ_LD * 4;
+  static unsigned attr = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr & (1u << dev))) {
+    cudaFuncSetAttribute(ce_grad_quant_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(ce_grad_quant_kernel<__nv_bfloat16>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(ce_grad_quant_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr |= (1u << dev);
+  }
+  dim3 grid((unsigned)((V + 127) / 128), (unsigned)((M + 127) / 128));
+  if (dtype == KSD8_F32) ce_grad_quant_kernel<float><<<grid, 256, smem, stream>>>(a);
+  else if (dtype == KSD8_BF16) ce_grad_quant_kernel<__nv_bfloat16><<<grid, 256, smem, stream>>>(a);
+  else ce_grad_quant_kernel<__half><<<grid, 256, smem, stream>>>(a);
+  return KSD8_OK;
 }
 
 int ksd8_topk_rows_launch(const void* vals, int dtype, const int64_t* idx, int64_t M, int64_t C,

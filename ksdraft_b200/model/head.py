@@ -95,6 +95,30 @@ def ce_grad(logits: torch.Tensor, targets: torch.Tensor, vstart: int, gmax: torc
     return d
 
 
+def ce_grad_quant(logits: torch.Tensor, targets: torch.Tensor, vstart: int, gmax: torch.Tensor,
+                  gsum: torch.Tensor, scale: float):
+    """The shard's dlogits ((softmax - onehot) * scale) quantised along the
+    vocabulary (M, Vp) and along the tokens (V_local, Mp), both zero-padded to
+    multiples of 128 for the backward GEMMs; the codes equal quantize_last_dim /
+    quantize_cols of ce_grad's fp32 output."""
+    _lib.require_cuda(logits, targets)
+    M, V = logits.shape
+    Vp, Mp = -(-V // GROUP_SIZE) * GROUP_SIZE, -(-M // GROUP_SIZE) * GROUP_SIZE
+    dev = logits.device
+    dq = torch.empty(M, Vp, dtype=torch.int8, device=dev)
+    dqs = torch.empty(M, Vp // GROUP_SIZE, dtype=torch.float16, device=dev)
+    dqt = torch.empty(V, Mp, dtype=torch.int8, device=dev)
+    dqts = torch.empty(V, Mp // GROUP_SIZE, dtype=torch.float16, device=dev)
+    t = targets.to(torch.int64).contiguous()
+    rc = _lib.lib().ksd8_ce_grad_quant(
+        logits.data_ptr(), _lib.dtype_code(logits), M, V, logits.stride(0) if M > 1 else V,
+        t.data_ptr(), vstart, gmax.contiguous().data_ptr(), gsum.contiguous().data_ptr(),
+        float(scale), dq.data_ptr(), Vp, dqs.data_ptr(), dqt.data_ptr(), Mp, dqts.data_ptr(),
+        None, _lib.stream_ptr(dev))
+    _lib.check(rc, "ce_grad_quant")
+    return dq, dqs, dqt, dqts
+
+
 def topk_rows(vals: torch.Tensor, k: int, offset: int = 0, ids: torch.Tensor | None = None):
     """Per-row top-k of a (M, C) tensor: (values fp32 (M, k), ids int64 (M, k)),
     descending, ties to the smaller id; ids = offset + column or ids[row, col]."""
@@ -155,19 +179,18 @@ class _HeadCE(torch.autograd.Function):
         M = logits.shape[0]
         # d(mean)/d(logit) = (softmax - onehot) / M, times the upstream scalar
         scale = float(grad_loss) / M
-        dl = ce_grad(logits, targets, head.vstart, gmax, gsum, scale)
-        wq, ws = head.weight_codes()
+        # q(dl) along the vocabulary and along the tokens, straight from the
+        # logits (dl itself is never written)
+        dq, dsc, dlT_q, dlT_s = ce_grad_quant(logits, targets, head.vstart, gmax, gsum, scale)
+        wT_q, wT_s = head.weight_codes_t()                       # (d, Vp) along V
         # dx = q(dl) @ q(W^T)^T over this shard's vocabulary, summed over ranks
-        dq, dsc = quantize_last_dim(dl)
-        wT_q, wT_s = quantize_cols(wq, x_scales=ws)             # (d, V_local) along V
-        dx = gemm_out(_pad_k(dq), dsc, _pad_k(wT_q), wT_s)
+        dx = gemm_out(dq, dsc, wT_q, wT_s)
         _, world = _world(head.group)
         if world > 1:
             dist.all_reduce(dx, group=head.group)
         # dW_shard = q(dl^T) @ q(x^T)^T, contracted over the tokens
-        dlT_q, dlT_s = quantize_cols(dl)                         # (V_local, M)
         xT_q, xT_s = quantize_cols(x2)                           # (d, M)
-        dw = gemm_out(_pad_k(dlT_q), dlT_s, _pad_k(xT_q), xT_s)
+        dw = gemm_out(dlT_q, dlT_s, _pad_k(xT_q), xT_s)
         return dx.reshape(ctx.x_shape).to(ctx.x_dtype), dw, None, None
 
 
@@ -192,6 +215,7 @@ class VocabParallelHead(torch.nn.Module):
         self.vstart = start
         self.weight = torch.nn.Parameter(shard.detach().float().clone())
         self._codes = None
+        self._codes_t = None
         self._version = None
 
     @property
@@ -199,11 +223,22 @@ class VocabParallelHead(torch.nn.Module):
         return self.weight.shape[0]
 
     def weight_codes(self):
+        """Per-row GS128 codes of the shard, re-quantised when the master changes."""
         v = self.weight._version
         if self._codes is None or self._version != v:
             self._codes = quantize_last_dim(self.weight.detach())
+            self._codes_t = None
             self._version = v
         return self._codes
+
+    def weight_codes_t(self):
+        """Codes of W^T (d, Vp) quantised along the vocabulary (zero-padded to a
+        multiple of 128), cached with the row codes they are derived from."""
+        wq, ws = self.weight_codes()
+        if self._codes_t is None:
+            tq, ts = quantize_cols(wq, x_scales=ws)
+            self._codes_t = (_pad_k(tq), ts)
+        return self._codes_t
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         """This shard's logits (M, V_local) fp32 for x (..., d)."""

@@ -56,6 +56,25 @@ def test_topk_rows_exact_with_ties(k):
     np.testing.assert_array_equal(mi.cpu().numpy(), np.take_along_axis(ids.numpy(), order2, 1))
 
 
+@pytest.mark.parametrize("M,V", [(300, 1003), (256, 2048), (1, 130)])
+def test_ce_grad_quant_equals_quantised_ce_grad(M, V):
+    """The fused kernel's codes == quantize_last_dim / quantize_cols of ce_grad."""
+    from ksdraft_b200.kernels.quant import quantize_cols, quantize_last_dim
+    from ksdraft_b200.model.head import ce_grad, ce_grad_quant, ce_partials
+    g = torch.Generator().manual_seed(M + V)
+    logits = (torch.randn(M, V, generator=g) * 4).cuda()
+    t = torch.randint(0, V + 300, (M,), generator=g).cuda()
+    mx, sm, _ = ce_partials(logits, t, 0)
+    dl = ce_grad(logits, t, 0, mx, sm, 1.0 / M)
+    dq, dqs, dqt, dqts = ce_grad_quant(logits, t, 0, mx, sm, 1.0 / M)
+    rq, rs = quantize_last_dim(dl)
+    tq, ts = quantize_cols(dl)
+    assert torch.equal(dq[:, :V], rq) and not dq[:, V:].any()
+    assert torch.equal(dqs.view(torch.int16), rs.view(torch.int16))
+    assert torch.equal(dqt[:, :M], tq) and not dqt[:, M:].any()
+    assert torch.equal(dqts.view(torch.int16), ts.view(torch.int16))
+
+
 def _head_case(M=256, d=256, V=2048, seed=4):
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(M, d, generator=g).to(torch.bfloat16)
