@@ -151,35 +151,70 @@ __global__ void __launch_bounds__(256) ce_grad_quant_kernel(CeGQArgs a) {
   const int64_t r0 = (int64_t)blockIdx.y * 128, c0 = (int64_t)blockIdx.x * 128;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t vgroups = (a.V + 127) / 128;
-  for (int i = 0; i < 16; ++i) {
-    const int rr = warp * 16 + i;
-    const int64_t r = r0 + rr;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (r < a.M) {
-      const T* lr = reinterpret_cast<const T*>(a.logits) + r * a.ld;
-      const float mx = a.gmax[r];
-      const float inv = 1.f / a.gsum[r];
-      const int64_t t = a.targets[r] - a.vstart;
+  // per-row statistics, one row per lane (rows 16w .. 16w + 15)
+  float st_mx = 0.f, st_inv = 0.f;
+  int64_t st_t = -1;
+  if (lane < 16 && r0 + warp * 16 + lane < a.M) {
+    const int64_t r = r0 + warp * 16 + lane;
+    st_mx = a.gmax[r];
+    st_inv = 1.f / a.gsum[r];
+    st_t = a.targets[r] - a.vstart;
+  }
+  const bool vec = sizeof(T) == 4 && (a.ld & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0 && c0 + 128 <= a.V;
+  for (int i0 = 0; i0 < 16; i0 += 4) {
+    float v[4][4];
+    // the 4 rows' loads first (all in flight together)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t c = c0 + lane * 4 + j;
-        if (c < a.V) {
-          const float p = ex2_approx((ld_val(lr + c) - mx) * LOG2E) * inv;
-          v[j] = (p - (c == t ? 1.f : 0.f)) * a.scale;
+    for (int u = 0; u < 4; ++u) {
+      const int64_t r = r0 + warp * 16 + i0 + u;
+      const T* lr = reinterpret_cast<const T*>(a.logits) + r * a.ld;
+      if (r < a.M && vec) {
+        const float4 q = __ldcs(reinterpret_cast<const float4*>(lr + c0 + lane * 4));
+        v[u][0] = q.x; v[u][1] = q.y; v[u][2] = q.z; v[u][3] = q.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t c = c0 + lane * 4 + j;
+          v[u][j] = (r < a.M && c < a.V) ? ld_val(lr + c) : 0.f;
         }
       }
     }
+    float m[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) gt[rr * CGQ_LD + lane * 4 + j] = v[j];
-    if (r < a.M) {
-      float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-      m = warp_max(m);
+    for (int u = 0; u < 4; ++u) {
+      const int rr = warp * 16 + i0 + u;
+      const int64_t r = r0 + rr;
+      const float mx = __shfl_sync(0xffffffffu, st_mx, i0 + u);
+      const float inv = __shfl_sync(0xffffffffu, st_inv, i0 + u);
+      const int64_t t = __shfl_sync(0xffffffffu, st_t, i0 + u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t c = c0 + lane * 4 + j;
+        float d = 0.f;
+        if (r < a.M && c < a.V) {
+          const float p = ex2_approx((v[u][j] - mx) * LOG2E) * inv;
+          d = (p - (c == t ? 1.f : 0.f)) * a.scale;
+        }
+        v[u][j] = d;
+        gt[rr * CGQ_LD + lane * 4 + j] = d;
+      }
+      m[u] = fmaxf(fmaxf(fabsf(v[u][0]), fabsf(v[u][1])), fmaxf(fabsf(v[u][2]), fabsf(v[u][3])));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) m[u] = fmaxf(m[u], __shfl_xor_sync(0xffffffffu, m[u], o));
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t r = r0 + warp * 16 + i0 + u;
+      if (r >= a.M) continue;
       __half sh;
-      const float sc = gs_scale_fast(m, &sh);
+      const float sc = gs_scale_fast(m[u], &sh);
       const float rcp = rcp_approx(sc);
       int q[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) q[j] = gs_code_fast(v[j], sc, rcp);
+      for (int j = 0; j < 4; ++j) q[j] = gs_code_fast(v[u][j], sc, rcp);
       int8_t* out = a.dq + r * a.ldq + c0 + lane * 4;
       if ((reinterpret_cast<uintptr_t>(out) & 3) == 0) {
         *reinterpret_cast<char4*>(out) = make_char4((char)q[0], (char)q[1], (char)q[2], (char)q[3]);
