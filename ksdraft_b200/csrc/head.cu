@@ -152,14 +152,17 @@ __global__ void __launch_bounds__(256) ce_grad_quant_kernel(CeGQArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t vgroups = (a.V + 127) / 128;
   // per-row statistics, one row per lane (rows 16w .. 16w + 15)
+  // (the target as a column of this tile, -1 when it lies elsewhere)
   float st_mx = 0.f, st_inv = 0.f;
-  int64_t st_t = -1;
+  int st_t = -1;
   if (lane < 16 && r0 + warp * 16 + lane < a.M) {
     const int64_t r = r0 + warp * 16 + lane;
     st_mx = a.gmax[r];
     st_inv = 1.f / a.gsum[r];
-    st_t = a.targets[r] - a.vstart;
+    const int64_t t = a.targets[r] - a.vstart - c0;
+    st_t = (t >= 0 && t < 128) ? (int)t : -1;
   }
+  const int vrem = (int)min((int64_t)128, a.V - c0);  // valid columns of this tile
   const bool vec = sizeof(T) == 4 && (a.ld & 3) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0 && c0 + 128 <= a.V;
   for (int i0 = 0; i0 < 16; i0 += 4) {
@@ -187,14 +190,15 @@ __global__ void __launch_bounds__(256) ce_grad_quant_kernel(CeGQArgs a) {
       const int64_t r = r0 + rr;
       const float mx = __shfl_sync(0xffffffffu, st_mx, i0 + u);
       const float inv = __shfl_sync(0xffffffffu, st_inv, i0 + u);
-      const int64_t t = __shfl_sync(0xffffffffu, st_t, i0 + u);
+      const int t = __shfl_sync(0xffffffffu, st_t, i0 + u);
+      const bool row_ok = r < a.M;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int64_t c = c0 + lane * 4 + j;
+        const int cl = lane * 4 + j;
         float d = 0.f;
-        if (r < a.M && c < a.V) {
+        if (row_ok && cl < vrem) {
           const float p = ex2_approx((v[u][j] - mx) * LOG2E) * inv;
-          d = (p - (c == t ? 1.f : 0.f)) * a.scale;
+          d = (p - (cl == t ? 1.f : 0.f)) * a.scale;
         }
         v[u][j] = d;
         gt[rr * CGQ_LD + lane * 4 + j] = d;
