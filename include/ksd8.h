@@ -82,6 +82,11 @@ extern "C" {
 #define KSD8_NL_INT8 2
 
 int ksd8_version(void);
+/* SMs per device that the persistent kernels (GEMM, VJP) leave free, for
+ * collectives running at the same time (e.g. NCCL capped to that many CTAs):
+ * their grids shrink to sm_count - n.  Process-wide, 0 by default. */
+int ksd8_set_sm_reserve(int n);
+int ksd8_get_sm_reserve(void);
 const char* ksd8_status_string(int status);
 /* Last CUDA runtime error seen by a launch in this thread (cudaError_t as int). */
 int ksd8_last_cuda_error(void);

@@ -52,6 +52,8 @@ SIGNATURES: dict[str, list] = {
                                    vp, vp],
     "ksd8_adamw_step": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp],
     "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
+    "ksd8_set_sm_reserve": [i32],
+    "ksd8_get_sm_reserve": [],
     "ksd8_ce_partials": [vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp],
     "ksd8_ce_grad": [vp, i32, i64, i64, i64, vp, i64, vp, vp, f32, vp, i64, vp, vp],
     "ksd8_ce_grad_quant": [vp, i32, i64, i64, i64, vp, i64, vp, vp, f32, vp, i64, vp, vp, i64, vp,

@@ -1,6 +1,7 @@
 // extern "C" boundary of libksd8: argument validation on the host, then the
 // launches of quant.cu / gemm_sm100.cu / ks3.cu / rosa.cu on the caller's stream.
 // Shape, dtype and alignment errors return a status before anything launches.
+#include <atomic>
 #include <cstdio>
 
 #include "common.cuh"
@@ -84,6 +85,16 @@ const char* ksd8_status_string(int status) {
 }
 
 int ksd8_last_cuda_error(void) { return g_last_cuda_error; }
+
+static std::atomic<int> g_sm_reserve{0};
+
+int ksd8_set_sm_reserve(int n) {
+  if (n < 0 || n > 1024) return KSD8_ERR_ARG;
+  g_sm_reserve.store(n);
+  return KSD8_OK;
+}
+
+int ksd8_get_sm_reserve(void) { return g_sm_reserve.load(); }
 
 int ksd8_sm_count(int device) {
   int n = 0;

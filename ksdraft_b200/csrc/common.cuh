@@ -18,6 +18,13 @@
 
 #include "../../include/ksd8.h"
 
+// Host: grid of a persistent kernel, leaving ksd8_get_sm_reserve() SMs to
+// concurrent collectives (capi.cu holds the setting).
+static inline int ksd8_persistent_ctas(int sm_count) {
+  const int n = sm_count - ksd8_get_sm_reserve();
+  return n < 1 ? 1 : n;
+}
+
 #ifndef KSD8_SUSPEND_NS
 #define KSD8_SUSPEND_NS 20000u  // suspend-time hint of one try_wait (woken on completion)
 #endif

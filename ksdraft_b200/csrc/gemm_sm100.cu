@@ -648,7 +648,7 @@ static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t 
   if (!make_tmap_i8(&ta, a, args.M, k, BM)) return KSD8_ERR_LAUNCH;
   if (!make_tmap_i8(&tb, w, args.N, k, BN / CG)) return KSD8_ERR_LAUNCH;
   const int tiles = ((args.M + BM * CG - 1) / (BM * CG)) * ((args.N + BN - 1) / BN);
-  const int sms = sm_count_cached();
+  const int sms = ksd8_persistent_ctas(sm_count_cached());
   const int units = sms / CG;
   const int grid = (tiles < units ? tiles : units) * CG;
   if constexpr (RegSplit<(4 + EPI_WARPS) * 32>::on) {
@@ -707,7 +707,7 @@ int ksd8_gemm_launch(const int8_t* a, const void* a_scales, const int8_t* w, con
     return launch_gemm<128, 4, 4, true, 1>(a, w, args, k, stream);
   }
   const int64_t tiles_m = (m + 127) / 128;
-  const int64_t sms = sm_count_cached();
+  const int64_t sms = ksd8_persistent_ctas(sm_count_cached());
   // At least one full wave of 128 x 128 tiles: 8 epilogue warps of 64 columns
   // each, 4 TMEM accumulator buffers, accumulator released before the math.
   if (tiles_m * ((n + 127) / 128) >= sms)

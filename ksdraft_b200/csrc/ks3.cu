@@ -956,7 +956,8 @@ int ksd8_ks3_vjp_launch(const void* value, const void* coords, int64_t m, int64_
   a.dct_codes = dct_codes; a.dct_scales = reinterpret_cast<__half*>(dct_scales);
   a.partials = partials;
   const int64_t tiles = (charts / VJP_TC) * ((m + VJP_TM - 1) / VJP_TM);
-  const int64_t grid = tiles < sm_count[dev] ? tiles : sm_count[dev];  // one CTA per SM
+  const int64_t ctas = ksd8_persistent_ctas(sm_count[dev]);           // one CTA per SM
+  const int64_t grid = tiles < ctas ? tiles : ctas;
   ks3_vjp_kernel<<<(unsigned)grid, VJP_THREADS, VJP_SMEM, stream>>>(tv, tx, a, status);
   return KSD8_OK;
 }

@@ -108,18 +108,33 @@ class AdamW:
 
     @torch.no_grad()
     def step(self) -> None:
+        self.begin_step()
+        for i in range(len(self.params)):
+            self.update(i)
+
+    def begin_step(self) -> None:
+        """Advance the step count (bias correction) once; then update() each tensor."""
         self.step_count += 1
+
+    @torch.no_grad()
+    def update(self, index: int) -> None:
+        """AdamW on one parameter tensor for the current step (a data-parallel
+        step updates each tensor as soon as its gradient's mean is complete)."""
         lib = _lib.lib()
-        for p, (m, v) in zip(self.params, self.state):
-            g = p.grad
-            if g is None:
-                continue
+        p = self.params[index]
+        m, v = self.state[index]
+        g = p.grad
+        if g is not None:
             g = g.contiguous()
             rc = lib.ksd8_adamw_step(p.data_ptr(), g.data_ptr(), _lib.dtype_code(g), m.data_ptr(),
                                      v.data_ptr(), p.numel(), self.lr, self.betas[0],
                                      self.betas[1], self.eps, self.wd, self.step_count, None,
                                      _lib.stream_ptr(p.device))
             _lib.check(rc, "adamw_step")
+
+
+# SMs per GPU left to NCCL while gradient reductions overlap the backward.
+SM_RESERVE = 16
 
 
 def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
@@ -131,6 +146,9 @@ def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
+            # NCCL's kernels then fit in the SMs the persistent kernels leave
+            # free while a gradient reduction overlaps the backward
+            os.environ.setdefault("NCCL_MAX_CTAS", str(SM_RESERVE))
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
     return rank, world, local
 
@@ -143,8 +161,9 @@ class KS3DataParallelStep:
         self.params = [cell.master_down, cell.master_up, cell.master_coefficients,
                        cell.master_raw_scale, cell.master_raw_shift]
         self.grads = FlatGrads(self.params)
-        self.named = dict(zip(("down", "up", "coefficients", "raw_scale", "raw_shift"),
-                              self.params))
+        names = ("down", "up", "coefficients", "raw_scale", "raw_shift")
+        self.named = dict(zip(names, self.params))
+        self.index = {n: i for i, n in enumerate(names)}
         self.grad_views = {name: p.grad for name, p in self.named.items()}
         self.group = group
         self.opt = AdamW(self.params, lr=lr)
@@ -156,13 +175,27 @@ class KS3DataParallelStep:
         accumulation pass runs and nothing waits for the GPU."""
         from ..kernels.ks3_int8 import ks3_backward, ks3_train_forward
         y, saved = ks3_train_forward(self.cell, x.detach())
-        pending = []
+        lib = _lib.lib()
+        pending = []          # (parameter indices, works) in launch order
+        overlapping = [False]
 
         def on_grad(names):   # each gradient's mean over the ranks starts as soon as it exists
             params = [self.named[n] for n in names]
-            pending.extend(allreduce_mean_async(self.grads.span(params), self.group))
-        ks3_backward(self.cell, grad_out, *saved, x.shape, grads_into=self.grad_views,
-                     on_grad=on_grad)
-        wait_all(pending)
-        self.opt.step()
+            works = allreduce_mean_async(self.grads.span(params), self.group)
+            if works and not overlapping[0]:
+                # from here on the persistent kernels share the GPU with NCCL
+                _lib.check(lib.ksd8_set_sm_reserve(SM_RESERVE), "set_sm_reserve")
+                overlapping[0] = True
+            pending.append(([self.index[n] for n in names], works))
+        try:
+            ks3_backward(self.cell, grad_out, *saved, x.shape, grads_into=self.grad_views,
+                         on_grad=on_grad)
+            self.opt.begin_step()
+            for indices, works in pending:  # update each tensor once its mean is complete
+                wait_all(works)
+                for i in indices:
+                    self.opt.update(i)
+        finally:
+            if overlapping[0]:
+                lib.ksd8_set_sm_reserve(0)
         return y

@@ -70,3 +70,17 @@ def test_cpu_tensors_are_rejected_not_computed():
         _match_payload_sign(b, b, b)
     with pytest.raises(TypeError):
         quantize_last_dim(torch.ones(2, 4, dtype=torch.int32))
+
+
+def test_sm_reserve_setting_is_host_only_and_bounded():
+    from ksdraft_b200 import _lib
+    lib = _lib.load()
+    assert lib.ksd8_get_sm_reserve() == 0
+    try:
+        assert lib.ksd8_set_sm_reserve(16) == 0
+        assert lib.ksd8_get_sm_reserve() == 16
+        assert lib.ksd8_set_sm_reserve(-1) == _lib.ERR_ARG
+        assert lib.ksd8_set_sm_reserve(100000) == _lib.ERR_ARG
+        assert lib.ksd8_get_sm_reserve() == 16      # a rejected value changes nothing
+    finally:
+        assert lib.ksd8_set_sm_reserve(0) == 0
