@@ -65,6 +65,9 @@ extern "C" {
 #define KSD8_Q_ROUND_F16 1   /* round the input through fp16 first (x.float().to(float16)) */
 #define KSD8_Q_DITHER 2      /* add PTQR rounding dither from the Philox4x32-10 counter RNG */
 #define KSD8_Q_RELU 4        /* not used by the reference path; reserved */
+#define KSD8_Q_PLAIN_LOADS 8 /* use the thread-load kernels instead of the bulk/TMA-staged
+                                ones (identical results; the staged kernels need 16-byte
+                                aligned rows and are chosen by default when they apply) */
 
 /* ---- GEMM epilogue flags ---- */
 #define KSD8_EPI_CLAMP_F16 1  /* fp16 output: saturate +-inf to +-65504 (ks3_int8.py:241-242) */

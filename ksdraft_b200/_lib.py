@@ -21,7 +21,7 @@ ERR_SCRATCH_LIMIT = 9
 VJP_STATIC_MAX_PARTIALS = 1 << 21
 
 F32, F16, BF16, I8 = 0, 1, 2, 3
-Q_ROUND_F16, Q_DITHER = 1, 2
+Q_ROUND_F16, Q_DITHER, Q_PLAIN_LOADS = 1, 2, 8
 EPI_CLAMP_F16, EPI_BIAS, EPI_FLAG_NONFINITE, EPI_ROUND_F16, EPI_IF_STATUS = 1, 2, 4, 8, 16
 NL = {"fp32": 0, "fp16": 1, "int8": 2}
 

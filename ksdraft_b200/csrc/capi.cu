@@ -8,9 +8,9 @@
 
 // launchers defined in the kernel translation units
 int ksd8_quantize_rows_launch(const void*, int, int64_t, int64_t, int64_t, int, int, float,
-                              uint64_t, uint64_t, int8_t*, int64_t, void*, cudaStream_t);
+                              uint64_t, uint64_t, int8_t*, int64_t, void*, int*, cudaStream_t);
 int ksd8_quantize_cols_launch(const void*, int, const void*, int, int64_t, int64_t, int64_t, int,
-                              int8_t*, int64_t, void*, cudaStream_t);
+                              int8_t*, int64_t, void*, int*, cudaStream_t);
 int ksd8_philox_launch(uint64_t, uint64_t, int64_t, float*, cudaStream_t);
 int ksd8_gemm_launch(const int8_t*, const void*, const int8_t*, const void*, int64_t, int64_t,
                      int64_t, void*, int, int64_t, const float*, int, int*, cudaStream_t, bool);
@@ -105,20 +105,18 @@ int ksd8_sm_count(int device) {
 int ksd8_quantize_rows(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t ldx,
                        int group, int flags, float dither, uint64_t seed, uint64_t offset,
                        int8_t* codes, int64_t ldc, void* scales, int* status, void* stream) {
-  (void)status;
   if (!valid_float_dtype(x_dtype)) return KSD8_ERR_DTYPE;
   if (group != 128) return KSD8_ERR_UNSUPPORTED;
   if (rows < 0 || k < 0 || ldx < k || ldc < k) return KSD8_ERR_SHAPE;
   if ((rows > 0 && k > 0) && (!x || !codes || !scales)) return KSD8_ERR_ARG;
   if ((flags & KSD8_Q_DITHER) && !(dither >= 0.f)) return KSD8_ERR_ARG;
   return finish(ksd8_quantize_rows_launch(x, x_dtype, rows, k, ldx, group, flags, dither, seed,
-                                          offset, codes, ldc, scales, S(stream)));
+                                          offset, codes, ldc, scales, status, S(stream)));
 }
 
 int ksd8_quantize_cols(const void* x, int x_dtype, const void* x_scales, int x_group,
                        int64_t rows, int64_t cols, int64_t ldx, int group, int flags,
                        int8_t* codes_t, int64_t ldct, void* scales_t, int* status, void* stream) {
-  (void)status;
   if (!(valid_float_dtype(x_dtype) || x_dtype == KSD8_I8)) return KSD8_ERR_DTYPE;
   if (group != 128) return KSD8_ERR_UNSUPPORTED;
   if (x_dtype == KSD8_I8 && (!x_scales || x_group <= 0)) return KSD8_ERR_ARG;
@@ -126,7 +124,7 @@ int ksd8_quantize_cols(const void* x, int x_dtype, const void* x_scales, int x_g
   if (rows < 0 || cols < 0 || ldx < cols || ldct < rows) return KSD8_ERR_SHAPE;
   if ((rows > 0 && cols > 0) && (!x || !codes_t || !scales_t)) return KSD8_ERR_ARG;
   return finish(ksd8_quantize_cols_launch(x, x_dtype, x_scales, x_group, rows, cols, ldx, flags,
-                                          codes_t, ldct, scales_t, S(stream)));
+                                          codes_t, ldct, scales_t, status, S(stream)));
 }
 
 int ksd8_w8a8_gemm(const int8_t* a, const void* a_scales, const int8_t* w, const void* w_scales,

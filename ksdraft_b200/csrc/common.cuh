@@ -139,11 +139,37 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (this CTA), completion counted on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_load_g2s(void* smem_dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Orders this thread's generic-proxy accesses of shared memory before later
 // async-proxy (TMA) accesses of the same bytes (a buffer refilled by TMA
 // after threads read or wrote it).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Host: SM count of the current device (cached per device).
+static inline int current_sm_count() {
+  static int n[32] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 32) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    n[dev] = v;
+  }
+  return n[dev];
 }
 
 // Host: cuTensorMapEncodeTiled through the runtime's driver entry point
@@ -297,6 +323,13 @@ __device__ __forceinline__ float gs_scale(float amax, __half* out_h) {
   __half h = __float2half_rn(s);
   if (out_h) *out_h = h;
   return __half2float(h);
+}
+
+// max that propagates NaN (a NaN distance sends the value to the exact path).
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 
 // Symmetric int8 code: round-half-even(x / scale), saturated to [-127, 127].

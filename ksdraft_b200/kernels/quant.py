@@ -7,8 +7,12 @@ Contract (ksdraft/kernels/quant.py:1-14, kept unchanged):
 - a last dimension that is not a multiple of 128 is zero-padded to the next
   group; the returned codes keep the original length.
 
-`quantize_last_dim` runs the `ksd8_quantize_rows` kernel (one warp per
-row-group).  There is no CPU path: non-CUDA inputs raise.
+`quantize_last_dim` runs `ksd8_quantize_rows`: contiguous rows of whole
+groups stream through shared memory by cp.async.bulk, anything else takes the
+thread-load kernel (one warp per row-group); `quantize_cols` stages 128 x 128
+tiles by TMA when the rows are 16-byte aligned.  `plain_loads=True` forces the
+thread-load kernels (identical results; the tests compare the two).  There is
+no CPU path: non-CUDA inputs raise.
 """
 
 from __future__ import annotations
@@ -45,11 +49,12 @@ def _rows_view(x: torch.Tensor) -> torch.Tensor:
 
 def quantize_rows_into(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, *,
                        round_f16: bool = False, dither: float = 0.0, seed: int = 0,
-                       offset: int = 0) -> None:
+                       offset: int = 0, plain_loads: bool = False) -> None:
     """Quantise the rows of a 2-D CUDA tensor into preallocated codes/scales."""
     _lib.require_cuda(x, codes, scales)
     R, K = x.shape
-    flags = (_lib.Q_ROUND_F16 if round_f16 else 0) | (_lib.Q_DITHER if dither > 0 else 0)
+    flags = (_lib.Q_ROUND_F16 if round_f16 else 0) | (_lib.Q_DITHER if dither > 0 else 0) | \
+        (_lib.Q_PLAIN_LOADS if plain_loads else 0)
     rc = _lib.lib().ksd8_quantize_rows(
         x.data_ptr(), _lib.dtype_code(x), R, K, x.stride(0) if R > 1 else K, GROUP_SIZE, flags,
         float(dither), seed & (2**64 - 1), offset & (2**64 - 1), codes.data_ptr(),
@@ -102,8 +107,8 @@ def dequantize_last_dim(codes: torch.Tensor, scales: torch.Tensor,
 
 
 def quantize_cols(x: torch.Tensor, *, x_scales: torch.Tensor | None = None,
-                  x_group: int = GROUP_SIZE, round_f16: bool = False
-                  ) -> tuple[torch.Tensor, torch.Tensor]:
+                  x_group: int = GROUP_SIZE, round_f16: bool = False,
+                  plain_loads: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
     """quantize_last_dim(x.t().contiguous()) in one pass, x 2-D (R, C).
 
     With int8 `x` and its `x_scales`, x is first dequantised (code * scale),
@@ -118,7 +123,8 @@ def quantize_cols(x: torch.Tensor, *, x_scales: torch.Tensor | None = None,
     scales = torch.empty(C, G, dtype=SCALE_DTYPE, device=x.device)
     rc = _lib.lib().ksd8_quantize_cols(
         x.data_ptr(), _lib.dtype_code(x), _lib.ptr(x_scales), x_group, R, C,
-        x.stride(0) if R > 1 else C, GROUP_SIZE, _lib.Q_ROUND_F16 if round_f16 else 0,
+        x.stride(0) if R > 1 else C, GROUP_SIZE,
+        (_lib.Q_ROUND_F16 if round_f16 else 0) | (_lib.Q_PLAIN_LOADS if plain_loads else 0),
         codes.data_ptr(), R, scales.data_ptr(), None, _lib.stream_ptr(x.device))
     _lib.check(rc, "quantize_cols")
     return codes, scales
