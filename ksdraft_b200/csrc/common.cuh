@@ -31,6 +31,9 @@ static inline int ksd8_persistent_ctas(int sm_count) {
 #ifndef KSD8_WAIT_NS
 #define KSD8_WAIT_NS 2000000000ull  // 2 s of global-timer time per wait
 #endif
+#ifndef KSD8_WAIT_BACKOFF_NS
+#define KSD8_WAIT_BACKOFF_NS 0      // optional __nanosleep between polls of a bounded wait
+#endif
 
 namespace ksd8 {
 
@@ -111,6 +114,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   uint32_t n = 0;
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, KSD8_SUSPEND_NS)) return true;
+    if (KSD8_WAIT_BACKOFF_NS) __nanosleep(KSD8_WAIT_BACKOFF_NS);
     if ((++n & 15u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > KSD8_WAIT_NS) {
@@ -148,6 +152,26 @@ __device__ __forceinline__ void bulk_load_g2s(void* smem_dst, const void* src, u
       ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
       "r"(smem_u32(bar))
       : "memory");
+}
+
+// 2D tiled TMA store shared (this CTA) -> global, tracked by the issuing
+// thread's bulk async-group.  Elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src,
+                                             int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// The issuing thread's committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// ... and have completed (global writes performed).
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // Orders this thread's generic-proxy accesses of shared memory before later

@@ -47,6 +47,7 @@ struct GemmArgs {
   long long ldo;
   int out_dtype;
   int epi_flags;
+  int tma_out;  // output tile staged in shared memory and written by TMA stores
 };
 
 constexpr int BM = 128;
@@ -56,7 +57,32 @@ constexpr int SBATCH = 4;  // groups of scales fetched per round by each scale w
 constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
 
-template <int BN, int EPI_WARPS, int STAGES, int CG>
+// fp16 pair of v, branch-free: with `clamp`, +-inf saturates to +-65504 (NaN
+// kept, as the reference's clamp of the fp16 tensor); `bad` collects an inf or
+// NaN half whose column is inside the output (lo_ok / hi_ok).
+__device__ __forceinline__ uint32_t h2_checked(float2 v, bool clamp, bool lo_ok, bool hi_ok,
+                                               bool& bad) {
+  __half2 h = __float22half2_rn(v);
+  if (clamp)
+    h = __hmin2_nan(__hmax2_nan(h, __float2half2_rn(-65504.f)), __float2half2_rn(65504.f));
+  const uint32_t b = *reinterpret_cast<uint32_t*>(&h);
+  bad |= (((b & 0x7C00u) == 0x7C00u) & lo_ok) | (((b & 0x7C000000u) == 0x7C000000u) & hi_ok);
+  return b;
+}
+
+// Output staging (scaled output, one CTA per 128 x 128 tile): the tile in the
+// output type as 128-byte-wide column boxes (4 of 32 fp32 columns or 2 of 64
+// fp16 / bf16 columns) with the 128-byte swizzle.  Each epilogue warp owns a
+// 32-row x CPT-column region and writes it with its own TMA stores (boxes of
+// 32 rows), so no barrier is shared across warps.
+template <int BN, bool PARTIALS, int CG>
+struct OutStage {
+  static constexpr bool on = !PARTIALS && CG == 1 && BN == 128;
+  static constexpr int BYTES = on ? BM * BN * 4 : 0;  // sized for fp32
+  static constexpr int BOX_BYTES = BM * 128;
+};
+
+template <int BN, int EPI_WARPS, int STAGES, int CG, bool PARTIALS = false>
 struct GemmSmem {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = (BN / CG) * BK;  // a CTA pair splits W's rows
@@ -64,7 +90,8 @@ struct GemmSmem {
   static constexpr int SCALE_FLOATS = BM + BN;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = STAGES * A_BYTES;
-  static constexpr int OFF_SCALE = STAGES * STAGE_BYTES;
+  static constexpr int OFF_OUT = STAGES * STAGE_BYTES;  // 1024-byte aligned (swizzle)
+  static constexpr int OFF_SCALE = OFF_OUT + OutStage<BN, PARTIALS, CG>::BYTES;
   static constexpr int OFF_BAR = OFF_SCALE + SRING * SCALE_FLOATS * 4;
   static constexpr int NBUF = 512 / BN < 4 ? 512 / BN : 4;  // TMEM accumulator buffers
   static constexpr int N_BARS = 2 * STAGES + 2 * NBUF + 2 * SRING;
@@ -116,10 +143,16 @@ struct RegSplit {
   static constexpr bool on = false;
   static constexpr int launch = 0, role = 0, epi = 0;
 };
+#ifndef KSD8_RS384_ROLE
+#define KSD8_RS384_ROLE 88
+#endif
+#ifndef KSD8_RS384_EPI
+#define KSD8_RS384_EPI 208
+#endif
 template <>
 struct RegSplit<384> {
   static constexpr bool on = true;
-  static constexpr int launch = 168, role = 88, epi = 208;
+  static constexpr int launch = 168, role = KSD8_RS384_ROLE, epi = KSD8_RS384_EPI;
 };
 template <>
 struct RegSplit<640> {
@@ -134,8 +167,9 @@ static_assert(128 * RegSplit<640>::role + 512 * RegSplit<640>::epi <= 640 * RegS
 template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS, int CG>
 __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                     const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
-  using L = GemmSmem<BN, EPI_WARPS, STAGES, CG>;
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+  using L = GemmSmem<BN, EPI_WARPS, STAGES, CG, PARTIALS>;
   static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per MMA");
   using RS = RegSplit<(4 + EPI_WARPS) * 32>;
   constexpr bool REGSPLIT = RS::on;
@@ -166,6 +200,8 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   uint64_t* acc_empty = bars + 2 * STAGES + NBUF;
   uint64_t* s_full = bars + 2 * STAGES + 2 * NBUF;
   uint64_t* s_empty = bars + 2 * STAGES + 2 * NBUF + SRING;
+  using OS = OutStage<BN, PARTIALS, CG>;
+  uint8_t* sOut = smem + L::OFF_OUT;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
@@ -204,6 +240,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (OS::on && args.tma_out) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     if constexpr (CG == 2) {
@@ -372,6 +409,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     float2 acc[CPT / 2];
     bool ok = true;
     int gg = 0;
+    int kt = 0;  // tiles of this CTA written so far (staging-buffer phase)
     for (int tile = unit; ok && tile < n_tiles; tile += n_units) {
       const int m0 = (tile % tiles_m) * BM * CG + rank * BM, n0 = (tile / tiles_m) * BN;
 #pragma unroll
@@ -480,6 +518,89 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
         }
       }
 
+      if constexpr (OS::on) {
+        if (args.tma_out) {
+          // Staged output: bias / FP16 handoff / clamp in registers, the tile
+          // into shared memory (128-byte swizzle: row r's 16-byte chunk c at
+          // c ^ (r & 7), conflict-free across a warp's 32 rows), then TMA
+          // stores issued by one thread while the other warps go on with the
+          // next tile's groups.
+          const int m = m0 + row;
+          const int nb = n0 + col0;
+          const bool row_ok = m < args.M;
+          // this warp's stores of the previous tile have read its region
+          if (kt > 0 && lane == 0) bulk_wait_group_read0();
+          __syncwarp();
+          {
+            if ((args.epi_flags & KSD8_EPI_BIAS) && args.bias) {
+#pragma unroll
+              for (int i = 0; i < CPT / 2; ++i) {
+                const int n = nb + 2 * i;
+                acc[i].x = __fadd_rn(acc[i].x, n < args.N ? args.bias[n] : 0.f);
+                acc[i].y = __fadd_rn(acc[i].y, n + 1 < args.N ? args.bias[n + 1] : 0.f);
+              }
+            }
+            bool bad = false;
+            uint8_t* orow = sOut + row * 128;
+            const int sw = row & 7;
+            if (args.out_dtype == KSD8_F32) {
+              if (args.epi_flags & KSD8_EPI_ROUND_F16) {  // FP16 gradient handoff
+#pragma unroll
+                for (int i = 0; i < CPT / 2; ++i) {
+                  const int n = nb + 2 * i;
+                  const uint32_t hb = h2_checked(acc[i], false, row_ok & (n < args.N),
+                                                 row_ok & (n + 1 < args.N), bad);
+                  acc[i] = __half22float2(*reinterpret_cast<const __half2*>(&hb));
+                }
+              }
+#pragma unroll
+              for (int q = 0; q < CPT / 4; ++q) {
+                const int cgi = col0 / 4 + q;  // 16-byte chunk within the tile row
+                *reinterpret_cast<float4*>(orow + (cgi >> 3) * OS::BOX_BYTES +
+                                           (((cgi & 7) ^ sw) << 4)) =
+                    make_float4(acc[2 * q].x, acc[2 * q].y, acc[2 * q + 1].x, acc[2 * q + 1].y);
+              }
+            } else {
+              const bool f16 = args.out_dtype == KSD8_F16;
+              const bool clamp = f16 && (args.epi_flags & KSD8_EPI_CLAMP_F16);
+#pragma unroll
+              for (int q = 0; q < CPT / 8; ++q) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const float2 v = acc[4 * q + u];
+                  if (f16) {
+                    const int n = nb + 2 * (4 * q + u);
+                    pk[u] = h2_checked(v, clamp, row_ok & (n < args.N), row_ok & (n + 1 < args.N),
+                                       bad);
+                  } else {
+                    const __nv_bfloat162 h = __float22bfloat162_rn(v);
+                    pk[u] = *reinterpret_cast<const uint32_t*>(&h);
+                  }
+                }
+                const int cgi = col0 / 8 + q;
+                *reinterpret_cast<uint4*>(orow + (cgi >> 3) * OS::BOX_BYTES +
+                                          (((cgi & 7) ^ sw) << 4)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              }
+            }
+            if (bad && (args.epi_flags & KSD8_EPI_FLAG_NONFINITE))
+              record_error(args.status, KSD8_ERR_NONFINITE);
+          }
+          fence_proxy_async_smem();  // generic writes before the TMA engine reads them
+          __syncwarp();
+          if (lane == 0) {
+            const int esz = args.out_dtype == KSD8_F32 ? 4 : 2;
+            const int bx0 = col0 * esz / 128;
+            for (int bx = bx0; bx < bx0 + CPT * esz / 128; ++bx)
+              tma_store_2d(&tmC, sOut + bx * OS::BOX_BYTES + quad * 32 * 128,
+                           n0 + bx * (128 / esz), m0 + quad * 32);
+            bulk_commit_group();
+          }
+          ++kt;
+          continue;
+        }
+      }
       if constexpr (!PARTIALS) {
         const int m = m0 + row;
         if (ok && m < args.M) {
@@ -498,11 +619,9 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
             bool bad = false;
 #pragma unroll
             for (int i = 0; i < CPT / 2; ++i) {
-              const __half2 h = __float22half2_rn(acc[i]);
               const int n = nb + 2 * i;
-              bad |= (n < args.N) && (__hisinf(__low2half(h)) || __hisnan(__low2half(h)));
-              bad |= (n + 1 < args.N) && (__hisinf(__high2half(h)) || __hisnan(__high2half(h)));
-              acc[i] = __half22float2(h);
+              const uint32_t hb = h2_checked(acc[i], false, n < args.N, n + 1 < args.N, bad);
+              acc[i] = __half22float2(*reinterpret_cast<const __half2*>(&hb));
             }
             if (bad && (args.epi_flags & KSD8_EPI_FLAG_NONFINITE))
               record_error(args.status, KSD8_ERR_NONFINITE);
@@ -555,19 +674,8 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
               uint32_t pk[4];
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
-                __half2 h = __float22half2_rn(acc[i + u]);
-                if (clamp) {
-                  if (__hisinf(__low2half(h)))
-                    h = __halves2half2(__float2half_rn(acc[i + u].x > 0.f ? 65504.f : -65504.f),
-                                       __high2half(h));
-                  if (__hisinf(__high2half(h)))
-                    h = __halves2half2(__low2half(h),
-                                       __float2half_rn(acc[i + u].y > 0.f ? 65504.f : -65504.f));
-                }
                 const int n = nb + 2 * (i + u);
-                bad |= (n < args.N) && (__hisinf(__low2half(h)) || __hisnan(__low2half(h)));
-                bad |= (n + 1 < args.N) && (__hisinf(__high2half(h)) || __hisnan(__high2half(h)));
-                pk[u] = *reinterpret_cast<uint32_t*>(&h);
+                pk[u] = h2_checked(acc[i + u], clamp, n < args.N, n + 1 < args.N, bad);
               }
               if (vec) {
                 *reinterpret_cast<uint4*>(o + 2 * i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -589,6 +697,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     }
   }
 
+  if (OS::on && args.tma_out && warp >= 4 && lane == 0) bulk_wait_group0();  // staged stores done
   tc_fence_before();
   if constexpr (CG == 2) cluster_sync();  // the leader's MMAs read the peer's shared memory
   else __syncthreads();
@@ -630,10 +739,30 @@ static int sm_count_cached() {
   return n[dev];
 }
 
+// Output (m, n) row stride ldo in the output dtype, as 128-byte-wide boxes of
+// 32 rows with the 128-byte swizzle (the staging layout of the epilogue).
+static bool make_tmap_out(CUtensorMap* map, void* ptr, int dtype, int64_t m, int64_t n,
+                          int64_t ldo) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return false;
+  const int esz = dtype == KSD8_F32 ? 4 : 2;
+  const CUtensorMapDataType dt = dtype == KSD8_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == KSD8_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ldo * esz) % 16) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
+  cuuint64_t strides[1] = {(cuuint64_t)(ldo * esz)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esz), 32u};  // one epilogue warp's rows
+  cuuint32_t estr[2] = {1u, 1u};
+  return enc(map, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int EPI_WARPS, int STAGES, bool PARTIALS, int CG>
 static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t k,
                        cudaStream_t stream) {
-  using L = GemmSmem<BN, EPI_WARPS, STAGES, CG>;
+  using L = GemmSmem<BN, EPI_WARPS, STAGES, CG, PARTIALS>;
   auto kern = w8a8_gemm_kernel<BN, EPI_WARPS, STAGES, PARTIALS, CG>;
   static unsigned attr_dev_mask = 0;  // per-device opt-in to > 48 KB of shared memory
   int dev = 0;
@@ -644,9 +773,12 @@ static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t 
       return KSD8_ERR_LAUNCH;
     attr_dev_mask |= (1u << dev);
   }
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   if (!make_tmap_i8(&ta, a, args.M, k, BM)) return KSD8_ERR_LAUNCH;
   if (!make_tmap_i8(&tb, w, args.N, k, BN / CG)) return KSD8_ERR_LAUNCH;
+  memset(&tc, 0, sizeof(tc));
+  args.tma_out = OutStage<BN, PARTIALS, CG>::on &&
+                 make_tmap_out(&tc, args.out, args.out_dtype, args.M, args.N, args.ldo);
   const int tiles = ((args.M + BM * CG - 1) / (BM * CG)) * ((args.N + BN - 1) / BN);
   const int sms = ksd8_persistent_ctas(sm_count_cached());
   const int units = sms / CG;
@@ -675,9 +807,9 @@ static int launch_gemm(const int8_t* a, const int8_t* w, GemmArgs args, int64_t 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, ta, tb, args) != cudaSuccess) return KSD8_ERR_LAUNCH;
+    if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, args) != cudaSuccess) return KSD8_ERR_LAUNCH;
   } else {
-    kern<<<grid, (4 + EPI_WARPS) * 32, L::ALLOC, stream>>>(ta, tb, args);
+    kern<<<grid, (4 + EPI_WARPS) * 32, L::ALLOC, stream>>>(ta, tb, tc, args);
   }
   return KSD8_OK;
 }

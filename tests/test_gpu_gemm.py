@@ -171,3 +171,19 @@ def test_int8_linear_ste_grads():
     y.square().mean().backward()
     assert x.grad is not None and torch.isfinite(x.grad).all()
     assert lin.weight.grad is not None and torch.isfinite(lin.weight.grad).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(70, 13, 256), (129, 201, 384), (300, 136, 128)])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_gemm_staged_and_direct_output_paths(oracle, M, N, K, out_dtype):
+    """Rows whose byte length is not a multiple of 16 take the direct-store
+    epilogue, the others the shared-memory staged TMA stores (ragged edges
+    clipped); both give the canonical bits in every output dtype."""
+    from ksdraft_b200.kernels.gemm import gemm_out
+    rng = np.random.default_rng(M + N + K)
+    ac, as_ = _q(oracle, rng.standard_normal((M, K)).astype(np.float32))
+    wc, ws = _q(oracle, (rng.standard_normal((N, K)) * 0.05).astype(np.float32))
+    y = gemm_out(ac, as_, wc, ws, out_dtype=out_dtype).cpu()
+    y_can = torch.from_numpy(oracle.w8a8_gemm_canonical(
+        ac.cpu().numpy(), as_.cpu().numpy(), wc.cpu().numpy(), ws.cpu().numpy()))
+    assert torch.equal(y, y_can.to(out_dtype))
