@@ -60,13 +60,14 @@ constexpr float MAGIC_F = 12582912.0f;
 // fp16 pair of v, branch-free: with `clamp`, +-inf saturates to +-65504 (NaN
 // kept, as the reference's clamp of the fp16 tensor); `bad` collects an inf or
 // NaN half whose column is inside the output (lo_ok / hi_ok).
-__device__ __forceinline__ uint32_t h2_checked(float2 v, bool clamp, bool lo_ok, bool hi_ok,
-                                               bool& bad) {
+__device__ __forceinline__ uint32_t h2_checked(float2 v, bool clamp, bool check, bool lo_ok,
+                                               bool hi_ok, bool& bad) {
   __half2 h = __float22half2_rn(v);
   if (clamp)
     h = __hmin2_nan(__hmax2_nan(h, __float2half2_rn(-65504.f)), __float2half2_rn(65504.f));
   const uint32_t b = *reinterpret_cast<uint32_t*>(&h);
-  bad |= (((b & 0x7C00u) == 0x7C00u) & lo_ok) | (((b & 0x7C000000u) == 0x7C000000u) & hi_ok);
+  if (check)  // only when the caller asked for the non-finite flag
+    bad |= (((b & 0x7C00u) == 0x7C00u) & lo_ok) | (((b & 0x7C000000u) == 0x7C000000u) & hi_ok);
   return b;
 }
 
@@ -541,6 +542,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
               }
             }
             bool bad = false;
+            const bool check = (args.epi_flags & KSD8_EPI_FLAG_NONFINITE) != 0;
             uint8_t* orow = sOut + row * 128;
             const int sw = row & 7;
             if (args.out_dtype == KSD8_F32) {
@@ -548,7 +550,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
 #pragma unroll
                 for (int i = 0; i < CPT / 2; ++i) {
                   const int n = nb + 2 * i;
-                  const uint32_t hb = h2_checked(acc[i], false, row_ok & (n < args.N),
+                  const uint32_t hb = h2_checked(acc[i], false, check, row_ok & (n < args.N),
                                                  row_ok & (n + 1 < args.N), bad);
                   acc[i] = __half22float2(*reinterpret_cast<const __half2*>(&hb));
                 }
@@ -571,7 +573,8 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
                   const float2 v = acc[4 * q + u];
                   if (f16) {
                     const int n = nb + 2 * (4 * q + u);
-                    pk[u] = h2_checked(v, clamp, row_ok & (n < args.N), row_ok & (n + 1 < args.N),
+                    pk[u] = h2_checked(v, clamp, check, row_ok & (n < args.N),
+                                       row_ok & (n + 1 < args.N),
                                        bad);
                   } else {
                     const __nv_bfloat162 h = __float22bfloat162_rn(v);
@@ -617,10 +620,11 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
           if (args.out_dtype == KSD8_F32 && (args.epi_flags & KSD8_EPI_ROUND_F16)) {
             // FP16 gradient handoff into an fp32 buffer: store float(fp16(acc))
             bool bad = false;
+            const bool check = (args.epi_flags & KSD8_EPI_FLAG_NONFINITE) != 0;
 #pragma unroll
             for (int i = 0; i < CPT / 2; ++i) {
               const int n = nb + 2 * i;
-              const uint32_t hb = h2_checked(acc[i], false, n < args.N, n + 1 < args.N, bad);
+              const uint32_t hb = h2_checked(acc[i], false, check, n < args.N, n + 1 < args.N, bad);
               acc[i] = __half22float2(*reinterpret_cast<const __half2*>(&hb));
             }
             if (bad && (args.epi_flags & KSD8_EPI_FLAG_NONFINITE))
@@ -668,6 +672,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
             __half* o = reinterpret_cast<__half*>(args.out) + (size_t)m * args.ldo + nb;
             const bool clamp = args.epi_flags & KSD8_EPI_CLAMP_F16;
             bool bad = false;
+            const bool check = (args.epi_flags & KSD8_EPI_FLAG_NONFINITE) != 0;
             const bool vec = full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
 #pragma unroll
             for (int i = 0; i < CPT / 2; i += 4) {
@@ -675,7 +680,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 const int n = nb + 2 * (i + u);
-                pk[u] = h2_checked(acc[i + u], clamp, n < args.N, n + 1 < args.N, bad);
+                pk[u] = h2_checked(acc[i + u], clamp, check, n < args.N, n + 1 < args.N, bad);
               }
               if (vec) {
                 *reinterpret_cast<uint4*>(o + 2 * i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
