@@ -387,6 +387,13 @@ def run_profile_case(case: str, iters: int) -> None:
     elif case == "quant":
         x = torch.randn(TOKENS, CHARTS, device=dev, generator=g)
         fn = lambda: quantize_last_dim(x)  # noqa: E731
+    elif case == "quant_dither":
+        # the master weight of the down projection, PTQR dither 0.5 (forward re-pack)
+        from ksdraft_b200.kernels.quant import quantize_rows_into
+        w = torch.randn(CHARTS, D_MODEL, device=dev, generator=g) * 0.02
+        wc = torch.empty(CHARTS, D_MODEL, dtype=torch.int8, device=dev)
+        ws = torch.empty(CHARTS, D_MODEL // 128, dtype=torch.float16, device=dev)
+        fn = lambda: quantize_rows_into(w, wc, ws, dither=0.5, seed=1)  # noqa: E731
     elif case == "quant_cols":
         x = torch.randn(TOKENS, CHARTS, device=dev, generator=g).to(torch.bfloat16)
         fn = lambda: quantize_cols(x)  # noqa: E731
@@ -475,7 +482,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", default=None,
-                    help="run one kernel (gemm | quant | quant_cols) a few times, for ncu")
+                    help="run one kernel (gemm | quant | quant_dither | quant_cols | requant_t | "
+                         "spine | vjp | head | rosa) a few times, for ncu")
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
     if args.profile_case:
