@@ -28,6 +28,7 @@
  *   ksd8_ks3_spine_table      the (chart, LUT index)-only part of ks3_int8.py:206-227
  *   ksd8_ks3_vjp              ksdraft/kernels/ks3_int8.py:354-410 (geometry VJP, dc, its two quantisations)
  *   ksd8_ks3_vjp_reduce       ksdraft/kernels/ks3_int8.py:381-395 (column reductions, STE factors)
+ *   ksd8_ks3_vjp_reduce_f32   the same, fp32 outputs (handoff values for the masters' grads)
  *   ksd8_rosa_pack_bits       ksdraft/model/rosa.py:156-158 (bits = proj > 0) and the int8 bit inputs
  *                             of rosa.py:40 _match_payload_sign
  *   ksd8_rosa_match           ksdraft/model/rosa.py:40-98 _match_payload_sign (+ payload multiply of :164)
@@ -188,6 +189,14 @@ int ksd8_ks3_vjp(const void* value, const void* coords, int64_t m, int64_t chart
 int ksd8_ks3_vjp_reduce(const float* partials, int64_t n_tiles, int64_t charts,
                         const float* raw_scale, const float* raw_shift, void* dcoeff16,
                         void* dscale16, void* dshift16, int* status, void* stream);
+
+/* ksd8_ks3_vjp_reduce with fp32 outputs holding float(fp16 value): the
+ * gradients as the fp32 masters receive them after the FP16 handoff
+ * (ks3_int8.py:426-429), written straight into a training step's gradient
+ * buffer.  Same status behaviour. */
+int ksd8_ks3_vjp_reduce_f32(const float* partials, int64_t n_tiles, int64_t charts,
+                            const float* raw_scale, const float* raw_shift, float* dcoeff32,
+                            float* dscale32, float* dshift32, int* status, void* stream);
 
 /* Pack Rosa symbol bits: bit(stream, t) = x[b*sb + t*st + s*ss] > 0 with
  * stream = b*S + s, into words (streams, ceil(T/64)) uint64, bit t%64 of

@@ -25,7 +25,7 @@ int ksd8_ks3_vjp_launch(const void*, const void*, int64_t, int64_t, const int8_t
                         const int8_t*, const void*, const int8_t*, const void*, int8_t*, void*,
                         int8_t*, void*, float*, int*, cudaStream_t);
 int ksd8_ks3_vjp_reduce_launch(const float*, int64_t, int64_t, const float*, const float*, void*,
-                               void*, void*, int*, cudaStream_t);
+                               void*, void*, int*, cudaStream_t, float*, float*, float*);
 int ksd8_rosa_pack_bits_launch(const void*, int, int64_t, int64_t, int64_t, int64_t, int64_t,
                                int64_t, uint64_t*, cudaStream_t);
 int ksd8_rosa_match_launch(const uint64_t*, const uint64_t*, const uint64_t*, int64_t, int64_t,
@@ -238,7 +238,20 @@ int ksd8_ks3_vjp_reduce(const float* partials, int64_t n_tiles, int64_t charts,
                      !dshift16))
     return KSD8_ERR_ARG;
   return finish(ksd8_ks3_vjp_reduce_launch(partials, n_tiles, charts, raw_scale, raw_shift,
-                                           dcoeff16, dscale16, dshift16, status, S(stream)));
+                                           dcoeff16, dscale16, dshift16, status, S(stream),
+                                           nullptr, nullptr, nullptr));
+}
+
+int ksd8_ks3_vjp_reduce_f32(const float* partials, int64_t n_tiles, int64_t charts,
+                            const float* raw_scale, const float* raw_shift, float* dcoeff32,
+                            float* dscale32, float* dshift32, int* status, void* stream) {
+  if (n_tiles < 0 || charts < 0) return KSD8_ERR_SHAPE;
+  if (charts > 0 && (!partials || !raw_scale || !raw_shift || !dcoeff32 || !dscale32 ||
+                     !dshift32))
+    return KSD8_ERR_ARG;
+  return finish(ksd8_ks3_vjp_reduce_launch(partials, n_tiles, charts, raw_scale, raw_shift,
+                                           nullptr, nullptr, nullptr, status, S(stream),
+                                           dcoeff32, dscale32, dshift32));
 }
 
 int ksd8_rosa_pack_bits(const void* x, int x_dtype, int64_t batch, int64_t t_len,
@@ -434,5 +447,6 @@ extern "C" int ksd8_ks3_vjp_static(const void* value, const void* coords, int64_
                                   partials, status, S(stream)));
   if (rc != KSD8_OK) return rc;
   return finish(ksd8_ks3_vjp_reduce_launch(partials, n_tiles, charts, raw_scale, raw_shift,
-                                           dcoeff16, dscale16, dshift16, status, S(stream)));
+                                           dcoeff16, dscale16, dshift16, status, S(stream),
+                                           nullptr, nullptr, nullptr));
 }

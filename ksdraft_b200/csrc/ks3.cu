@@ -788,7 +788,8 @@ constexpr int VRED_CHARTS = 32;
 __global__ void __launch_bounds__(VRED_CHARTS * 8)
     ks3_vjp_reduce_kernel(const float* partials, int64_t n_tiles, int64_t charts,
                           const float* raw_scale, const float* raw_shift, __half* dcoeff,
-                          __half* dscale, __half* dshift, int* status) {
+                          __half* dscale, __half* dshift, float* dcoeff32, float* dscale32,
+                          float* dshift32, int* status) {
   __shared__ float sums[8][VRED_CHARTS];
   const int lc = threadIdx.x % VRED_CHARTS, k = threadIdx.x / VRED_CHARTS;
   const int64_t c = (int64_t)blockIdx.x * VRED_CHARTS + lc;
@@ -817,7 +818,8 @@ __global__ void __launch_bounds__(VRED_CHARTS * 8)
   for (int q = 0; q < 6; ++q) {
     const __half h = __float2half_rn(s[q]);
     bad |= __hisinf(h) || __hisnan(h);
-    dcoeff[c * 6 + q] = h;
+    if (dcoeff32) dcoeff32[c * 6 + q] = __half2float(h);
+    else dcoeff[c * 6 + q] = h;
   }
   const float sig = 1.f / (1.f + expf(-raw_scale[c]));
   const float th = tanhf(raw_shift[c]);
@@ -826,8 +828,13 @@ __global__ void __launch_bounds__(VRED_CHARTS * 8)
   const __half ds = __float2half_rn(__fmul_rn(dscale_t, sig));
   const __half dh = __float2half_rn(__fmul_rn(dshift_t, __fsub_rn(1.f, __fmul_rn(th, th))));
   bad |= __hisinf(ds) || __hisnan(ds) || __hisinf(dh) || __hisnan(dh);
-  dscale[c] = ds;
-  dshift[c] = dh;
+  if (dscale32) {  // the fp16 values as the fp32 masters receive them
+    dscale32[c] = __half2float(ds);
+    dshift32[c] = __half2float(dh);
+  } else {
+    dscale[c] = ds;
+    dshift[c] = dh;
+  }
   if (bad) record_error(status, KSD8_ERR_NONFINITE);
 }
 
@@ -964,11 +971,13 @@ int ksd8_ks3_vjp_launch(const void* value, const void* coords, int64_t m, int64_
 
 int ksd8_ks3_vjp_reduce_launch(const float* partials, int64_t n_tiles, int64_t charts,
                                const float* raw_scale, const float* raw_shift, void* dcoeff16,
-                               void* dscale16, void* dshift16, int* status, cudaStream_t stream) {
+                               void* dscale16, void* dshift16, int* status, cudaStream_t stream,
+                               float* dcoeff32, float* dscale32, float* dshift32) {
   if (charts == 0) return KSD8_OK;
   ks3_vjp_reduce_kernel<<<(unsigned)((charts + VRED_CHARTS - 1) / VRED_CHARTS), VRED_CHARTS * 8,
                           0, stream>>>(
       partials, n_tiles, charts, raw_scale, raw_shift, reinterpret_cast<__half*>(dcoeff16),
-      reinterpret_cast<__half*>(dscale16), reinterpret_cast<__half*>(dshift16), status);
+      reinterpret_cast<__half*>(dscale16), reinterpret_cast<__half*>(dshift16), dcoeff32,
+      dscale32, dshift32, status);
   return KSD8_OK;
 }

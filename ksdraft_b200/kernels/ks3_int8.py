@@ -349,22 +349,27 @@ def ks3_backward(cell, grad_out, xq, xs, hq, hs, coords, input_shape, check_hand
                           cell.warp_shift_scales.data_ptr(), dcq.data_ptr(), dcs.data_ptr(),
                           dctq.data_ptr(), dcts.data_ptr(), partials.data_ptr(), None, stream)
     _lib.check(rc, "ks3_vjp")
-    dcoeff = torch.empty(C, cell.subspace_rank, 6, dtype=FP16, device=dev)
-    dscale = torch.empty(C, dtype=FP16, device=dev)
-    dshift = torch.empty(C, dtype=FP16, device=dev)
     raw_scale = cell.warp_scale_raw.float().contiguous()
     raw_shift = cell.warp_shift_raw.float().contiguous()
-    rc = lib.ksd8_ks3_vjp_reduce(partials.data_ptr(), n_tiles, C, raw_scale.data_ptr(),
-                                 raw_shift.data_ptr(), dcoeff.data_ptr(), dscale.data_ptr(),
-                                 dshift.data_ptr(), flags[0:1].data_ptr(), stream)
-    _lib.check(rc, "ks3_vjp_reduce")
     if grads_into is not None:
         # dcoeff / dscale / dshift are fp16 already in the reference (:387-394):
-        # the handoff hands them over unchanged, the masters see float(fp16)
-        grads_into["coefficients"].copy_(dcoeff.view_as(grads_into["coefficients"]))
-        grads_into["raw_scale"].copy_(dscale.view_as(grads_into["raw_scale"]))
-        grads_into["raw_shift"].copy_(dshift.view_as(grads_into["raw_shift"]))
+        # the handoff hands them over unchanged and the masters see float(fp16),
+        # which the reduction writes straight into the gradient buffer
+        outs = [grads_into[n] for n in ("coefficients", "raw_scale", "raw_shift")]
+        assert all(t.is_contiguous() and t.dtype == torch.float32 for t in outs)
+        rc = lib.ksd8_ks3_vjp_reduce_f32(partials.data_ptr(), n_tiles, C, raw_scale.data_ptr(),
+                                         raw_shift.data_ptr(), *(t.data_ptr() for t in outs),
+                                         flags[0:1].data_ptr(), stream)
+        _lib.check(rc, "ks3_vjp_reduce_f32")
         notify(("coefficients", "raw_scale", "raw_shift"))
+    else:
+        dcoeff = torch.empty(C, cell.subspace_rank, 6, dtype=FP16, device=dev)
+        dscale = torch.empty(C, dtype=FP16, device=dev)
+        dshift = torch.empty(C, dtype=FP16, device=dev)
+        rc = lib.ksd8_ks3_vjp_reduce(partials.data_ptr(), n_tiles, C, raw_scale.data_ptr(),
+                                     raw_shift.data_ptr(), dcoeff.data_ptr(), dscale.data_ptr(),
+                                     dshift.data_ptr(), flags[0:1].data_ptr(), stream)
+        _lib.check(rc, "ks3_vjp_reduce")
 
     # ddown = q(dc^T) @ q(x^T)^T, quantised along tokens (ks3_int8.py:417-420)
     xT_q, xT_s = quantize_cols(xq, x_scales=xs, x_group=cell.group)
