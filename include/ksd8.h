@@ -35,6 +35,8 @@
  *   ksd8_rosa_timemix_quantize ksdraft/model/rosa.py:128-133 _shifted followed by the per-token
  *                             quantisation of Int8Linear.forward (ksdraft/kernels/linear.py:69)
  *   ksd8_adamw_step           torch.optim.AdamW.step over fp32 masters (ksdraft/train/__init__.py:166)
+ *   ksd8_adamw_step_scaled    the same after gradient clipping (ksdraft/train/__init__.py:165)
+ *   ksd8_grad_clip_coef       torch.nn.utils.clip_grad_norm_ norm and coefficient (:165)
  */
 #ifndef KSD8_H_
 #define KSD8_H_
@@ -230,6 +232,22 @@ int ksd8_rosa_timemix_quantize(const void* x, int x_dtype, int64_t batch, int64_
 int ksd8_adamw_step(float* param, const void* grad, int grad_dtype, float* exp_avg,
                     float* exp_avg_sq, int64_t n, float lr, float beta1, float beta2, float eps,
                     float weight_decay, int step, int* status, void* stream);
+
+/* The same step with the gradient multiplied by *grad_scale (device memory):
+ * the clip coefficient of ksd8_grad_clip_coef, applied without a host round
+ * trip (torch.nn.utils.clip_grad_norm_ then AdamW, ksdraft/train/__init__.py:165-166). */
+int ksd8_adamw_step_scaled(float* param, const void* grad, int grad_dtype, float* exp_avg,
+                           float* exp_avg_sq, int64_t n, float lr, float beta1, float beta2,
+                           float eps, float weight_decay, int step, const float* grad_scale,
+                           int* status, void* stream);
+
+/* Global L2 norm of n fp32 gradients and torch's clip coefficient:
+ * out[0] = norm, out[1] = min(1, max_norm / (norm + 1e-6))
+ * (torch.nn.utils.clip_grad_norm_, ksdraft/train/__init__.py:165).  scratch:
+ * 592 floats of device memory; the partial sums are added in a fixed order. */
+#define KSD8_GRAD_CLIP_SCRATCH 592
+int ksd8_grad_clip_coef(const float* grad, int64_t n, float max_norm, float* scratch,
+                        float* out, int* status, void* stream);
 
 /* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);

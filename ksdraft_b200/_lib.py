@@ -22,6 +22,7 @@ VJP_STATIC_MAX_PARTIALS = 1 << 21
 
 F32, F16, BF16, I8 = 0, 1, 2, 3
 Q_ROUND_F16, Q_DITHER, Q_PLAIN_LOADS = 1, 2, 8
+GRAD_CLIP_SCRATCH = 592  # KSD8_GRAD_CLIP_SCRATCH
 EPI_CLAMP_F16, EPI_BIAS, EPI_FLAG_NONFINITE, EPI_ROUND_F16, EPI_IF_STATUS = 1, 2, 4, 8, 16
 NL = {"fp32": 0, "fp16": 1, "int8": 2}
 
@@ -52,6 +53,8 @@ SIGNATURES: dict[str, list] = {
     "ksd8_rosa_timemix_quantize": [vp, i32, i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                    vp, vp],
     "ksd8_adamw_step": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp],
+    "ksd8_adamw_step_scaled": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp, vp],
+    "ksd8_grad_clip_coef": [vp, i64, f32, vp, vp, vp, vp],
     "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
     "ksd8_set_sm_reserve": [i32],
     "ksd8_get_sm_reserve": [],

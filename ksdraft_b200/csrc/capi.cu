@@ -44,7 +44,8 @@ int ksd8_ce_grad_quant_launch(const void*, int, int64_t, int64_t, int64_t, const
                               const float*, const float*, float, int8_t*, int64_t, void*, int8_t*,
                               int64_t, void*, cudaStream_t);
 int ksd8_adamw_launch(float*, const void*, int, float*, float*, int64_t, float, float, float,
-                      float, float, int, cudaStream_t);
+                      float, float, int, cudaStream_t, const float*);
+int ksd8_grad_clip_launch(const float*, int64_t, float, float*, float*, cudaStream_t);
 
 static thread_local int g_last_cuda_error = 0;
 
@@ -304,7 +305,29 @@ int ksd8_adamw_step(float* param, const void* grad, int grad_dtype, float* exp_a
   if (step < 1) return KSD8_ERR_ARG;
   if (n > 0 && (!param || !grad || !exp_avg || !exp_avg_sq)) return KSD8_ERR_ARG;
   return finish(ksd8_adamw_launch(param, grad, grad_dtype, exp_avg, exp_avg_sq, n, lr, beta1,
-                                  beta2, eps, weight_decay, step, S(stream)));
+                                  beta2, eps, weight_decay, step, S(stream), nullptr));
+}
+
+int ksd8_adamw_step_scaled(float* param, const void* grad, int grad_dtype, float* exp_avg,
+                           float* exp_avg_sq, int64_t n, float lr, float beta1, float beta2,
+                           float eps, float weight_decay, int step, const float* grad_scale,
+                           int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(grad_dtype)) return KSD8_ERR_DTYPE;
+  if (n < 0) return KSD8_ERR_SHAPE;
+  if (step < 1) return KSD8_ERR_ARG;
+  if (n > 0 && (!param || !grad || !exp_avg || !exp_avg_sq || !grad_scale)) return KSD8_ERR_ARG;
+  return finish(ksd8_adamw_launch(param, grad, grad_dtype, exp_avg, exp_avg_sq, n, lr, beta1,
+                                  beta2, eps, weight_decay, step, S(stream), grad_scale));
+}
+
+int ksd8_grad_clip_coef(const float* grad, int64_t n, float max_norm, float* scratch,
+                        float* out, int* status, void* stream) {
+  (void)status;
+  if (n < 0) return KSD8_ERR_SHAPE;
+  if (!(max_norm > 0.f)) return KSD8_ERR_ARG;
+  if (!scratch || !out || (n > 0 && !grad)) return KSD8_ERR_ARG;
+  return finish(ksd8_grad_clip_launch(grad, n, max_norm, scratch, out, S(stream)));
 }
 
 int ksd8_ce_partials(const void* logits, int dtype, int64_t m, int64_t v_local, int64_t ld,

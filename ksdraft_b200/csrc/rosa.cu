@@ -320,13 +320,17 @@ __global__ void __launch_bounds__(256) rosa_timemix_quant_kernel(TimemixArgs a) 
 
 __global__ void adamw_kernel(float* p, const void* g, int gdt, float* m, float* v, int64_t n,
                              float lr, float b1, float b2, float eps, float wd, float bc1,
-                             float bc2_sqrt) {
+                             float bc2_sqrt, const float* gscale) {
+  // gradient clipping (torch.nn.utils.clip_grad_norm_): grads *= coefficient,
+  // read from device memory so that no host round trip decides it
+  const float gs = gscale ? *gscale : 1.f;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const float gr = gdt == KSD8_F16 ? __half2float(reinterpret_cast<const __half*>(g)[i])
-                     : gdt == KSD8_BF16
-                         ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[i])
-                         : reinterpret_cast<const float*>(g)[i];
+    float gr = gdt == KSD8_F16 ? __half2float(reinterpret_cast<const __half*>(g)[i])
+               : gdt == KSD8_BF16
+                   ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[i])
+                   : reinterpret_cast<const float*>(g)[i];
+    if (gscale) gr = __fmul_rn(gr, gs);
     float pi = p[i] * (1.f - lr * wd);
     const float mi = b1 * m[i] + (1.f - b1) * gr;
     const float vi = b2 * v[i] + (1.f - b2) * gr * gr;
@@ -338,9 +342,65 @@ __global__ void adamw_kernel(float* p, const void* g, int gdt, float* m, float* 
   }
 }
 
+// Sum of squares of n fp32 values: per-block partial sums (fixed tree order)
+// into partials[blockIdx.x].
+constexpr int GN_BLOCKS = 592;  // 4 x 148
+__global__ void __launch_bounds__(256) grad_sumsq_kernel(const float* g, int64_t n,
+                                                         float* partials) {
+  float s = 0.f;
+  const int64_t n4 = (reinterpret_cast<uintptr_t>(g) & 15) == 0 ? n / 4 : 0;
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 q = g4[i];
+    s = fmaf(q.x, q.x, s);
+    s = fmaf(q.y, q.y, s);
+    s = fmaf(q.z, q.z, s);
+    s = fmaf(q.w, q.w, s);
+  }
+  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    s = fmaf(g[i], g[i], s);
+  __shared__ float red[8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    partials[blockIdx.x] = t;
+  }
+}
+
+// One block: norm = sqrt(sum of the partials in block order), clip
+// coefficient = min(1, max_norm / (norm + 1e-6)) as torch's clip_grad_norm_.
+__global__ void __launch_bounds__(32) grad_clip_coef_kernel(const float* partials, int nparts,
+                                                            float max_norm, float* out) {
+  float s = 0.f;
+  for (int i = threadIdx.x; i < nparts; i += 32) s += partials[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (threadIdx.x == 0) {
+    const float norm = sqrtf(s);
+    out[0] = norm;
+    out[1] = fminf(__fdiv_rn(max_norm, __fadd_rn(norm, 1e-6f)), 1.f);
+  }
+}
+
 }  // namespace ksd8
 
 using namespace ksd8;
+
+int ksd8_grad_clip_launch(const float* grad, int64_t n, float max_norm, float* scratch,
+                          float* out, cudaStream_t stream) {
+  int64_t blocks = (n + 1023) / 1024;
+  if (blocks < 1) blocks = 1;
+  if (blocks > GN_BLOCKS) blocks = GN_BLOCKS;
+  grad_sumsq_kernel<<<(unsigned)blocks, 256, 0, stream>>>(grad, n, scratch);
+  grad_clip_coef_kernel<<<1, 32, 0, stream>>>(scratch, (int)blocks, max_norm, out);
+  return KSD8_OK;
+}
 
 int ksd8_rosa_pack_bits_launch(const void* x, int x_dtype, int64_t batch, int64_t t_len,
                                int64_t streams, int64_t sb, int64_t st, int64_t ss,
@@ -447,13 +507,14 @@ int ksd8_rosa_timemix_launch(const void* x, int x_dtype, int64_t batch, int64_t 
 }
 
 int ksd8_adamw_launch(float* p, const void* g, int gdt, float* m, float* v, int64_t n, float lr,
-                      float b1, float b2, float eps, float wd, int step, cudaStream_t stream) {
+                      float b1, float b2, float eps, float wd, int step, cudaStream_t stream,
+                      const float* gscale) {
   if (n == 0) return KSD8_OK;
   const float bc1 = 1.f - powf(b1, (float)step);
   const float bc2 = 1.f - powf(b2, (float)step);
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   adamw_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p, g, gdt, m, v, n, lr, b1, b2, eps, wd, bc1,
-                                                      sqrtf(bc2));
+                                                      sqrtf(bc2), gscale);
   return KSD8_OK;
 }

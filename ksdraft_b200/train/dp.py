@@ -117,20 +117,39 @@ class AdamW:
         self.step_count += 1
 
     @torch.no_grad()
-    def update(self, index: int) -> None:
+    def update(self, index: int, grad_scale: torch.Tensor | None = None) -> None:
         """AdamW on one parameter tensor for the current step (a data-parallel
-        step updates each tensor as soon as its gradient's mean is complete)."""
+        step updates each tensor as soon as its gradient's mean is complete).
+        `grad_scale`: a one-element fp32 device tensor the gradient is
+        multiplied by first (the clip coefficient of clip_grad_norm)."""
         lib = _lib.lib()
         p = self.params[index]
         m, v = self.state[index]
         g = p.grad
         if g is not None:
             g = g.contiguous()
-            rc = lib.ksd8_adamw_step(p.data_ptr(), g.data_ptr(), _lib.dtype_code(g), m.data_ptr(),
-                                     v.data_ptr(), p.numel(), self.lr, self.betas[0],
-                                     self.betas[1], self.eps, self.wd, self.step_count, None,
-                                     _lib.stream_ptr(p.device))
+            args = (p.data_ptr(), g.data_ptr(), _lib.dtype_code(g), m.data_ptr(), v.data_ptr(),
+                    p.numel(), self.lr, self.betas[0], self.betas[1], self.eps, self.wd,
+                    self.step_count)
+            if grad_scale is None:
+                rc = lib.ksd8_adamw_step(*args, None, _lib.stream_ptr(p.device))
+            else:
+                rc = lib.ksd8_adamw_step_scaled(*args, grad_scale.data_ptr(), None,
+                                                _lib.stream_ptr(p.device))
             _lib.check(rc, "adamw_step")
+
+
+def clip_grad_norm(flat: torch.Tensor, max_norm: float, scratch: torch.Tensor,
+                   out: torch.Tensor) -> torch.Tensor:
+    """torch.nn.utils.clip_grad_norm_ over one flat fp32 gradient buffer, on the
+    device: out[0] = total L2 norm, out[1] = min(1, max_norm / (norm + 1e-6)),
+    the factor AdamW applies (ksdraft/train/__init__.py:165).  Nothing waits
+    for the GPU; returns out."""
+    rc = _lib.lib().ksd8_grad_clip_coef(flat.data_ptr(), flat.numel(), float(max_norm),
+                                        scratch.data_ptr(), out.data_ptr(), None,
+                                        _lib.stream_ptr(flat.device))
+    _lib.check(rc, "grad_clip_coef")
+    return out
 
 
 # SMs per GPU left to NCCL while gradient reductions overlap the backward.
@@ -158,7 +177,7 @@ def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
 class KS3DataParallelStep:
     """fwd + bwd + gradient all-reduce + AdamW for one trainable KS3Int8Cell."""
 
-    def __init__(self, cell, lr: float = 3e-4, group=None):
+    def __init__(self, cell, lr: float = 3e-4, group=None, grad_clip: float | None = 1.0):
         self.cell = cell
         self.params = [cell.master_down, cell.master_up, cell.master_coefficients,
                        cell.master_raw_scale, cell.master_raw_shift]
@@ -169,6 +188,17 @@ class KS3DataParallelStep:
         self.grad_views = {name: p.grad for name, p in self.named.items()}
         self.group = group
         self.opt = AdamW(self.params, lr=lr)
+        # the reference trainer clips the global gradient norm to 1.0 before
+        # AdamW (ksdraft/train/__init__.py:39,165); None disables it
+        self.grad_clip = grad_clip
+        dev = self.grads.buffer.device
+        self._clip_scratch = torch.empty(_lib.GRAD_CLIP_SCRATCH, device=dev)
+        self._clip_out = torch.zeros(2, device=dev)
+
+    @property
+    def last_grad_norm(self) -> torch.Tensor:
+        """The total gradient norm of the last step (device tensor, no sync)."""
+        return self._clip_out[0]
 
     def __call__(self, x: torch.Tensor, grad_out: torch.Tensor) -> torch.Tensor:
         """One step.  The backward writes every parameter gradient straight into
@@ -193,10 +223,19 @@ class KS3DataParallelStep:
             ks3_backward(self.cell, grad_out, *saved, x.shape, grads_into=self.grad_views,
                          on_grad=on_grad)
             self.opt.begin_step()
-            for indices, works in pending:  # update each tensor once its mean is complete
-                wait_all(works)
-                for i in indices:
-                    self.opt.update(i)
+            if self.grad_clip:
+                # clip-norm over all reduced gradients, then AdamW on every tensor
+                for _, works in pending:
+                    wait_all(works)
+                clip_grad_norm(self.grads.buffer, self.grad_clip, self._clip_scratch,
+                               self._clip_out)
+                for i in range(len(self.params)):
+                    self.opt.update(i, grad_scale=self._clip_out[1:2])
+            else:
+                for indices, works in pending:  # update each tensor once its mean is complete
+                    wait_all(works)
+                    for i in indices:
+                        self.opt.update(i)
         finally:
             if overlapping[0]:
                 lib.ksd8_set_sm_reserve(0)

@@ -75,3 +75,33 @@ def test_data_parallel_step_runs_and_updates():
     assert torch.equal(step.grad_views["down"].reshape(ga[0].shape), ga[0])
     assert torch.equal(step.grad_views["up"].reshape(ga[1].shape), ga[1])
     assert not torch.equal(before, q.master_down.detach())
+
+
+@pytest.mark.parametrize("scale", [1e-2, 30.0])
+def test_data_parallel_step_clips_like_torch(scale):
+    """clip_grad_norm_(1.0) + AdamW of the reference trainer (train/__init__.py:
+    165-166) against torch on the same gradients: the norm is computed and
+    applied on the device; with small gradients the coefficient is 1."""
+    from ksdraft_b200.train.dp import KS3DataParallelStep
+    q = _cell(256, 384, 6)
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(256, 256, device="cuda", generator=gen).to(torch.bfloat16)
+    g = (torch.randn(256, 256, device="cuda", generator=gen) * scale).to(torch.bfloat16)
+    step = KS3DataParallelStep(q, grad_clip=1.0)
+    params = step.params
+    before = [p.detach().clone() for p in params]
+    step(x, g)
+    torch.cuda.synchronize()
+    grads = [p.grad.detach().clone() for p in params]
+    norm = torch.linalg.vector_norm(torch.cat([t.reshape(-1) for t in grads]))
+    torch.testing.assert_close(step.last_grad_norm, norm, rtol=1e-5, atol=0)
+    coef = torch.clamp(1.0 / (norm + 1e-6), max=1.0)
+    ref = [b.clone().requires_grad_(True) for b in before]
+    for r, gr in zip(ref, grads):
+        r.grad = gr * coef
+    opt = torch.optim.AdamW(ref, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    opt.step()
+    for p, r in zip(params, ref):
+        torch.testing.assert_close(p.detach(), r.detach(), rtol=1e-6, atol=1e-7)
+    if scale > 1:
+        assert float(coef) < 1.0
