@@ -36,6 +36,7 @@
  *                             quantisation of Int8Linear.forward (ksdraft/kernels/linear.py:69)
  *   ksd8_adamw_step           torch.optim.AdamW.step over fp32 masters (ksdraft/train/__init__.py:166)
  *   ksd8_adamw_step_scaled    the same after gradient clipping (ksdraft/train/__init__.py:165)
+ *   ksd8_adamw_multi          the same over several tensors in one launch
  *   ksd8_grad_clip_coef       torch.nn.utils.clip_grad_norm_ norm and coefficient (:165)
  */
 #ifndef KSD8_H_
@@ -240,6 +241,15 @@ int ksd8_adamw_step_scaled(float* param, const void* grad, int grad_dtype, float
                            float* exp_avg_sq, int64_t n, float lr, float beta1, float beta2,
                            float eps, float weight_decay, int step, const float* grad_scale,
                            int* status, void* stream);
+
+/* ksd8_adamw_step (grad_scale NULL) or ksd8_adamw_step_scaled over `count`
+ * (<= KSD8_ADAMW_MULTI) tensors in one launch; the pointer and size arrays are
+ * host memory, all gradients of one dtype.  Same arithmetic per element. */
+#define KSD8_ADAMW_MULTI 8
+int ksd8_adamw_multi(int count, float* const* params, const void* const* grads, int grad_dtype,
+                     float* const* exp_avgs, float* const* exp_avg_sqs, const int64_t* numels,
+                     float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                     const float* grad_scale, int* status, void* stream);
 
 /* Global L2 norm of n fp32 gradients and torch's clip coefficient:
  * out[0] = norm, out[1] = min(1, max_norm / (norm + 1e-6))

@@ -55,6 +55,7 @@ SIGNATURES: dict[str, list] = {
     "ksd8_adamw_step": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp],
     "ksd8_adamw_step_scaled": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp, vp],
     "ksd8_grad_clip_coef": [vp, i64, f32, vp, vp, vp, vp],
+    "ksd8_adamw_multi": [i32, vp, vp, i32, vp, vp, vp, f32, f32, f32, f32, f32, i32, vp, vp, vp],
     "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
     "ksd8_set_sm_reserve": [i32],
     "ksd8_get_sm_reserve": [],

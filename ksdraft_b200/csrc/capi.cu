@@ -46,6 +46,9 @@ int ksd8_ce_grad_quant_launch(const void*, int, int64_t, int64_t, int64_t, const
 int ksd8_adamw_launch(float*, const void*, int, float*, float*, int64_t, float, float, float,
                       float, float, int, cudaStream_t, const float*);
 int ksd8_grad_clip_launch(const float*, int64_t, float, float*, float*, cudaStream_t);
+int ksd8_adamw_multi_launch(int, float* const*, const void* const*, int, float* const*,
+                            float* const*, const int64_t*, float, float, float, float, float,
+                            int, const float*, cudaStream_t);
 
 static thread_local int g_last_cuda_error = 0;
 
@@ -319,6 +322,26 @@ int ksd8_adamw_step_scaled(float* param, const void* grad, int grad_dtype, float
   if (n > 0 && (!param || !grad || !exp_avg || !exp_avg_sq || !grad_scale)) return KSD8_ERR_ARG;
   return finish(ksd8_adamw_launch(param, grad, grad_dtype, exp_avg, exp_avg_sq, n, lr, beta1,
                                   beta2, eps, weight_decay, step, S(stream), grad_scale));
+}
+
+int ksd8_adamw_multi(int count, float* const* params, const void* const* grads, int grad_dtype,
+                     float* const* exp_avgs, float* const* exp_avg_sqs, const int64_t* numels,
+                     float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                     const float* grad_scale, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(grad_dtype)) return KSD8_ERR_DTYPE;
+  if (count < 0 || count > KSD8_ADAMW_MULTI) return KSD8_ERR_UNSUPPORTED;
+  if (step < 1) return KSD8_ERR_ARG;
+  if (count > 0 && (!params || !grads || !exp_avgs || !exp_avg_sqs || !numels))
+    return KSD8_ERR_ARG;
+  for (int k = 0; k < count; ++k) {
+    if (numels[k] < 0) return KSD8_ERR_SHAPE;
+    if (numels[k] > 0 && (!params[k] || !grads[k] || !exp_avgs[k] || !exp_avg_sqs[k]))
+      return KSD8_ERR_ARG;
+  }
+  return finish(ksd8_adamw_multi_launch(count, params, grads, grad_dtype, exp_avgs, exp_avg_sqs,
+                                        numels, lr, beta1, beta2, eps, weight_decay, step,
+                                        grad_scale, S(stream)));
 }
 
 int ksd8_grad_clip_coef(const float* grad, int64_t n, float max_norm, float* scratch,

@@ -565,11 +565,7 @@ __device__ __forceinline__ __half2 vjp_pair(const uint16_t* ttab, const VjpPair&
       __hmul2_rn(dd, u),
       __hmul2_rn(dd, q.scale)};
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float2 f = __half22float2(terms[k]);
-    acc[k].x += f.x;
-    acc[k].y += f.y;
-  }
+  for (int k = 0; k < 8; ++k) acc[k] = __fadd2_rn(acc[k], __half22float2(terms[k]));
   return __hadd2_rn(value, dmean);
 }
 

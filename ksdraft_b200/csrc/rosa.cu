@@ -342,6 +342,44 @@ __global__ void adamw_kernel(float* p, const void* g, int gdt, float* m, float* 
   }
 }
 
+// AdamW over up to KSD8_ADAMW_MULTI tensors in one launch (same arithmetic as
+// adamw_kernel); every thread walks the tensors in order.
+struct AdamwMulti {
+  float* p[KSD8_ADAMW_MULTI];
+  const void* g[KSD8_ADAMW_MULTI];
+  float* m[KSD8_ADAMW_MULTI];
+  float* v[KSD8_ADAMW_MULTI];
+  int64_t n[KSD8_ADAMW_MULTI];
+  int count;
+};
+
+__global__ void adamw_multi_kernel(AdamwMulti t, int gdt, float lr, float b1, float b2, float eps,
+                                   float wd, float bc1, float bc2_sqrt, const float* gscale) {
+  const float gs = gscale ? *gscale : 1.f;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int k = 0; k < t.count; ++k) {
+    float* p = t.p[k];
+    float* m = t.m[k];
+    float* v = t.v[k];
+    const void* g = t.g[k];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < t.n[k]; i += stride) {
+      float gr = gdt == KSD8_F16 ? __half2float(reinterpret_cast<const __half*>(g)[i])
+                 : gdt == KSD8_BF16
+                     ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[i])
+                     : reinterpret_cast<const float*>(g)[i];
+      if (gscale) gr = __fmul_rn(gr, gs);
+      float pi = p[i] * (1.f - lr * wd);
+      const float mi = b1 * m[i] + (1.f - b1) * gr;
+      const float vi = b2 * v[i] + (1.f - b2) * gr * gr;
+      m[i] = mi;
+      v[i] = vi;
+      const float denom = sqrtf(vi) / bc2_sqrt + eps;
+      pi -= (lr / bc1) * mi / denom;
+      p[i] = pi;
+    }
+  }
+}
+
 // Sum of squares of n fp32 values: per-block partial sums (fixed tree order)
 // into partials[blockIdx.x].
 constexpr int GN_BLOCKS = 592;  // 4 x 148
@@ -391,6 +429,31 @@ __global__ void __launch_bounds__(32) grad_clip_coef_kernel(const float* partial
 }  // namespace ksd8
 
 using namespace ksd8;
+
+int ksd8_adamw_multi_launch(int count, float* const* params, const void* const* grads, int gdt,
+                            float* const* m, float* const* v, const int64_t* numels, float lr,
+                            float b1, float b2, float eps, float wd, int step,
+                            const float* gscale, cudaStream_t stream) {
+  AdamwMulti t;
+  int64_t total = 0;
+  t.count = count;
+  for (int k = 0; k < count; ++k) {
+    t.p[k] = params[k];
+    t.g[k] = grads[k];
+    t.m[k] = m[k];
+    t.v[k] = v[k];
+    t.n[k] = numels[k];
+    total += numels[k];
+  }
+  if (total == 0) return KSD8_OK;
+  const float bc1 = 1.f - powf(b1, (float)step);
+  const float bc2 = 1.f - powf(b2, (float)step);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  adamw_multi_kernel<<<(unsigned)blocks, 256, 0, stream>>>(t, gdt, lr, b1, b2, eps, wd, bc1,
+                                                            sqrtf(bc2), gscale);
+  return KSD8_OK;
+}
 
 int ksd8_grad_clip_launch(const float* grad, int64_t n, float max_norm, float* scratch,
                           float* out, cudaStream_t stream) {

@@ -139,6 +139,32 @@ class AdamW:
             _lib.check(rc, "adamw_step")
 
 
+    @torch.no_grad()
+    def update_all(self, grad_scale: torch.Tensor | None = None) -> None:
+        """update() of every tensor with a gradient, in one kernel launch
+        (tensors sharing one gradient dtype, at most 8)."""
+        import ctypes as C
+        items = [(p, self.state[i], p.grad.contiguous()) for i, p in enumerate(self.params)
+                 if p.grad is not None]
+        if not items:
+            return
+        dt = {_lib.dtype_code(g) for _, _, g in items}
+        if len(items) > 8 or len(dt) != 1:
+            for i in range(len(self.params)):
+                self.update(i, grad_scale)
+            return
+        n = len(items)
+        ptrs = lambda ts: (C.c_void_p * n)(*[t.data_ptr() for t in ts])  # noqa: E731
+        numels = (C.c_int64 * n)(*[p.numel() for p, _, _ in items])
+        rc = _lib.lib().ksd8_adamw_multi(
+            n, ptrs([p for p, _, _ in items]), ptrs([g for _, _, g in items]), dt.pop(),
+            ptrs([s[0] for _, s, _ in items]), ptrs([s[1] for _, s, _ in items]), numels,
+            self.lr, self.betas[0], self.betas[1], self.eps, self.wd, self.step_count,
+            grad_scale.data_ptr() if grad_scale is not None else None, None,
+            _lib.stream_ptr(items[0][0].device))
+        _lib.check(rc, "adamw_multi")
+
+
 def clip_grad_norm(flat: torch.Tensor, max_norm: float, scratch: torch.Tensor,
                    out: torch.Tensor) -> torch.Tensor:
     """torch.nn.utils.clip_grad_norm_ over one flat fp32 gradient buffer, on the
@@ -229,8 +255,7 @@ class KS3DataParallelStep:
                     wait_all(works)
                 clip_grad_norm(self.grads.buffer, self.grad_clip, self._clip_scratch,
                                self._clip_out)
-                for i in range(len(self.params)):
-                    self.opt.update(i, grad_scale=self._clip_out[1:2])
+                self.opt.update_all(grad_scale=self._clip_out[1:2])
             else:
                 for indices, works in pending:  # update each tensor once its mean is complete
                     wait_all(works)
