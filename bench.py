@@ -340,6 +340,9 @@ def run_ours(args) -> None:
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
+        if world == 1 and not args.no_side:
+            del flush, x_dev, g_dev
+            line["side"] = side_measurements(dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = {k: v for k, v in cpu_baseline().items()
                                     if k != "sec_per_sample"}
@@ -368,16 +371,22 @@ def rosa_ids(B: int, T: int, seed: int = 0, vocab: int = 150144):
     return ids
 
 
-def run_profile_case(case: str, iters: int) -> None:
-    """One kernel of the layer step at its config-2 shape, `iters` launches after
-    one warm-up (for ncu captures: small, single-kernel, ends by itself)."""
+def profile_case_fn(case: str, dev):
+    """The callable of one profile case on `dev` (built once, inputs resident)."""
     import torch
 
     from ksdraft_b200.kernels.gemm import gemm_out
     from ksdraft_b200.kernels.quant import quantize_cols, quantize_last_dim
-    dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
-    if case == "gemm":
+    if case == "gemm_config1":
+        # BASELINE config 1: A (256, 1536) N(0,1), W (1536, 1536) N(0,0.02), GS128, fp32 out
+        a = torch.randn(256, D_MODEL, device=dev, generator=g)
+        w = torch.randn(D_MODEL, D_MODEL, device=dev, generator=g) * 0.02
+        ac, as_ = quantize_last_dim(a)
+        wc, ws = quantize_last_dim(w)
+        out = torch.empty(256, D_MODEL, device=dev)
+        fn = lambda: gemm_out(ac, as_, wc, ws, out=out)  # noqa: E731
+    elif case == "gemm":
         a = torch.randint(-127, 128, (TOKENS, D_MODEL), dtype=torch.int8, device=dev, generator=g)
         w = torch.randint(-127, 128, (CHARTS, D_MODEL), dtype=torch.int8, device=dev, generator=g)
         sa = (torch.rand(TOKENS, D_MODEL // 128, device=dev, generator=g) * 0.01).half()
@@ -462,6 +471,52 @@ def run_profile_case(case: str, iters: int) -> None:
                                  strides=(T * S, S, 1))
     else:
         raise SystemExit(f"unknown profile case {case}")
+    return fn
+
+
+def time_on_device(fn, iters: int) -> float:
+    """ms per call of fn over `iters` back-to-back calls, CUDA events on the
+    current stream.  The GPU is held by a spin kernel while the CPU enqueues,
+    so host launch overhead does not enter the figure."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(int(2e6) + iters * int(2e5))  # covers the enqueue of `iters` calls
+    ev0.record()
+    for _ in range(iters):
+        fn()
+    ev1.record()
+    torch.cuda.synchronize()
+    return ev0.elapsed_time(ev1) / iters
+
+
+def side_measurements(dev) -> dict:
+    """1-GPU figures of the other BASELINE configurations, measured after the
+    main line (outside its timed region): config 1 (W8A8 GEMM fwd), config 3
+    (Rosa stream matcher, B 4 x T 4096 x 512 streams) and the LM head
+    (4096 tokens x vocab 150144 on one GPU, forward + backward)."""
+    out = {}
+    ms = time_on_device(profile_case_fn("gemm_config1", dev), 200)
+    ops = 2 * 256 * D_MODEL * D_MODEL
+    out["config1_gemm"] = {"shape": [256, D_MODEL, D_MODEL], "ms": ms,
+                           "tops": ops / (ms / 1e3) / 1e12, "unit": "TOP/s",
+                           "note": "operands L2-resident (the whole problem is 2.8 MB)"}
+    ms = time_on_device(profile_case_fn("rosa", dev), 5)
+    out["config3_rosa_match"] = {"shape": [4, 4096, 512], "ms": ms,
+                                 "positions_per_s": 4 * 4096 * 512 / (ms / 1e3)}
+    ms = time_on_device(profile_case_fn("head", dev), 3)
+    out["lm_head_fwd_bwd"] = {"tokens": TOKENS, "vocab": 150144, "ms": ms,
+                              "tokens_per_s": TOKENS / (ms / 1e3)}
+    return out
+
+
+def run_profile_case(case: str, iters: int) -> None:
+    """One kernel of the layer step at its config-2 shape, `iters` launches after
+    one warm-up (for ncu captures: small, single-kernel, ends by itself)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    fn = profile_case_fn(case, dev)
     fn()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -481,8 +536,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-side", action="store_true",
+                    help="skip the 1-GPU side figures (configs 1 and 3, LM head)")
     ap.add_argument("--profile-case", default=None,
-                    help="run one kernel (gemm | quant | quant_dither | quant_cols | requant_t | "
+                    help="run one kernel (gemm | gemm_config1 | quant | quant_dither | quant_cols | "
+                         "requant_t | "
                          "spine | vjp | head | rosa) a few times, for ncu")
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
