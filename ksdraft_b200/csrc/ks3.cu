@@ -386,15 +386,21 @@ __global__ void __launch_bounds__(256) ks3_spine_int8_fast_kernel(SpineFastArgs 
       const float scale = gs_scale_fast(mx[k], &sh);
       const float rcp = rcp_approx(scale);
       int8_t* out = a.h_codes + r * a.charts + cbase;
-      const int q0 = gs_code_fast(h[k][0], scale, rcp), q1 = gs_code_fast(h[k][1], scale, rcp);
-      const int q2 = gs_code_fast(h[k][2], scale, rcp), q3 = gs_code_fast(h[k][3], scale, rcp);
-      if (full && ((reinterpret_cast<uintptr_t>(out) & 3) == 0)) {
-        *reinterpret_cast<char4*>(out) = make_char4((char)q0, (char)q1, (char)q2, (char)q3);
+      uint32_t word;
+      if (gs_scale_is_normal(mx[k], scale)) {
+        word = gs_code4_normal(h[k], scale, rcp);
       } else {
-        const int q[4] = {q0, q1, q2, q3};
+        word = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          if (cbase + i < a.charts) out[i] = (int8_t)q[i];
+          word |= ((uint32_t)gs_code_fast(h[k][i], scale, rcp) & 0xFFu) << (8 * i);
+      }
+      if (full && ((reinterpret_cast<uintptr_t>(out) & 3) == 0)) {
+        *reinterpret_cast<uint32_t*>(out) = word;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (cbase + i < a.charts) out[i] = (int8_t)((word >> (8 * i)) & 0xFFu);
       }
       if (lane == 0) a.h_scales[r * groups + g] = sh;
     }
@@ -672,9 +678,17 @@ __global__ void __launch_bounds__(VJP_THREADS, 1)
         __half shq;
         const float s = gs_scale_fast(mx, &shq);
         const float rcp = rcp_approx(s);
-        *reinterpret_cast<char4*>(a.dc_codes + r * a.charts + cbase) =
-            make_char4((char)gs_code_fast(d01.x, s, rcp), (char)gs_code_fast(d01.y, s, rcp),
-                       (char)gs_code_fast(d23.x, s, rcp), (char)gs_code_fast(d23.y, s, rcp));
+        const float dv[4] = {d01.x, d01.y, d23.x, d23.y};
+        uint32_t word;
+        if (gs_scale_is_normal(mx, s)) {
+          word = gs_code4_normal(dv, s, rcp);
+        } else {
+          word = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            word |= ((uint32_t)gs_code_fast(dv[i], s, rcp) & 0xFFu) << (8 * i);
+        }
+        *reinterpret_cast<uint32_t*>(a.dc_codes + r * a.charts + cbase) = word;
         if (lane == 0) a.dc_scales[r * gcharts + cg] = shq;
       }
     }
@@ -733,18 +747,25 @@ __global__ void __launch_bounds__(VJP_THREADS, 1)
       const int64_t c = cg * VJP_TC + cc;
       const int64_t rb = m0 + quarter * 32;
       int8_t* out = a.dct_codes + c * a.m + rb;
+      const bool col_normal = gs_scale_is_normal(mx, s);
       if (rb + 32 <= a.m && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
 #pragma unroll
         for (int v = 0; v < 2; ++v) {
           uint32_t w4[4];
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
-            uint32_t word = 0;
+            float cv[4];
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const int rr = quarter * 32 + v * 16 + jj * 4 + b;
-              const int q = gs_code_fast(__half2float(vtile[rr * VJP_TC + cc]), s, rcp);
-              word |= (uint32_t)(q & 0xFF) << (8 * b);
+            for (int b = 0; b < 4; ++b)
+              cv[b] = __half2float(vtile[(quarter * 32 + v * 16 + jj * 4 + b) * VJP_TC + cc]);
+            uint32_t word;
+            if (col_normal) {
+              word = gs_code4_normal(cv, s, rcp);
+            } else {
+              word = 0;
+#pragma unroll
+              for (int b = 0; b < 4; ++b)
+                word |= ((uint32_t)gs_code_fast(cv[b], s, rcp) & 0xFFu) << (8 * b);
             }
             w4[jj] = word;
           }

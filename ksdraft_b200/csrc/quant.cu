@@ -215,57 +215,6 @@ __device__ __forceinline__ void lds4(const uint8_t* p, float (&v)[4]) {
   }
 }
 
-// Four codes of one 128-wide group (common scale, rcp = RN(1/scale) within 1
-// ulp), packed byte e = element e.  The scale is a normal fp16 number and not
-// clamped above, so |y| <= 127.07: the 1.5 * 2^23 shifter's low byte is the
-// code and no saturation applies; an element within 2^-13 of a rounding tie
-// sends the four to the IEEE path.
-static __device__ __noinline__ uint32_t gs_code4_exact(float x0, float x1, float x2, float x3,
-                                                       float scale) {
-  return ((uint32_t)gs_code(x0, scale) & 0xFFu) | (((uint32_t)gs_code(x1, scale) & 0xFFu) << 8) |
-         (((uint32_t)gs_code(x2, scale) & 0xFFu) << 16) |
-         (((uint32_t)gs_code(x3, scale) & 0xFFu) << 24);
-}
-
-__device__ __forceinline__ uint32_t gs_code4_normal(const float (&v)[4], float scale, float rcp) {
-  const float2 rc = make_float2(rcp, rcp);
-  const float2 mg = make_float2(12582912.f, 12582912.f), nmg = make_float2(-12582912.f, -12582912.f);
-  const float2 y01 = __fmul2_rn(make_float2(v[0], v[1]), rc);
-  const float2 y23 = __fmul2_rn(make_float2(v[2], v[3]), rc);
-  const float2 t01 = __fadd2_rn(y01, mg), t23 = __fadd2_rn(y23, mg);
-  const float2 d01 = __ffma2_rn(y01, make_float2(-1.f, -1.f), __fadd2_rn(t01, nmg));
-  const float2 d23 = __ffma2_rn(y23, make_float2(-1.f, -1.f), __fadd2_rn(t23, nmg));
-  const float dm =
-      fmax_nan(fmax_nan(fabsf(d01.x), fabsf(d01.y)), fmax_nan(fabsf(d23.x), fabsf(d23.y)));
-  if (!(dm < 0.4998779296875f)) return gs_code4_exact(v[0], v[1], v[2], v[3], scale);
-  return __byte_perm(__byte_perm(__float_as_uint(t01.x), __float_as_uint(t01.y), 0x0040),
-                     __byte_perm(__float_as_uint(t23.x), __float_as_uint(t23.y), 0x0040), 0x5410);
-}
-
-// Bounded wait of the staged quantisers: the mbarrier wait with a suspend hint
-// by default; KSD8_Q_SPIN_WAIT polls without it (same bound, same abort).
-__device__ __forceinline__ bool q_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                       int* status) {
-#ifdef KSD8_Q_SPIN_WAIT
-  uint64_t t0 = 0;
-  for (uint32_t n = 0;; ++n) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((n & 63u) == 63u) {
-      if (*abort_flag) return false;
-      const uint64_t now = globaltimer_ns();
-      if (t0 == 0) t0 = now;
-      if (now - t0 > KSD8_WAIT_NS) {
-        *abort_flag = 1;
-        record_error(status, KSD8_ERR_DEVICE_TIMEOUT);
-        return false;
-      }
-    }
-  }
-#else
-  return mbar_wait(bar, parity, abort_flag, status);
-#endif
-}
-
 // Dithered version (ksdraft/train/stages.py:42-48): noise = RN((U - 0.5) * d2)
 // computed as one fma(U, d2, -d2 / 2) (U - 0.5 is exact, so the single rounding
 // is the same); t = RN(y + noise) is clamped to +-127 before the shifter

@@ -163,9 +163,15 @@ __global__ void __launch_bounds__(512) rosa_match_kernel(MatchArgs a) {
 // When level 12 hits, the keys sharing those 12 bits are walked newest first
 // through per-position links for the exact length (up to the cap); the walk
 // stops at the first key reaching min(max_len, t).
-constexpr int RP_LEVELS = 12;
-constexpr int RP_TBL = 1 << (RP_LEVELS + 1);   // levels 1..12 at offsets 2^L - 2 (8190 used)
-constexpr int RP_WARPS = 8;                    // streams per CTA (fewer when T is long)
+#ifndef KSD8_RP_LEVELS
+#define KSD8_RP_LEVELS 12
+#endif
+#ifndef KSD8_RP_WARPS
+#define KSD8_RP_WARPS 8
+#endif
+constexpr int RP_LEVELS = KSD8_RP_LEVELS;      // table levels 1..RP_LEVELS (<= 12)
+constexpr int RP_TBL = 1 << (RP_LEVELS + 1);   // level L at offset 2^L - 2
+constexpr int RP_WARPS = KSD8_RP_WARPS;        // streams per CTA (fewer when T is long)
 constexpr int RP_TMAX = 8192;                  // links are uint16 positions + 1
 
 __device__ __forceinline__ int rp_off(int L) { return (1 << L) - 2; }
