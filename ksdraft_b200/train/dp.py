@@ -220,19 +220,64 @@ class KS3DataParallelStep:
         dev = self.grads.buffer.device
         self._clip_scratch = torch.empty(_lib.GRAD_CLIP_SCRATCH, device=dev)
         self._clip_out = torch.zeros(2, device=dev)
+        self._copy_stream = torch.cuda.Stream(device=dev) if dev.type == "cuda" else None
+        self._dev_bufs: dict[str, torch.Tensor] = {}
 
     @property
     def last_grad_norm(self) -> torch.Tensor:
         """The total gradient norm of the last step (device tensor, no sync)."""
         return self._clip_out[0]
 
-    def __call__(self, x: torch.Tensor, grad_out: torch.Tensor) -> torch.Tensor:
+    def _to_device(self, t: torch.Tensor, name: str, stream=None) -> torch.Tensor:
+        """A host tensor copied into this step's device buffer `name` (allocated
+        on first use), on `stream` or the current stream; device tensors pass."""
+        if t.is_cuda:
+            return t
+        dev = self.grads.buffer.device
+        buf = self._dev_bufs.get(name)
+        if buf is None or buf.shape != t.shape or buf.dtype != t.dtype:
+            buf = torch.empty(t.shape, dtype=t.dtype, device=dev)
+            self._dev_bufs[name] = buf
+        with torch.cuda.stream(stream or torch.cuda.current_stream(dev)):
+            buf.copy_(t, non_blocking=True)
+        return buf
+
+    def __call__(self, x: torch.Tensor, grad_out: torch.Tensor,
+                 y_out: torch.Tensor | None = None) -> torch.Tensor:
         """One step.  The backward writes every parameter gradient straight into
         the flat fp32 buffer (as the reference's autograd would leave it after
         the FP16 handoff and the cast to fp32), so no zeroing, casting or
-        accumulation pass runs and nothing waits for the GPU."""
+        accumulation pass runs and nothing waits for the GPU.
+
+        x and grad_out may be host tensors (pinned for asynchronous copies):
+        x is copied before the forward, grad_out on a copy stream while the
+        forward runs.  With `y_out` (a pinned host tensor) the forward output is
+        copied back on the copy stream while the backward runs; the current
+        stream waits for both copies before the step returns, so anything timed
+        or ordered after the call includes them."""
         from ..kernels.ks3_int8 import ks3_backward, ks3_train_forward
+        dev = self.grads.buffer.device
+        main = torch.cuda.current_stream(dev)
+        copy = self._copy_stream
+        host_io = not grad_out.is_cuda or y_out is not None
+        if host_io:
+            copy.wait_stream(main)  # the previous step is done with the device buffers
+        x = self._to_device(x, "x")
+        g_ready = None
+        if not grad_out.is_cuda:
+            grad_out = self._to_device(grad_out, "grad_out", copy)
+            g_ready = torch.cuda.Event()
+            g_ready.record(copy)
         y, saved = ks3_train_forward(self.cell, x.detach())
+        if y_out is not None:
+            y_done = torch.cuda.Event()
+            y_done.record(main)
+            copy.wait_event(y_done)
+            with torch.cuda.stream(copy):
+                y_out.copy_(y.detach(), non_blocking=True)
+            y.record_stream(copy)
+        if g_ready is not None:
+            main.wait_event(g_ready)
         lib = _lib.lib()
         pending = []          # (parameter indices, works) in launch order
         overlapping = [False]
@@ -264,4 +309,6 @@ class KS3DataParallelStep:
         finally:
             if overlapping[0]:
                 lib.ksd8_set_sm_reserve(0)
+        if host_io:
+            main.wait_stream(copy)
         return y
