@@ -107,16 +107,19 @@ def test_data_parallel_step_clips_like_torch(scale):
         assert float(coef) < 1.0
 
 
-def test_data_parallel_step_host_io_matches_device_io():
+@pytest.mark.parametrize("tokens", [256, 1024])
+def test_data_parallel_step_host_io_matches_device_io(tokens):
     """Host inputs and a host output buffer (copies overlapped with the step on
-    a copy stream) give the same output and the same update as device tensors."""
+    a copy stream; with 1024 tokens x arrives in 4 row chunks that are
+    quantised and projected as they land) give the same output and the same
+    update as device tensors."""
     from ksdraft_b200.train.dp import KS3DataParallelStep
     gen = torch.Generator(device="cuda").manual_seed(10)
-    x = torch.randn(256, 256, device="cuda", generator=gen).to(torch.bfloat16)
-    g = (torch.randn(256, 256, device="cuda", generator=gen) * 1e-2).to(torch.bfloat16)
+    x = torch.randn(tokens, 256, device="cuda", generator=gen).to(torch.bfloat16)
+    g = (torch.randn(tokens, 256, device="cuda", generator=gen) * 1e-2).to(torch.bfloat16)
     steps = [KS3DataParallelStep(_cell(256, 384, 6)) for _ in range(2)]
     x_h, g_h = x.cpu().pin_memory(), g.cpu().pin_memory()
-    y_h = torch.empty(256, 256, dtype=torch.bfloat16).pin_memory()
+    y_h = torch.empty(tokens, 256, dtype=torch.bfloat16).pin_memory()
     for _ in range(2):  # two steps: the reused device buffers and copy stream
         y_dev = steps[0](x, g)
         y_ret = steps[1](x_h, g_h, y_out=y_h)
