@@ -251,7 +251,9 @@ def run_ours(args) -> None:
     q = KS3Int8Cell(cell.to(dev), nonlinear="int8", trainable=True)
     q._dither = DITHER
     q._dither_seed = 20260101
-    step = KS3DataParallelStep(q)
+    # gradient clipping as the reference trainer (max norm 1.0); KSD8_GRAD_CLIP=0 disables it
+    clip = float(os.environ.get("KSD8_GRAD_CLIP", "1.0"))
+    step = KS3DataParallelStep(q, grad_clip=clip if clip > 0 else None)
 
     gen = torch.Generator().manual_seed(1000 + rank)  # each rank its own tokens
     x_host = torch.randn(TOKENS, D_MODEL, generator=gen).to(torch.bfloat16).pin_memory()
