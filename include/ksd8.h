@@ -38,6 +38,7 @@
  *   ksd8_adamw_step_scaled    the same after gradient clipping (ksdraft/train/__init__.py:165)
  *   ksd8_adamw_multi          the same over several tensors in one launch
  *   ksd8_grad_clip_coef       torch.nn.utils.clip_grad_norm_ norm and coefficient (:165)
+ *   ksd8_fp16_tanh_table      the fp16 torch.tanh of ksdraft/kernels/ks3_int8.py:366-367 (parity probe)
  */
 #ifndef KSD8_H_
 #define KSD8_H_
@@ -259,6 +260,11 @@ int ksd8_adamw_multi(int count, float* const* params, const void* const* grads, 
 int ksd8_grad_clip_coef(const float* grad, int64_t n, float max_norm, float* scratch,
                         float* out, int* status, void* stream);
 
+/* Parity probe: out[i] = bits of the fp16 tanh the KS3 kernels use for the
+ * fp16 value with bits i, i < n <= 0x7C00 (correctly rounded; the reference's
+ * CPU torch.tanh on fp16, ksdraft/kernels/ks3_int8.py:366-367, gives the same). */
+int ksd8_fp16_tanh_table(int64_t n, uint16_t* out, void* stream);
+
 /* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);
 
@@ -325,6 +331,8 @@ int ksd8_topk_rows(const void* vals, int dtype, const int64_t* idx, int64_t m, i
  *   - Set-up: the first call on each device (with that device current) looks
  *     up the array's device address once with cudaGetSymbolAddress and caches
  *     it; make that first call before any stream capture on the device.
+ *     The cache is never refreshed, so a device reset (cudaDeviceReset) after
+ *     the first call is not supported.  Devices 0..31 only (as ksd8_ks3_vjp).
  *   - Nothing in the scratch needs clearing: the VJP writes every partial the
  *     reduction then reads.
  *   - Calls that overlap on one device (other streams, other host threads)

@@ -3,7 +3,7 @@
 Modules mirror the reference package layout for the path:
   ksdraft_b200.kernels   quantize_last_dim, dequantize_last_dim, w8a8_gemm,
                          Int8Linear, KS3Int8Cell/_KS3Int8Train, project_fused
-  ksdraft_b200.model     _match_payload_sign, RosaMixer, KS3
+  ksdraft_b200.model     _match_payload_sign, RosaMixer, the vocab-sharded LM head
   ksdraft_b200.train     quantize_last_dim_dithered, data-parallel step helpers
   ksdraft_b200.install   rebinds those names inside an importable `ksdraft`
 All compute runs in libksd8.so (hand-written sm_100a CUDA behind a C ABI).

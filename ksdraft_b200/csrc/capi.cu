@@ -12,6 +12,7 @@ int ksd8_quantize_rows_launch(const void*, int, int64_t, int64_t, int64_t, int, 
 int ksd8_quantize_cols_launch(const void*, int, const void*, int, int64_t, int64_t, int64_t, int,
                               int8_t*, int64_t, void*, int*, cudaStream_t);
 int ksd8_philox_launch(uint64_t, uint64_t, int64_t, float*, cudaStream_t);
+int ksd8_fp16_tanh_table_launch(int64_t, uint16_t*, cudaStream_t);
 int ksd8_gemm_launch(const int8_t*, const void*, const int8_t*, const void*, int64_t, int64_t,
                      int64_t, void*, int, int64_t, const float*, int, int*, cudaStream_t, bool);
 int ksd8_ks3_pack_launch(const float*, const float*, const float*, int64_t, int8_t*, void*,
@@ -408,6 +409,12 @@ int ksd8_topk_rows(const void* vals, int dtype, const int64_t* idx, int64_t m, i
                                       S(stream)));
 }
 
+int ksd8_fp16_tanh_table(int64_t n, uint16_t* out, void* stream) {
+  if (n < 0 || n > 0x7C00) return KSD8_ERR_SHAPE;
+  if (n > 0 && !out) return KSD8_ERR_ARG;
+  return finish(ksd8_fp16_tanh_table_launch(n, out, S(stream)));
+}
+
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream) {
   if (n < 0) return KSD8_ERR_SHAPE;
   if (n > 0 && !out) return KSD8_ERR_ARG;
@@ -433,7 +440,7 @@ int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, v
 static __device__ __align__(256) float g_vjp_scratch[KSD8_VJP_STATIC_MAX_PARTIALS];
 
 namespace {
-constexpr int kMaxDevices = 64;
+constexpr int kMaxDevices = 32;  // the same device limit as the VJP launcher's per-device state
 std::mutex g_vjp_scratch_mu;
 float* g_vjp_scratch_ptr[kMaxDevices] = {};
 

@@ -26,6 +26,37 @@ __device__ __forceinline__ float hmul(float a, float b) { return hr(__fmul_rn(a,
 __device__ __forceinline__ float hadd(float a, float b) { return hr(__fadd_rn(a, b)); }
 __device__ __forceinline__ float hsub(float a, float b) { return hr(__fsub_rn(a, b)); }
 
+// fp16(tanh(a)) correctly rounded, for an fp16 value a >= 0 given by its bits.
+// The reference takes tanh of fp16 values on the CPU (ks3_int8.py:366-367,
+// and tanh of fp16-valued fp32 in the 'fp16' spine, :189-192); for every fp16
+// input that result equals the correctly rounded fp16 tanh (checked
+// exhaustively against torch.tanh by the tests).  tanhf is within a few fp32
+// ulps, so its fp16 rounding can only be wrong when it lands next to an fp16
+// rounding midpoint; those rare inputs are redone in double precision, where
+// rounding double -> fp32 -> fp16 is exact rounding (24 >= 2 * 11 + 2).
+__device__ __forceinline__ uint16_t tanh16_bits(uint16_t abits) {
+  const float x = __half2float(__ushort_as_half(abits));
+  const float f = tanhf(x);
+  const __half h = __float2half_rn(f);
+  const uint16_t hb = __half_as_ushort(h);
+  const float hf = __half2float(h);
+  if (f == hf) return hb;
+  const uint16_t nb = f > hf ? (uint16_t)(hb + 1) : (uint16_t)(hb - 1);  // fp16 neighbour
+  const float mid = 0.5f * (hf + __half2float(__ushort_as_half(nb)));   // exact in fp32
+  if (fabsf(f - mid) > ldexpf(fabsf(f), -19)) return hb;
+  return __half_as_ushort(__float2half_rn(__double2float_rn(tanh((double)x))));
+}
+
+// Signed fp16 tanh of a value carried in fp32 (an fp16 value).
+__device__ __forceinline__ float tanh16(float v16) {
+  const uint16_t b = __half_as_ushort(__float2half_rn(v16));
+  const uint16_t m = b & 0x7FFFu;
+  uint16_t r;
+  if (m >= 0x7C00u) r = m > 0x7C00u ? m : 0x3C00u;  // nan stays, +-inf -> +-1
+  else r = m < 0x4600u ? tanh16_bits(m) : 0x3C00u;   // |a| >= 6: fp16(tanh) is 1
+  return __half2float(__ushort_as_half((uint16_t)(r | (b & 0x8000u))));
+}
+
 // _round_div127 (ks3_int8.py:57-66): truncating division, then the +-63
 // remainder correction.
 __device__ __forceinline__ int round_div127(int v) {
@@ -103,9 +134,9 @@ __device__ __forceinline__ float spine_int8(float x, const ChartParams& p, const
 // NL == 1 ('fp16') composed path (ks3_int8.py:186-203).
 __device__ __forceinline__ float spine_fp16(float x, const ChartParams& p) {
   const float th = hr(__fmul_rn(x, 0.25f));
-  const float t = hr(__fmul_rn(4.0f, tanhf(th)));
+  const float t = hr(__fmul_rn(4.0f, tanh16(th)));
   const float warp = hr(__fmul_rn(p.scale, __fadd_rn(t, p.shift)));
-  const float z = hr(tanhf(warp));
+  const float z = tanh16(warp);
   const float c0 = (float)p.c[0], c1 = (float)p.c[1], c2 = (float)p.c[2];
   const float c3 = (float)p.c[3], c4 = (float)p.c[4], c5 = (float)p.c[5];
   const float a = hr(2.f * c0 - 2.f * c1 + c2 + c3);  // exact integers
@@ -478,8 +509,9 @@ constexpr int VJP_WARPS = VJP_THREADS / 32;
 constexpr int VJP_ROWS_PER_WARP = VJP_TM / VJP_WARPS;
 
 // fp16(tanh(a)) of an fp16 value through the shared-memory table: entry i
-// holds fp16(tanhf(fp16 with bits i)) for |a| < 6 (above it the fp16 result is
-// 1.0); tanh is odd, so the sign bit is carried over.
+// holds the correctly rounded fp16 tanh of the fp16 value with bits i
+// (tanh16_bits) for |a| < 6 (above it the fp16 result is 1.0); tanh is odd,
+// so the sign bit is carried over.
 __device__ __forceinline__ __half2 tanh16x2(const uint16_t* tab, __half2 x) {
   const uint32_t b = *reinterpret_cast<const uint32_t*>(&x);
   const uint32_t m0 = b & 0x7FFFu, m1 = (b >> 16) & 0x7FFFu;
@@ -626,9 +658,7 @@ __global__ void __launch_bounds__(VJP_THREADS, 1)
     tma_prefetch_desc(&tm_coords);
     for (int64_t i = 0; i < 2 && t_begin + i < t_end; ++i) issue(i);
   }
-  for (int i = threadIdx.x; i < TANH_N; i += blockDim.x)
-    ttab[i] = __half_as_ushort(__float2half_rn(tanhf(__half2float(__ushort_as_half(
-        (unsigned short)i)))));
+  for (int i = threadIdx.x; i < TANH_N; i += blockDim.x) ttab[i] = tanh16_bits((uint16_t)i);
   __syncthreads();
 
   int64_t cur_cg = -1;
@@ -858,6 +888,17 @@ __global__ void __launch_bounds__(VRED_CHARTS * 8)
 }  // namespace ksd8
 
 using namespace ksd8;
+
+__global__ void tanh16_table_kernel(int64_t n, uint16_t* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = tanh16_bits((uint16_t)i);
+}
+
+int ksd8_fp16_tanh_table_launch(int64_t n, uint16_t* out, cudaStream_t stream) {
+  if (n == 0) return KSD8_OK;
+  tanh16_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(n, out);
+  return KSD8_OK;
+}
 
 int ksd8_ks3_pack_launch(const float* coeffs, const float* raw_scale, const float* raw_shift,
                          int64_t charts, int8_t* spine_codes, void* spine_scale, int8_t* ws_codes,

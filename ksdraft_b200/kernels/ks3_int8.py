@@ -22,6 +22,8 @@ Backward:
 
 from __future__ import annotations
 
+from types import SimpleNamespace
+
 import torch
 from torch import nn
 
@@ -42,6 +44,40 @@ def make_tanh_lut(device) -> torch.Tensor:
     idx = torch.arange(-128, 128, dtype=torch.float32)
     lut = (torch.tanh(idx * (TANH_DOMAIN / 127.0)) * 127.0).round().clamp(-127.0, 127.0)
     return lut.to(torch.int8).to(device)
+
+
+def ks3_weights(down: torch.Tensor, up: torch.Tensor, coefficients: torch.Tensor,
+                raw_scale: torch.Tensor, raw_shift: torch.Tensor) -> SimpleNamespace:
+    """A plain holder of one KS3 decoder's five fp32 tensors under the attribute
+    names KS3Int8Cell reads from the reference's fp32 cell: down.weight
+    (charts, d), up.weight (d, charts), coefficients (charts, 6), raw_scale and
+    raw_shift (charts,), num_charts and subspace_rank (rank-1 charts only)."""
+    charts = down.shape[0]
+    if coefficients.numel() != charts * 6:
+        raise NotImplementedError("ksdraft_b200 implements rank-1 charts (subspace_rank == 1)")
+    return SimpleNamespace(down=SimpleNamespace(weight=down), up=SimpleNamespace(weight=up),
+                           coefficients=coefficients.reshape(charts, 6), raw_scale=raw_scale,
+                           raw_shift=raw_shift, num_charts=charts, subspace_rank=1)
+
+
+def init_ks3_weights(d_model: int, charts: int, *, generator: torch.Generator | None = None,
+                     device=None, std: float = 0.02, coeff_std: float = 0.05) -> SimpleNamespace:
+    """Seeded synthetic KS3 weights for benches and tests: projections N(0, std)
+    (the BASELINE configs' weight init), spine coefficients N(0, coeff_std),
+    warp raw scale 0.75 and raw shift 0.  Drawn on `generator`'s device."""
+    gdev = generator.device if generator is not None else torch.device("cpu")
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=generator, device=gdev)
+    w = ks3_weights(randn(charts, d_model) * std, randn(d_model, charts) * std,
+                    randn(charts, 6) * coeff_std, torch.full((charts,), 0.75, device=gdev),
+                    torch.zeros(charts, device=gdev))
+    if device is not None:
+        for t in (w.down, w.up):
+            t.weight = t.weight.to(device)
+        w.coefficients = w.coefficients.to(device)
+        w.raw_scale, w.raw_shift = w.raw_scale.to(device), w.raw_shift.to(device)
+    return w
 
 
 def _pack_device(t: torch.Tensor) -> torch.device:

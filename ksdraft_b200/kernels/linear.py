@@ -73,14 +73,56 @@ class Int8Linear(nn.Module):
         return y.reshape(*x.shape[:-1], self.out_features).to(x.dtype)
 
     def fake_quant_forward(self, x: torch.Tensor) -> torch.Tensor:
-        """STE path: fp32 GEMM on quantise-dequantised operands (autograd-safe)."""
+        """STE path (linear.py:75-97): fp32 GEMM on quantise-dequantised operands.
+
+        The weight is quantised without grad (straight through); the input's
+        quantisation carries the reference's scale gradient (ste_input_grad)."""
         self._quantize_weight()
         w = dequantize_last_dim(self.weight_codes.detach().float(), self.weight_scales.detach()) \
             + (self.weight - self.weight.detach())
         x2 = x.reshape(-1, x.shape[-1]).float()
-        codes, scales = quantize_last_dim(x2.detach())
-        xq = dequantize_last_dim(codes, scales) + (x2 - x2.detach())
+        xq = _QuantSTE.apply(x2)
         y = xq @ w.reshape(self.out_features, self.in_features).T
         if self.bias is not None:
             y = y + self.bias.float()
         return y.reshape(*x.shape[:-1], self.out_features).to(x.dtype)
+
+
+def ste_input_grad(x: torch.Tensor, codes: torch.Tensor, gx: torch.Tensor) -> torch.Tensor:
+    """Input gradient of the reference's STE quantisation (linear.py:92-93).
+
+    quantize_last_dim runs on the grad-carrying input there, so besides the
+    straight-through gx the GS128 scale = fp16(clamp(amax / 127, 2^-24, 65504))
+    (quant.py:47-49) passes a gradient: per group G = sum(gx * codes), rounded to
+    fp16 where it crosses the fp16 scale tensor, / 127, only inside the clamp
+    range, split evenly over the elements tied at amax, times their sign.
+    x, codes, gx: (M, K) on the device; returns gx + that term (fp32)."""
+    M, K = x.shape
+    pad = -K % GROUP_SIZE
+    xp = torch.nn.functional.pad(x.float(), (0, pad)).reshape(M, -1, GROUP_SIZE)
+    cp = torch.nn.functional.pad(codes.float(), (0, pad)).reshape(M, -1, GROUP_SIZE)
+    gp = torch.nn.functional.pad(gx.float(), (0, pad)).reshape(M, -1, GROUP_SIZE)
+    a = xp.abs()
+    amax = a.amax(-1, keepdim=True)
+    tie = a == amax
+    g16 = (gp * cp).sum(-1, keepdim=True).to(torch.float16).float()
+    s32 = amax / 127.0
+    inside = (s32 >= 2.0**-24) & (s32 <= 65504.0)
+    share = torch.where(inside, g16 / 127.0 / tie.sum(-1, keepdim=True), 0.0)
+    extra = torch.where(tie, torch.sign(xp) * share, 0.0)
+    return gx.float() + extra.reshape(M, -1)[:, :K]
+
+
+class _QuantSTE(torch.autograd.Function):
+    """deq(q(x)) with the reference's STE gradient (ste_input_grad)."""
+
+    @staticmethod
+    def forward(ctx, x2):
+        codes, scales = quantize_last_dim(x2.detach())
+        ctx.save_for_backward(x2.detach(), codes)
+        return dequantize_last_dim(codes, scales)
+
+    @staticmethod
+    def backward(ctx, g):
+        x2, codes = ctx.saved_tensors
+        return ste_input_grad(x2, codes, g)

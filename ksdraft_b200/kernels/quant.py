@@ -32,9 +32,11 @@ def _padded_length(n: int, group: int = GROUP_SIZE) -> int:
 
 
 def _check_group(group: int) -> None:
+    """The GS128 grid is the one this build implements (the north-star layout);
+    any other group is rejected as an invalid argument, as the reference rejects
+    groups its kernels cannot tile (ks3_triton.py:185-186)."""
     if group != GROUP_SIZE:
-        raise NotImplementedError(
-            f"ksdraft_b200 implements the GS128 grid only (group={group} requested)")
+        raise ValueError(f"ksdraft_b200 implements the GS128 grid only (group={group} requested)")
 
 
 def _rows_view(x: torch.Tensor) -> torch.Tensor:

@@ -1,6 +1,5 @@
-"""Model-side ops of the hot path: the Rosa mixer and the KS3 weight container."""
+"""Model-side ops of the hot path: the Rosa mixer and the vocab-sharded LM head."""
 
 from .rosa import RosaMixer, _match_payload_sign
-from .ks3 import KS3
 
-__all__ = ["RosaMixer", "_match_payload_sign", "KS3"]
+__all__ = ["RosaMixer", "_match_payload_sign"]

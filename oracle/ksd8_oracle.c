@@ -35,6 +35,18 @@ static inline float hmul(float a, float b) { return hr(a * b); }
 static inline float hadd(float a, float b) { return hr(a + b); }
 static inline float hsub(float a, float b) { return hr(a - b); }
 
+/* fp16 tanh of an fp16 value, correctly rounded: the reference's CPU
+ * torch.tanh on fp16 (ks3_int8.py:366-367) and on fp16-valued fp32 followed
+ * by .to(float16) (:189-192) give exactly this for every fp16 input (the tests
+ * check all of them).  double tanh, then double -> fp32 -> fp16 (an exact
+ * rounding, 24 >= 2 * 11 + 2). */
+static inline float tanh16r(float v16) { return hr((float)tanh((double)v16)); }
+
+/* tanh16r over the fp16 bit patterns 0..n-1 (non-negative values). */
+void or_tanh16_table(int64_t n, f16bits* out) {
+  for (int64_t i = 0; i < n; ++i) out[i] = f2h(tanh16r(h2f((f16bits)i)));
+}
+
 /* GS scale of quant.py:47-49: fp32 amax/127, clamp [2^-24, 65504], round via fp16. */
 static inline float gs_scale(float amax, f16bits* out) {
   float s = amax / 127.0f;
@@ -249,9 +261,9 @@ float or_spine1(float x, const int8_t* cc, float ps, float scale, float shift,
   }
   if (nl == 1) {
     float th = hr(x * 0.25f);
-    float t = hr(4.0f * tanhf(th));
+    float t = hr(4.0f * tanh16r(th));
     float warp = hr(scale * (t + shift));
-    float z = hr(tanhf(warp));
+    float z = tanh16r(warp);
     float a = hr((float)(2 * c0 - 2 * c1 + c2 + c3));
     float b = hr((float)(-3 * c0 + 3 * c1 - 2 * c2 - c3));
     float poly = hadd(hmul(a, t), b);
@@ -344,9 +356,9 @@ void or_ks3_vjp(const f16bits* value, const f16bits* coords, int64_t m, int64_t 
     for (int64_t r = 0; r < m; ++r) {
       const float v = h2f(value[r * charts + c]);
       const float x16 = h2f(coords[r * charts + c]);
-      const float t = hmul(4.f, hr(tanhf(hmul(x16, 0.25f))));
+      const float t = hmul(4.f, tanh16r(hmul(x16, 0.25f)));
       const float u = hadd(t, shift);
-      const float z = hr(tanhf(hmul(scale, u)));
+      const float z = tanh16r(hmul(scale, u));
       float sp = hadd(hmul(cubic, t), quad);
       sp = hadd(hmul(sp, t), c2);
       sp = hadd(hmul(sp, t), c0);

@@ -40,6 +40,7 @@ def lib() -> C.CDLL:
             "or_ks3_vjp": [P, P, i64, i64, P, P, P, P, P, P, P, P],
             "or_rosa_match_bruteforce": [P, P, P, i64, i64, i32, P, P, P],
             "or_rosa_match_dp": [P, P, P, i64, i64, i32, P, P, P, P, i32],
+            "or_tanh16_table": [i64, P],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -210,6 +211,61 @@ def lm_head_ce(x, w, targets):
 
 
 # ------------------------------------------------------------------ KS3
+
+def ste_scale_grad(x: np.ndarray, codes: np.ndarray, gx: np.ndarray) -> np.ndarray:
+    """The gradient the reference's STE input path sends through the GS128 scale
+    (ksdraft/kernels/linear.py:92-93 quantises the grad-carrying input, so the
+    scale = fp16(clamp(amax / 127)) of quant.py:47-49 is differentiable): per
+    group, G = sum(gx * codes) rounded to fp16 (the gradient crosses the fp16
+    scale tensor), / 127, inside the clamp range only, split evenly over the
+    elements tied at amax, times sign(x).  x, codes, gx: (M, K)."""
+    M, K = x.shape
+    Kp = -(-K // 128) * 128
+    G = Kp // 128
+
+    def pad(a):
+        out = np.zeros((M, Kp), np.float32)
+        out[:, :K] = a
+        return out.reshape(M, G, 128)
+    xp, cp, gp = pad(x), pad(codes), pad(gx)
+    a = np.abs(xp)
+    amax = a.max(-1, keepdims=True)
+    tie = a == amax
+    n_tie = tie.sum(-1, keepdims=True)
+    g16 = (gp * cp).sum(-1, keepdims=True).astype(np.float16).astype(np.float32)
+    s32 = amax / np.float32(127.0)
+    inside = (s32 >= np.float32(2.0**-24)) & (s32 <= np.float32(65504.0))
+    extra = np.where(tie, np.sign(xp) * (g16 / np.float32(127.0)) / n_tie, 0.0) * inside
+    return extra.reshape(M, Kp)[:, :K].astype(np.float32)
+
+
+def int8_linear_ste(x, w, b, gy):
+    """Int8Linear training forward + backward (ksdraft/kernels/linear.py:75-97):
+    y = deq(q(x)) @ deq(q(w))^T + b in fp32; dW = gy^T deq(q(x)) (straight
+    through the weight quantiser, which runs without grad, :46-56); dx = gy
+    deq(q(w)) plus the scale term of ste_scale_grad; db = sum gy."""
+    xq, xs = quantize_rows_c(x)
+    wq, ws = quantize_rows_c(w)
+    xd = dequantize_last_dim(xq, xs)
+    wd = dequantize_last_dim(wq, ws)
+    y = xd @ wd.T
+    if b is not None:
+        y = y + b
+    gx = gy @ wd
+    dx = gx + ste_scale_grad(x, xq.astype(np.float32), gx)
+    dw = gy.T @ xd
+    db = gy.sum(0) if b is not None else None
+    return y.astype(np.float32), dx, dw.astype(np.float32), db
+
+
+def tanh16_table(n: int = 0x4600) -> np.ndarray:
+    """uint16 bits of the correctly rounded fp16 tanh of the fp16 values with bits
+    0..n-1 (what the reference's CPU torch.tanh gives for fp16 inputs,
+    ks3_int8.py:366-367)."""
+    out = np.empty(n, np.uint16)
+    lib().or_tanh16_table(n, _p(out))
+    return out
+
 
 def make_tanh_lut() -> np.ndarray:
     """ks3_int8.py:50-54 restated: round(tanh(i * 3.2/127) * 127), i in [-128, 127]."""

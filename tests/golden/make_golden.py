@@ -1,6 +1,6 @@
 """Generate the golden fixtures of tests/golden/ by running the REFERENCE itself.
 
-    python tests/golden/make_golden.py [--ref /path/to/ksdraft-checkout]
+    python tests/golden/make_golden.py --ref /path/to/ksdraft-checkout [--only TOPIC ...]
 
 Imports the reference package (curvedinf/ksdraft) read-only and runs its own
 CPU tier on seeded inputs; writes one compressed .npz per topic.  Only this
@@ -11,6 +11,7 @@ GPU box never needs the reference at run time.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -173,8 +174,38 @@ def gen_ks3_layer():
     x = torch.randn(M, d).to(torch.bfloat16).requires_grad_(True)
     gout = (torch.randn(M, d) * 1e-2).to(torch.bfloat16)
     y = q(x)
-    y.backward(gout)
-    out = dict(x=f32(x), grad=f32(gout), down=f32(q.master_down), up=f32(q.master_up),
+    # record the backward's own intermediates (ks3_int8.py:345-424) by wrapping
+    # the module-level quantiser and GEMM it calls, in call order
+    import ksdraft.kernels.ks3_int8 as K
+    rec_q, rec_g = [], []
+    orig_q, orig_g = K.quantize_last_dim, K.w8a8_gemm
+
+    def q_rec(t, group=128):
+        r = orig_q(t, group)
+        rec_q.append((t.detach().clone(), r))
+        return r
+
+    def g_rec(*a):
+        r = orig_g(*a)
+        rec_g.append(r.detach().clone())
+        return r
+    K.quantize_last_dim, K.w8a8_gemm = q_rec, g_rec
+    try:
+        y.backward(gout)
+    finally:
+        K.quantize_last_dim, K.w8a8_gemm = orig_q, orig_g
+    # quantiser calls: g, up^T, dc, down^T, dc^T, x^T, g^T, h^T; GEMMs: value, dx, ddown, dup
+    assert len(rec_q) == 8 and len(rec_g) == 4, (len(rec_q), len(rec_g))
+    dc = rec_q[2][0]
+    bwd = dict(dc=f32(dc), dcq=i8(rec_q[2][1][0]), dcs=f16(rec_q[2][1][1]),
+               downT_q=i8(rec_q[3][1][0]), downT_s=f16(rec_q[3][1][1]),
+               dcT_q=i8(rec_q[4][1][0]), dcT_s=f16(rec_q[4][1][1]),
+               xT_q=i8(rec_q[5][1][0]), xT_s=f16(rec_q[5][1][1]),
+               gT_q=i8(rec_q[6][1][0]), gT_s=f16(rec_q[6][1][1]),
+               hT_q=i8(rec_q[7][1][0]), hT_s=f16(rec_q[7][1][1]),
+               value_bwd=f16(rec_g[0]), dx32=f32(rec_g[1]), ddown32=f32(rec_g[2]),
+               dup32=f32(rec_g[3]))
+    out = dict(**bwd, x=f32(x), grad=f32(gout), down=f32(q.master_down), up=f32(q.master_up),
                coefficients=f32(q.master_coefficients), raw_scale=f32(q.master_raw_scale),
                raw_shift=f32(q.master_raw_shift), y=f32(y), dx=f32(x.grad),
                ddown=f32(q.master_down.grad), dup=f32(q.master_up.grad),
@@ -232,18 +263,58 @@ def gen_rosa():
     save("rosa", **out)
 
 
+def gen_tanh16():
+    """torch.tanh on every non-negative finite fp16 value (the op of
+    ks3_int8.py:366-367), as uint16 bits."""
+    bits = torch.arange(0, 0x7C00, dtype=torch.int32).to(torch.int16)
+    t = torch.tanh(bits.view(torch.float16))
+    save("tanh16", bits=t.view(torch.int16).numpy().view(np.uint16))
+
+
+def gen_linear():
+    """Int8Linear STE training forward/backward (linear.py:75-97) and the eval W8A8
+    forward (:62-73), small shapes, on the reference's CPU tier."""
+    from ksdraft.kernels.linear import Int8Linear
+    out = {}
+    g = torch.Generator().manual_seed(21)
+    for i, (M, K, N, bias) in enumerate(((64, 256, 96, True), (37, 300, 128, False),
+                                         (128, 512, 200, True))):
+        lin = Int8Linear(K, N, bias=bias)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(N, K, generator=g) * 0.05)
+            if bias:
+                lin.bias.copy_(torch.randn(N, generator=g) * 0.1)
+        x = (torch.randn(M, K, generator=g) * 2).requires_grad_(True)
+        gy = torch.randn(M, N, generator=g) * 1e-2
+        lin.train()
+        y = lin(x)
+        y.backward(gy)
+        out.update({f"c{i}_x": f32(x), f"c{i}_w": f32(lin.weight), f"c{i}_gy": f32(gy),
+                    f"c{i}_y": f32(y), f"c{i}_dx": f32(x.grad), f"c{i}_dw": f32(lin.weight.grad)})
+        if bias:
+            out.update({f"c{i}_b": f32(lin.bias), f"c{i}_db": f32(lin.bias.grad)})
+        lin.eval()
+        with torch.no_grad():
+            out[f"c{i}_y_eval"] = f32(lin(x.detach()))
+    save("linear", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("KSD8_REFERENCE"),
+                    help="checkout of the reference package (or set KSD8_REFERENCE)")
+    ap.add_argument("--only", nargs="*", default=None, help="topics to regenerate")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("--ref (or KSD8_REFERENCE) must name the reference checkout")
     sys.path.insert(0, args.ref)
     torch.set_num_threads(8)
-    gen_quant()
-    gen_dither()
-    gen_gemm()
-    gen_ks3()
-    gen_ks3_layer()
-    gen_rosa()
+    topics = {"quant": gen_quant, "dither": gen_dither, "gemm": gen_gemm, "ks3_spine": gen_ks3,
+              "ks3_layer": gen_ks3_layer, "rosa": gen_rosa, "tanh16": gen_tanh16,
+              "linear": gen_linear}
+    for name, fn in topics.items():
+        if args.only is None or name in args.only:
+            fn()
 
 
 if __name__ == "__main__":

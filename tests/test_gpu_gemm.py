@@ -162,15 +162,32 @@ def test_int8_linear_eval_matches_oracle(oracle):
     assert _rel(y, y_fp) < 0.05            # tests/test_int8.py:43-55 contract
 
 
-def test_int8_linear_ste_grads():
+def test_int8_linear_ste_grads_match_reference(golden):
+    """Training forward + backward of Int8Linear (STE, linear.py:75-97) against
+    the reference's own CPU run: y, dx (with the scale-gradient term), dW, db."""
     from ksdraft_b200.kernels.linear import Int8Linear
-    torch.manual_seed(2)
-    lin = Int8Linear.from_float(torch.nn.Linear(64, 32, bias=True).cuda())
-    x = torch.randn(4, 64, device="cuda", requires_grad=True)
-    y = lin.fake_quant_forward(x)
-    y.square().mean().backward()
-    assert x.grad is not None and torch.isfinite(x.grad).all()
-    assert lin.weight.grad is not None and torch.isfinite(lin.weight.grad).all()
+    g = golden("linear")
+    for i in range(3):
+        w = torch.from_numpy(g[f"c{i}_w"])
+        has_b = f"c{i}_b" in g
+        lin = Int8Linear(w.shape[1], w.shape[0], bias=has_b).cuda()
+        with torch.no_grad():
+            lin.weight.copy_(w)
+            if has_b:
+                lin.bias.copy_(torch.from_numpy(g[f"c{i}_b"]))
+        lin.train()
+        x = torch.from_numpy(g[f"c{i}_x"]).cuda().requires_grad_(True)
+        y = lin(x)
+        y.backward(torch.from_numpy(g[f"c{i}_gy"]).cuda())
+        assert _rel(y.detach().cpu().numpy(), g[f"c{i}_y"]) < 1e-5
+        assert _rel(x.grad.cpu().numpy(), g[f"c{i}_dx"]) < 1e-5, i
+        assert _rel(lin.weight.grad.cpu().numpy(), g[f"c{i}_dw"]) < 1e-5
+        if has_b:
+            assert _rel(lin.bias.grad.cpu().numpy(), g[f"c{i}_db"]) < 1e-5
+        lin.eval()
+        with torch.no_grad():
+            ye = lin(x.detach()).cpu().numpy()
+        assert _rel(ye, g[f"c{i}_y_eval"]) < 1e-5    # W8A8 eval vs the reference tier
 
 
 @pytest.mark.parametrize("M,N,K", [(70, 13, 256), (129, 201, 384), (300, 136, 128)])

@@ -9,14 +9,9 @@ pytestmark = pytest.mark.gpu
 
 
 def _cell(d, C, seed):
-    from ksdraft_b200.kernels.ks3_int8 import KS3Int8Cell
-    from ksdraft_b200.model.ks3 import KS3
-    torch.manual_seed(seed)
-    cell = KS3(d, C)
-    with torch.no_grad():
-        cell.down.weight.normal_(0, 0.02)
-        cell.up.weight.normal_(0, 0.02)
-    return KS3Int8Cell(cell.cuda(), nonlinear="int8", trainable=True)
+    from ksdraft_b200.kernels.ks3_int8 import KS3Int8Cell, init_ks3_weights
+    cell = init_ks3_weights(d, C, generator=torch.Generator().manual_seed(seed), device="cuda")
+    return KS3Int8Cell(cell, nonlinear="int8", trainable=True)
 
 
 def _autograd_grads(q, x, g):

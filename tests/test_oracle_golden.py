@@ -212,3 +212,54 @@ def test_rosa_python_definition(oracle):
         q, k, v = (rng.integers(0, 2, T).tolist() for _ in range(3))
         s, _, _ = oracle.rosa_match(np.array([q]), np.array([k]), np.array([v]))
         assert s[0].tolist() == oracle.rosa_sign_python(q, k, v)
+
+
+def test_tanh16_table_matches_reference(golden, oracle):
+    """The fp16 tanh of the KS3 backward (torch.tanh on fp16, ks3_int8.py:366-367)
+    on every non-negative finite fp16 input: the oracle's correctly rounded table
+    equals the reference's op bit for bit."""
+    ref = golden("tanh16")["bits"]
+    np.testing.assert_array_equal(oracle.tanh16_table(ref.size), ref)
+    # and the same op on this machine's torch, fp16 and fp16-valued fp32 inputs
+    x = torch.from_numpy(np.arange(ref.size, dtype=np.uint16).view(np.float16))
+    np.testing.assert_array_equal(torch.tanh(x).numpy().view(np.uint16), ref)
+    np.testing.assert_array_equal(torch.tanh(x.float()).half().numpy().view(np.uint16), ref)
+
+
+def test_vjp_reproduces_reference_dc(golden, oracle):
+    """Fed the reference's own value and coordinates, the oracle VJP gives the
+    reference's dc (value + dmean, ks3_int8.py:354-402) bit for bit, and both of
+    its quantisations (:410, :418)."""
+    g = golden("ks3_layer")
+    pack = oracle.ks3_pack(g["coefficients"].reshape(-1, 6), g["raw_scale"], g["raw_shift"])
+    dc, sums = oracle.ks3_vjp(g["value"], g["coords"], pack)
+    np.testing.assert_array_equal(dc.astype(np.float32), g["dc"])
+    dcq, dcs = oracle.quantize_rows_c(dc)
+    np.testing.assert_array_equal(dcq, g["dcq"])
+    np.testing.assert_array_equal(dcs.view(np.uint16), g["dcs"].view(np.uint16))
+    dcTq, dcTs = oracle.quantize_rows_c(np.ascontiguousarray(dc.T))
+    np.testing.assert_array_equal(dcTq, g["dcT_q"])
+    np.testing.assert_array_equal(dcTs.view(np.uint16), g["dcT_s"].view(np.uint16))
+    dcoeff, dscale, dshift = oracle.ks3_vjp_finish(sums, g["raw_scale"], g["raw_shift"])
+    for got, ref in ((dcoeff, g["dcoeff"]), (dscale, g["dscale"]), (dshift, g["dshift"])):
+        got = np.asarray(got, np.float32).reshape(-1)
+        assert _rel(got, ref.reshape(-1)) < 1e-3
+
+
+def test_int8_linear_ste_matches_reference(golden, oracle):
+    """Int8Linear STE (linear.py:75-97) restated with the oracle quantiser and an
+    fp32 matmul, including the gradient that crosses the input's GS128 scale:
+    forward and gradients within fp32 summation-order noise."""
+    g = golden("linear")
+    for i in range(3):
+        b = g.get(f"c{i}_b")
+        y, dx, dw, db = oracle.int8_linear_ste(g[f"c{i}_x"], g[f"c{i}_w"], b, g[f"c{i}_gy"])
+        assert _rel(y, g[f"c{i}_y"]) < 1e-5
+        assert _rel(dx, g[f"c{i}_dx"]) < 1e-5
+        assert _rel(dw, g[f"c{i}_dw"]) < 1e-5
+        if b is not None:
+            assert _rel(db, g[f"c{i}_db"]) < 1e-5
+        # without the scale term the input gradient is far off: the term is real
+        wq, ws = oracle.quantize_rows_c(g[f"c{i}_w"])
+        plain = g[f"c{i}_gy"] @ oracle.dequantize_last_dim(wq, ws)
+        assert _rel(plain, g[f"c{i}_dx"]) > 0.1
