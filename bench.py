@@ -1,22 +1,26 @@
-"""Benchmark: KSDraft INT8 training step of one KS3 decoder layer.
+"""Benchmark: the KSDraft INT8 training step (BASELINE config 4 by default).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+                    [--workload config4|config2]
 
-Workload (per GPU, weak scaling): one KS3 decoder layer at d_model=1536 with
-5888 charts, 4096 tokens (batch 8 x seq 512), INT8-native forward + backward
-(W8A8 GS128 forward, dgrad and wgrad GEMMs, fused spine / VJP cell), PTQR
-dither 0.5 LSB on the weight quantisation from a counter RNG, then the
-data-parallel gradient all-reduce (NCCL, N > 1) and an AdamW step on the fp32
-masters.  Inputs are synthetic: hidden states bf16 N(0,1), upstream gradient
-bf16 N(0,1e-2), weights N(0,0.02) (canonical KS3 init for the spine).
+config4 (the metric's "train tokens/sec"): the full 24-layer KSDraft model at
+d_model=1536 (5888 KS3 charts, 512 Rosa streams, vocab 150144 with the head
+tied to the embedding), global batch 16 x 2048 tokens of Zipf(1.1) ids with
+repeated spans plus bf16 N(0,1) teacher states (teacher_dim 384), weights
+N(0,0.02).  One step = forward, CE + transfer-space loss, backward, the
+data-parallel gradient mean (NCCL, N > 1), clip_grad_norm_(1.0) and AdamW.
+The global batch is fixed, 16/N sequences per GPU ("scaling": "strong").
+
+config2: one KS3 decoder layer INT8 fwd+bwd (+ DP all-reduce + AdamW) at 4096
+tokens per GPU (weak scaling), the round-1 workload, kept as a second line.
 
 `value`  tokens/s of the whole job with inputs resident in HBM, device-timed
          with CUDA events per step (L2 flushed between steps), max over ranks.
 `e2e`    the same step through the public API with pinned host inputs copied
-         in and the layer output copied out inside the timed region.
-`roofline` the W8A8 GEMM (the dominant kernel): algorithmic ops per launch /
-         its CUDA-event duration inside the timed steps, against 2x the
-         measured dense bf16 peak of MEASURED_PEAKS.json (int8 = 2x bf16 rate).
+         in and the loss read back inside the timed region.
+`roofline` the W8A8 GEMM (the dominant kernel): algorithmic ops of every GEMM
+         launch / their summed CUDA-event durations inside the timed steps,
+         against 2x the measured dense bf16 peak (int8 = 2x the bf16 rate).
 `cpu_baseline` / `--impl reference`: the reference's own torch CPU tier
          (installed unmodified in baseline/_ref) on the same step, timed on the
          host cores for the steps that fit a time budget (the count is printed).
@@ -40,8 +44,21 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 D_MODEL, CHARTS, TOKENS, BATCH, SEQ = 1536, 5888, 4096, 8, 512
+C4_BATCH, C4_SEQ, C4_TEACHER = 16, 2048, 384
+REF_C4_TOKENS = int(os.environ.get("KSD8_REF_TOKENS", "128"))
 METRIC = "W8A8 GS128 GEMM TOPS; KSDraft INT8 train tokens/sec at 1/2/4/8 B200"
 DITHER = 0.5
+
+
+def config4(n: int) -> dict:
+    return {"workload": "BASELINE config 4: full KSDraft INT8 training step, 24 layers, "
+                        "d_model=1536, vocab=150144, 512 Rosa streams, 5888 KS3 charts, "
+                        "global batch 16 x 2048 tokens, DP over the GPUs",
+            "model": "KSDraft 24 x (Rosa + DSpine + KS3) d_model=1536 vocab=150144",
+            "global_batch": C4_BATCH, "seq_len": C4_SEQ, "tokens_per_step": C4_BATCH * C4_SEQ,
+            "sequences_per_gpu": C4_BATCH // n, "parallelism": f"dp{n}",
+            "teacher_dim": C4_TEACHER, "activations": "bf16 residual stream",
+            "l2": "flushed between timed steps (256 MiB write); step working set > L2"}
 
 
 def config(n: int) -> dict:
@@ -139,6 +156,44 @@ def reference_layer_step(tokens: int = TOKENS):
     return step, ref.__file__
 
 
+def reference_draft_step(tokens: int = REF_C4_TOKENS):
+    """The reference's own config-4 step on the host cores, on one sequence of
+    `tokens` tokens: KSDraftModel (24 layers, d_model 1536, vocab 150144, 512
+    streams, 5888 charts, teacher_dim 384) converted by to_int8 with trainable
+    KS3 cells, in training mode (the CPU hard Rosa path, rosa.py:150-165), then
+    distillation_losses, backward, clip_grad_norm_(1.0) and AdamW
+    (ksdraft/train/__init__.py:145-166)."""
+    import torch
+    ref = import_reference()
+    from ksdraft.config import KSDraftConfig
+    from ksdraft.kernels.ks3_int8 import KS3Int8Cell
+    from ksdraft.model import KSDraftModel
+    from ksdraft.model.int8_convert import to_int8
+    from ksdraft.train import distillation_losses
+    torch.set_num_threads(os.cpu_count() or 1)
+    torch.manual_seed(0)
+    cfg = KSDraftConfig(d_model=D_MODEL, layers=24, rosa_streams=512, ks3_charts=CHARTS)
+    model = KSDraftModel(cfg, teacher_dim=C4_TEACHER)
+    q = to_int8(model)
+    for blk, src in zip(q.blocks, model.blocks):
+        blk.ffn = KS3Int8Cell(src.ffn, 128, "int8", trainable=True)
+    del model
+    q.train()
+    opt = torch.optim.AdamW(q.parameters(), lr=3e-4, weight_decay=0.01)
+    ids = torch.from_numpy(rosa_ids(1, tokens + 1, seed=7))
+    states = torch.randn(1, tokens, C4_TEACHER).to(torch.bfloat16)
+
+    def step():
+        logits, feats = q(ids[:, :-1], teacher_states=states)
+        loss, _ = distillation_losses(logits, ids, feats, q.embedding.weight, None, None,
+                                      0.5, 0.0)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(q.parameters(), 1.0)
+        opt.step()
+    return step, ref.__file__
+
+
 def port_layer_step(tokens: int = 128):
     """Stand-in when the reference is not installed: the oracle port of the same
     layer step (oracle/, C + numpy with OpenMP) on `tokens` tokens."""
@@ -162,10 +217,27 @@ def cpu_layer_inputs(tokens: int, seed: int = 0):
     return x, down, up, coeffs, rs, rh, g
 
 
-def cpu_measure(steps: int, warmup: int, budget_s: float) -> dict:
-    """The reference's CPU tier on the config-2 step (full 4096 tokens), timed on
-    all host cores for as many of `steps` as fit in budget_s."""
+def cpu_measure(steps: int, warmup: int, budget_s: float, workload: str = "config2") -> dict:
+    """The reference's CPU tier on the workload's step, timed on all host cores for
+    as many of `steps` as fit in budget_s.  config2: the full 4096-token layer
+    step; config4: the full 24-layer model step on one sequence of
+    REF_C4_TOKENS tokens (a full 32768-token CPU step would take hours)."""
     import torch
+    if workload == "config4":
+        if import_reference() is None:
+            raise RuntimeError("the config-4 reference arm needs the reference installed in "
+                               "baseline/_ref")
+        step, where = reference_draft_step(REF_C4_TOKENS)
+        times = _timed_steps(step, steps, warmup, budget_s)
+        sec = statistics.median(times)
+        return {"value": REF_C4_TOKENS / sec, "unit": "tokens/s",
+                "cores": torch.get_num_threads(), "kind": "reference",
+                "sample": f"the reference's own 24-layer KSDraftModel int8 tier (to_int8, "
+                          f"trainable KS3, CPU hard Rosa path, float head) training step "
+                          f"(fwd, CE+transfer loss, bwd, clip, AdamW) on 1 x {REF_C4_TOKENS} "
+                          f"tokens, torch CPU tier from baseline/_ref; median of "
+                          f"{len(times)} timed steps",
+                "sec_per_step": sec, "steps_timed": len(times), "tokens_per_step": REF_C4_TOKENS}
     if import_reference() is not None:
         step, where = reference_layer_step(TOKENS)
         tokens, kind = TOKENS, "reference"
@@ -183,8 +255,8 @@ def cpu_measure(steps: int, warmup: int, budget_s: float) -> dict:
             "sec_per_step": sec, "steps_timed": len(times), "tokens_per_step": tokens}
 
 
-def cpu_baseline() -> dict:
-    m = cpu_measure(steps=2, warmup=1, budget_s=60)
+def cpu_baseline(workload: str = "config2") -> dict:
+    m = cpu_measure(steps=2, warmup=1, budget_s=60, workload=workload)
     return {k: m[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
 
@@ -193,12 +265,14 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     m = cpu_measure(steps=max(1, args.steps), warmup=max(1, min(args.warmup, 1)),
-                    budget_s=REF_BUDGET_S)
+                    budget_s=REF_BUDGET_S, workload=args.workload)
+    c4 = args.workload == "config4"
     line = {"impl": "reference", "metric": METRIC, "value": m["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": m["steps_timed"], "steps_requested": args.steps,
             "warmup": 1, "ms_per_step": m["sec_per_step"] * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic", "config": config(1),
+            "higher_is_better": True, "scaling": "strong" if c4 else "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": config4(args.gpus) if c4 else config(1),
             "cpu_baseline": {k: m[k] for k in ("kind", "cores", "sample", "value", "unit")},
             "e2e": {"value": m["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -434,6 +508,126 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def _roofline_from_gemms(gemm, peaks) -> tuple[dict, dict]:
+    """Aggregate W8A8 GEMM figures: total algorithmic ops / total event time."""
+    gemm_ms = [d for d, _ in gemm]
+    ops = [o for _, o in gemm]
+    total_ms = sum(gemm_ms)
+    achieved = sum(ops) / (total_ms / 1e3) / 1e12 if total_ms > 0 else None
+    peak_int8 = 2.0 * peaks["bf16"]
+    traffic = gemm_traffic()
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peak_int8, "unit": "TFLOP/s",
+            "frac": achieved / peak_int8 if achieved else None, "traffic": traffic,
+            "kernel": "w8a8_gemm_kernel (tcgen05 kind::i8): sum of 2*M*N*K over every GEMM "
+                      "launch in the timed steps / sum of their CUDA-event durations",
+            "peak_note": f"2 x {peaks['src']} dense bf16 TF/s (int8 rate = 2x bf16)"}
+    info = {"launches": len(gemm_ms), "total_ms": total_ms,
+            "avg_ms": statistics.mean(gemm_ms) if gemm_ms else None, "tops": achieved}
+    return roof, info
+
+
+def run_config4(args) -> None:
+    """BASELINE config 4 on N GPUs (one process each): the full training step."""
+    import torch
+    import torch.distributed as dist
+
+    from ksdraft_b200 import _lib
+    from ksdraft_b200.kernels.gemm import GemmTimer
+    from ksdraft_b200.train.dp import init_distributed
+    from ksdraft_b200.train.draft_step import DraftShape, DraftTrainStep
+
+    rank, world, local = init_distributed(timeout_s=600)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if C4_BATCH % world:
+        raise SystemExit(f"global batch {C4_BATCH} does not split over {world} GPUs")
+    B = C4_BATCH // world
+    group = dist.group.WORLD if world > 1 else None
+    step = DraftTrainStep(DraftShape(), dev, seed=1234, group=group)   # same weights on every rank
+    # this rank's sequences: Zipf(1.1) ids with repeated spans (as config 3), teacher states
+    ids = rosa_ids(C4_BATCH, C4_SEQ + 1, seed=4)[rank * B:(rank + 1) * B]
+    tok_host = torch.from_numpy(ids).pin_memory()
+    gen = torch.Generator().manual_seed(100 + rank)
+    ts_host = torch.randn(B, C4_SEQ, C4_TEACHER, generator=gen).to(torch.bfloat16).pin_memory()
+    tok_dev, ts_dev = tok_host.to(dev), ts_host.to(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(tok_dev, ts_dev)
+    barrier()
+
+    times = []
+    launches0 = _lib.LAUNCHES
+    with ClockSampler(local) as clocks, GemmTimer() as gt:
+        for _ in range(args.steps):
+            flush.zero_()
+            barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            step(tok_dev, ts_dev)
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+    launches = (_lib.LAUNCHES - launches0) // max(1, args.steps)
+    gemm = gt.durations_ms()
+    total_ms = torch.tensor([sum(times)], device=dev)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    total_ms = float(total_ms.item())
+
+    # end to end: host ids and teacher states copied in, the loss read back
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    e2e_times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        loss = step(tok_host, ts_host)
+        loss_host.copy_(loss.detach().reshape(1), non_blocking=True)
+        e.record()
+        torch.cuda.synchronize()
+        e2e_times.append(s.elapsed_time(e))
+    e2e_ms = torch.tensor([sum(e2e_times)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+    gn = float(step.last_grad_norm)
+
+    if rank == 0:
+        tokens_total = C4_BATCH * C4_SEQ * args.steps
+        peaks = load_peaks()
+        roof, ginfo = _roofline_from_gemms(gemm, peaks)
+        ginfo["share_of_step"] = ginfo["total_ms"] / sum(times) if times else None
+        line = {
+            "metric": METRIC, "value": tokens_total / (total_ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config4(world),
+            "roofline": roof, "gemm": ginfo,
+            "e2e": {"value": tokens_total / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": world * (tok_host.numel() * 8 + ts_host.numel() * 2),
+                    "d2h_bytes_per_step": world * 4},
+            "gpu_launches": launches, "loss": float(loss_host.item()), "grad_norm": gn,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_side:
+            del step, tok_dev, ts_dev, flush
+            torch.cuda.empty_cache()
+            line["side"] = side_measurements(dev)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline("config4")
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def rosa_ids(B: int, T: int, seed: int = 0, vocab: int = 150144):
     """Config-3 token ids: Zipf(1.1) over the vocabulary, then repeated spans of
     length 8-64 copied from earlier positions until 10% of positions are covered."""
@@ -617,6 +811,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("config4", "config2"), default="config4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-side", action="store_true",
                     help="skip the 1-GPU side figures (configs 1 and 3, LM head)")
@@ -632,6 +827,8 @@ def main() -> None:
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "config4":
+        run_config4(args)
     else:
         run_ours(args)
 

@@ -120,9 +120,9 @@ int ksd8_quantize_cols(const void* x, int x_dtype, const void* x_scales, int x_g
                        int64_t rows, int64_t cols, int64_t ldx, int group, int flags,
                        int8_t* codes_t, int64_t ldct, void* scales_t, int* status, void* stream);
 
-/* Y(M,N) = sum_g float(A_g . W_g^T) * (sa[m,g] * sw[n,g]), int32 dot per
+/* Y(M,N) = sum_g float(A_g . W_g^T) * sa[m,g] * sw[n,g], int32 dot per
  * 128-wide K group on tcgen05 tensor cores, fp32 group sum in the canonical
- * order acc = fmaf(float(dot_g), sa*sw, acc) for g = 0..G-1.
+ * order acc = fmaf(RN(float(dot_g) * sa[m,g]), sw[n,g], acc) for g = 0..G-1.
  * a: (m, k) int8, row stride k; w: (n, k) int8, row stride k; k % 128 == 0,
  * group must be 128; a_scales (m, k/128), w_scales (n, k/128) fp16.
  * out_dtype: KSD8_F32 / KSD8_F16 / KSD8_BF16, row stride ldo. */
@@ -218,6 +218,11 @@ int ksd8_rosa_match(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw, 
                     int64_t streams, int64_t t_len, int max_len, const float* payload,
                     void* out, int out_dtype, int64_t ob, int64_t ot, int64_t os,
                     int32_t* match_len, int32_t* match_end, int* status, void* stream);
+
+/* Matcher kernel behind ksd8_rosa_match (process-wide, identical results):
+ * 0 = prefix tables processed 32 positions per warp step (default), 1 = prefix
+ * tables one position per step, 2 = window scan (always used for T >= 8192). */
+int ksd8_rosa_set_algorithm(int algo);
 
 /* Rosa time-shift mix + per-token GS quantisation of the three projection
  * inputs: x (B, T, d) bf16/f32; mix_q/k/v (d) fp32 = sigmoid(time_mix_*);

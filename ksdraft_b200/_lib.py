@@ -58,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "ksd8_adamw_multi": [i32, vp, vp, i32, vp, vp, vp, f32, f32, f32, f32, f32, i32, vp, vp, vp],
     "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
     "ksd8_fp16_tanh_table": [i64, vp, vp],
+    "ksd8_rosa_set_algorithm": [i32],
     "ksd8_set_sm_reserve": [i32],
     "ksd8_get_sm_reserve": [],
     "ksd8_ce_partials": [vp, i32, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp],

@@ -13,6 +13,7 @@ int ksd8_quantize_cols_launch(const void*, int, const void*, int, int64_t, int64
                               int8_t*, int64_t, void*, int*, cudaStream_t);
 int ksd8_philox_launch(uint64_t, uint64_t, int64_t, float*, cudaStream_t);
 int ksd8_fp16_tanh_table_launch(int64_t, uint16_t*, cudaStream_t);
+int ksd8_rosa_algorithm(int);
 int ksd8_gemm_launch(const int8_t*, const void*, const int8_t*, const void*, int64_t, int64_t,
                      int64_t, void*, int, int64_t, const float*, int, int*, cudaStream_t, bool);
 int ksd8_ks3_pack_launch(const float*, const float*, const float*, int64_t, int8_t*, void*,
@@ -407,6 +408,12 @@ int ksd8_topk_rows(const void* vals, int dtype, const int64_t* idx, int64_t m, i
   if (m > 0 && (!vals || !out_vals || !out_ids)) return KSD8_ERR_ARG;
   return finish(ksd8_topk_rows_launch(vals, dtype, idx, m, c, ld, k, offset, out_vals, out_ids,
                                       S(stream)));
+}
+
+int ksd8_rosa_set_algorithm(int algo) {
+  if (algo < 0 || algo > 2) return KSD8_ERR_ARG;
+  ksd8_rosa_algorithm(algo);
+  return KSD8_OK;
 }
 
 int ksd8_fp16_tanh_table(int64_t n, uint16_t* out, void* stream) {

@@ -6,8 +6,13 @@
 // group, per-row fp16 scales of both operands promoted to fp32, fp32 sum over
 // groups).  The fp32 group sum is evaluated in one fixed order so that the
 // CPU oracle reproduces it bit for bit:
-//     s   = sa[m,g] * sw[n,g]                (fp32, round to nearest)
-//     acc = fmaf(float(dot_g[m,n]), s, acc)  for g = 0 .. G-1, acc0 = 0
+//     t   = RN(float(dot_g[m,n]) * sa[m,g])  (one rounding: dot is exact in fp32)
+//     acc = fmaf(t, sw[n,g], acc)            for g = 0 .. G-1, acc0 = 0
+// Two packed FMAs per output and group: t comes straight from the biased
+// accumulator bits F = 1.5 * 2^23 + dot as fma(F, sa, -1.5 * 2^23 * sa) --
+// the product F * sa is exact inside the FMA and -1.5 * 2^23 * sa is exact in
+// fp32 (an fp16 scale has 11 significant bits), so the single rounding gives
+// RN(dot * sa) with no separate int -> float conversion.
 //
 // Persistent, warp-specialised kernel; each CTA walks output tiles of
 // 128 x BN (static round robin) and, inside a tile, the K groups:
@@ -31,8 +36,8 @@
 // Conversion trick: every accumulator is pre-set (tcgen05.st) to the bit
 // pattern of 1.5 * 2^23, so after the group's MMAs it holds that pattern
 // plus the int32 dot product, i.e. the fp32 number 12582912 + dot (exact for
-// |dot| < 2^22; here |dot| <= 128 * 128 * 128 = 2^21).  One packed fp32
-// subtraction gives float(dot) with no int->float conversion.
+// |dot| < 2^22; here |dot| <= 128 * 128 * 128 = 2^21), which the first FMA of
+// the group sum consumes directly (see above).
 #include "common.cuh"
 
 namespace ksd8 {
@@ -406,7 +411,6 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
       }
     }
 
-    const float2 neg_magic = make_float2(-MAGIC_F, -MAGIC_F);
     float2 acc[CPT / 2];
     bool ok = true;
     int gg = 0;
@@ -426,6 +430,8 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
         const float* sc = sScale + slot * L::SCALE_FLOATS;
         const float sa = sc[row];
         const float2 sa2 = make_float2(sa, sa);
+        const float ca = __fmul_rn(-MAGIC_F, sa);  // exact: sa has 11 significant bits
+        const float2 ca2 = make_float2(ca, ca);
         const float* sw = sc + BM + col0;
         const uint32_t tb = t_row + buf * BN + col0;
         if constexpr (EARLY) {
@@ -461,12 +467,12 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
             for (int j = 0; j < CPT; j += 4) {
               const float4 w4 = *reinterpret_cast<const float4*>(sw + j);
               const int o = j / 2;
-              const float2 d0 = __fadd2_rn(
-                  make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), neg_magic);
-              const float2 d1 = __fadd2_rn(
-                  make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])), neg_magic);
-              acc[o] = __ffma2_rn(d0, __fmul2_rn(sa2, make_float2(w4.x, w4.y)), acc[o]);
-              acc[o + 1] = __ffma2_rn(d1, __fmul2_rn(sa2, make_float2(w4.z, w4.w)), acc[o + 1]);
+              const float2 t0 = __ffma2_rn(
+                  make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), sa2, ca2);
+              const float2 t1 = __ffma2_rn(
+                  make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])), sa2, ca2);
+              acc[o] = __ffma2_rn(t0, make_float2(w4.x, w4.y), acc[o]);
+              acc[o + 1] = __ffma2_rn(t1, make_float2(w4.z, w4.w), acc[o + 1]);
             }
           }
           __syncwarp();
@@ -495,13 +501,13 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
               for (int j = 0; j < LDW; j += 4) {
                 const float4 w4 = *reinterpret_cast<const float4*>(sw + c * LDW + j);
                 const int o = (c * LDW + j) / 2;
-                const float2 d0 = __fadd2_rn(
-                    make_float2(__uint_as_float(rc[j]), __uint_as_float(rc[j + 1])), neg_magic);
-                const float2 d1 = __fadd2_rn(
-                    make_float2(__uint_as_float(rc[j + 2]), __uint_as_float(rc[j + 3])),
-                    neg_magic);
-                acc[o] = __ffma2_rn(d0, __fmul2_rn(sa2, make_float2(w4.x, w4.y)), acc[o]);
-                acc[o + 1] = __ffma2_rn(d1, __fmul2_rn(sa2, make_float2(w4.z, w4.w)), acc[o + 1]);
+                const float2 t0 = __ffma2_rn(
+                    make_float2(__uint_as_float(rc[j]), __uint_as_float(rc[j + 1])), sa2, ca2);
+                const float2 t1 = __ffma2_rn(
+                    make_float2(__uint_as_float(rc[j + 2]), __uint_as_float(rc[j + 3])), sa2,
+                    ca2);
+                acc[o] = __ffma2_rn(t0, make_float2(w4.x, w4.y), acc[o]);
+                acc[o + 1] = __ffma2_rn(t1, make_float2(w4.z, w4.w), acc[o + 1]);
               }
             }
             tmem_st_magic_w<LDW>(tb + c * LDW);

@@ -271,6 +271,151 @@ __global__ void __launch_bounds__(RP_WARPS * 32) rosa_match_prefix_kernel(MatchA
   }
 }
 
+// ---------------------------------------------------------------- chunked matcher
+//
+// The same prefix tables, processed 32 positions at a time: lane i owns query
+// t = t0 + i and key j = t0 - 1 + i.  The tables hold the keys j <= t0 - 2
+// (inserted by earlier chunks); each lane reads its query's 12 levels itself
+// (independent loads) and walks the level-12 chain when it hits; the keys of
+// the chunk itself (t0 - 1 <= j <= t - 1) are compared directly, broadcast by
+// shuffles.  A longest match found among the chunk's keys is later than any
+// table key, so it wins ties.  Then the chunk's 32 keys are inserted into
+// every level at once: lanes whose prefixes collide are grouped with
+// match_any, the highest lane (latest key) writes the level entry, and the
+// level-12 links point each key at the next older key of its group (or at the
+// previous head).  About 12 warp instructions per position instead of ~175
+// for the one-position-per-step walk, with 12 independent table loads per
+// lane instead of a dependent chain.
+#ifndef KSD8_RC_WARPS
+#define KSD8_RC_WARPS 16
+#endif
+constexpr int RC_WARPS = KSD8_RC_WARPS;  // streams per CTA, up to what shared memory holds
+
+__global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_chunk_kernel(MatchArgs a,
+                                                                          int stride) {
+  extern __shared__ __align__(16) uint8_t rsm_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t stream = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (stream >= a.batch * a.streams) return;  // the whole warp: no CTA barrier below
+  const int64_t T = a.t_len;
+  const int64_t nw = (T + 63) / 64;
+  uint8_t* base = rsm_raw + (size_t)warp * stride;
+  uint16_t* tbl = reinterpret_cast<uint16_t*>(base);
+  uint16_t* prev = tbl + RP_TBL;
+  uint64_t* sq = reinterpret_cast<uint64_t*>(base + (((size_t)RP_TBL + T) * 2 + 15) / 16 * 16);
+  uint64_t* sk = sq + nw;
+  uint64_t* sv = sk + nw;
+  for (int i = lane; i < RP_TBL / 8; i += 32) reinterpret_cast<uint4*>(tbl)[i] = make_uint4(0, 0, 0, 0);
+  for (int64_t i = lane; i < nw; i += 32) {
+    sq[i] = a.qw[stream * nw + i];
+    sk[i] = a.kw[stream * nw + i];
+    sv[i] = a.vw[stream * nw + i];
+  }
+  __syncwarp();
+  const int64_t b = stream / a.streams, s = stream % a.streams;
+  const float pay = a.payload ? a.payload[s] : 1.f;
+  const unsigned full = 0xffffffffu;
+  for (int64_t t0 = 0; t0 < T; t0 += 32) {
+    const int64_t t = t0 + lane;
+    const bool valid = t < T;
+    const uint64_t wq = valid ? window_sm(sq, t) : 0ull;
+    const int cap = valid ? (int)min((int64_t)a.max_len, t) : 0;
+    const int64_t jk = t0 - 1 + lane;                  // this lane's key
+    const bool kin = jk >= 0 && jk < T;
+    const uint64_t wk = kin ? window_sm(sk, jk) : 0ull;
+
+    // keys of earlier chunks: the highest level whose L-bit prefix is present
+    uint32_t hit[RP_LEVELS];
+#pragma unroll
+    for (int L = 1; L <= RP_LEVELS; ++L)
+      hit[L - 1] = L <= cap ? tbl[rp_off(L) + (int)(wq >> (64 - L))] : 0u;
+    int best = 0;
+    int64_t bestj = -1;
+#pragma unroll
+    for (int L = 1; L <= RP_LEVELS; ++L)
+      if (hit[L - 1]) {
+        best = L;
+        bestj = (int64_t)hit[L - 1] - 1;
+      }
+    if (best == RP_LEVELS && cap > RP_LEVELS) {
+      // exact length among the keys sharing the top RP_LEVELS bits, newest first
+      const uint32_t head = hit[RP_LEVELS - 1];
+      best = 0;
+      bestj = -1;
+      for (uint32_t c = head; c != 0;) {
+        const int64_t j = (int64_t)c - 1;
+        const uint64_t x = wq ^ window_sm(sk, j);
+        int l = x == 0ull ? 64 : __clzll((long long)x);
+        l = min(l, (int)min((int64_t)cap, j + 1));
+        if (l > best) {
+          best = l;
+          bestj = j;
+          if (best == cap) break;
+        }
+        c = prev[j];
+      }
+    }
+    // keys of this chunk, j = t0 - 1 + i for i <= lane (j <= t - 1), compared directly
+    int lc = 0;
+    int64_t jc = -1;
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) {
+      const uint64_t wki = __shfl_sync(full, wk, i);
+      const int64_t j = t0 - 1 + i;
+      if (i <= lane && j >= 0) {
+        const uint64_t x = wq ^ wki;
+        int l = x == 0ull ? 64 : __clzll((long long)x);
+        l = min(l, (int)min((int64_t)cap, j + 1));
+        if (l > 0 && l >= lc) {
+          lc = l;
+          jc = j;
+        }
+      }
+    }
+    if (lc > 0 && lc >= best) {
+      best = lc;
+      bestj = jc;
+    }
+    if (valid) {
+      float sign = -1.f;
+      if (bestj >= 0) {
+        const int64_t succ = bestj + 1;
+        sign = ((sv[succ >> 6] >> (succ & 63)) & 1ull) ? 1.f : -1.f;
+      }
+      const float o = pay * sign;
+      const int64_t oo = b * a.ob + t * a.ot + s * a.os;
+      if (a.out_dtype == KSD8_F32)
+        reinterpret_cast<float*>(a.out)[oo] = o;
+      else if (a.out_dtype == KSD8_BF16)
+        reinterpret_cast<__nv_bfloat16*>(a.out)[oo] = __float2bfloat16_rn(o);
+      else
+        reinterpret_cast<__half*>(a.out)[oo] = __float2half_rn(o);
+      if (a.match_len) a.match_len[stream * T + t] = best;
+      if (a.match_end) a.match_end[stream * T + t] = (int32_t)bestj;
+    }
+
+    // insert this chunk's keys: level L takes key j when j >= L - 1
+    __syncwarp();  // every lane has finished reading the tables of this chunk
+#pragma unroll
+    for (int L = 1; L <= RP_LEVELS; ++L) {
+      const bool ins = kin && jk >= L - 1;
+      const unsigned im = __ballot_sync(full, ins);
+      if (ins) {
+        const int idx = rp_off(L) + (int)(wk >> (64 - L));
+        const unsigned grp = __match_any_sync(im, idx);
+        if (L == RP_LEVELS) {
+          const unsigned lower = grp & ((1u << lane) - 1u);
+          prev[jk] = lower ? (uint16_t)(t0 + (31 - __clz((int)lower)))  // (t0-1+i) + 1
+                           : tbl[idx];
+        }
+        __syncwarp(im);  // the old head is read before the newest key replaces it
+        if (lane == 31 - __clz((int)grp)) tbl[idx] = (uint16_t)(jk + 1);
+      }
+      __syncwarp();
+    }
+  }
+}
+
 struct TimemixArgs {
   const void* x;
   int64_t batch, t_len, d;
@@ -501,6 +646,15 @@ int ksd8_rosa_pack_bits_launch(const void* x, int x_dtype, int64_t batch, int64_
   return KSD8_OK;
 }
 
+// Matcher selection (process-wide): 0 = chunked prefix tables (default),
+// 1 = one position per step prefix tables, 2 = window scan.  Streams of 8192 or
+// more positions always take the window scan.  algo < 0 only reads.
+int ksd8_rosa_algorithm(int algo) {
+  static int g_algo = 0;
+  if (algo >= 0 && algo <= 2) g_algo = algo;
+  return g_algo;
+}
+
 int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
                            int64_t batch, int64_t streams, int64_t t_len, int max_len,
                            const float* payload, void* out, int out_dtype, int64_t ob, int64_t ot,
@@ -521,7 +675,8 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
   a.qw = qw; a.kw = kw; a.vw = vw; a.batch = batch; a.streams = streams; a.t_len = t_len;
   a.max_len = max_len; a.payload = payload; a.out = out; a.out_dtype = out_dtype;
   a.ob = ob; a.ot = ot; a.os = os; a.match_len = match_len; a.match_end = match_end;
-  if (t_len < RP_TMAX) {
+  const int algo = ksd8_rosa_algorithm(-1);
+  if (t_len < RP_TMAX && algo != 2) {
     static unsigned prefix_attr = 0;
     // bytes per warp: tables + links (16-byte aligned), then 3 x ceil(T/64) words
     // (a multiple of 16 bytes, so that every warp's region keeps the 16-byte
@@ -529,18 +684,25 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
     const int stride = (int)(((((size_t)RP_TBL + t_len) * 2 + 15) / 16 * 16 +
                               3 * 8 * (size_t)((t_len + 63) / 64) + 15) / 16 * 16);
     int nwarps = (int)((227 * 1024) / (size_t)stride);
-    if (nwarps > RP_WARPS) nwarps = RP_WARPS;
+    const int cap_warps = algo == 1 ? RP_WARPS : RC_WARPS;
+    if (nwarps > cap_warps) nwarps = cap_warps;
     const size_t psmem = (size_t)nwarps * stride;
     if (!(prefix_attr & (1u << dev))) {
       if (cudaFuncSetAttribute(rosa_match_prefix_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-          cudaSuccess)
+              cudaSuccess ||
+          cudaFuncSetAttribute(rosa_match_chunk_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+              cudaSuccess)
         return KSD8_ERR_LAUNCH;
       prefix_attr |= (1u << dev);
     }
     const int64_t n = batch * streams;
-    rosa_match_prefix_kernel<<<(unsigned)((n + nwarps - 1) / nwarps), nwarps * 32, psmem,
-                               stream>>>(a, stride);
+    const unsigned grid = (unsigned)((n + nwarps - 1) / nwarps);
+    if (algo == 1)
+      rosa_match_prefix_kernel<<<grid, nwarps * 32, psmem, stream>>>(a, stride);
+    else
+      rosa_match_chunk_kernel<<<grid, nwarps * 32, psmem, stream>>>(a, stride);
     return KSD8_OK;
   }
   int threads = 512;

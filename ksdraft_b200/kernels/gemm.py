@@ -4,7 +4,7 @@
 signature, checks and padding (gemm.py:60-74) and returns fp32 (M, N).  The
 work runs in `ksd8_w8a8_gemm`: tcgen05 kind::i8 MMAs fed by TMA, an int32
 accumulator per 128-wide K group in TMEM, and the fp32 group sum
-acc = fmaf(float(dot_g), sa*sw, acc) in the epilogue.
+acc = fmaf(RN(float(dot_g) * sa), sw, acc) in the epilogue.
 
 `gemm_out` is the internal form used by the fused cells: output dtype
 (fp32/bf16/fp16), a row-stride, an optional fp32 bias, fp16 saturation and a

@@ -158,6 +158,20 @@ def _pad_k(t: torch.Tensor) -> torch.Tensor:
     return torch.nn.functional.pad(t, (0, pad)) if pad else t
 
 
+def check_targets(targets: torch.Tensor, vocab: int) -> None:
+    """Targets must index the vocabulary: F.cross_entropy raises on anything
+    else.  Its ignore_index (-100) is rejected too: the reference trainer never
+    produces such targets (ksdraft/train/__init__.py:75-77), and a silent
+    mean over fewer rows would differ from what this head computes.  One host
+    read of the min and max."""
+    if targets.numel() == 0:
+        return
+    lo, hi = int(targets.min()), int(targets.max())
+    if lo < 0 or hi >= vocab:
+        raise ValueError(f"targets must lie in [0, {vocab}); got [{lo}, {hi}]"
+                         + (" (ignore_index targets are not supported)" if lo == -100 else ""))
+
+
 class _HeadCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, targets, head):
@@ -190,16 +204,28 @@ class _HeadCE(torch.autograd.Function):
             dist.all_reduce(dx, group=head.group)
         # dW_shard = q(dl^T) @ q(x^T)^T, contracted over the tokens
         xT_q, xT_s = quantize_cols(x2)                           # (d, M)
-        dw = gemm_out(dlT_q, dlT_s, _pad_k(xT_q), xT_s)
+        if head.tied is not None:
+            # tied to the full embedding master: its gradient rows of this shard
+            dw = torch.zeros_like(head.tied)
+            gemm_out(dlT_q, dlT_s, _pad_k(xT_q), xT_s,
+                     out=dw[head.vstart:head.vstart + head.v_local])
+        else:
+            dw = gemm_out(dlT_q, dlT_s, _pad_k(xT_q), xT_s)
         return dx.reshape(ctx.x_shape).to(ctx.x_dtype), dw, None, None
 
 
 class VocabParallelHead(torch.nn.Module):
     """One rank's vocab shard of a W8A8 GS128 LM head.
 
-    weight: the full (vocab, d) master (e.g. the tied embedding, draft.py:51)
-    or this rank's (V_local, d) shard with `vstart` given; the shard is kept as
-    an fp32 master parameter and re-quantised per row when it changes."""
+    weight: either the tied embedding master itself -- a (vocab, d) fp32
+    nn.Parameter, as the reference ties head and embedding (draft.py:51) -- in
+    which case the head reads its rows [vstart, vstart + V_local) in place and
+    its weight gradient lands in those rows of the embedding's gradient (zero
+    elsewhere), so embedding and head stay one tensor; or a plain tensor (the
+    full master, or this rank's (V_local, d) shard with `vstart` given), copied
+    into an untied fp32 parameter of the shard.  Codes are re-quantised when
+    the master's version changes (in-place torch updates); code that updates it
+    outside torch calls invalidate()."""
 
     def __init__(self, weight: torch.Tensor, vocab: int | None = None, group=None,
                  vstart: int | None = None):
@@ -207,24 +233,44 @@ class VocabParallelHead(torch.nn.Module):
         rank, world = _world(group)
         self.group = group
         self.vocab = int(vocab if vocab is not None else weight.shape[0])
+        tie = isinstance(weight, torch.nn.Parameter) and vstart is None and \
+            weight.dtype == torch.float32 and weight.shape[0] == self.vocab
         if vstart is None:
             start, size = vocab_shard(self.vocab, rank, world)
-            shard = weight[start:start + size]
         else:
-            start, shard = int(vstart), weight
+            start, size = int(vstart), weight.shape[0]
         self.vstart = start
-        self.weight = torch.nn.Parameter(shard.detach().float().clone())
+        self._size = size
+        if tie:
+            self.tied = weight                  # not registered again: the embedding owns it
+            self._own = None
+        else:
+            self.tied = None
+            shard = weight[start:start + size] if vstart is None else weight
+            self._own = torch.nn.Parameter(shard.detach().float().clone())
         self._codes = None
         self._codes_t = None
         self._version = None
 
     @property
+    def weight(self) -> torch.Tensor:
+        """This rank's (V_local, d) fp32 rows (a view of the tied embedding)."""
+        if self.tied is not None:
+            return self.tied[self.vstart:self.vstart + self._size]
+        return self._own
+
+    @property
     def v_local(self) -> int:
-        return self.weight.shape[0]
+        return self._size
+
+    def invalidate(self) -> None:
+        self._codes = None
+        self._codes_t = None
 
     def weight_codes(self):
         """Per-row GS128 codes of the shard, re-quantised when the master changes."""
-        v = self.weight._version
+        src = self.tied if self.tied is not None else self._own
+        v = src._version
         if self._codes is None or self._version != v:
             self._codes = quantize_last_dim(self.weight.detach())
             self._codes_t = None
@@ -249,7 +295,9 @@ class VocabParallelHead(torch.nn.Module):
 
     def cross_entropy(self, x: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """Mean cross-entropy over the whole vocabulary (all ranks' shards)."""
-        return _HeadCE.apply(x, self.weight, targets, self)
+        check_targets(targets, self.vocab)
+        master = self.tied if self.tied is not None else self._own
+        return _HeadCE.apply(x, master, targets, self)
 
     def topk(self, x: torch.Tensor, k: int):
         """Global top-k (values, vocab ids) per row over every rank's shard."""

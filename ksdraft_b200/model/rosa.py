@@ -145,10 +145,10 @@ class RosaMixer(nn.Module):
         _lib.require_cuda(x)
         if self._fused_int8_eval():
             return rosa_forward_int8(self, x)
-        if self.training:
-            raise NotImplementedError(
-                "Rosa counterfactual-credit training is outside this build; "
-                "use eval() for the hard forward")
+        # Training takes the reference's hard path (rosa.py:154-165, the path it
+        # runs when no credit engine is present): gradients reach the payload
+        # scales and the output projection only; the counterfactual credits of
+        # HardRosaGPU (T <= 63) are not part of this build.
         q_in, k_in, v_in = self._shifted(x)
         qbits = (self.q_proj(q_in) > 0).to(torch.int8)
         kbits = (self.k_proj(k_in) > 0).to(torch.int8)
@@ -162,8 +162,8 @@ class RosaMixer(nn.Module):
 @torch.no_grad()
 def rosa_forward_int8(mixer: RosaMixer, x: torch.Tensor) -> torch.Tensor:
     """Fused W8A8 evaluation forward of a RosaMixer whose projections are Int8Linear."""
-    from ..kernels.gemm import gemm_out
-    from ..kernels.quant import quantize_cols
+    from ..kernels.gemm import _validate_and_pad, gemm_out
+    from ..kernels.quant import quantize_last_dim
     B, T, d = x.shape
     S = mixer.streams
     dev = x.device
@@ -190,18 +190,15 @@ def rosa_forward_int8(mixer: RosaMixer, x: torch.Tensor) -> torch.Tensor:
                         out_dtype=torch.float32,
                         bias=lin.bias.detach() if lin.bias is not None else None)
         words.append(pack_bits(proj, B, T, S, T * S, S, 1))
-    mixed = torch.empty(B, S, T, dtype=out_dtype, device=dev)
+    # the match writes payload * sign token-major, (B, T, S): the out_proj input
+    # rows (rosa.py:164-165) quantised along the streams with no transpose
+    mixed = torch.empty(B, T, S, dtype=out_dtype, device=dev)
     match_words(*words, B, S, T, _default_max_len(T, None), payload=mixer.payload, out=mixed,
-                strides=(S * T, 1, T))
-    # out_proj input: (B, T, S) tokens quantised along streams
+                strides=(T * S, S, 1))
     lin = mixer.out_proj
     lin._quantize_weight()
-    oq = torch.empty(B * T, S, dtype=torch.int8, device=dev)
-    os_ = torch.empty(B * T, (S + 127) // 128, dtype=torch.float16, device=dev)
-    for b in range(B):
-        cq, cs = quantize_cols(mixed[b])
-        oq[b * T:(b + 1) * T].copy_(cq)
-        os_[b * T:(b + 1) * T].copy_(cs)
-    y = gemm_out(oq, os_, lin.weight_codes, lin.weight_scales, out_dtype=out_dtype,
+    oq, os_ = quantize_last_dim(mixed.reshape(B * T, S))
+    oq, wq = _validate_and_pad(oq, os_, lin.weight_codes, lin.weight_scales, 128)
+    y = gemm_out(oq, os_, wq, lin.weight_scales, out_dtype=out_dtype,
                  bias=lin.bias.detach() if lin.bias is not None else None)
     return y.reshape(B, T, d).to(x.dtype)

@@ -151,7 +151,7 @@ void or_dequantize_rows(const int8_t* codes, const f16bits* scales, int64_t rows
 
 /* ---------------------------------------------------------------- W8A8 GEMM
  * Per-group int32 dot products of gemm.py:34-45 and the canonical fp32 group
- * sum acc = fmaf(float(dot_g), sa*sw, acc), g = 0..G-1.  k % 128 == 0. */
+ * sum acc = fmaf(RN(float(dot_g) * sa), sw, acc), g = 0..G-1.  k % 128 == 0. */
 void or_w8a8_gemm(const int8_t* a, const f16bits* as, const int8_t* w, const f16bits* ws,
                   int64_t m, int64_t n, int64_t k, float* out, int32_t* partials) {
   const int64_t G = k / 128;
@@ -165,8 +165,9 @@ void or_w8a8_gemm(const int8_t* a, const f16bits* as, const int8_t* w, const f16
         int32_t dot = 0;
         for (int t = 0; t < 128; ++t) dot += (int32_t)ap[t] * (int32_t)wp[t];
         if (partials) partials[(g * m + i) * n + j] = dot;
-        float s = h2f(as[i * G + g]) * h2f(ws[j * G + g]);
-        acc = fmaf((float)dot, s, acc);
+        /* t = RN(dot * sa) ((float)dot is exact), then one fused step with sw */
+        const float t = (float)dot * h2f(as[i * G + g]);
+        acc = fmaf(t, h2f(ws[j * G + g]), acc);
       }
       out[i * n + j] = acc;
     }

@@ -408,6 +408,44 @@ def rosa_match(q, k, v, max_match_len=None, method="bruteforce"):
     return sign, L, E
 
 
+def _bf16(a: np.ndarray) -> np.ndarray:
+    """Round fp32 values to bfloat16 (round to nearest even), returned as fp32."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
+def rosa_mixer_int8_eval(x, sig_q, sig_k, sig_v, w, b, payload, w_out, b_out):
+    """RosaMixer evaluation forward after to_int8 (ksdraft/model/rosa.py:128-165
+    with Int8Linear eval projections, ksdraft/kernels/linear.py:62-73) on bf16
+    activations, in this build's fixed GEMM group order.
+
+    x (B, T, d) fp32 holding bf16 values; sig_* (d,) fp32 sigmoid(time_mix_*)
+    as the module computes it (torch.sigmoid on the parameter's device);
+    w / b: dicts 'q','k','v' of (S, d) / (S,) fp32; payload (S,); w_out (d, S),
+    b_out (d,).  Returns y (B, T, d) fp32 holding bf16 values."""
+    x = np.asarray(x, np.float32)
+    B, T, d = x.shape
+    S = payload.shape[0]
+    prev = np.concatenate([np.zeros((B, 1, d), np.float32), x[:, :-1]], 1)
+    diff = _bf16(x - prev)                              # (x - prev) in x's dtype
+    bits = {}
+    for c, sig in (("q", sig_q), ("k", sig_k), ("v", sig_v)):
+        xin = (prev + diff * np.asarray(sig, np.float32)).reshape(B * T, d)   # fp32
+        aq, as_ = quantize_rows_c(xin)
+        wq, ws = quantize_rows_c(w[c])
+        proj = w8a8_gemm_canonical(aq, as_, wq, ws) + b[c].astype(np.float32)
+        bits[c] = (_bf16(proj) > 0).reshape(B, T, S).transpose(0, 2, 1).reshape(B * S, T)
+    sign, _, _ = rosa_match(bits["q"].astype(np.int8), bits["k"].astype(np.int8),
+                            bits["v"].astype(np.int8), method="dp")
+    out = payload.astype(np.float32)[None, :, None] * sign.reshape(B, S, T)
+    o = _bf16(out.transpose(0, 2, 1).reshape(B * T, S))     # .to(x.dtype)
+    oq, os_ = quantize_rows_c(o)
+    wq, ws = quantize_rows_c(w_out)
+    y = w8a8_gemm_canonical(oq, os_, wq, ws) + b_out.astype(np.float32)
+    return _bf16(y).reshape(B, T, d)
+
+
 def rosa_sign_python(q, k, v):
     """Pure-Python brute force of the definition (tests/test_rosa.py:7-22 semantics,
     no length cap); small cases only."""

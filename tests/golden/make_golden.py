@@ -299,6 +299,62 @@ def gen_linear():
     save("linear", **out)
 
 
+def gen_draft_step():
+    """One training step of a small KSDraftModel on the reference's int8 tier
+    (to_int8 with trainable KS3 cells, hard Rosa path on the CPU, float head):
+    the trainer's step body (train/__init__.py:145-163) up to the gradients."""
+    from ksdraft.config import KSDraftConfig
+    from ksdraft.kernels.ks3_int8 import KS3Int8Cell
+    from ksdraft.model import KSDraftModel
+    from ksdraft.model.int8_convert import to_int8
+    from ksdraft.train import distillation_losses
+    cfg = KSDraftConfig(vocab_size=512, layers=2, d_model=128, rosa_streams=128, ks3_charts=256)
+    torch.manual_seed(0)
+    model = KSDraftModel(cfg, teacher_dim=64)
+    rng = np.random.default_rng(0)
+    with torch.no_grad():
+        for name, t in model.state_dict().items():
+            leaf = name.rsplit(".", 1)[-1]
+            if "norm" in name and leaf == "weight" or name.endswith("ln_attn.weight") \
+                    or name.endswith("ln_ffn.weight"):
+                v = 1.0 + 0.1 * rng.standard_normal(t.shape)
+            elif leaf in ("bias", "gate_bias") or leaf.startswith("time_mix"):
+                v = 0.1 * rng.standard_normal(t.shape)
+            elif leaf == "payload":
+                v = 1.0 + 0.2 * rng.standard_normal(t.shape)
+            elif leaf == "raw_scale":
+                v = rng.uniform(0.3, 1.2, t.shape)
+            elif leaf == "raw_shift":
+                v = rng.uniform(-0.5, 0.5, t.shape)
+            elif leaf == "coefficients":
+                v = 0.05 * rng.standard_normal(t.shape)
+            else:
+                v = 0.05 * rng.standard_normal(t.shape)
+            t.copy_(torch.from_numpy(v.astype(np.float32)))
+    weights = {k: f32(v) for k, v in model.state_dict().items() if k != "head.weight"}
+    q = to_int8(model)
+    for blk, src in zip(q.blocks, model.blocks):
+        blk.ffn = KS3Int8Cell(src.ffn, 128, "int8", trainable=True)
+    q.train()
+    g = torch.Generator().manual_seed(3)
+    tokens = torch.randint(0, cfg.vocab_size, (2, 65), generator=g)
+    states = torch.randn(2, 64, 64, generator=g)
+    logits, feats = q(tokens[:, :-1], teacher_states=states)
+    loss, parts = distillation_losses(logits, tokens, feats, q.embedding.weight, None, None,
+                                      0.5, 0.0)
+    loss.backward()
+    grads = {}
+    for name, p in q.named_parameters():
+        key = name.replace("ffn.master_down", "ffn.down.weight") \
+            .replace("ffn.master_up", "ffn.up.weight").replace("ffn.master_", "ffn.")
+        if p.grad is not None:
+            grads["grad." + key] = f32(p.grad)
+    assert "grad.blocks.0.rosa.q_proj.weight" not in grads   # the hard-symbol boundary
+    save("draft_step", tokens=tokens.numpy(), states=f32(states), loss=np.float32(loss.item()),
+         ce=np.float32(parts["ce"]), transfer=np.float32(parts["transfer"]),
+         **{"w." + k: v for k, v in weights.items()}, **grads)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("KSD8_REFERENCE"),
@@ -311,7 +367,7 @@ def main():
     torch.set_num_threads(8)
     topics = {"quant": gen_quant, "dither": gen_dither, "gemm": gen_gemm, "ks3_spine": gen_ks3,
               "ks3_layer": gen_ks3_layer, "rosa": gen_rosa, "tanh16": gen_tanh16,
-              "linear": gen_linear}
+              "linear": gen_linear, "draft_step": gen_draft_step}
     for name, fn in topics.items():
         if args.only is None or name in args.only:
             fn()

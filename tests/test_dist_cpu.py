@@ -180,3 +180,62 @@ def test_peer_death_ends_collective_with_error(tmp_path):
     res = json.loads(Path(tmp_path, "fail0.json").read_text())
     assert res["error"] is not None                 # detected, not hung
     assert res["seconds"] < 60
+
+
+# ---------------------------------------------------------------- full-model step
+
+def _sparse_rows_worker(rank, world, port, out):
+    _init(rank, world, port)
+    from ksdraft_b200.train.dp import allreduce_mean_async, wait_all
+    from ksdraft_b200.train.draft_step import gather_sparse_rows
+    V, d = 10, 4
+    g = torch.Generator().manual_seed(rank)
+    dense = torch.randn(V, d, generator=g)
+    ids = torch.randint(0, V, (6,), generator=g)
+    rows = torch.randn(6, d, generator=g)
+    # the step's order: dense head gradient averaged asynchronously, sparse rows
+    # gathered afterwards and added once the mean is complete
+    grad = dense.clone()
+    pending = allreduce_mean_async(grad, dist.group.WORLD)
+    all_ids, all_rows = gather_sparse_rows(ids, rows, world, dist.group.WORLD)
+    wait_all(pending)
+    grad.index_add_(0, all_ids, all_rows)
+    full = dense.clone()
+    full.index_add_(0, ids, rows)                    # this rank's whole gradient
+    Path(out, f"sp{rank}.json").write_text(json.dumps({"grad": grad.tolist(),
+                                                      "full": full.tolist()}))
+    dist.destroy_process_group()
+
+
+def test_embedding_sparse_rows_mean_over_ranks(tmp_path):
+    """The tied embedding's gradient (dense head part + sparse gathered rows) equals
+    the mean over ranks of each rank's full dense gradient."""
+    assert _run(_sparse_rows_worker, 2, tmp_path) == [0, 0]
+    r = [json.loads(Path(tmp_path, f"sp{i}.json").read_text()) for i in range(2)]
+    want = (np.array(r[0]["full"]) + np.array(r[1]["full"])) / 2
+    for i in range(2):
+        np.testing.assert_allclose(np.array(r[i]["grad"]), want, rtol=1e-6, atol=1e-6)
+
+
+def test_draft_param_layout_and_token_check():
+    """Flat layout of the full step: reference state-dict names, every block one
+    contiguous span in backward order, 64-element alignment; token range check."""
+    from ksdraft_b200.train.draft_step import (DraftShape, FlatParams, _frozen_shapes,
+                                               check_tokens)
+    s = DraftShape(vocab=300, layers=3, d_model=128, streams=128, charts=256, teacher_dim=64)
+    f = FlatParams(s, "cpu")
+    assert f.names[0] == "embedding.weight" and f.names[-1] == "input_norm.bias"
+    assert all(off % 64 == 0 for off in f.offsets.values())
+    spans = [f.block_span[layer] for layer in reversed(range(3))]
+    assert [a for a, _ in spans] == sorted(a for a, _ in spans)
+    for layer in range(3):
+        a, b = f.block_span[layer]
+        assert all(n.startswith(f"blocks.{layer}.") for n in f.names[a:b])
+        assert f.block_grad_span(layer).numel() >= sum(
+            int(np.prod(f.shapes[n])) for n in f.names[a:b])
+    assert "blocks.0.ffn.down.weight" in f.names and "blocks.0.rosa.payload" in f.names
+    assert not any(n.endswith(k) for n in f.names for k, _ in _frozen_shapes(s))
+    check_tokens(torch.tensor([[0, 299]]), 300)
+    for bad in (torch.tensor([[0, 300]]), torch.tensor([[-100, 2]])):
+        with pytest.raises(ValueError):
+            check_tokens(bad, 300)

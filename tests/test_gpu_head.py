@@ -121,3 +121,38 @@ def test_two_vocab_shards_match_the_whole_head():
                        ids=torch.cat([c[1] for c in cands], 1))
     fv, fi = full.topk(xd, k)
     assert torch.equal(mi, fi) and torch.equal(mv, fv)
+
+
+def test_head_at_config_shape_tied_vs_oracle(oracle):
+    """The LM head at the model's shape (d 1536, vocab 150144) on a few hundred
+    tokens, tied to an embedding parameter (draft.py:51): logits bit-exact, loss
+    within 1e-5, dx within 1e-3 and the weight gradient within 1e-3, landing in
+    the embedding's own gradient."""
+    from ksdraft_b200.model.head import VocabParallelHead
+    M, d, V = 160, 1536, 150144
+    x, w, t = _head_case(M=M, d=d, V=V, seed=11)
+    emb = torch.nn.Parameter(w.cuda())
+    head = VocabParallelHead(emb)
+    assert head.tied is emb and head.weight.data_ptr() == emb.data_ptr()
+    xd = x.cuda().requires_grad_(True)
+    loss = head.cross_entropy(xd, t.cuda())
+    loss.backward()
+    ref_loss, ref_logits, ref_dx, ref_dw = oracle.lm_head_ce(x.float().numpy(), w.numpy(),
+                                                             t.numpy())
+    np.testing.assert_array_equal(head.logits(x.cuda()).cpu().numpy(), ref_logits)
+    assert abs(float(loss.detach()) - ref_loss) <= 1e-5 * abs(ref_loss)
+    dx_ref = torch.from_numpy(ref_dx).to(torch.bfloat16).float().numpy()
+    assert _rel(xd.grad.float().cpu().numpy(), dx_ref) < 1e-3
+    assert emb.grad is not None and emb.grad.shape == (V, d)
+    assert _rel(emb.grad.cpu().numpy(), ref_dw) < 1e-3
+
+
+def test_head_rejects_out_of_range_targets():
+    from ksdraft_b200.model.head import VocabParallelHead
+    x, w, t = _head_case(M=8, V=256)
+    head = VocabParallelHead(w.cuda())
+    for bad in (256, -100, -1):
+        tb = t.clone()
+        tb[3] = bad
+        with pytest.raises(ValueError):
+            head.cross_entropy(x.cuda(), tb.cuda())

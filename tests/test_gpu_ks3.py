@@ -117,14 +117,15 @@ def test_ks3_layer_vs_reference_golden(golden):
     y.backward(gout)
     ry = _rel(y.float().detach().cpu().numpy(), g["y"])
     print(f"y rel-L2 vs reference end to end = {ry:.2e}")
-    assert ry < 1e-2
+    assert ry < 1e-3
     assert y.dtype == torch.bfloat16 and x.grad.dtype == torch.bfloat16
     assert q.master_down.grad is not None and q.master_up.grad is not None
-    for name, got, tol in (("dx", x.grad, 5e-2), ("ddown", q.master_down.grad, 5e-2),
-                           ("dup", q.master_up.grad, 5e-2),
-                           ("dcoeff", q.master_coefficients.grad, 5e-2),
-                           ("dscale", q.master_raw_scale.grad, 5e-2),
-                           ("dshift", q.master_raw_shift.grad, 5e-2)):
+    # 1e-3 relative L2 for every output and gradient
+    for name, got, tol in (("dx", x.grad, 1e-3), ("ddown", q.master_down.grad, 1e-3),
+                           ("dup", q.master_up.grad, 1e-3),
+                           ("dcoeff", q.master_coefficients.grad, 1e-3),
+                           ("dscale", q.master_raw_scale.grad, 1e-3),
+                           ("dshift", q.master_raw_shift.grad, 1e-3)):
         r = _rel(got.float().cpu().numpy().reshape(-1), g[name].reshape(-1))
         print(f"{name} rel-L2 vs reference end to end = {r:.2e}")
         assert r < tol, (name, r)

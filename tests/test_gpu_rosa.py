@@ -51,6 +51,40 @@ def test_match_indices_vs_oracle(oracle, S, T):
     np.testing.assert_array_equal(E.cpu().numpy(), Eo)
 
 
+@pytest.fixture
+def rosa_algorithm():
+    """Select a matcher kernel for one test, restoring the default after it."""
+    from ksdraft_b200 import _lib
+
+    def use(algo):
+        _lib.check(_lib.lib().ksd8_rosa_set_algorithm(algo), "rosa_set_algorithm")
+    yield use
+    use(0)
+
+
+@pytest.mark.parametrize("algo", [0, 1, 2])
+@pytest.mark.parametrize("S,T,max_len", [(16, 31, None), (16, 32, None), (16, 97, None),
+                                         (40, 700, None), (8, 2048, None), (8, 700, 5),
+                                         (8, 700, 12), (8, 700, 13), (5, 3000, 40)])
+def test_match_kernels_agree_with_oracle(oracle, rosa_algorithm, algo, S, T, max_len):
+    """Every matcher kernel (chunked prefix tables, per-position prefix tables,
+    window scan) gives the oracle's signs, lengths and endpoints, across chunk
+    boundaries, around the 12-level table depth and with explicit caps; highly
+    repetitive streams make many prefix collisions inside one 32-position chunk."""
+    from ksdraft_b200.model.rosa import match_payload_sign_with_indices
+    rosa_algorithm(algo)
+    rng = np.random.default_rng(S * 7 + T)
+    q, k, v = _streams(rng, S, T)
+    q[: S // 2] = (np.arange(T) % 3 == 0).astype(np.int8)      # periodic: dense collisions
+    k[: S // 2] = (np.arange(T) % 3 == 1).astype(np.int8)
+    args = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    s, L, E = match_payload_sign_with_indices(*args, max_match_len=max_len)
+    so, Lo, Eo = oracle.rosa_match(q, k, v, max_match_len=max_len, method="dp")
+    np.testing.assert_array_equal(L.cpu().numpy(), Lo)
+    np.testing.assert_array_equal(E.cpu().numpy(), Eo)
+    np.testing.assert_array_equal(s.cpu().numpy(), so)
+
+
 def test_match_all_zero_and_no_match():
     from ksdraft_b200.model.rosa import _match_payload_sign
     q = torch.tensor([[1, 1, 1]], dtype=torch.int8).cuda()
@@ -81,16 +115,73 @@ def test_match_batched_layout_and_payload(oracle):
     assert torch.equal(out.cpu(), torch.from_numpy(want).to(torch.bfloat16))
 
 
-def test_rosa_mixer_int8_eval_runs():
-    from ksdraft_b200.kernels.linear import Int8Linear
+def _mixer(d, S, seed):
     from ksdraft_b200.model.rosa import RosaMixer
-    torch.manual_seed(0)
-    m = RosaMixer(256, 128).cuda().eval()
+    torch.manual_seed(seed)
+    m = RosaMixer(d, S).cuda()
     with torch.no_grad():
+        for n in ("q_proj", "k_proj", "v_proj"):
+            getattr(m, n).weight.normal_(0, 0.02)
+            getattr(m, n).bias.normal_(0, 0.02)
         m.out_proj.weight.normal_(0, 0.05)
+        m.out_proj.bias.normal_(0, 0.05)
+        for n in ("time_mix_q", "time_mix_k", "time_mix_v"):
+            getattr(m, n).normal_(0, 1.0)
+        m.payload.uniform_(0.5, 1.5)
+    return m
+
+
+def test_rosa_mixer_int8_eval_vs_oracle(oracle):
+    """The fused W8A8 evaluation forward of RosaMixer after to_int8 (time-shift
+    mix + per-token quantisation kernel, q/k/v GEMMs with bias, bit packing,
+    match with the payload, out_proj) at B 2, T 1024, 512 streams, d 1536, on
+    token-like inputs with repeated spans: bit-exact against the oracle."""
+    from ksdraft_b200.kernels.linear import Int8Linear
+    B, T, d, S = 2, 1024, 1536, 512
+    m = _mixer(d, S, 0)
     for n in ("q_proj", "k_proj", "v_proj", "out_proj"):
         setattr(m, n, Int8Linear.from_float(getattr(m, n)))
-    x = torch.randn(2, 96, 256, device="cuda").to(torch.bfloat16)
+    m.eval()
+    g = torch.Generator().manual_seed(1)
+    emb = torch.randn(4096, d, generator=g)
+    ids = torch.randint(0, 4096, (B, T), generator=g)
+    ids[:, 600:700] = ids[:, 100:200]                          # repeated spans -> long matches
+    x = emb[ids].to(torch.bfloat16)
     with torch.no_grad():
-        y = m(x)
-    assert y.shape == x.shape and y.dtype == torch.bfloat16 and torch.isfinite(y.float()).all()
+        y = m(x.cuda())
+    sig = [torch.sigmoid(getattr(m, f"time_mix_{c}").detach().float()).cpu().numpy()
+           for c in "qkv"]
+    w = {c: getattr(m, f"{c}_proj").weight.detach().cpu().numpy() for c in "qkv"}
+    b = {c: getattr(m, f"{c}_proj").bias.detach().cpu().numpy() for c in "qkv"}
+    y_o = oracle.rosa_mixer_int8_eval(x.float().numpy(), *sig, w, b,
+                                      m.payload.detach().cpu().numpy(),
+                                      m.out_proj.weight.detach().cpu().numpy(),
+                                      m.out_proj.bias.detach().cpu().numpy())
+    assert y.dtype == torch.bfloat16 and y.shape == (B, T, d)
+    np.testing.assert_array_equal(y.float().cpu().numpy(), y_o)
+
+
+def test_rosa_mixer_training_hard_path():
+    """Training mode takes the reference's hard path (rosa.py:154-165): gradients
+    reach payload and out_proj only, equal to autograd of the composition."""
+    from ksdraft_b200.model.rosa import _match_payload_sign
+    B, T, d, S = 2, 200, 256, 128
+    m = _mixer(d, S, 3).train()
+    x = torch.randn(B, T, d, device="cuda")
+    y = m(x)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    with torch.no_grad():
+        q_in, k_in, v_in = m._shifted(x)
+        bits = [(getattr(m, f"{c}_proj")(i) > 0).to(torch.int8).permute(0, 2, 1)
+                for c, i in zip("qkv", (q_in, k_in, v_in))]
+        sign = _match_payload_sign(*bits)
+    pay = m.payload.detach().clone().requires_grad_(True)
+    wo = m.out_proj.weight.detach().clone().requires_grad_(True)
+    bo = m.out_proj.bias.detach().clone().requires_grad_(True)
+    yr = torch.nn.functional.linear((pay[None, :, None] * sign).permute(0, 2, 1), wo, bo)
+    yr.backward(gy)
+    assert torch.allclose(y, yr, rtol=1e-5, atol=1e-6)
+    assert torch.allclose(m.payload.grad, pay.grad, rtol=1e-4, atol=1e-5)
+    assert torch.allclose(m.out_proj.weight.grad, wo.grad, rtol=1e-4, atol=1e-5)
+    assert m.q_proj.weight.grad is None and m.time_mix_q.grad is None

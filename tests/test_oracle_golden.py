@@ -166,12 +166,13 @@ def test_ks3_layer_end_to_end_within_tolerance(golden, oracle):
     g = golden("ks3_layer")
     r = oracle.ks3_layer(g["x"], g["down"], g["up"], g["coefficients"], g["raw_scale"],
                          g["raw_shift"], g["grad"])
-    y_bf16 = torch.from_numpy(r["y"]).to(torch.bfloat16).float().numpy()
-    assert _rel(y_bf16, g["y"]) < 1e-2
-    for name, tol in (("dx", 5e-2), ("ddown", 5e-2), ("dup", 5e-2), ("dcoeff", 5e-2),
-                      ("dscale", 5e-2), ("dshift", 5e-2)):
+    # y and dx are bf16 in the reference run (the input dtype)
+    bf = lambda a: torch.from_numpy(np.asarray(a, np.float32)).to(torch.bfloat16).float().numpy()
+    assert _rel(bf(r["y"]), g["y"]) < 1e-3
+    r = dict(r, dx=bf(r["dx"]))
+    for name in ("dx", "ddown", "dup", "dcoeff", "dscale", "dshift"):
         ref = g[name].reshape(np.asarray(r[name]).shape)
-        assert _rel(r[name], ref) < tol, (name, _rel(r[name], ref))
+        assert _rel(r[name], ref) < 1e-3, (name, _rel(r[name], ref))
 
 
 def test_rosa_matches_reference(golden, oracle):
