@@ -12,17 +12,21 @@ Where the reference module holds more than the hot path, single functions
 are patched instead:
   ksdraft/model/rosa.py:40      _match_payload_sign (RosaMixer.forward looks
                                 it up at call time, rosa.py:161)
+  ksdraft/kernels/rosa_credit_gpu.py:23  the same function as HardRosaGPU binds it
   ksdraft/train/stages.py:27    quantize_last_dim_dithered
 """
 
 from __future__ import annotations
 
 import importlib
+import importlib.util
 import sys
 
 KERNEL_MODULES = ("quant", "gemm", "linear", "ks3_int8", "ks3_triton")
 PATCHED_FUNCTIONS = (
     ("model.rosa", "_match_payload_sign", "ksdraft_b200.model.rosa"),
+    # bound by name at import (rosa_credit_gpu.py:23): HardRosaGPU's re-matches
+    ("kernels.rosa_credit_gpu", "_match_payload_sign", "ksdraft_b200.model.rosa"),
     ("train.stages", "quantize_last_dim_dithered", "ksdraft_b200.train.stages"),
 )
 
@@ -47,6 +51,8 @@ def install(package: str = "ksdraft") -> dict[str, str]:
     for name in KERNEL_MODULES:     # attribute access (ksdraft.kernels.gemm) too
         setattr(parent, name, sys.modules[f"{package}.kernels.{name}"])
     for sub, func, mine_name in PATCHED_FUNCTIONS:
+        if importlib.util.find_spec(f"{package}.{sub}") is None:
+            continue   # a reference version without this module
         ref_mod = importlib.import_module(f"{package}.{sub}")
         mine = importlib.import_module(mine_name)
         setattr(ref_mod, func, getattr(mine, func))

@@ -390,7 +390,8 @@ class DraftTrainStep:
             o = (sign * payload).to(self.act).reshape(B * T, S)     # rosa.py:164-165
             oq, os_ = quantize_last_dim(o)
             wq, ws = quantize_last_dim(self.flat.p(pre + "rosa.out_proj.weight"))
-            r = gemm_out(oq, os_, wq, ws, out_dtype=self.act,
+            oqp, wqp = _validate_and_pad(oq, os_, wq, ws, GROUP_SIZE)   # streams % 128
+            r = gemm_out(oqp, os_, wqp, ws, out_dtype=self.act,
                          bias=self.flat.p(pre + "rosa.out_proj.bias"))
         return r, (sign, o, oq, os_, wq, ws)
 

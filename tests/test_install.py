@@ -22,6 +22,7 @@ FILES = {
     "ksdraft/kernels/linear.py": "Int8Linear = 'reference'\n",
     "ksdraft/kernels/ks3_int8.py": "KS3Int8Cell = 'reference'\n",
     "ksdraft/kernels/ks3_triton.py": "project_fused = 'reference'\n",
+    "ksdraft/kernels/rosa_credit_gpu.py": "from ..model.rosa import _match_payload_sign\n",
     "ksdraft/model/__init__.py": "",
     "ksdraft/model/rosa.py":
         "_match_payload_sign = 'reference'\n"
@@ -71,9 +72,11 @@ def test_install_rebinds_modules_and_functions(tmp_path):
         assert rosa.RosaMixer().forward() is r._match_payload_sign   # looked up at call time
         assert stages.quantize_last_dim_dithered is s.quantize_last_dim_dithered
         assert stages.wtv_loss() == 'kept'                             # rest untouched
+        import ksdraft.kernels.rosa_credit_gpu as cg
+        assert cg._match_payload_sign is r._match_payload_sign         # bound by name
         print(len(done))
     """))
-    assert out.strip() == "7"
+    assert out.strip() == "8"
 
 
 def test_install_refuses_after_reference_import(tmp_path):
