@@ -580,6 +580,16 @@ def run_config4(args) -> None:
         dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
     total_ms = float(total_ms.item())
 
+    # one more step with phase marks (outside the timed region): where the time goes
+    marks = []
+    step.phase_marks = marks
+    step(tok_dev, ts_dev)
+    torch.cuda.synchronize()
+    step.phase_marks = None
+    phases = {}
+    for (name, ev), (_, nxt) in zip(marks, marks[1:]):
+        phases[name] = phases.get(name, 0.0) + ev.elapsed_time(nxt)
+
     # end to end: host ids and teacher states copied in, the loss read back
     loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
     e2e_times = []
@@ -614,6 +624,7 @@ def run_config4(args) -> None:
                     "h2d_bytes_per_step": world * (tok_host.numel() * 8 + ts_host.numel() * 2),
                     "d2h_bytes_per_step": world * 4},
             "gpu_launches": launches, "loss": float(loss_host.item()), "grad_norm": gn,
+            "phases_ms": {k: round(v, 3) for k, v in phases.items()},
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_side:
@@ -728,6 +739,29 @@ def profile_case_fn(case: str, dev):
             xd = x.detach().requires_grad_(True)
             head.weight.grad = None
             head.cross_entropy(xd, tg).backward()
+    elif case == "rosa_mixer":
+        # config 3 end to end: RosaMixer(1536, 512) after to_int8 (Int8Linear q/k/v/out
+        # projections N(0, 0.02)), evaluation forward on x = E[ids], E bf16 N(0, 1)
+        # over the vocabulary, ids Zipf(1.1) with repeated spans, B 4 x T 4096
+        from ksdraft_b200.kernels.linear import Int8Linear
+        from ksdraft_b200.model.rosa import RosaMixer
+        B, T, S = 4, 4096, 512
+        torch.manual_seed(0)
+        m = RosaMixer(D_MODEL, S).to(dev)
+        with torch.no_grad():
+            for n in ("q_proj", "k_proj", "v_proj", "out_proj"):
+                getattr(m, n).weight.normal_(0, 0.02)
+                getattr(m, n).bias.zero_()
+        for n in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            setattr(m, n, Int8Linear.from_float(getattr(m, n)))
+        m.eval()
+        E = torch.randn(150144, D_MODEL, device=dev, generator=g).to(torch.bfloat16)
+        x = E[torch.from_numpy(rosa_ids(B, T, seed=0)).to(dev)]
+        del E
+
+        def fn():
+            with torch.no_grad():
+                m(x)
     elif case == "rosa":
         # config 3: batch 4 x seq 4096, 512 streams (2048 stream sequences); bits
         # from Zipf(1.1) ids with repeated spans (length 8-64, 10% of positions)
@@ -780,7 +814,14 @@ def side_measurements(dev) -> dict:
                            "note": "operands L2-resident (the whole problem is 2.8 MB)"}
     ms = time_on_device(profile_case_fn("rosa", dev), 5)
     out["config3_rosa_match"] = {"shape": [4, 4096, 512], "ms": ms,
-                                 "positions_per_s": 4 * 4096 * 512 / (ms / 1e3)}
+                                 "positions_per_s": 4 * 4096 * 512 / (ms / 1e3),
+                                 "note": "matcher alone on hash bits of the ids"}
+    ms = time_on_device(profile_case_fn("rosa_mixer", dev), 5)
+    out["config3_rosa_mixer"] = {"shape": [4, 4096, 512, D_MODEL], "ms": ms,
+                                 "tokens_per_s": 4 * 4096 / (ms / 1e3),
+                                 "gemm_gop": 4 * 2 * 4 * 4096 * D_MODEL * 512 / 1e9,
+                                 "note": "RosaMixer int8 eval forward on E[Zipf ids]: time-mix "
+                                         "+ quantise, 3 W8A8 GEMMs, bits, match, out_proj"}
     ms = time_on_device(profile_case_fn("head", dev), 3)
     out["lm_head_fwd_bwd"] = {"tokens": TOKENS, "vocab": 150144, "ms": ms,
                               "tokens_per_s": TOKENS / (ms / 1e3)}
@@ -817,8 +858,8 @@ def main() -> None:
                     help="skip the 1-GPU side figures (configs 1 and 3, LM head)")
     ap.add_argument("--profile-case", default=None,
                     help="run one kernel (gemm | gemm_config1 | quant | quant_dither | quant_cols | "
-                         "requant_t | "
-                         "spine | vjp | head | rosa) a few times, for ncu")
+                         "requant_t | spine | vjp | head | rosa | rosa_mixer) a few times, "
+                         "for ncu")
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
     if args.profile_case:

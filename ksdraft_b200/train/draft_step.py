@@ -303,6 +303,14 @@ class DraftTrainStep:
         self._frozen_codes = {}
         self._ln_leaves = {}
         self.last = {}
+        self.phase_marks = None   # a list to record (phase name, CUDA event) marks into
+
+    def _mark(self, name: str) -> None:
+        """Start phase `name` (device-side timing of the step's parts, when enabled)."""
+        if self.phase_marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.phase_marks.append((name, ev))
 
     # ---- parameters --------------------------------------------------------
 
@@ -440,7 +448,7 @@ class DraftTrainStep:
         teacher_states = self._to_device(teacher_states)
         inp, tgt = tokens[:, :-1], tokens[:, 1:]
         B, T = inp.shape
-        M, d = B * T, s.d_model
+        M, d = B * T, self.shape.d_model
         lib = _lib.lib()
         world = dist.get_world_size(self.group) if (self.group is not None or (
             dist.is_available() and dist.is_initialized())) else 1
@@ -456,9 +464,11 @@ class DraftTrainStep:
 
         try:
             loss = self._run(inp, tgt, teacher_states, B, T, M, d, reduce_span, world)
+            self._mark("reduce_wait")
             self._finish_grads(pending)
             if update:
                 self._update()
+            self._mark("end")
         finally:
             if overlapping[0]:
                 lib.ksd8_set_sm_reserve(0)
@@ -472,6 +482,7 @@ class DraftTrainStep:
         tids = tgt.reshape(-1)
 
         # ---- forward: embedding, input norm, teacher projection (draft.py:68-74)
+        self._mark("embed_fwd")
         x0 = E.index_select(0, ids).to(act).requires_grad_(True)
         with torch.enable_grad():
             x1 = self._ln(x0, "input_norm")
@@ -492,7 +503,9 @@ class DraftTrainStep:
         t_norm = F.normalize(E.index_select(0, tids).float(), dim=-1)   # transfer targets
         ts_terms = []
         for layer in range(s.layers):
+            self._mark("rosa_fwd")
             r, rosa_saved = self._rosa_forward(layer, x.view(B, T, d))
+            self._mark("dspine_ln_fwd")
             h = (x + r).view(B, T, d)
             W = self._dspine_weights(layer, leaf=True)
             h_leaf = h.detach().requires_grad_(True)
@@ -502,6 +515,7 @@ class DraftTrainStep:
                 h2d = h2.detach().requires_grad_(True)
                 b = self._ln(h2d, f"blocks.{layer}.ln_ffn")
             cell = self.cells[layer]
+            self._mark("ks3_fwd")
             k, ks3_saved = ks3_train_forward(cell, b.detach().reshape(M, d))
             x = (h2d.detach().reshape(M, d) + k)
             with torch.no_grad():
@@ -511,6 +525,7 @@ class DraftTrainStep:
             p_prev_first = p[:, :1, :]
 
         # ---- head + loss (draft.py:82, train/__init__.py:77-94)
+        self._mark("head_fwd")
         xL = x.detach().requires_grad_(True)
         with torch.enable_grad():
             xf = self._ln(xL, "output_norm")
@@ -525,6 +540,7 @@ class DraftTrainStep:
         self.last = {"ce": ce.detach(), "transfer": ts.detach()}
 
         # ---- backward: head (W8A8 dgrad / wgrad on the fused CE gradient codes)
+        self._mark("head_bwd")
         dq, dsc, dlT_q, dlT_s = ce_grad_quant(logits, tids, 0, gmax, gsum, 1.0 / M)
         del logits
         EqT = quantize_cols(Eq, x_scales=Es)
@@ -550,7 +566,9 @@ class DraftTrainStep:
             cell = self.cells[layer]
             views = {n: self.flat.g(pre + KS3_MASTERS[n]).view_as(getattr(cell, "master_" + n))
                      for n in KS3_MASTERS}
+            self._mark("ks3_bwd")
             db = ks3_backward(cell, dx.to(act), *ks3_saved, (M, d), grads_into=views)
+            self._mark("dspine_ln_bwd")
             with torch.enable_grad():
                 b.backward(db.reshape(b.shape))
             self._ln_param_grads(f"{pre}ln_ffn")
@@ -570,12 +588,14 @@ class DraftTrainStep:
                 self.flat.g(pre + _dspine_name(n)).copy_(t.grad)
             dp_next_first = pf_leaf.grad if pf_leaf is not None else None
             dh = h_leaf.grad.reshape(M, d).float()
+            self._mark("rosa_bwd")
             self._rosa_backward(layer, dh, rosa_saved)
             reduce_span(self.flat.block_grad_span(layer))
             dx = dh
             saved[layer] = None
 
         # ---- backward: teacher projection, input norm, embedding rows
+        self._mark("embed_bwd")
         if ts_saved is not None:
             with _ste_matmul_precision(self.act):
                 torch.matmul(dx.t(), dequantize_last_dim(*ts_saved),
@@ -603,6 +623,7 @@ class DraftTrainStep:
         self.flat.g("embedding.weight").index_add_(0, ids, rows)
 
     def _update(self):
+        self._mark("clip_adamw")
         self.step_count += 1
         lib = _lib.lib()
         stream = _lib.stream_ptr(self.dev)

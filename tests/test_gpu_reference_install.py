@@ -142,6 +142,7 @@ def test_reference_model_trainer_and_export_on_ksdraft_b200(tmp_path):
             for n, p in model.named_parameters():
                 if p.dim() == 2 and "embedding" not in n:
                     p.normal_(0, 0.02)
+        model.eval()
         q = to_int8(model).eval()
         tokens = torch.randint(0, 512, (2, 64), device=dev)
         with torch.no_grad():
