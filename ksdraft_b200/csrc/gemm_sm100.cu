@@ -57,15 +57,8 @@ struct GemmArgs {
 
 constexpr int BM = 128;
 constexpr int BK = 128;    // one GS128 group of int8 = one 128-byte swizzled row
-// Epilogue pipelining across K groups (0 = off): the TMEM load of group g + 1
-// is issued before the arithmetic of group g; 1 releases group g's
-// accumulator before its arithmetic, 2 after it.
-#ifndef KSD8_GEMM_PIPE
-#define KSD8_GEMM_PIPE 0
-#endif
-constexpr int PIPE = KSD8_GEMM_PIPE;
 constexpr int SRING = 16;  // scale ring slots
-constexpr int SBATCH = PIPE ? 2 : 4;  // groups of scales fetched per round by each scale warp
+constexpr int SBATCH = 4;  // groups of scales fetched per round by each scale warp
 constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
 
@@ -157,10 +150,10 @@ struct RegSplit {
   static constexpr int launch = 0, role = 0, epi = 0;
 };
 #ifndef KSD8_RS384_ROLE
-#define KSD8_RS384_ROLE (KSD8_GEMM_PIPE ? 40 : 88)
+#define KSD8_RS384_ROLE 88
 #endif
 #ifndef KSD8_RS384_EPI
-#define KSD8_RS384_EPI (KSD8_GEMM_PIPE ? 232 : 208)
+#define KSD8_RS384_EPI 208
 #endif
 template <>
 struct RegSplit<384> {
@@ -426,88 +419,6 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
       const int m0 = (tile % tiles_m) * BM * CG + rank * BM, n0 = (tile / tiles_m) * BN;
 #pragma unroll
       for (int i = 0; i < CPT / 2; ++i) acc[i] = make_float2(0.f, 0.f);
-      if constexpr (PIPE != 0 && EARLY && !PARTIALS) {
-        // Pipelined over the tile's groups: ra / rb alternate as the slice of the
-        // group being reduced and of the next group, whose TMEM load is in
-        // flight during this group's arithmetic.
-        uint32_t ra[CPT], rb[CPT];
-        {
-          const int buf = gg % NBUF;
-          if (!mbar_wait(&acc_full[buf], (gg / NBUF) & 1, abort_flag, args.status)) ok = false;
-          tc_fence_after();
-          if (ok)
-#pragma unroll
-            for (int c = 0; c < CPT / 32; ++c)
-              tmem_ld_32x32b_x32(t_row + buf * BN + col0 + c * 32,
-                                 *reinterpret_cast<uint32_t(*)[32]>(ra + c * 32));
-        }
-#define KSD8_PIPE_STEP(CUR, NXT, GI)                                                        \
-        {                                                                                    \
-          const int gi = (GI);                                                               \
-          const int gq = gg + gi;                                                            \
-          const int buf = gq % NBUF;                                                         \
-          const int slot = gq % SRING;                                                       \
-          const uint32_t tb = t_row + buf * BN + col0;                                       \
-          tmem_wait_ld();                                                                    \
-          _Pragma("unroll") for (int c = 0; c < CPT / 8; ++c) tmem_st_magic_x8(tb + c * 8);  \
-          if (gi + 1 < G) {                                                                  \
-            const int nb = (gq + 1) % NBUF;                                                  \
-            if (!mbar_wait(&acc_full[nb], ((gq + 1) / NBUF) & 1, abort_flag, args.status))  \
-              ok = false;                                                                    \
-            tc_fence_after();                                                                \
-            if (ok)                                                                          \
-              _Pragma("unroll") for (int c = 0; c < CPT / 32; ++c)                           \
-                tmem_ld_32x32b_x32(t_row + nb * BN + col0 + c * 32,                          \
-                                   *reinterpret_cast<uint32_t(*)[32]>(NXT + c * 32));        \
-          }                                                                                  \
-          if (PIPE == 1) {                                                                   \
-            tmem_wait_st();                                                                  \
-            tc_fence_before();                                                               \
-            __syncwarp();                                                                    \
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);                                     \
-          }                                                                                  \
-          if (ok && !mbar_wait(&s_full[slot], (gq / SRING) & 1, abort_flag, args.status))    \
-            ok = false;                                                                      \
-          if (ok) {                                                                          \
-            const float* sc = sScale + slot * L::SCALE_FLOATS;                               \
-            const float sa = sc[row];                                                        \
-            const float2 sa2 = make_float2(sa, sa);                                          \
-            const float ca = __fmul_rn(-MAGIC_F, sa);                                        \
-            const float2 ca2 = make_float2(ca, ca);                                          \
-            const float* sw = sc + BM + col0;                                                \
-            _Pragma("unroll") for (int j = 0; j < CPT; j += 4) {                             \
-              const float4 w4 = *reinterpret_cast<const float4*>(sw + j);                    \
-              const int o = j / 2;                                                           \
-              const float2 t0 = __ffma2_rn(                                                  \
-                  make_float2(__uint_as_float(CUR[j]), __uint_as_float(CUR[j + 1])), sa2,    \
-                  ca2);                                                                      \
-              const float2 t1 = __ffma2_rn(                                                  \
-                  make_float2(__uint_as_float(CUR[j + 2]), __uint_as_float(CUR[j + 3])),     \
-                  sa2, ca2);                                                                 \
-              acc[o] = __ffma2_rn(t0, make_float2(w4.x, w4.y), acc[o]);                      \
-              acc[o + 1] = __ffma2_rn(t1, make_float2(w4.z, w4.w), acc[o + 1]);              \
-            }                                                                                \
-          }                                                                                  \
-          if (PIPE == 2) {                                                                   \
-            tmem_wait_st();                                                                  \
-            tc_fence_before();                                                               \
-            __syncwarp();                                                                    \
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);                                     \
-          }                                                                                  \
-          __syncwarp();                                                                      \
-          if (lane == 0) mbar_arrive(&s_empty[slot]);                                        \
-        }
-        for (int g = 0; g < G; g += 2) {
-          KSD8_PIPE_STEP(ra, rb, g)
-          if (!ok) break;
-          if (g + 1 < G) KSD8_PIPE_STEP(rb, ra, g + 1)
-          if (!ok) break;
-        }
-#undef KSD8_PIPE_STEP
-        tmem_wait_ld();   // nothing in flight on any exit path
-        tmem_wait_st();
-        gg += G;
-      } else
       for (int g = 0; g < G; ++g, ++gg) {
         const int buf = gg % NBUF;
         const uint32_t aph = (gg / NBUF) & 1;

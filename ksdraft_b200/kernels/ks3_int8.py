@@ -252,8 +252,8 @@ class KS3Int8Cell(nn.Module):
 
     def _project(self, xq: torch.Tensor, xs: torch.Tensor):
         """coords = fp16 clamp(xq @ down^T); h codes/scales of the spine features."""
-        coords = gemm_out(xq, xs, self.down_codes, self.down_scales, out_dtype=FP16,
-                          clamp_f16=True)
+        coords = gemm_out(_pad_k(xq), xs, _pad_k(self.down_codes), self.down_scales,
+                          out_dtype=FP16, clamp_f16=True)
         hq, hs = spine_quant(coords, self.spine_codes, self.spine_scale, self.warp_scale_codes,
                              self.warp_scale_scales, self.warp_shift_codes,
                              self.warp_shift_scales, self.tanh_lut, self.nonlinear)
@@ -268,7 +268,8 @@ class KS3Int8Cell(nn.Module):
         x2 = x.reshape(-1, x.shape[-1])
         xq, xs = quantize_last_dim(x2, self.group)
         hq, hs, _ = self._project(xq, xs)
-        y = gemm_out(hq, hs, self.up_codes, self.up_scales, out_dtype=self._out_dtype(x))
+        y = gemm_out(_pad_k(hq), hs, _pad_k(self.up_codes), self.up_scales,
+                     out_dtype=self._out_dtype(x))
         return y.reshape(*x.shape[:-1], self.out_features)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -305,7 +306,8 @@ class _KS3Int8Train(torch.autograd.Function):
 
 
 def _pad_k(codes: torch.Tensor) -> torch.Tensor:
-    """Zero codes up to the next multiple of 128 along the last dim."""
+    """Zero codes up to the next multiple of 128 along the last dim (a partial
+    final group contributes nothing, gemm.py:71-73)."""
     pad = -codes.shape[-1] % GROUP_SIZE
     return torch.nn.functional.pad(codes, (0, pad)) if pad else codes
 
@@ -318,7 +320,8 @@ def ks3_train_forward(cell, inputs):
     x = inputs.reshape(-1, inputs.shape[-1])
     xq, xs = quantize_last_dim(x, cell.group)
     hq, hs, coords = cell._project(xq, xs)
-    y = gemm_out(hq, hs, cell.up_codes, cell.up_scales, out_dtype=cell._out_dtype(inputs))
+    y = gemm_out(_pad_k(hq), hs, _pad_k(cell.up_codes), cell.up_scales,
+                 out_dtype=cell._out_dtype(inputs))
     return y.reshape(*inputs.shape[:-1], cell.out_features), (xq, xs, hq, hs, coords)
 
 

@@ -53,7 +53,7 @@ from ..kernels.gemm import _validate_and_pad, gemm_out
 from ..kernels.ks3_int8 import KS3Int8Cell, ks3_backward, ks3_train_forward, ks3_weights
 from ..kernels.linear import ste_input_grad
 from ..kernels.quant import GROUP_SIZE, dequantize_last_dim, quantize_cols, quantize_last_dim
-from ..model.head import ce_grad_quant, ce_partials, combine_ce_partials
+from ..model.head import ce_grad, ce_grad_quant, ce_partials, combine_ce_partials
 from ..model.rosa import _default_max_len, match_words, pack_bits
 from .dp import SM_RESERVE, allreduce_mean_async, wait_all
 
@@ -285,12 +285,19 @@ class DraftTrainStep:
 
     def __init__(self, shape: DraftShape, device, *, seed: int = 0, act_dtype=torch.bfloat16,
                  lr: float = 3e-4, weight_decay: float = 0.01, grad_clip: float | None = 1.0,
-                 transfer_weight: float = 0.5, group=None, params=None):
+                 transfer_weight: float = 0.5, group=None, params=None,
+                 head_mode: str = "w8a8"):
         self.shape = shape
         self.dev = torch.device(device)
         self.act = act_dtype
         self.lr, self.wd, self.grad_clip = lr, weight_decay, grad_clip
         self.transfer_weight = transfer_weight
+        if head_mode not in ("w8a8", "float"):
+            raise ValueError("head_mode must be 'w8a8' or 'float'")
+        # "w8a8": the north-star head (W8A8 logits, dgrad and wgrad on the fused CE
+        # gradient codes); "float": the reference int8 tier's float exception
+        # (int8_convert.py:8-12), an fp32 GEMM head, for parity checks
+        self.head_mode = head_mode
         self.group = group
         self.flat, self.frozen = params if params is not None else init_draft_params(
             shape, self.dev, seed)
@@ -529,9 +536,14 @@ class DraftTrainStep:
         xL = x.detach().requires_grad_(True)
         with torch.enable_grad():
             xf = self._ln(xL, "output_norm")
-        xfq, xfs = quantize_last_dim(xf.detach())
-        Eq, Es = quantize_last_dim(E)
-        logits = gemm_out(xfq, xfs, Eq, Es)                           # (M, V) fp32
+        if self.head_mode == "float":
+            xf32 = xf.detach().float()
+            with _ste_matmul_precision(torch.float32):
+                logits = xf32 @ E.t()                                  # (M, V) fp32
+        else:
+            xfq, xfs = quantize_last_dim(xf.detach())
+            Eq, Es = quantize_last_dim(E)
+            logits = gemm_out(xfq, xfs, Eq, Es)                       # (M, V) fp32
         mx, sm, tg = ce_partials(logits, tids, 0)
         gmax, gsum, loss_rows = combine_ce_partials(mx, sm, tg, None)
         ce = loss_rows.mean()
@@ -541,14 +553,22 @@ class DraftTrainStep:
 
         # ---- backward: head (W8A8 dgrad / wgrad on the fused CE gradient codes)
         self._mark("head_bwd")
-        dq, dsc, dlT_q, dlT_s = ce_grad_quant(logits, tids, 0, gmax, gsum, 1.0 / M)
-        del logits
-        EqT = quantize_cols(Eq, x_scales=Es)
-        EqT = (F.pad(EqT[0], (0, -EqT[0].shape[1] % GROUP_SIZE)), EqT[1])
-        dxf = gemm_out(dq, dsc, *EqT, out_dtype=torch.float32)
-        xfT = quantize_cols(xfq, x_scales=xfs)
-        xfT = (F.pad(xfT[0], (0, -M % GROUP_SIZE)), xfT[1])
-        gemm_out(dlT_q, dlT_s, *xfT, out=self.flat.g("embedding.weight"))   # tied: dE = dW_head
+        if self.head_mode == "float":
+            dl = ce_grad(logits, tids, 0, gmax, gsum, 1.0 / M)
+            del logits
+            with _ste_matmul_precision(torch.float32):
+                dxf = dl @ E
+                torch.matmul(dl.t(), xf32, out=self.flat.g("embedding.weight"))
+            del dl
+        else:
+            dq, dsc, dlT_q, dlT_s = ce_grad_quant(logits, tids, 0, gmax, gsum, 1.0 / M)
+            del logits
+            EqT = quantize_cols(Eq, x_scales=Es)
+            EqT = (F.pad(EqT[0], (0, -EqT[0].shape[1] % GROUP_SIZE)), EqT[1])
+            dxf = gemm_out(dq, dsc, *EqT, out_dtype=torch.float32)
+            xfT = quantize_cols(xfq, x_scales=xfs)
+            xfT = (F.pad(xfT[0], (0, -M % GROUP_SIZE)), xfT[1])
+            gemm_out(dlT_q, dlT_s, *xfT, out=self.flat.g("embedding.weight"))  # tied: dE = dW
         reduce_span(self.flat.g("embedding.weight"))
         with torch.enable_grad():
             xf.backward(dxf.to(act))

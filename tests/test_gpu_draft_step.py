@@ -23,19 +23,16 @@ def _rel(a, b):
     return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
 
 
-def _step(golden, act=torch.float32, grad_clip=1.0):
+def _step(golden, act=torch.float32, grad_clip=1.0, head_mode="w8a8"):
     from ksdraft_b200.train.draft_step import DraftShape, DraftTrainStep
     g = golden("draft_step")
-    st = DraftTrainStep(DraftShape(**SMALL), "cuda", act_dtype=act, grad_clip=grad_clip)
+    st = DraftTrainStep(DraftShape(**SMALL), "cuda", act_dtype=act, grad_clip=grad_clip,
+                        head_mode=head_mode)
     st.load_state_dict({k[2:]: torch.from_numpy(v) for k, v in g.items() if k.startswith("w.")})
     return g, st
 
 
-def test_draft_step_matches_reference_int8_tier(golden):
-    g, st = _step(golden)
-    tokens = torch.from_numpy(g["tokens"])
-    states = torch.from_numpy(g["states"])
-    loss = st.forward_backward(tokens, states)
+def _compare(g, st, loss):
     ce, tr = float(st.last["ce"]), float(st.last["transfer"])
     print(f"loss {float(loss):.6f} vs {float(g['loss']):.6f}; ce {ce:.6f} vs {float(g['ce']):.6f};"
           f" transfer {tr:.6f} vs {float(g['transfer']):.6f}")
@@ -53,8 +50,31 @@ def test_draft_step_matches_reference_int8_tier(golden):
     # every parameter the reference trains is trained here, and only those
     assert set(names) == set(st.flat.names)
     assert set(params) - set(names) == set(st.frozen)
-    assert max(worst.values()) < 5e-2, max(worst.items(), key=lambda kv: kv[1])
-    assert np.median(list(worst.values())) < 1e-2
+    return ce, tr, worst
+
+
+def test_draft_step_matches_reference_int8_tier(golden):
+    """With the reference int8 tier's own float head (int8_convert.py:8-12) the
+    full step's loss and every gradient are within 1e-3 of the reference run."""
+    g, st = _step(golden, head_mode="float")
+    loss = st.forward_backward(torch.from_numpy(g["tokens"]), torch.from_numpy(g["states"]))
+    ce, tr, worst = _compare(g, st, loss)
+    assert abs(ce - float(g["ce"])) < 1e-5 * abs(float(g["ce"]))
+    bad = {n: r for n, r in worst.items() if r >= 1e-3}
+    assert not bad, bad
+
+
+def test_draft_step_w8a8_head_vs_reference(golden):
+    """With the north-star W8A8 head (logits, dgrad, wgrad on int8 operands) the
+    step differs from the reference's float head by the head's quantisation:
+    the loss within 2e-3, gradients within 0.15 rel-L2 (sums over tokens such as
+    output_norm.bias the loosest), the median within 5%."""
+    g, st = _step(golden)
+    loss = st.forward_backward(torch.from_numpy(g["tokens"]), torch.from_numpy(g["states"]))
+    ce, tr, worst = _compare(g, st, loss)
+    assert abs(ce - float(g["ce"])) < 2e-3 * abs(float(g["ce"]))
+    assert max(worst.values()) < 0.15, max(worst.items(), key=lambda kv: kv[1])
+    assert np.median(list(worst.values())) < 5e-2
 
 
 def test_draft_step_trains_and_bf16_agrees(golden):

@@ -8,7 +8,8 @@ test cases for the int8 tier (tests/test_int8.py: quantiser error bound,
 padding, zero rows, GEMM parity with the fp32 tier at rtol 1e-4 / atol 1e-3,
 Int8Linear within 5% of fp32) and for Rosa (tests/test_rosa.py: the hand
 case, random short streams against a brute force, no match), then run a
-small KSDraftModel through to_int8, its eval forward, the reference Trainer
+small KSDraftModel through to_int8 (the reference's to_int8 cases: eval
+forward within 15% of fp32, training gradients flowing), the reference Trainer
 (warm-up stage, T = 32 so its CUDA Rosa credit path applies) and
 export / load_export with weights this build's training step produced."""
 
@@ -134,23 +135,44 @@ def test_reference_model_trainer_and_export_on_ksdraft_b200(tmp_path):
         from ksdraft.export import export_model, load_export
         from ksdraft_b200.train.draft_step import DraftShape, DraftTrainStep
         dev = "cuda"
+        # the reference's own to_int8 cases (tests/test_int8_convert.py), restated:
+        # a "woken" tiny model (head, out_proj and KS3 up drawn), eval forward
+        # within 15% of the float model, and training gradients that flow
+        tiny = KSDraftConfig(vocab_size=256, layers=2, d_model=96, head_size=32,
+                             rosa_streams=32, ks3_charts=64)
+        torch.manual_seed(0)
+        model = KSDraftModel(tiny).eval()
+        with torch.no_grad():
+            model.head.weight.normal_(0, 0.02)
+            for blk in model.blocks:
+                blk.rosa.out_proj.weight.normal_(0, 0.05)
+                blk.ffn.up.weight.normal_(0, 0.05)
+        model = model.to(dev)
+        tokens = torch.randint(0, 256, (2, 16), device=dev)
+        with torch.no_grad():
+            y_ref, _ = model(tokens)
+            y_q, _ = to_int8(model)(tokens)
+        rel = ((y_q - y_ref).norm() / y_ref.norm()).item()
+        assert torch.isfinite(y_q).all() and rel < 0.15, rel
+        torch.manual_seed(0)
+        wm = KSDraftModel(tiny, teacher_dim=96).train()
+        with torch.no_grad():
+            wm.head.weight.normal_(0, 0.02)
+            for blk in wm.blocks:
+                blk.rosa.out_proj.weight.normal_(0, 0.05)
+                blk.ffn.up.weight.normal_(0, 0.05)
+        conv = to_int8(wm.to(dev))
+        toks = torch.randint(0, 256, (2, 8), device=dev)
+        logits, _ = conv(toks, teacher_states=torch.randn(2, 8, 96, device=dev))
+        torch.nn.functional.cross_entropy(logits[:, :-1].flatten(0, 1),
+                                          toks[:, 1:].flatten()).backward()
+        grads = [p.grad for p in conv.parameters() if p.grad is not None]
+        assert grads and all(torch.isfinite(g).all() for g in grads)
+        qg = conv.blocks[0].rosa.q_proj.weight.grad        # the CUDA credit path
+        assert qg is not None and torch.isfinite(qg).all()
         cfg = KSDraftConfig(vocab_size=512, layers=2, d_model=128, rosa_streams=64,
                             ks3_charts=256)
-        torch.manual_seed(0)
-        model = KSDraftModel(cfg, device=dev)
-        with torch.no_grad():
-            for n, p in model.named_parameters():
-                if p.dim() == 2 and "embedding" not in n:
-                    p.normal_(0, 0.02)
-        model.eval()
-        q = to_int8(model).eval()
-        tokens = torch.randint(0, 512, (2, 64), device=dev)
-        with torch.no_grad():
-            li, _ = q(tokens)
-            lf, _ = model(tokens)
-        assert torch.isfinite(li).all()
-        rel = ((li - lf).norm() / lf.norm()).item()
-        assert rel < 0.1, rel
+        q = to_int8(KSDraftModel(cfg, device=dev))
         # the reference trainer, warm-up stage, on the int8 model (T = 32: the CUDA
         # Rosa training path with its counterfactual credits applies)
         ids = torch.randint(0, 512, (4096,)).tolist()
