@@ -561,20 +561,42 @@ def run_config4(args) -> None:
         step(tok_dev, ts_dev)
     barrier()
 
+    # one process per GPU alone: the forward + backward replay as one CUDA graph
+    # (no per-kernel host work); the GEMM events are recorded inside it
+    use_graph = world == 1 and not args.no_graph
+    gt = GemmTimer(external=True)
+    if use_graph:
+        launches0 = _lib.LAUNCHES
+        with gt:
+            step.capture(tok_dev, ts_dev)
+        captured = _lib.LAUNCHES - launches0
+
+        def run(tok, ts):
+            return step.replay(tok, ts)
+    else:
+        run = step
+
     times = []
+    gemm = []
     launches0 = _lib.LAUNCHES
-    with ClockSampler(local) as clocks, GemmTimer() as gt:
+    with ClockSampler(local) as clocks:
         for _ in range(args.steps):
             flush.zero_()
             barrier()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if not use_graph:
+                gt = GemmTimer().__enter__()
             s.record()
-            step(tok_dev, ts_dev)
+            run(tok_dev, ts_dev)
             e.record()
             torch.cuda.synchronize()
+            if not use_graph:
+                gt.__exit__()
             times.append(s.elapsed_time(e))
+            gemm += gt.durations_ms()
     launches = (_lib.LAUNCHES - launches0) // max(1, args.steps)
-    gemm = gt.durations_ms()
+    if use_graph:
+        launches += captured
     total_ms = torch.tensor([sum(times)], device=dev)
     if world > 1:
         dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
@@ -598,7 +620,7 @@ def run_config4(args) -> None:
         barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        loss = step(tok_host, ts_host)
+        loss = run(tok_host, ts_host)
         loss_host.copy_(loss.detach().reshape(1), non_blocking=True)
         e.record()
         torch.cuda.synchronize()
@@ -625,6 +647,7 @@ def run_config4(args) -> None:
                     "d2h_bytes_per_step": world * 4},
             "gpu_launches": launches, "loss": float(loss_host.item()), "grad_norm": gn,
             "phases_ms": {k: round(v, 3) for k, v in phases.items()},
+            "cuda_graph": use_graph,
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_side:
@@ -854,6 +877,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("config4", "config2"), default="config4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="config4 on one GPU: run the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-side", action="store_true",
                     help="skip the 1-GPU side figures (configs 1 and 3, LM head)")
     ap.add_argument("--profile-case", default=None,

@@ -21,11 +21,15 @@ from .quant import GROUP_SIZE, SCALE_DTYPE, _check_group  # noqa: F401 (referenc
 
 class GemmTimer:
     """Records a CUDA event pair around every GEMM launch while active
-    (on the launching stream); used by bench.py for the roofline figures."""
+    (on the launching stream); used by bench.py for the roofline figures.
+    With external=True the events may be recorded during CUDA-graph capture:
+    each replay of the graph then re-records them, and durations_ms() after a
+    replay gives that replay's GEMM times."""
 
     active: "GemmTimer | None" = None
 
-    def __init__(self):
+    def __init__(self, external: bool = False):
+        self.external = external
         self.pairs: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
 
     def __enter__(self):
@@ -80,7 +84,8 @@ def gemm_out(a_codes: torch.Tensor, a_scales: torch.Tensor, w_codes: torch.Tenso
         flags |= _lib.EPI_IF_STATUS
     timer = GemmTimer.active if not if_status else None  # predicated launches are not timed
     if timer is not None:
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0 = torch.cuda.Event(enable_timing=True, external=timer.external)
+        ev1 = torch.cuda.Event(enable_timing=True, external=timer.external)
         ev0.record()
     rc = _lib.lib().ksd8_w8a8_gemm(
         a_codes.data_ptr(), a_scales.data_ptr(), w_codes.data_ptr(), w_scales.data_ptr(), M, N, K,

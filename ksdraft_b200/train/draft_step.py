@@ -437,6 +437,50 @@ class DraftTrainStep:
 
     # ---- the step --------------------------------------------------------------
 
+    # ---- CUDA graph of the step ------------------------------------------------
+
+    def capture(self, tokens: torch.Tensor, teacher_states: torch.Tensor | None = None,
+                warmup: int = 2) -> None:
+        """Record forward + backward (everything up to the gradients) into one CUDA
+        graph over static device copies of `tokens` / `teacher_states` (shapes fixed
+        from here on); replay() then runs a step with no per-kernel host work.
+        Single process only (collectives are not captured).  Runs `warmup` eager
+        steps first (kernel attributes, cached codes) without updating the weights."""
+        if self.group is not None or (dist.is_available() and dist.is_initialized()
+                                      and dist.get_world_size() > 1):
+            raise RuntimeError("capture() runs single-process steps only")
+        check_tokens(tokens, self.shape.vocab)
+        self._g_tokens = tokens.to(self.dev).clone()
+        self._g_states = None if teacher_states is None else teacher_states.to(self.dev).clone()
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.forward_backward(self._g_tokens, self._g_states, _checked=True)
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        torch.cuda.synchronize(self.dev)
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph):
+            self._g_loss = self.forward_backward(self._g_tokens, self._g_states, _checked=True)
+            self._g_last = dict(self.last)
+        torch.cuda.synchronize(self.dev)
+
+    def replay(self, tokens: torch.Tensor, teacher_states: torch.Tensor | None = None,
+               update: bool = True) -> torch.Tensor:
+        """One step through the captured graph: copy the inputs (host or device)
+        into the static buffers, replay, then AdamW eagerly (its bias correction
+        changes every step).  Returns the loss tensor the graph writes."""
+        if tokens.device.type == "cpu":
+            check_tokens(tokens, self.shape.vocab)
+        self._g_tokens.copy_(tokens, non_blocking=True)
+        if self._g_states is not None:
+            self._g_states.copy_(teacher_states, non_blocking=True)
+        self._graph.replay()
+        self.last = self._g_last
+        if update:
+            self._update()
+        return self._g_loss
+
     def _to_device(self, t):
         if t is None or t.device == self.dev:
             return t
@@ -447,10 +491,11 @@ class DraftTrainStep:
         return self.forward_backward(tokens, teacher_states, update=True)
 
     def forward_backward(self, tokens: torch.Tensor, teacher_states: torch.Tensor | None = None,
-                         update: bool = False):
+                         update: bool = False, _checked: bool = False):
         """The step up to the (rank-averaged) gradients in self.flat.grad, plus the
         optimizer update when `update`.  Returns the loss (device scalar)."""
-        check_tokens(tokens, self.shape.vocab)
+        if not _checked:
+            check_tokens(tokens, self.shape.vocab)
         tokens = self._to_device(tokens)
         teacher_states = self._to_device(teacher_states)
         inp, tgt = tokens[:, :-1], tokens[:, 1:]
