@@ -221,7 +221,9 @@ int ksd8_rosa_match(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw, 
 
 /* Matcher kernel behind ksd8_rosa_match (process-wide, identical results):
  * 0 = prefix tables processed 32 positions per warp step (default), 1 = prefix
- * tables one position per step, 2 = window scan (always used for T >= 8192). */
+ * tables one position per step, 2 = window scan (always used for T >= 8192),
+ * 3 = sorted key windows with a max segment tree (O(log T) per position on any
+ * bit statistics; T <= 4096 + max_len - 1, else as 0). */
 int ksd8_rosa_set_algorithm(int algo);
 
 /* Rosa time-shift mix + per-token GS quantisation of the three projection

@@ -416,6 +416,233 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_chunk_kernel(MatchAr
   }
 }
 
+// ---------------------------------------------------------------- sorted-key matcher
+//
+// Exact, with O(log T) work per position whatever the bit statistics (the
+// level-12 chains of the prefix tables degenerate to O(T) walks on streams with
+// long runs, as the projections of trained or deep-layer activations give).
+//
+// The 64-bit window W(j) of a key determines its common-suffix length with a
+// query window: lcs = clz(Wq(t) ^ Wk(j)).  With the keys j >= R0 = max_len - 1
+// (whose window has at least max_len real bits) sorted by window value, the
+// keys sharing the top L bits with a query form one interval of ranks, and the
+// largest common prefix with any inserted key is reached at the inserted
+// predecessor or successor of the query's rank.  Per stream (one warp):
+//   - bitonic sort of the (window, j) pairs of the keys j in [R0, T-2];
+//   - 32 queries per step (lane = t0 + lane), against the keys inserted so far
+//     (j <= t0 - 2): binary search of the rank, inserted neighbours from a
+//     bitmap with a summary word, L = min(max lcp, cap_t), the rank interval of
+//     the L-bit prefix by two binary searches, and the latest endpoint in it
+//     from a max segment tree over ranks;
+//   - keys j < R0 (their window reaches before position 0, so a match is also
+//     capped at j + 1) and this step's own keys j in [t0-1, t-1] are compared
+//     directly (broadcast loads / shuffles);
+//   - then this step's keys are inserted (bitmap bits, segment-tree maxima;
+//     keys sharing a tree node are grouped with match_any and the latest wins).
+constexpr int RS_MAXNP = 4096;  // sorted keys per stream (T <= 4096 + R0)
+
+__device__ __forceinline__ bool rs_less(uint64_t wa, uint16_t ja, uint64_t wb, uint16_t jb) {
+  return wa < wb || (wa == wb && ja < jb);
+}
+
+// number of sorted windows < key (first rank with SW[rank] >= key); np a power of 2
+__device__ __forceinline__ int rs_lower_bound(const uint64_t* sw, int np, uint64_t key) {
+  int pos = 0;
+  for (int step = np >> 1; step > 0; step >>= 1)
+    if (sw[pos + step - 1] < key) pos += step;
+  return (pos == np - 1 && sw[pos] < key) ? np : pos;
+}
+
+// largest inserted rank < r (-1 if none); bitmap words bm (32 bits), summary sm[2]
+__device__ __forceinline__ int rs_pred(const uint32_t* bm, const uint64_t* sm, int r) {
+  if (r <= 0) return -1;
+  const int q = r - 1;
+  const int w = q >> 5;
+  const uint32_t m = bm[w] & (0xFFFFFFFFu >> (31 - (q & 31)));
+  if (m) return (w << 5) + 31 - __clz((int)m);
+  for (int h = w >> 6; h >= 0; --h) {
+    uint64_t sw = sm[h];
+    if (h == (w >> 6)) sw &= (w & 63) ? (~0ull >> (64 - (w & 63))) : 0ull;
+    if (sw) {
+      const int w2 = (h << 6) + 63 - __clzll((long long)sw);
+      return (w2 << 5) + 31 - __clz((int)bm[w2]);
+    }
+  }
+  return -1;
+}
+
+// smallest inserted rank >= r (-1 if none), ranks < np
+__device__ __forceinline__ int rs_succ(const uint32_t* bm, const uint64_t* sm, int r, int np) {
+  if (r >= np) return -1;
+  const int w = r >> 5;
+  const uint32_t m = bm[w] & (0xFFFFFFFFu << (r & 31));
+  if (m) return (w << 5) + __ffs((int)m) - 1;
+  const int nwords = np >> 5;
+  for (int h = w >> 6; (h << 6) < nwords; ++h) {
+    uint64_t sw = sm[h];
+    if (h == (w >> 6)) sw &= ((w & 63) == 63) ? 0ull : (~0ull << ((w & 63) + 1));
+    if (sw) {
+      const int w2 = (h << 6) + __ffsll((long long)sw) - 1;
+      return (w2 << 5) + __ffs((int)bm[w2]) - 1;
+    }
+  }
+  return -1;
+}
+
+__global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchArgs a, int np,
+                                                                           int stride) {
+  extern __shared__ __align__(16) uint8_t rsm_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t stream = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (stream >= a.batch * a.streams) return;  // the whole warp: no CTA barrier below
+  const int T = (int)a.t_len;
+  const int nw = (T + 63) / 64;
+  const int ml = a.max_len;
+  const int r0 = ml > 0 ? ml - 1 : 0;        // first key whose window has max_len real bits
+  const int nk = T - 1 - r0 > 0 ? T - 1 - r0 : 0;  // sorted keys j in [r0, T-2]
+  // per-warp layout: SW[np] u64 | seg[2np] u16 (holds SJ[np] while sorting) |
+  //                  rank_of[T] u16 | bm[np/32] u32 | sm[2] u64 | sq, sk, sv [nw] u64
+  uint8_t* base = rsm_raw + (size_t)warp * stride;
+  uint64_t* SW = reinterpret_cast<uint64_t*>(base);
+  uint16_t* seg = reinterpret_cast<uint16_t*>(SW + np);
+  uint16_t* SJ = seg;
+  uint16_t* rank_of = seg + 2 * np;
+  uint32_t* bm = reinterpret_cast<uint32_t*>(
+      base + (((size_t)np * 8 + (size_t)4 * np + (size_t)2 * T + 15) / 16 * 16));
+  uint64_t* sm = reinterpret_cast<uint64_t*>(bm + np / 32);
+  uint64_t* sq = sm + 2;
+  uint64_t* sk = sq + nw;
+  uint64_t* sv = sk + nw;
+  for (int i = lane; i < nw; i += 32) {
+    sq[i] = a.qw[stream * nw + i];
+    sk[i] = a.kw[stream * nw + i];
+    sv[i] = a.vw[stream * nw + i];
+  }
+  for (int i = lane; i < np / 32; i += 32) bm[i] = 0u;
+  if (lane < 2) sm[lane] = 0ull;
+  __syncwarp();
+  for (int i = lane; i < np; i += 32) {
+    const bool real = i < nk;
+    SW[i] = real ? window_sm(sk, r0 + i) : ~0ull;
+    SJ[i] = real ? (uint16_t)(r0 + i) : (uint16_t)0xFFFFu;
+  }
+  __syncwarp();
+  // bitonic sort of (SW, SJ) ascending
+  for (int k = 2; k <= np; k <<= 1) {
+    for (int jj = k >> 1; jj > 0; jj >>= 1) {
+      for (int i = lane; i < np; i += 32) {
+        const int l = i ^ jj;
+        if (l > i) {
+          const bool up = (i & k) == 0;
+          const uint64_t wi = SW[i], wl = SW[l];
+          const uint16_t ji = SJ[i], jl = SJ[l];
+          if (rs_less(wl, jl, wi, ji) == up) {
+            SW[i] = wl; SW[l] = wi;
+            SJ[i] = jl; SJ[l] = ji;
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+  for (int i = lane; i < nk; i += 32) rank_of[SJ[i]] = (uint16_t)i;
+  __syncwarp();
+  for (int i = lane; i < 2 * np; i += 32) seg[i] = 0;   // SJ is spent: the tree starts empty
+  __syncwarp();
+
+  const int64_t b = stream / a.streams, s = stream % a.streams;
+  const float pay = a.payload ? a.payload[s] : 1.f;
+  const unsigned full = 0xffffffffu;
+  for (int t0 = 0; t0 < T; t0 += 32) {
+    const int t = t0 + lane;
+    const bool valid = t < T;
+    const uint64_t wq = valid ? window_sm(sq, t) : 0ull;
+    const int cap = valid ? min(ml, t) : 0;
+    const int jk = t0 - 1 + lane;                       // this lane's key
+    const bool kin = jk >= 0 && jk < T;
+    const uint64_t wk = kin ? window_sm(sk, jk) : 0ull;
+    int best = 0, bestj = -1;
+    // sorted keys inserted by earlier steps (r0 <= j <= t0 - 2)
+    if (t0 - 2 >= r0 && cap > 0) {
+      const int r = rs_lower_bound(SW, np, wq);
+      const int p = rs_pred(bm, sm, r), q = rs_succ(bm, sm, r, np);
+      int lraw = 0;
+      if (p >= 0) { const uint64_t x = wq ^ SW[p]; lraw = x ? __clzll((long long)x) : 64; }
+      if (q >= 0) { const uint64_t x = wq ^ SW[q]; lraw = max(lraw, x ? __clzll((long long)x) : 64); }
+      const int L = min(lraw, cap);
+      if (L > 0) {
+        const uint64_t pre = L >= 64 ? wq : (wq >> (64 - L)) << (64 - L);
+        const uint64_t last = L >= 64 ? wq : pre | (~0ull >> L);
+        const int lo = rs_lower_bound(SW, np, pre);
+        const int hi = last == ~0ull ? np : rs_lower_bound(SW, np, last + 1);  // exclusive
+        int res = 0;
+        for (int l = lo + np, h = hi + np; l < h; l >>= 1, h >>= 1) {
+          if (l & 1) res = max(res, (int)seg[l++]);
+          if (h & 1) res = max(res, (int)seg[--h]);
+        }
+        best = L;
+        bestj = res - 1;
+      }
+    }
+    // keys j < r0: also capped at j + 1; only those with j >= best can improve
+    {
+      const int jhi = min(r0 - 1, t0 - 2);
+      int jlo = valid ? best : 0x7fffffff;
+      jlo = __reduce_min_sync(full, jlo);
+      int be = 0, bj = -1;
+      for (int j = jlo; j <= jhi; ++j) {
+        const uint64_t x = wq ^ window_sm(sk, j);
+        int l = x ? __clzll((long long)x) : 64;
+        l = min(l, min(cap, j + 1));
+        if (l > 0 && l >= be) { be = l; bj = j; }
+      }
+      if (be > best) { best = be; bestj = bj; }
+    }
+    // this step's own keys, j = t0 - 1 + i <= t - 1 (the latest: they win ties)
+    for (int i = 0; i < 32; ++i) {
+      const uint64_t wki = __shfl_sync(full, wk, i);
+      const int j = t0 - 1 + i;
+      if (i <= lane && j >= 0) {
+        const uint64_t x = wq ^ wki;
+        int l = x ? __clzll((long long)x) : 64;
+        l = min(l, min(cap, j + 1));
+        if (l > 0 && l >= best) { best = l; bestj = j; }
+      }
+    }
+    if (valid) {
+      float sign = -1.f;
+      if (bestj >= 0) {
+        const int succ = bestj + 1;
+        sign = ((sv[succ >> 6] >> (succ & 63)) & 1ull) ? 1.f : -1.f;
+      }
+      const float o = pay * sign;
+      const int64_t oo = b * a.ob + (int64_t)t * a.ot + s * a.os;
+      if (a.out_dtype == KSD8_F32)
+        reinterpret_cast<float*>(a.out)[oo] = o;
+      else if (a.out_dtype == KSD8_BF16)
+        reinterpret_cast<__nv_bfloat16*>(a.out)[oo] = __float2bfloat16_rn(o);
+      else
+        reinterpret_cast<__half*>(a.out)[oo] = __float2half_rn(o);
+      if (a.match_len) a.match_len[stream * a.t_len + t] = best;
+      if (a.match_end) a.match_end[stream * a.t_len + t] = bestj;
+    }
+    // insert this step's sorted keys (r0 <= j <= T - 2)
+    __syncwarp();
+    const bool ins = kin && jk >= r0 && jk <= T - 2;
+    const unsigned im = __ballot_sync(full, ins);
+    if (ins) {
+      const int r = rank_of[jk];
+      atomicOr(&bm[r >> 5], 1u << (r & 31));
+      atomicOr((unsigned long long*)&sm[r >> 11], 1ull << ((r >> 5) & 63));
+      for (int node = r + np; node >= 1; node >>= 1) {
+        const unsigned grp = __match_any_sync(im, node);
+        if (lane == 31 - __clz((int)grp)) seg[node] = (uint16_t)(jk + 1);
+      }
+    }
+    __syncwarp();
+  }
+}
+
 struct TimemixArgs {
   const void* x;
   int64_t batch, t_len, d;
@@ -647,11 +874,12 @@ int ksd8_rosa_pack_bits_launch(const void* x, int x_dtype, int64_t batch, int64_
 }
 
 // Matcher selection (process-wide): 0 = chunked prefix tables (default),
-// 1 = one position per step prefix tables, 2 = window scan.  Streams of 8192 or
+// 1 = one position per step prefix tables, 2 = window scan, 3 = sorted keys
+// (streams up to 4096 + max_len - 1 positions, else as 0).  Streams of 8192 or
 // more positions always take the window scan.  algo < 0 only reads.
 int ksd8_rosa_algorithm(int algo) {
   static int g_algo = 0;
-  if (algo >= 0 && algo <= 2) g_algo = algo;
+  if (algo >= 0 && algo <= 3) g_algo = algo;
   return g_algo;
 }
 
@@ -676,6 +904,34 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
   a.max_len = max_len; a.payload = payload; a.out = out; a.out_dtype = out_dtype;
   a.ob = ob; a.ot = ot; a.os = os; a.match_len = match_len; a.match_end = match_end;
   const int algo = ksd8_rosa_algorithm(-1);
+  if (algo == 3) {
+    // sorted-key matcher: per-warp keys, segment tree, rank table, bitmap, words
+    const int r0 = max_len > 0 ? max_len - 1 : 0;
+    const int64_t nk = t_len - 1 - r0 > 0 ? t_len - 1 - r0 : 0;
+    int np = 64;
+    while (np < nk) np <<= 1;
+    if (np <= RS_MAXNP) {
+      const size_t head = ((size_t)np * 12 + (size_t)t_len * 2 + 15) / 16 * 16;
+      const int stride = (int)((head + np / 8 + 16 + 24 * (size_t)((t_len + 63) / 64) + 15) /
+                               16 * 16);
+      int nwarps = (int)((227 * 1024) / (size_t)stride);
+      if (nwarps > RC_WARPS) nwarps = RC_WARPS;
+      if (nwarps >= 1) {
+        static unsigned sorted_attr = 0;
+        if (!(sorted_attr & (1u << dev))) {
+          if (cudaFuncSetAttribute(rosa_match_sorted_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+              cudaSuccess)
+            return KSD8_ERR_LAUNCH;
+          sorted_attr |= (1u << dev);
+        }
+        const int64_t n = batch * streams;
+        rosa_match_sorted_kernel<<<(unsigned)((n + nwarps - 1) / nwarps), nwarps * 32,
+                                   (size_t)nwarps * stride, stream>>>(a, np, stride);
+        return KSD8_OK;
+      }
+    }
+  }
   if (t_len < RP_TMAX && algo != 2) {
     static unsigned prefix_attr = 0;
     // bytes per warp: tables + links (16-byte aligned), then 3 x ceil(T/64) words

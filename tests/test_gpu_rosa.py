@@ -62,10 +62,11 @@ def rosa_algorithm():
     use(0)
 
 
-@pytest.mark.parametrize("algo", [0, 1, 2])
+@pytest.mark.parametrize("algo", [0, 1, 2, 3])
 @pytest.mark.parametrize("S,T,max_len", [(16, 31, None), (16, 32, None), (16, 97, None),
                                          (40, 700, None), (8, 2048, None), (8, 700, 5),
-                                         (8, 700, 12), (8, 700, 13), (5, 3000, 40)])
+                                         (8, 700, 12), (8, 700, 13), (5, 3000, 40),
+                                         (4, 4157, None), (6, 300, 64), (6, 200, 1)])
 def test_match_kernels_agree_with_oracle(oracle, rosa_algorithm, algo, S, T, max_len):
     """Every matcher kernel (chunked prefix tables, per-position prefix tables,
     window scan) gives the oracle's signs, lengths and endpoints, across chunk
@@ -77,6 +78,9 @@ def test_match_kernels_agree_with_oracle(oracle, rosa_algorithm, algo, S, T, max
     q, k, v = _streams(rng, S, T)
     q[: S // 2] = (np.arange(T) % 3 == 0).astype(np.int8)      # periodic: dense collisions
     k[: S // 2] = (np.arange(T) % 3 == 1).astype(np.int8)
+    for i in range(S // 2, S // 2 + S // 4):                   # long runs: long matches below
+        q[i] = (np.cumsum(rng.random(T) < 0.05) % 2).astype(np.int8)   # the cap, long chains
+        k[i] = (np.cumsum(rng.random(T) < 0.05) % 2).astype(np.int8)
     args = (torch.from_numpy(a).cuda() for a in (q, k, v))
     s, L, E = match_payload_sign_with_indices(*args, max_match_len=max_len)
     so, Lo, Eo = oracle.rosa_match(q, k, v, max_match_len=max_len, method="dp")
