@@ -566,10 +566,9 @@ def run_config4(args) -> None:
     use_graph = world == 1 and not args.no_graph
     gt = GemmTimer(external=True)
     if use_graph:
-        launches0 = _lib.LAUNCHES
         with gt:
             step.capture(tok_dev, ts_dev)
-        captured = _lib.LAUNCHES - launches0
+        captured = step.captured_launches
 
         def run(tok, ts):
             return step.replay(tok, ts)

@@ -32,6 +32,7 @@
  *   ksd8_rosa_pack_bits       ksdraft/model/rosa.py:156-158 (bits = proj > 0) and the int8 bit inputs
  *                             of rosa.py:40 _match_payload_sign
  *   ksd8_rosa_match           ksdraft/model/rosa.py:40-98 _match_payload_sign (+ payload multiply of :164)
+ *   ksd8_rosa_match_scratch   the same, adaptive matcher with caller scratch
  *   ksd8_rosa_timemix_quantize ksdraft/model/rosa.py:128-133 _shifted followed by the per-token
  *                             quantisation of Int8Linear.forward (ksdraft/kernels/linear.py:69)
  *   ksd8_adamw_step           torch.optim.AdamW.step over fp32 masters (ksdraft/train/__init__.py:166)
@@ -218,6 +219,17 @@ int ksd8_rosa_match(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw, 
                     int64_t streams, int64_t t_len, int max_len, const float* payload,
                     void* out, int out_dtype, int64_t ob, int64_t ot, int64_t os,
                     int32_t* match_len, int32_t* match_end, int* status, void* stream);
+
+/* ksd8_rosa_match with scratch (1 + batch * streams int32 of device memory) for
+ * the adaptive matcher (algorithm 0): the chunked prefix-table kernel runs
+ * every stream, and a stream whose level-12 chain walks exceed a budget (long
+ * runs make them O(T) per position) is handed, through the scratch list, to
+ * the sorted-key kernel, which rewrites all of its positions.  Same results. */
+int ksd8_rosa_match_scratch(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
+                            int64_t batch, int64_t streams, int64_t t_len, int max_len,
+                            const float* payload, void* out, int out_dtype, int64_t ob,
+                            int64_t ot, int64_t os, int32_t* match_len, int32_t* match_end,
+                            int32_t* scratch, int64_t scratch_len, int* status, void* stream);
 
 /* Matcher kernel behind ksd8_rosa_match (process-wide, identical results):
  * 0 = prefix tables processed 32 positions per warp step (default), 1 = prefix

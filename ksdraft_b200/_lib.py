@@ -50,6 +50,8 @@ SIGNATURES: dict[str, list] = {
     "ksd8_rosa_pack_bits": [vp, i32, i64, i64, i64, i64, i64, i64, vp, vp, vp],
     "ksd8_rosa_match": [vp, vp, vp, i64, i64, i64, i32, vp, vp, i32, i64, i64, i64, vp, vp, vp,
                         vp],
+    "ksd8_rosa_match_scratch": [vp, vp, vp, i64, i64, i64, i32, vp, vp, i32, i64, i64, i64, vp,
+                                vp, vp, i64, vp, vp],
     "ksd8_rosa_timemix_quantize": [vp, i32, i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                    vp, vp],
     "ksd8_adamw_step": [vp, vp, i32, vp, vp, i64, f32, f32, f32, f32, f32, i32, vp, vp],

@@ -32,7 +32,7 @@ int ksd8_rosa_pack_bits_launch(const void*, int, int64_t, int64_t, int64_t, int6
                                int64_t, uint64_t*, cudaStream_t);
 int ksd8_rosa_match_launch(const uint64_t*, const uint64_t*, const uint64_t*, int64_t, int64_t,
                            int64_t, int, const float*, void*, int, int64_t, int64_t, int64_t,
-                           int32_t*, int32_t*, cudaStream_t);
+                           int32_t*, int32_t*, cudaStream_t, int32_t*);
 int ksd8_rosa_timemix_launch(const void*, int, int64_t, int64_t, int64_t, const float*,
                              const float*, const float*, int8_t*, void*, int8_t*, void*, int8_t*,
                              void*, cudaStream_t);
@@ -282,7 +282,25 @@ int ksd8_rosa_match(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw, 
   if (t_len > 25600) return KSD8_ERR_UNSUPPORTED;  // key windows must fit in shared memory
   if (batch * streams * t_len > 0 && (!qw || !kw || !vw || !out)) return KSD8_ERR_ARG;
   return finish(ksd8_rosa_match_launch(qw, kw, vw, batch, streams, t_len, max_len, payload, out,
-                                       out_dtype, ob, ot, os, match_len, match_end, S(stream)));
+                                       out_dtype, ob, ot, os, match_len, match_end, S(stream),
+                                       nullptr));
+}
+
+int ksd8_rosa_match_scratch(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
+                            int64_t batch, int64_t streams, int64_t t_len, int max_len,
+                            const float* payload, void* out, int out_dtype, int64_t ob,
+                            int64_t ot, int64_t os, int32_t* match_len, int32_t* match_end,
+                            int32_t* scratch, int64_t scratch_len, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(out_dtype)) return KSD8_ERR_DTYPE;
+  if (batch < 0 || streams < 0 || t_len < 0) return KSD8_ERR_SHAPE;
+  if (max_len < 0 || max_len > 64) return KSD8_ERR_ARG;
+  if (t_len > 25600) return KSD8_ERR_UNSUPPORTED;
+  if (batch * streams * t_len > 0 && (!qw || !kw || !vw || !out)) return KSD8_ERR_ARG;
+  if (!scratch || scratch_len < 1 + batch * streams) return KSD8_ERR_SHAPE;
+  return finish(ksd8_rosa_match_launch(qw, kw, vw, batch, streams, t_len, max_len, payload, out,
+                                       out_dtype, ob, ot, os, match_len, match_end, S(stream),
+                                       scratch));
 }
 
 int ksd8_rosa_timemix_quantize(const void* x, int x_dtype, int64_t batch, int64_t t_len,

@@ -82,6 +82,11 @@ struct MatchArgs {
   int64_t ob, ot, os;
   int32_t* match_len;
   int32_t* match_end;
+  // adaptive matching: the chunked kernel hands a stream whose level-12 chain
+  // walks exceed the budget to the sorted kernel through redo = [count, ids...]
+  int32_t* redo;
+  int redo_budget;  // chain steps per position allowed on average
+  int redo_pass;    // 1: the sorted kernel runs only the listed streams
 };
 
 __global__ void __launch_bounds__(512) rosa_match_kernel(MatchArgs a) {
@@ -315,6 +320,7 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_chunk_kernel(MatchAr
   const int64_t b = stream / a.streams, s = stream % a.streams;
   const float pay = a.payload ? a.payload[s] : 1.f;
   const unsigned full = 0xffffffffu;
+  uint64_t walked = 0;   // chain steps of this stream so far (warp total)
   for (int64_t t0 = 0; t0 < T; t0 += 32) {
     const int64_t t = t0 + lane;
     const bool valid = t < T;
@@ -337,12 +343,13 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_chunk_kernel(MatchAr
         best = L;
         bestj = (int64_t)hit[L - 1] - 1;
       }
+    int steps = 0;
     if (best == RP_LEVELS && cap > RP_LEVELS) {
       // exact length among the keys sharing the top RP_LEVELS bits, newest first
       const uint32_t head = hit[RP_LEVELS - 1];
       best = 0;
       bestj = -1;
-      for (uint32_t c = head; c != 0;) {
+      for (uint32_t c = head; c != 0; ++steps) {
         const int64_t j = (int64_t)c - 1;
         const uint64_t x = wq ^ window_sm(sk, j);
         int l = x == 0ull ? 64 : __clzll((long long)x);
@@ -412,6 +419,18 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_chunk_kernel(MatchAr
         if (lane == 31 - __clz((int)grp)) tbl[idx] = (uint16_t)(jk + 1);
       }
       __syncwarp();
+    }
+    if (a.redo) {
+      // long runs make the chains long (O(T) per position): leave such a stream to
+      // the sorted matcher, which rewrites all of its positions
+      walked += __reduce_add_sync(full, (unsigned)steps);
+      if (t0 >= 96 && walked > (uint64_t)a.redo_budget * (uint64_t)(t0 + 32)) {
+        if (lane == 0) {
+          const int slot = atomicAdd(a.redo, 1);
+          a.redo[1 + slot] = (int32_t)stream;
+        }
+        return;
+      }
     }
   }
 }
@@ -493,7 +512,11 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchA
                                                                            int stride) {
   extern __shared__ __align__(16) uint8_t rsm_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t stream = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  int64_t stream = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (a.redo_pass) {  // only the streams the chunked kernel handed over
+    if (stream >= a.redo[0]) return;
+    stream = a.redo[1 + stream];
+  }
   if (stream >= a.batch * a.streams) return;  // the whole warp: no CTA barrier below
   const int T = (int)a.t_len;
   const int nw = (T + 63) / 64;
@@ -513,6 +536,7 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchA
   uint64_t* sq = sm + 2;
   uint64_t* sk = sq + nw;
   uint64_t* sv = sk + nw;
+  uint64_t* EW = sv + nw;   // windows of the keys j < r0 (at most 64)
   for (int i = lane; i < nw; i += 32) {
     sq[i] = a.qw[stream * nw + i];
     sk[i] = a.kw[stream * nw + i];
@@ -521,6 +545,7 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchA
   for (int i = lane; i < np / 32; i += 32) bm[i] = 0u;
   if (lane < 2) sm[lane] = 0ull;
   __syncwarp();
+  for (int i = lane; i < r0 && i < T; i += 32) EW[i] = window_sm(sk, i);
   for (int i = lane; i < np; i += 32) {
     const bool real = i < nk;
     SW[i] = real ? window_sm(sk, r0 + i) : ~0ull;
@@ -591,7 +616,7 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchA
       jlo = __reduce_min_sync(full, jlo);
       int be = 0, bj = -1;
       for (int j = jlo; j <= jhi; ++j) {
-        const uint64_t x = wq ^ window_sm(sk, j);
+        const uint64_t x = wq ^ EW[j];
         int l = x ? __clzll((long long)x) : 64;
         l = min(l, min(cap, j + 1));
         if (l > 0 && l >= be) { be = l; bj = j; }
@@ -883,11 +908,45 @@ int ksd8_rosa_algorithm(int algo) {
   return g_algo;
 }
 
+// The prefix-table matchers (chunked, or one position per step for algo 1).
+static int launch_chunk(const MatchArgs& a, int64_t t_len, int dev, int algo,
+                        cudaStream_t stream) {
+  static unsigned prefix_attr = 0;
+  // bytes per warp: tables + links (16-byte aligned), then 3 x ceil(T/64) words
+  // (a multiple of 16 bytes, so that every warp's region keeps the 16-byte
+  // alignment of its vector stores)
+  const int stride = (int)(((((size_t)RP_TBL + t_len) * 2 + 15) / 16 * 16 +
+                            3 * 8 * (size_t)((t_len + 63) / 64) + 15) / 16 * 16);
+  int nwarps = (int)((227 * 1024) / (size_t)stride);
+  const int cap_warps = algo == 1 ? RP_WARPS : RC_WARPS;
+  if (nwarps > cap_warps) nwarps = cap_warps;
+  const size_t psmem = (size_t)nwarps * stride;
+  if (!(prefix_attr & (1u << dev))) {
+    if (cudaFuncSetAttribute(rosa_match_prefix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(rosa_match_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             227 * 1024) != cudaSuccess)
+      return KSD8_ERR_LAUNCH;
+    prefix_attr |= (1u << dev);
+  }
+  const int64_t n = a.batch * a.streams;
+  const unsigned grid = (unsigned)((n + nwarps - 1) / nwarps);
+  if (algo == 1)
+    rosa_match_prefix_kernel<<<grid, nwarps * 32, psmem, stream>>>(a, stride);
+  else
+    rosa_match_chunk_kernel<<<grid, nwarps * 32, psmem, stream>>>(a, stride);
+  return KSD8_OK;
+}
+
+#ifndef KSD8_ROSA_REDO_BUDGET
+#define KSD8_ROSA_REDO_BUDGET 4
+#endif
+
 int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
                            int64_t batch, int64_t streams, int64_t t_len, int max_len,
                            const float* payload, void* out, int out_dtype, int64_t ob, int64_t ot,
                            int64_t os, int32_t* match_len, int32_t* match_end,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, int32_t* redo) {
   if (batch * streams == 0 || t_len == 0) return KSD8_OK;
   const size_t smem = (size_t)t_len * 8;
   static int attr_dev_mask = 0;
@@ -903,17 +962,25 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
   a.qw = qw; a.kw = kw; a.vw = vw; a.batch = batch; a.streams = streams; a.t_len = t_len;
   a.max_len = max_len; a.payload = payload; a.out = out; a.out_dtype = out_dtype;
   a.ob = ob; a.ot = ot; a.os = os; a.match_len = match_len; a.match_end = match_end;
+  a.redo = nullptr; a.redo_budget = 0; a.redo_pass = 0;
   const int algo = ksd8_rosa_algorithm(-1);
-  if (algo == 3) {
-    // sorted-key matcher: per-warp keys, segment tree, rank table, bitmap, words
-    const int r0 = max_len > 0 ? max_len - 1 : 0;
-    const int64_t nk = t_len - 1 - r0 > 0 ? t_len - 1 - r0 : 0;
-    int np = 64;
-    while (np < nk) np <<= 1;
-    if (np <= RS_MAXNP) {
+  // the sorted-key matcher's per-warp shared memory (keys, tree, ranks, bitmap, words)
+  const int r0 = max_len > 0 ? max_len - 1 : 0;
+  const int64_t nk = t_len - 1 - r0 > 0 ? t_len - 1 - r0 : 0;
+  int np = 64;
+  while (np < nk) np <<= 1;
+  const bool sorted_ok = np <= RS_MAXNP;
+  if (algo == 0 && redo && sorted_ok && t_len < RP_TMAX) {
+    // adaptive: chunked prefix tables, degenerate streams redone by the sorted kernel
+    if (cudaMemsetAsync(redo, 0, sizeof(int32_t), stream) != cudaSuccess) return KSD8_ERR_LAUNCH;
+    a.redo = redo;
+    a.redo_budget = KSD8_ROSA_REDO_BUDGET;
+  }
+  if (algo == 3 || a.redo) {
+    if (sorted_ok) {
       const size_t head = ((size_t)np * 12 + (size_t)t_len * 2 + 15) / 16 * 16;
-      const int stride = (int)((head + np / 8 + 16 + 24 * (size_t)((t_len + 63) / 64) + 15) /
-                               16 * 16);
+      const int stride = (int)((head + np / 8 + 16 + 24 * (size_t)((t_len + 63) / 64) + 512 +
+                                15) / 16 * 16);
       int nwarps = (int)((227 * 1024) / (size_t)stride);
       if (nwarps > RC_WARPS) nwarps = RC_WARPS;
       if (nwarps >= 1) {
@@ -926,41 +993,24 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
           sorted_attr |= (1u << dev);
         }
         const int64_t n = batch * streams;
+        if (!a.redo) {
+          rosa_match_sorted_kernel<<<(unsigned)((n + nwarps - 1) / nwarps), nwarps * 32,
+                                     (size_t)nwarps * stride, stream>>>(a, np, stride);
+          return KSD8_OK;
+        }
+        // adaptive: the chunked kernel first (below), then the listed streams here
+        const int rc = launch_chunk(a, t_len, dev, algo, stream);
+        if (rc != KSD8_OK) return rc;
+        MatchArgs r = a;
+        r.redo_pass = 1;
         rosa_match_sorted_kernel<<<(unsigned)((n + nwarps - 1) / nwarps), nwarps * 32,
-                                   (size_t)nwarps * stride, stream>>>(a, np, stride);
+                                   (size_t)nwarps * stride, stream>>>(r, np, stride);
         return KSD8_OK;
       }
     }
+    a.redo = nullptr;
   }
-  if (t_len < RP_TMAX && algo != 2) {
-    static unsigned prefix_attr = 0;
-    // bytes per warp: tables + links (16-byte aligned), then 3 x ceil(T/64) words
-    // (a multiple of 16 bytes, so that every warp's region keeps the 16-byte
-    // alignment of its vector stores)
-    const int stride = (int)(((((size_t)RP_TBL + t_len) * 2 + 15) / 16 * 16 +
-                              3 * 8 * (size_t)((t_len + 63) / 64) + 15) / 16 * 16);
-    int nwarps = (int)((227 * 1024) / (size_t)stride);
-    const int cap_warps = algo == 1 ? RP_WARPS : RC_WARPS;
-    if (nwarps > cap_warps) nwarps = cap_warps;
-    const size_t psmem = (size_t)nwarps * stride;
-    if (!(prefix_attr & (1u << dev))) {
-      if (cudaFuncSetAttribute(rosa_match_prefix_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-              cudaSuccess ||
-          cudaFuncSetAttribute(rosa_match_chunk_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-              cudaSuccess)
-        return KSD8_ERR_LAUNCH;
-      prefix_attr |= (1u << dev);
-    }
-    const int64_t n = batch * streams;
-    const unsigned grid = (unsigned)((n + nwarps - 1) / nwarps);
-    if (algo == 1)
-      rosa_match_prefix_kernel<<<grid, nwarps * 32, psmem, stream>>>(a, stride);
-    else
-      rosa_match_chunk_kernel<<<grid, nwarps * 32, psmem, stream>>>(a, stride);
-    return KSD8_OK;
-  }
+  if (t_len < RP_TMAX && algo != 2) return launch_chunk(a, t_len, dev, algo, stream);
   int threads = 512;
   if (t_len <= 256) threads = 256;
   rosa_match_kernel<<<(unsigned)(batch * streams), threads, smem, stream>>>(a);

@@ -52,10 +52,12 @@ def match_words(qw, kw, vw, batch: int, streams: int, t_len: int, max_len: int, 
         ml = torch.empty(batch * streams, t_len, dtype=torch.int32, device=dev)
         me = torch.empty(batch * streams, t_len, dtype=torch.int32, device=dev)
     pay = payload.detach().float().contiguous() if payload is not None else None
-    rc = _lib.lib().ksd8_rosa_match(
+    # scratch of the adaptive matcher: [count, stream ids handed to the sorted kernel]
+    scratch = torch.empty(1 + batch * streams, dtype=torch.int32, device=dev)
+    rc = _lib.lib().ksd8_rosa_match_scratch(
         qw.data_ptr(), kw.data_ptr(), vw.data_ptr(), batch, streams, t_len, max(0, max_len),
         _lib.ptr(pay), out.data_ptr(), _lib.dtype_code(out), *strides, _lib.ptr(ml),
-        _lib.ptr(me), None, _lib.stream_ptr(dev))
+        _lib.ptr(me), scratch.data_ptr(), scratch.numel(), None, _lib.stream_ptr(dev))
     _lib.check(rc, "rosa_match")
     return ml, me
 

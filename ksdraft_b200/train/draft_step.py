@@ -452,6 +452,8 @@ class DraftTrainStep:
         check_tokens(tokens, self.shape.vocab)
         self._g_tokens = tokens.to(self.dev).clone()
         self._g_states = None if teacher_states is None else teacher_states.to(self.dev).clone()
+        from ..kernels.gemm import GemmTimer
+        timer, GemmTimer.active = GemmTimer.active, None   # a GEMM timer sees the graph only
         side = torch.cuda.Stream(self.dev)
         side.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(side):
@@ -459,10 +461,13 @@ class DraftTrainStep:
                 self.forward_backward(self._g_tokens, self._g_states, _checked=True)
         torch.cuda.current_stream(self.dev).wait_stream(side)
         torch.cuda.synchronize(self.dev)
+        GemmTimer.active = timer
         self._graph = torch.cuda.CUDAGraph()
+        launches0 = _lib.LAUNCHES
         with torch.cuda.graph(self._graph):
             self._g_loss = self.forward_backward(self._g_tokens, self._g_states, _checked=True)
             self._g_last = dict(self.last)
+        self.captured_launches = _lib.LAUNCHES - launches0   # ksd8 kernels per replay
         torch.cuda.synchronize(self.dev)
 
     def replay(self, tokens: torch.Tensor, teacher_states: torch.Tensor | None = None,
