@@ -5,11 +5,14 @@
 
 config4 (the metric's "train tokens/sec"): the full 24-layer KSDraft model at
 d_model=1536 (5888 KS3 charts, 512 Rosa streams, vocab 150144 with the head
-tied to the embedding), global batch 16 x 2048 tokens of Zipf(1.1) ids with
-repeated spans plus bf16 N(0,1) teacher states (teacher_dim 384), weights
-N(0,0.02).  One step = forward, CE + transfer-space loss, backward, the
-data-parallel gradient mean (NCCL, N > 1), clip_grad_norm_(1.0) and AdamW.
-The global batch is fixed, 16/N sequences per GPU ("scaling": "strong").
+tied to the embedding), batch 16 x 2048 tokens of Zipf(1.1) ids with repeated
+spans plus bf16 N(0,1) teacher states (teacher_dim 384), weights N(0,0.02).
+One step = forward, CE + transfer-space loss, backward, the data-parallel
+gradient mean (NCCL, N > 1), clip_grad_norm_(1.0) and AdamW.  Each rank runs
+the reference trainer's per-process batch of 16 sequences (ksdraft/train has
+no data parallelism of its own; DP replicates its step), so the global batch
+is 16 N ("scaling": "weak"); --global-batch 16 fixes the global batch instead
+(16/N sequences per GPU, "scaling": "strong").
 
 config2: one KS3 decoder layer INT8 fwd+bwd (+ DP all-reduce + AdamW) at 4096
 tokens per GPU (weak scaling), the round-1 workload, kept as a second line.
@@ -50,13 +53,14 @@ METRIC = "W8A8 GS128 GEMM TOPS; KSDraft INT8 train tokens/sec at 1/2/4/8 B200"
 DITHER = 0.5
 
 
-def config4(n: int) -> dict:
+def config4(n: int, per_gpu: int = C4_BATCH) -> dict:
     return {"workload": "BASELINE config 4: full KSDraft INT8 training step, 24 layers, "
                         "d_model=1536, vocab=150144, 512 Rosa streams, 5888 KS3 charts, "
-                        "global batch 16 x 2048 tokens, DP over the GPUs",
+                        f"batch {per_gpu} x 2048 tokens per GPU, DP over the GPUs",
             "model": "KSDraft 24 x (Rosa + DSpine + KS3) d_model=1536 vocab=150144",
-            "global_batch": C4_BATCH, "seq_len": C4_SEQ, "tokens_per_step": C4_BATCH * C4_SEQ,
-            "sequences_per_gpu": C4_BATCH // n, "parallelism": f"dp{n}",
+            "global_batch": per_gpu * n, "seq_len": C4_SEQ,
+            "tokens_per_step": per_gpu * n * C4_SEQ,
+            "sequences_per_gpu": per_gpu, "parallelism": f"dp{n}",
             "teacher_dim": C4_TEACHER, "activations": "bf16 residual stream",
             "l2": "flushed between timed steps (256 MiB write); step working set > L2"}
 
@@ -270,9 +274,11 @@ def run_reference(args) -> None:
     line = {"impl": "reference", "metric": METRIC, "value": m["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": m["steps_timed"], "steps_requested": args.steps,
             "warmup": 1, "ms_per_step": m["sec_per_step"] * 1e3,
-            "higher_is_better": True, "scaling": "strong" if c4 else "weak",
+            "higher_is_better": True,
+            "scaling": "strong" if (c4 and args.global_batch is not None) else "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": config4(args.gpus) if c4 else config(1),
+            "config": (config4(args.gpus, args.global_batch // args.gpus
+                               if args.global_batch else C4_BATCH) if c4 else config(1)),
             "cpu_baseline": {k: m[k] for k in ("kind", "cores", "sample", "value", "unit")},
             "e2e": {"value": m["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -539,13 +545,17 @@ def run_config4(args) -> None:
     rank, world, local = init_distributed(timeout_s=600)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if C4_BATCH % world:
-        raise SystemExit(f"global batch {C4_BATCH} does not split over {world} GPUs")
-    B = C4_BATCH // world
+    strong = args.global_batch is not None
+    if strong:
+        if args.global_batch % world:
+            raise SystemExit(f"global batch {args.global_batch} does not split over {world} GPUs")
+        B = args.global_batch // world
+    else:
+        B = C4_BATCH
     group = dist.group.WORLD if world > 1 else None
     step = DraftTrainStep(DraftShape(), dev, seed=1234, group=group)   # same weights on every rank
     # this rank's sequences: Zipf(1.1) ids with repeated spans (as config 3), teacher states
-    ids = rosa_ids(C4_BATCH, C4_SEQ + 1, seed=4)[rank * B:(rank + 1) * B]
+    ids = rosa_ids(B * world, C4_SEQ + 1, seed=4)[rank * B:(rank + 1) * B]
     tok_host = torch.from_numpy(ids).pin_memory()
     gen = torch.Generator().manual_seed(100 + rank)
     ts_host = torch.randn(B, C4_SEQ, C4_TEACHER, generator=gen).to(torch.bfloat16).pin_memory()
@@ -567,7 +577,7 @@ def run_config4(args) -> None:
     gt = GemmTimer(external=True)
     if use_graph:
         with gt:
-            step.capture(tok_dev, ts_dev)
+            step.capture(tok_dev, ts_dev, phase_marks=True)
         captured = step.captured_launches
 
         def run(tok, ts):
@@ -601,15 +611,19 @@ def run_config4(args) -> None:
         dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
     total_ms = float(total_ms.item())
 
-    # one more step with phase marks (outside the timed region): where the time goes
-    marks = []
-    step.phase_marks = marks
-    step(tok_dev, ts_dev)
-    torch.cuda.synchronize()
-    step.phase_marks = None
-    phases = {}
-    for (name, ev), (_, nxt) in zip(marks, marks[1:]):
-        phases[name] = phases.get(name, 0.0) + ev.elapsed_time(nxt)
+    # where the time goes: the phase events of the last timed step (inside the
+    # graph) or of one more eager step (outside the timed region)
+    if use_graph:
+        phases = step.graph_phases()
+    else:
+        marks = []
+        step.phase_marks = marks
+        step(tok_dev, ts_dev)
+        torch.cuda.synchronize()
+        step.phase_marks = None
+        phases = {}
+        for (name, ev), (_, nxt) in zip(marks, marks[1:]):
+            phases[name] = phases.get(name, 0.0) + ev.elapsed_time(nxt)
 
     # end to end: host ids and teacher states copied in, the loss read back
     loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
@@ -631,15 +645,16 @@ def run_config4(args) -> None:
     gn = float(step.last_grad_norm)
 
     if rank == 0:
-        tokens_total = C4_BATCH * C4_SEQ * args.steps
+        tokens_total = B * world * C4_SEQ * args.steps
         peaks = load_peaks()
         roof, ginfo = _roofline_from_gemms(gemm, peaks)
         ginfo["share_of_step"] = ginfo["total_ms"] / sum(times) if times else None
         line = {
             "metric": METRIC, "value": tokens_total / (total_ms / 1e3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config4(world),
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if strong else "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config4(world, B),
             "roofline": roof, "gemm": ginfo,
             "e2e": {"value": tokens_total / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": world * (tok_host.numel() * 8 + ts_host.numel() * 2),
@@ -876,6 +891,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("config4", "config2"), default="config4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="config4: fix the global batch (strong scaling) instead of "
+                         "16 sequences per GPU")
     ap.add_argument("--no-graph", action="store_true",
                     help="config4 on one GPU: run the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-side", action="store_true",

@@ -311,11 +311,14 @@ class DraftTrainStep:
         self._ln_leaves = {}
         self.last = {}
         self.phase_marks = None   # a list to record (phase name, CUDA event) marks into
+        self._capturing = False
 
     def _mark(self, name: str) -> None:
-        """Start phase `name` (device-side timing of the step's parts, when enabled)."""
+        """Start phase `name` (device-side timing of the step's parts, when enabled;
+        during capture the events become nodes of the graph, re-recorded by every
+        replay)."""
         if self.phase_marks is not None:
-            ev = torch.cuda.Event(enable_timing=True)
+            ev = torch.cuda.Event(enable_timing=True, external=self._capturing)
             ev.record()
             self.phase_marks.append((name, ev))
 
@@ -440,12 +443,14 @@ class DraftTrainStep:
     # ---- CUDA graph of the step ------------------------------------------------
 
     def capture(self, tokens: torch.Tensor, teacher_states: torch.Tensor | None = None,
-                warmup: int = 2) -> None:
+                warmup: int = 2, phase_marks: bool = False) -> None:
         """Record forward + backward (everything up to the gradients) into one CUDA
         graph over static device copies of `tokens` / `teacher_states` (shapes fixed
         from here on); replay() then runs a step with no per-kernel host work.
         Single process only (collectives are not captured).  Runs `warmup` eager
-        steps first (kernel attributes, cached codes) without updating the weights."""
+        steps first (kernel attributes, cached codes) without updating the weights.
+        With phase_marks, the phase events are captured too (graph_marks), for
+        graph_phases() after a replay."""
         if self.group is not None or (dist.is_available() and dist.is_initialized()
                                       and dist.get_world_size() > 1):
             raise RuntimeError("capture() runs single-process steps only")
@@ -464,9 +469,16 @@ class DraftTrainStep:
         GemmTimer.active = timer
         self._graph = torch.cuda.CUDAGraph()
         launches0 = _lib.LAUNCHES
-        with torch.cuda.graph(self._graph):
-            self._g_loss = self.forward_backward(self._g_tokens, self._g_states, _checked=True)
-            self._g_last = dict(self.last)
+        marks, self.phase_marks = self.phase_marks, ([] if phase_marks else None)
+        self._capturing = True
+        try:
+            with torch.cuda.graph(self._graph):
+                self._g_loss = self.forward_backward(self._g_tokens, self._g_states,
+                                                     _checked=True)
+                self._g_last = dict(self.last)
+        finally:
+            self._capturing = False
+            self.graph_marks, self.phase_marks = self.phase_marks, marks
         self.captured_launches = _lib.LAUNCHES - launches0   # ksd8 kernels per replay
         torch.cuda.synchronize(self.dev)
 
@@ -485,6 +497,14 @@ class DraftTrainStep:
         if update:
             self._update()
         return self._g_loss
+
+    def graph_phases(self) -> dict:
+        """ms per phase of the last replay (phase_marks captured), summed by name."""
+        marks = self.graph_marks or []
+        out = {}
+        for (name, ev), (_, nxt) in zip(marks, marks[1:]):
+            out[name] = out.get(name, 0.0) + ev.elapsed_time(nxt)
+        return out
 
     def _to_device(self, t):
         if t is None or t.device == self.dev:
