@@ -8,11 +8,9 @@ d_model=1536 (5888 KS3 charts, 512 Rosa streams, vocab 150144 with the head
 tied to the embedding), batch 16 x 2048 tokens of Zipf(1.1) ids with repeated
 spans plus bf16 N(0,1) teacher states (teacher_dim 384), weights N(0,0.02).
 One step = forward, CE + transfer-space loss, backward, the data-parallel
-gradient mean (NCCL, N > 1), clip_grad_norm_(1.0) and AdamW.  Each rank runs
-the reference trainer's per-process batch of 16 sequences (ksdraft/train has
-no data parallelism of its own; DP replicates its step), so the global batch
-is 16 N ("scaling": "weak"); --global-batch 16 fixes the global batch instead
-(16/N sequences per GPU, "scaling": "strong").
+gradient mean (NCCL, N > 1), clip_grad_norm_(1.0) and AdamW.  The global batch
+is fixed at 16 sequences, 16/N per GPU ("scaling": "strong");
+--per-gpu-batch K runs K sequences on every rank instead ("scaling": "weak").
 
 config2: one KS3 decoder layer INT8 fwd+bwd (+ DP all-reduce + AdamW) at 4096
 tokens per GPU (weak scaling), the round-1 workload, kept as a second line.
@@ -53,10 +51,13 @@ METRIC = "W8A8 GS128 GEMM TOPS; KSDraft INT8 train tokens/sec at 1/2/4/8 B200"
 DITHER = 0.5
 
 
-def config4(n: int, per_gpu: int = C4_BATCH) -> dict:
+def config4(n: int, per_gpu: int | None = None) -> dict:
+    per_gpu = C4_BATCH // n if per_gpu is None else per_gpu
     return {"workload": "BASELINE config 4: full KSDraft INT8 training step, 24 layers, "
                         "d_model=1536, vocab=150144, 512 Rosa streams, 5888 KS3 charts, "
-                        f"batch {per_gpu} x 2048 tokens per GPU, DP over the GPUs",
+                        + (f"batch {per_gpu} x 2048 tokens per GPU" if per_gpu * n != C4_BATCH
+                           else f"global batch {C4_BATCH} x 2048 tokens ({per_gpu} per GPU)")
+                        + ", DP over the GPUs",
             "model": "KSDraft 24 x (Rosa + DSpine + KS3) d_model=1536 vocab=150144",
             "global_batch": per_gpu * n, "seq_len": C4_SEQ,
             "tokens_per_step": per_gpu * n * C4_SEQ,
@@ -275,10 +276,10 @@ def run_reference(args) -> None:
             "n_gpus": args.gpus, "steps": m["steps_timed"], "steps_requested": args.steps,
             "warmup": 1, "ms_per_step": m["sec_per_step"] * 1e3,
             "higher_is_better": True,
-            "scaling": "strong" if (c4 and args.global_batch is not None) else "weak",
+            "scaling": "strong" if (c4 and args.per_gpu_batch is None) else "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": (config4(args.gpus, args.global_batch // args.gpus
-                               if args.global_batch else C4_BATCH) if c4 else config(1)),
+            "config": (config4(args.gpus, args.per_gpu_batch or C4_BATCH // args.gpus)
+                       if c4 else config(1)),
             "cpu_baseline": {k: m[k] for k in ("kind", "cores", "sample", "value", "unit")},
             "e2e": {"value": m["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -545,13 +546,13 @@ def run_config4(args) -> None:
     rank, world, local = init_distributed(timeout_s=600)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    strong = args.global_batch is not None
+    strong = args.per_gpu_batch is None
     if strong:
-        if args.global_batch % world:
-            raise SystemExit(f"global batch {args.global_batch} does not split over {world} GPUs")
-        B = args.global_batch // world
+        if C4_BATCH % world:
+            raise SystemExit(f"global batch {C4_BATCH} does not split over {world} GPUs")
+        B = C4_BATCH // world
     else:
-        B = C4_BATCH
+        B = args.per_gpu_batch
     group = dist.group.WORLD if world > 1 else None
     step = DraftTrainStep(DraftShape(), dev, seed=1234, group=group)   # same weights on every rank
     # this rank's sequences: Zipf(1.1) ids with repeated spans (as config 3), teacher states
@@ -571,9 +572,9 @@ def run_config4(args) -> None:
         step(tok_dev, ts_dev)
     barrier()
 
-    # one process per GPU alone: the forward + backward replay as one CUDA graph
-    # (no per-kernel host work); the GEMM events are recorded inside it
-    use_graph = world == 1 and not args.no_graph
+    # forward + backward (with the gradient collectives) replay as one CUDA
+    # graph (no per-kernel host work); the GEMM events are recorded inside it
+    use_graph = not args.no_graph
     gt = GemmTimer(external=True)
     if use_graph:
         with gt:
@@ -664,6 +665,9 @@ def run_config4(args) -> None:
             "cuda_graph": use_graph,
             "clocks": clocks.summary(),
         }
+    step.release()
+    torch.cuda.synchronize()
+    if rank == 0:
         if world == 1 and not args.no_side:
             del step, tok_dev, ts_dev, flush
             torch.cuda.empty_cache()
@@ -891,9 +895,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("config4", "config2"), default="config4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--global-batch", type=int, default=None,
-                    help="config4: fix the global batch (strong scaling) instead of "
-                         "16 sequences per GPU")
+    ap.add_argument("--per-gpu-batch", type=int, default=None,
+                    help="config4: this many sequences on every rank (weak scaling) "
+                         "instead of the global batch of 16 split over the ranks")
     ap.add_argument("--no-graph", action="store_true",
                     help="config4 on one GPU: run the step eagerly instead of as a CUDA graph")
     ap.add_argument("--no-side", action="store_true",

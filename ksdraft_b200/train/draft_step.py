@@ -447,13 +447,16 @@ class DraftTrainStep:
         """Record forward + backward (everything up to the gradients) into one CUDA
         graph over static device copies of `tokens` / `teacher_states` (shapes fixed
         from here on); replay() then runs a step with no per-kernel host work.
-        Single process only (collectives are not captured).  Runs `warmup` eager
-        steps first (kernel attributes, cached codes) without updating the weights.
-        With phase_marks, the phase events are captured too (graph_marks), for
-        graph_phases() after a replay."""
-        if self.group is not None or (dist.is_available() and dist.is_initialized()
-                                      and dist.get_world_size() > 1):
-            raise RuntimeError("capture() runs single-process steps only")
+        Data parallel over NCCL, the gradient all-reduces and the embedding-row
+        all-gathers are captured too (every rank captures and replays the same
+        sequence; release() before destroying the process group).  Runs `warmup`
+        eager steps first (kernel attributes, cached codes, communicators)
+        without updating the weights.  With phase_marks, the phase events are
+        captured too (graph_marks), for graph_phases() after a replay."""
+        if (dist.is_available() and dist.is_initialized()
+                and dist.get_world_size(self.group) > 1
+                and dist.get_backend(self.group) != "nccl"):
+            raise RuntimeError("capture() of a data-parallel step needs the NCCL backend")
         check_tokens(tokens, self.shape.vocab)
         self._g_tokens = tokens.to(self.dev).clone()
         self._g_states = None if teacher_states is None else teacher_states.to(self.dev).clone()
@@ -472,7 +475,9 @@ class DraftTrainStep:
         marks, self.phase_marks = self.phase_marks, ([] if phase_marks else None)
         self._capturing = True
         try:
-            with torch.cuda.graph(self._graph):
+            # thread-local capture mode: the process group's watchdog thread keeps
+            # polling its events while this thread captures
+            with torch.cuda.graph(self._graph, capture_error_mode="thread_local"):
                 self._g_loss = self.forward_backward(self._g_tokens, self._g_states,
                                                      _checked=True)
                 self._g_last = dict(self.last)
@@ -497,6 +502,11 @@ class DraftTrainStep:
         if update:
             self._update()
         return self._g_loss
+
+    def release(self) -> None:
+        """Drop the captured graph (and the collectives it holds)."""
+        self._graph = None
+        self.graph_marks = None
 
     def graph_phases(self) -> dict:
         """ms per phase of the last replay (phase_marks captured), summed by name."""
