@@ -780,6 +780,26 @@ def profile_case_fn(case: str, dev):
             xd = x.detach().requires_grad_(True)
             head.weight.grad = None
             head.cross_entropy(xd, tg).backward()
+    elif case in ("rosa_layer", "rosa_runs"):
+        # config-4 layer shape, 16 x 2048 positions x 512 streams: independent fair
+        # bits (rosa_layer; the chunked matcher keeps every stream) or bits that
+        # flip with probability 0.1 per position (rosa_runs; long runs as deep-layer
+        # projections give them, most streams handed to the sorted-key matcher)
+        from ksdraft_b200.model.rosa import match_words, pack_bits
+        B, T, S = 16, 2048, 512
+        if case == "rosa_layer":
+            bits = [(torch.rand(B, T, S, device=dev, generator=g) > 0.5).to(torch.int8)
+                    for _ in range(3)]
+        else:
+            bits = []
+            for _ in range(3):
+                flips = (torch.rand(B, T, S, device=dev, generator=g) < 0.1).to(torch.int32)
+                bits.append((torch.cumsum(flips, 1) & 1).to(torch.int8))
+        words = [pack_bits(b, B, T, S, T * S, S, 1) for b in bits]
+        del bits
+        out = torch.empty(B, T, S, dtype=torch.bfloat16, device=dev)
+        fn = lambda: match_words(*words, B, S, T, 62, out=out,  # noqa: E731
+                                 strides=(T * S, S, 1))
     elif case == "rosa_mixer":
         # config 3 end to end: RosaMixer(1536, 512) after to_int8 (Int8Linear q/k/v/out
         # projections N(0, 0.02)), evaluation forward on x = E[ids], E bf16 N(0, 1)

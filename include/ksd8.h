@@ -40,6 +40,12 @@
  *   ksd8_adamw_multi          the same over several tensors in one launch
  *   ksd8_grad_clip_coef       torch.nn.utils.clip_grad_norm_ norm and coefficient (:165)
  *   ksd8_fp16_tanh_table      the fp16 torch.tanh of ksdraft/kernels/ks3_int8.py:366-367 (parity probe)
+ *   ksd8_dspine_ln_fwd        ksdraft/model/spine.py:64-69 AdjacentInjection.forward (gate and
+ *                             injection combine around the low-rank GEMMs) followed by the
+ *                             block's ln_ffn (ksdraft/model/block.py:41)
+ *   ksd8_dspine_ln_bwd        the autograd backward of the same (LayerNorm, sigmoid gate)
+ *   ksd8_transfer_rows        ksdraft/train/__init__.py:80-84, the transfer-space term per token
+ *   ksd8_transfer_bwd         its gradient (the F.normalize backward) for a loss coefficient
  */
 #ifndef KSD8_H_
 #define KSD8_H_
@@ -283,6 +289,48 @@ int ksd8_grad_clip_coef(const float* grad, int64_t n, float max_norm, float* scr
  * fp16 value with bits i, i < n <= 0x7C00 (correctly rounded; the reference's
  * CPU torch.tanh on fp16, ksdraft/kernels/ks3_int8.py:366-367, gives the same). */
 int ksd8_fp16_tanh_table(int64_t n, uint16_t* out, void* stream);
+
+/* ---- DSpine injection + ln_ffn, transfer-space loss rows ----
+ *
+ * Row-major (M, d) tensors of dtype KSD8_F32 / KSD8_BF16 / KSD8_F16 (the
+ * activation dtype T), d a multiple of 128 and at most 2048, every pointer
+ * 16-byte aligned.  fp32 arithmetic inside; gate_bias, ln_w, ln_b are fp32
+ * masters, rounded to T first (a T-typed module's parameters). */
+
+/* h2 = T(h + sigmoid(zsum + gate_bias) * inj);  out = T(LayerNorm(h2) * ln_w + ln_b)
+ * (biased variance, eps), mean / rstd (M) fp32 saved for the backward.
+ * zsum = gate_q(h) + gate_p(p_prev) and inj = inject(p_prev) are the caller's
+ * low-rank GEMM outputs (spine.py:66-69). */
+int ksd8_dspine_ln_fwd(const void* h, const void* zsum, const void* inj, int dtype, int64_t m,
+                       int64_t d, const float* gate_bias, const float* ln_w, const float* ln_b,
+                       float eps, void* h2, void* out, float* mean, float* rstd, int* status,
+                       void* stream);
+
+/* Backward of ksd8_dspine_ln_fwd given db = dL/d(out) (T) and dres = the
+ * gradient reaching h2 directly (fp32, the block's residual):
+ *   dh2 = dres + LayerNorm backward of db (fp32),
+ *   dinj = T(dh2 g),  dz = T(dh2 inj g (1 - g)),  g = sigmoid(zsum + gate_bias);
+ * column sums into partials (n_parts, 3, d) fp32: [0] sum db * xhat (ln_w grad),
+ * [1] sum db (ln_b grad), [2] sum dz (gate_bias grad); the caller adds the
+ * n_parts rows (each covers ceil(M / n_parts) consecutive tokens). */
+int ksd8_dspine_ln_bwd(const void* h2, const float* mean, const float* rstd, const void* db,
+                       const float* dres, const void* zsum, const void* inj, int dtype, int64_t m,
+                       int64_t d, const float* gate_bias, const float* ln_w, float* dh2, void* dz,
+                       void* dinj, float* partials, int64_t n_parts, int* status, void* stream);
+
+/* Transfer-space rows: norm[t] = |p_t|, dot[t] = <p_t, e_t> and
+ * term[t] = 1 - dot[t] / max(norm[t], 1e-12), for p (M, d) of dtype T and the
+ * normalised next-token embeddings e (M, d) fp32. */
+int ksd8_transfer_rows(const void* p, int dtype, const float* e, int64_t m, int64_t d,
+                       float* norm, float* dot, float* term, int* status, void* stream);
+
+/* Gradient of coef * sum_t term[t]:  dp = T(coef * dterm/dp + pgrad + first[t / t_len]
+ * on the rows t % t_len == 0) and e_grad -= coef * p_t / max(|p_t|, 1e-12).
+ * pgrad (M, d) T and first (M / t_len, d) fp32 are optional addends (NULL). */
+int ksd8_transfer_bwd(const void* p, int dtype, const float* e, const float* norm,
+                      const float* dot, int64_t m, int64_t d, float coef, const void* pgrad,
+                      const float* first, int64_t t_len, void* dp, float* e_grad, int* status,
+                      void* stream);
 
 /* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);

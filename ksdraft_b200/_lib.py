@@ -60,6 +60,11 @@ SIGNATURES: dict[str, list] = {
     "ksd8_adamw_multi": [i32, vp, vp, i32, vp, vp, vp, f32, f32, f32, f32, f32, i32, vp, vp, vp],
     "ksd8_philox_uniform": [u64, u64, i64, vp, vp],
     "ksd8_fp16_tanh_table": [i64, vp, vp],
+    "ksd8_dspine_ln_fwd": [vp, vp, vp, i32, i64, i64, vp, vp, vp, f32, vp, vp, vp, vp, vp, vp],
+    "ksd8_dspine_ln_bwd": [vp, vp, vp, vp, vp, vp, vp, i32, i64, i64, vp, vp, vp, vp, vp, vp,
+                           i64, vp, vp],
+    "ksd8_transfer_rows": [vp, i32, vp, i64, i64, vp, vp, vp, vp, vp],
+    "ksd8_transfer_bwd": [vp, i32, vp, vp, vp, i64, i64, f32, vp, vp, i64, vp, vp, vp, vp],
     "ksd8_rosa_set_algorithm": [i32],
     "ksd8_set_sm_reserve": [i32],
     "ksd8_get_sm_reserve": [],

@@ -48,6 +48,17 @@ int ksd8_ce_grad_quant_launch(const void*, int, int64_t, int64_t, int64_t, const
 int ksd8_adamw_launch(float*, const void*, int, float*, float*, int64_t, float, float, float,
                       float, float, int, cudaStream_t, const float*);
 int ksd8_grad_clip_launch(const float*, int64_t, float, float*, float*, cudaStream_t);
+int ksd8_dspine_ln_fwd_launch(const void*, const void*, const void*, int, int64_t, int64_t,
+                              const float*, const float*, const float*, float, void*, void*,
+                              float*, float*, cudaStream_t);
+int ksd8_dspine_ln_bwd_launch(const void*, const float*, const float*, const void*, const float*,
+                              const void*, const void*, int, int64_t, int64_t, const float*,
+                              const float*, float*, void*, void*, float*, int64_t, cudaStream_t);
+int ksd8_transfer_rows_launch(const void*, int, const float*, int64_t, int64_t, float*, float*,
+                              float*, cudaStream_t);
+int ksd8_transfer_bwd_launch(const void*, int, const float*, const float*, const float*, int64_t,
+                             int64_t, float, const void*, const float*, int64_t, void*, float*,
+                             cudaStream_t);
 int ksd8_adamw_multi_launch(int, float* const*, const void* const*, int, float* const*,
                             float* const*, const int64_t*, float, float, float, float, float,
                             int, const float*, cudaStream_t);
@@ -527,4 +538,73 @@ extern "C" int ksd8_ks3_vjp_static(const void* value, const void* coords, int64_
   return finish(ksd8_ks3_vjp_reduce_launch(partials, n_tiles, charts, raw_scale, raw_shift,
                                            dcoeff16, dscale16, dshift16, status, S(stream),
                                            nullptr, nullptr, nullptr));
+}
+
+// ---- DSpine injection + ln_ffn, transfer-space loss rows ----
+
+static bool dspine_width_ok(int64_t d) { return d > 0 && d % 128 == 0 && d <= 2048; }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int ksd8_dspine_ln_fwd(const void* h, const void* zsum, const void* inj, int dtype, int64_t m,
+                       int64_t d, const float* gate_bias, const float* ln_w, const float* ln_b,
+                       float eps, void* h2, void* out, float* mean, float* rstd, int* status,
+                       void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  if (m < 0 || !dspine_width_ok(d)) return KSD8_ERR_SHAPE;
+  if (!(eps > 0.f)) return KSD8_ERR_ARG;
+  if (m > 0 && (!h || !zsum || !inj || !gate_bias || !ln_w || !ln_b || !h2 || !out || !mean ||
+                !rstd))
+    return KSD8_ERR_ARG;
+  if (m > 0 && !(aligned16(h) && aligned16(zsum) && aligned16(inj) && aligned16(h2) &&
+                 aligned16(out) && aligned16(gate_bias) && aligned16(ln_w) && aligned16(ln_b)))
+    return KSD8_ERR_ALIGN;
+  return finish(ksd8_dspine_ln_fwd_launch(h, zsum, inj, dtype, m, d, gate_bias, ln_w, ln_b, eps,
+                                          h2, out, mean, rstd, S(stream)));
+}
+
+int ksd8_dspine_ln_bwd(const void* h2, const float* mean, const float* rstd, const void* db,
+                       const float* dres, const void* zsum, const void* inj, int dtype, int64_t m,
+                       int64_t d, const float* gate_bias, const float* ln_w, float* dh2, void* dz,
+                       void* dinj, float* partials, int64_t n_parts, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  if (m < 0 || !dspine_width_ok(d)) return KSD8_ERR_SHAPE;
+  if (n_parts <= 0 || n_parts > INT32_MAX || !partials || !gate_bias || !ln_w) return KSD8_ERR_ARG;
+  if (m > 0 && (!h2 || !mean || !rstd || !db || !dres || !zsum || !inj || !dh2 || !dz || !dinj))
+    return KSD8_ERR_ARG;
+  if (m > 0 && !(aligned16(h2) && aligned16(db) && aligned16(dres) && aligned16(zsum) &&
+                 aligned16(inj) && aligned16(dh2) && aligned16(dz) && aligned16(dinj) &&
+                 aligned16(partials) && aligned16(gate_bias) && aligned16(ln_w)))
+    return KSD8_ERR_ALIGN;
+  return finish(ksd8_dspine_ln_bwd_launch(h2, mean, rstd, db, dres, zsum, inj, dtype, m, d,
+                                          gate_bias, ln_w, dh2, dz, dinj, partials, n_parts,
+                                          S(stream)));
+}
+
+int ksd8_transfer_rows(const void* p, int dtype, const float* e, int64_t m, int64_t d,
+                       float* norm, float* dot, float* term, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  if (m < 0 || !dspine_width_ok(d)) return KSD8_ERR_SHAPE;
+  if (m > 0 && (!p || !e || !norm || !dot || !term)) return KSD8_ERR_ARG;
+  if (m > 0 && !(aligned16(p) && aligned16(e))) return KSD8_ERR_ALIGN;
+  return finish(ksd8_transfer_rows_launch(p, dtype, e, m, d, norm, dot, term, S(stream)));
+}
+
+int ksd8_transfer_bwd(const void* p, int dtype, const float* e, const float* norm,
+                      const float* dot, int64_t m, int64_t d, float coef, const void* pgrad,
+                      const float* first, int64_t t_len, void* dp, float* e_grad, int* status,
+                      void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  if (m < 0 || !dspine_width_ok(d)) return KSD8_ERR_SHAPE;
+  if (first && (t_len <= 0 || m % t_len != 0)) return KSD8_ERR_SHAPE;
+  if (m > 0 && (!p || !e || !norm || !dot || !dp || !e_grad)) return KSD8_ERR_ARG;
+  if (m > 0 && !(aligned16(p) && aligned16(e) && aligned16(dp) && aligned16(e_grad) &&
+                 (!pgrad || aligned16(pgrad)) && (!first || aligned16(first))))
+    return KSD8_ERR_ALIGN;
+  return finish(ksd8_transfer_bwd_launch(p, dtype, e, norm, dot, m, d, coef, pgrad, first,
+                                         first ? t_len : 1, dp, e_grad, S(stream)));
 }

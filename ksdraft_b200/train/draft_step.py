@@ -21,9 +21,12 @@ What runs where:
     reference's scale gradient), the KS3 cells (the all-INT8 forward and
     backward), the tied LM head (W8A8 logits, CE partials, the fused CE
     gradient quantiser and W8A8 dgrad / wgrad), AdamW and gradient clipping.
-  * The float exceptions of the reference's int8 tier stay torch
-    (int8_convert.py:8-12): LayerNorms and the DSpine low-rank injection run
-    as small autograd segments in the activation dtype.
+  * The float exceptions of the reference's int8 tier (int8_convert.py:8-12)
+    run in the activation dtype: the DSpine low-rank injection as five cuBLAS
+    GEMMs around one ksd8 kernel that applies the gate and ln_ffn (and one for
+    their backward, train/injection.py), the transfer-space term and its
+    gradient as ksd8 row kernels; input_norm and output_norm are torch
+    LayerNorm segments.
   * Gradients follow the reference's hard-symbol boundary (rosa.py:21-29): the
     Rosa q/k/v projections, their time mixes and ln_attn receive no gradient,
     so AdamW leaves them untouched, as torch.optim.AdamW skips parameters
@@ -55,6 +58,7 @@ from ..kernels.linear import ste_input_grad
 from ..kernels.quant import GROUP_SIZE, dequantize_last_dim, quantize_cols, quantize_last_dim
 from ..model.head import ce_grad, ce_grad_quant, ce_partials, combine_ce_partials
 from ..model.rosa import _default_max_len, match_words, pack_bits
+from . import injection
 from .dp import SM_RESERVE, allreduce_mean_async, wait_all
 
 
@@ -204,25 +208,6 @@ def init_draft_params(shape: DraftShape, device, seed: int = 0, std: float = 0.0
     return flat, frozen
 
 
-def _shift_tokens(t: torch.Tensor) -> torch.Tensor:
-    """(B, T, d) -> the previous position's vector, zeros at t = 0 (F.pad(..)[:, :-1])."""
-    return F.pad(t, (0, 0, 1, 0))[:, :-1, :]
-
-
-def _dspine(h, p_first, W, act):
-    """AdjacentInjection (spine.py:56-58) on (B, T, d): returns (h + gate * inject(p_prev), p).
-    W holds the fp32 masters; the low-rank GEMMs run in the activation dtype."""
-    W = {k: v.to(act) for k, v in W.items()}
-    p = F.linear(F.linear(h, W["feature_down"]), W["feature_up"])
-    p_prev = _shift_tokens(p)
-    if p_first is not None:
-        p_prev = torch.cat([p_first, p_prev[:, 1:, :]], dim=1)
-    gate = torch.sigmoid(F.linear(F.linear(h, W["gate_q.down"]), W["gate_q.up"])
-                         + F.linear(F.linear(p_prev, W["gate_p.down"]), W["gate_p.up"])
-                         + W["gate_bias"])
-    return h + gate * F.linear(F.linear(p_prev, W["inject.down"]), W["inject.up"]), p
-
-
 class _ste_matmul_precision:
     """The straight-through backward GEMMs of Int8Linear (linear.py:88-94) are fp32
     in the reference.  With bf16 activations (whose values TF32 holds exactly)
@@ -287,6 +272,7 @@ class DraftTrainStep:
                  lr: float = 3e-4, weight_decay: float = 0.01, grad_clip: float | None = 1.0,
                  transfer_weight: float = 0.5, group=None, params=None,
                  head_mode: str = "w8a8"):
+        injection.check_width(shape.d_model)
         self.shape = shape
         self.dev = torch.device(device)
         self.act = act_dtype
@@ -429,14 +415,8 @@ class DraftTrainStep:
         # o = (payload * sign).to(act): d payload[s] = sum over tokens of do * sign
         torch.sum(do * sign.reshape(B * T, S).float(), 0, out=self.flat.g(pre + "payload"))
 
-    def _dspine_weights(self, layer: int, leaf: bool):
-        W = {}
-        for n in DSPINE:
-            t = self.flat.p(f"blocks.{layer}.{_dspine_name(n)}")
-            if leaf:
-                t = t.detach().requires_grad_(True)
-            W[n] = t
-        return W
+    def _dspine_weights(self, layer: int):
+        return {n: self.flat.p(f"blocks.{layer}.{_dspine_name(n)}") for n in DSPINE}
 
     # ---- the step --------------------------------------------------------------
 
@@ -584,32 +564,28 @@ class DraftTrainStep:
             x = x + gemm_out(tqp, tsc, wqp, ws, out_dtype=act)      # Int8Linear fwd
             ts_saved = (tq, tsc)
 
-        # ---- blocks
+        # ---- blocks: Rosa, DSpine injection + ln_ffn, KS3 (block.py:34-42)
         saved = []
-        p_prev_first = None
+        p_first = None
         t_norm = F.normalize(E.index_select(0, tids).float(), dim=-1)   # transfer targets
         ts_terms = []
         for layer in range(s.layers):
+            pre = f"blocks.{layer}."
             self._mark("rosa_fwd")
             r, rosa_saved = self._rosa_forward(layer, x.view(B, T, d))
             self._mark("dspine_ln_fwd")
-            h = (x + r).view(B, T, d)
-            W = self._dspine_weights(layer, leaf=True)
-            h_leaf = h.detach().requires_grad_(True)
-            pf_leaf = None if p_prev_first is None else p_prev_first.detach().requires_grad_(True)
-            with torch.enable_grad():
-                h2, p = _dspine(h_leaf, pf_leaf, W, act)
-                h2d = h2.detach().requires_grad_(True)
-                b = self._ln(h2d, f"blocks.{layer}.ln_ffn")
-            cell = self.cells[layer]
+            iw = injection.InjectionWeights(self._dspine_weights(layer), act)
+            b, h2, p, inj_saved = injection.forward(
+                x + r, p_first, iw, self.flat.p(pre + "ln_ffn.weight"),
+                self.flat.p(pre + "ln_ffn.bias"), B, T)
+            term, rows = injection.transfer_rows(p, t_norm)
+            ts_terms.append(term.mean())
             self._mark("ks3_fwd")
-            k, ks3_saved = ks3_train_forward(cell, b.detach().reshape(M, d))
-            x = (h2d.detach().reshape(M, d) + k)
-            with torch.no_grad():
-                fn = F.normalize(p.detach().float().reshape(M, d), dim=-1)
-                ts_terms.append((1.0 - (fn * t_norm).sum(-1)).mean())
-            saved.append((rosa_saved, W, h_leaf, pf_leaf, h2, p, h2d, b, ks3_saved))
-            p_prev_first = p[:, :1, :]
+            k, ks3_saved = ks3_train_forward(self.cells[layer], b)
+            del b
+            x = h2 + k
+            saved.append((rosa_saved, inj_saved, rows, ks3_saved))
+            p_first = p.view(B, T, d)[:, 0]
 
         # ---- head + loss (draft.py:82, train/__init__.py:77-94)
         self._mark("head_fwd")
@@ -660,8 +636,10 @@ class DraftTrainStep:
         coef = self.transfer_weight / max(1, s.layers) / M
         dt_norm = torch.zeros(M, d, dtype=torch.float32, device=self.dev)
         dp_next_first = None
+        n_parts = max(1, min(M, 4 * torch.cuda.get_device_properties(self.dev)
+                                 .multi_processor_count))
         for layer in reversed(range(s.layers)):
-            (rosa_saved, W, h_leaf, pf_leaf, h2, p, h2d, b, ks3_saved) = saved[layer]
+            (rosa_saved, inj_saved, rows, ks3_saved) = saved[layer]
             pre = f"blocks.{layer}."
             cell = self.cells[layer]
             views = {n: self.flat.g(pre + KS3_MASTERS[n]).view_as(getattr(cell, "master_" + n))
@@ -669,25 +647,13 @@ class DraftTrainStep:
             self._mark("ks3_bwd")
             db = ks3_backward(cell, dx.to(act), *ks3_saved, (M, d), grads_into=views)
             self._mark("dspine_ln_bwd")
-            with torch.enable_grad():
-                b.backward(db.reshape(b.shape))
-            self._ln_param_grads(f"{pre}ln_ffn")
-            dh2 = dx.view(B, T, d) + h2d.grad.float()
-            # transfer-space loss gradient of this block's p (and of its targets)
-            with torch.no_grad():
-                u = p.detach().float().reshape(M, d)
-                fn = F.normalize(u, dim=-1)
-                dp = _normalize_bwd(u, -coef * t_norm)
-                dt_norm -= coef * fn
-                dp = dp.view(B, T, d)
-                if dp_next_first is not None:
-                    dp[:, :1, :] += dp_next_first.float()
-            with torch.enable_grad():
-                torch.autograd.backward([h2, p], [dh2.to(act), dp.to(act)])
-            for n, t in W.items():
-                self.flat.g(pre + _dspine_name(n)).copy_(t.grad)
-            dp_next_first = pf_leaf.grad if pf_leaf is not None else None
-            dh = h_leaf.grad.reshape(M, d).float()
+            grads = {n: self.flat.g(pre + _dspine_name(n)) for n in DSPINE}
+            grads["ln_w"] = self.flat.g(pre + "ln_ffn.weight")
+            grads["ln_b"] = self.flat.g(pre + "ln_ffn.bias")
+            # injection + ln_ffn backward, with this block's transfer-space term
+            dh, dp_next_first = injection.backward(
+                inj_saved, db.reshape(M, d), dx, B, T, t_norm, dt_norm, rows, coef,
+                dp_next_first, grads, n_parts)
             self._mark("rosa_bwd")
             self._rosa_backward(layer, dh, rosa_saved)
             reduce_span(self.flat.block_grad_span(layer))
