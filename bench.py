@@ -46,6 +46,7 @@ sys.path.insert(0, str(ROOT))
 
 D_MODEL, CHARTS, TOKENS, BATCH, SEQ = 1536, 5888, 4096, 8, 512
 C4_BATCH, C4_SEQ, C4_TEACHER = 16, 2048, 384
+C5_CONTEXTS, C5_CONTEXT_LEN, C5_BLOCK, C5_TOPK = 64, 8192, 8, 8
 REF_C4_TOKENS = int(os.environ.get("KSD8_REF_TOKENS", "128"))
 METRIC = "W8A8 GS128 GEMM TOPS; KSDraft INT8 train tokens/sec at 1/2/4/8 B200"
 DITHER = 0.5
@@ -268,6 +269,11 @@ def cpu_baseline(workload: str = "config2") -> dict:
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload == "config5":
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "the reference has no incremental decode or proposal API (only "
+                          "whole-sequence forwards, ksdraft/model/draft.py:58-82)"}), flush=True)
         return
     m = cpu_measure(steps=max(1, args.steps), warmup=max(1, min(args.warmup, 1)),
                     budget_s=REF_BUDGET_S, workload=args.workload)
@@ -541,9 +547,9 @@ def run_config4(args) -> None:
     from ksdraft_b200 import _lib
     from ksdraft_b200.kernels.gemm import GemmTimer
     from ksdraft_b200.train.dp import init_distributed
-    from ksdraft_b200.train.draft_step import DraftShape, DraftTrainStep
+    from ksdraft_b200.train.draft_step import DRAFT_SM_RESERVE, DraftShape, DraftTrainStep
 
-    rank, world, local = init_distributed(timeout_s=600)
+    rank, world, local = init_distributed(timeout_s=600, nccl_max_ctas=DRAFT_SM_RESERVE)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     strong = args.per_gpu_batch is None
@@ -674,6 +680,138 @@ def run_config4(args) -> None:
             line["side"] = side_measurements(dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline("config4")
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def config5(n: int) -> dict:
+    return {"workload": "BASELINE config 5: KSDraft INT8 draft serving, 64 concurrent contexts "
+                        "of 8192 Zipf(1.1) tokens with bf16 N(0,1) teacher states, blocks of 8 "
+                        "appended positions per context per step through 24 layers at "
+                        "d_model=1536, top-8 candidates from the W8A8 GS128 LM head (vocab "
+                        "150144) sharded by vocab over the GPUs",
+            "model": "KSDraft 24 x (Rosa + DSpine + KS3) d_model=1536 vocab=150144",
+            "contexts": C5_CONTEXTS, "context_len": C5_CONTEXT_LEN, "block": C5_BLOCK,
+            "topk": C5_TOPK, "tokens_per_step": C5_CONTEXTS * C5_BLOCK,
+            "contexts_per_gpu": C5_CONTEXTS // n,
+            "parallelism": f"contexts split over {n} GPU(s), head sharded by vocab",
+            "activations": "bf16", "l2": "step working set (decode state, weights) > L2"}
+
+
+def run_config5(args) -> None:
+    """BASELINE config 5 on N GPUs: prefill the contexts (untimed), then time
+    `steps` propose() calls of one 8-position block per context."""
+    import torch
+    import torch.distributed as dist
+
+    from ksdraft_b200 import _lib
+    from ksdraft_b200.kernels.gemm import GemmTimer
+    from ksdraft_b200.model.drafter import KSDraftDrafter
+    from ksdraft_b200.train.dp import init_distributed
+    from ksdraft_b200.train.draft_step import DraftShape, init_draft_params
+
+    rank, world, local = init_distributed(timeout_s=600)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if C5_CONTEXTS % world:
+        raise SystemExit(f"{C5_CONTEXTS} contexts do not split over {world} GPUs")
+    shape = DraftShape()
+    flat, frozen = init_draft_params(shape, dev, seed=1234)   # same weights on every rank
+    state = {n: flat.p(n) for n in flat.names}
+    state.update(frozen)
+    group = dist.group.WORLD if world > 1 else None
+    n_steps = args.warmup + 2 * args.steps
+    cap = C5_CONTEXT_LEN + n_steps * C5_BLOCK
+    drafter = KSDraftDrafter(state, shape, dev, contexts=C5_CONTEXTS, capacity=cap,
+                             group=group)
+    del flat, frozen, state
+    torch.cuda.empty_cache()
+    T = cap
+    ids = torch.from_numpy(rosa_ids(C5_CONTEXTS, T, seed=5))
+    gen = torch.Generator().manual_seed(55)
+    # teacher states of every position, generated in context blocks (bf16 N(0, 1))
+    states = torch.empty(C5_CONTEXTS, T, C4_TEACHER, dtype=torch.bfloat16)
+    for c in range(C5_CONTEXTS):
+        states[c] = torch.randn(T, C4_TEACHER, generator=gen).to(torch.bfloat16)
+    ids_pin, states_pin = ids.pin_memory(), states.pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    t_pre = time.perf_counter()
+    drafter.prefill(ids[:, :C5_CONTEXT_LEN], states[:, :C5_CONTEXT_LEN], topk=C5_TOPK)
+    barrier()
+    prefill_s = time.perf_counter() - t_pre
+    pos = C5_CONTEXT_LEN
+
+    def block(p, host=False):
+        sl = slice(p, p + C5_BLOCK)
+        if host:
+            return states_pin[:, sl], ids_pin[:, sl]
+        return states_dev[:, sl], ids_dev[:, sl]
+
+    # device-resident inputs of the timed device-side steps
+    ids_dev = ids.to(dev)
+    states_dev = states.to(dev)
+    for _ in range(args.warmup):
+        drafter.propose(*block(pos), topk=C5_TOPK)
+        pos += C5_BLOCK
+    barrier()
+    times, gemm = [], []
+    launches0 = _lib.LAUNCHES
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            gt = GemmTimer().__enter__()
+            s.record()
+            drafter.propose(*block(pos), topk=C5_TOPK)
+            e.record()
+            torch.cuda.synchronize()
+            gt.__exit__()
+            gemm += gt.durations_ms()
+            times.append(s.elapsed_time(e))
+            pos += C5_BLOCK
+    launches = (_lib.LAUNCHES - launches0) // max(1, args.steps)
+    total = torch.tensor([sum(times)], device=dev)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    total_ms = float(total.item())
+    # end to end: host ids and teacher states in, the candidate ids back to the host
+    out_host = torch.empty(C5_CONTEXTS, C5_BLOCK, C5_TOPK, dtype=torch.int64).pin_memory()
+    e2e = []
+    for _ in range(args.steps):
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        cand, _, _ = drafter.propose(*block(pos, host=True), topk=C5_TOPK)
+        out_host.copy_(cand, non_blocking=True)
+        e.record()
+        torch.cuda.synchronize()
+        e2e.append(s.elapsed_time(e))
+        pos += C5_BLOCK
+    e2e_t = torch.tensor([sum(e2e)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    tok = C5_CONTEXTS * C5_BLOCK * args.steps
+    if rank == 0:
+        roof, ginfo = _roofline_from_gemms(gemm, load_peaks())
+        line = {
+            "metric": METRIC, "value": tok / (total_ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": config5(world), "roofline": roof, "gemm": ginfo,
+            "e2e": {"value": tok / (float(e2e_t.item()) / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": C5_CONTEXTS * C5_BLOCK * (8 + C4_TEACHER * 2),
+                    "d2h_bytes_per_step": C5_CONTEXTS * C5_BLOCK * C5_TOPK * 8},
+            "gpu_launches": launches, "prefill_s": prefill_s,
+            "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -913,7 +1051,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("config4", "config2"), default="config4")
+    ap.add_argument("--workload", choices=("config4", "config2", "config5"), default="config4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--per-gpu-batch", type=int, default=None,
                     help="config4: this many sequences on every rank (weak scaling) "
@@ -936,6 +1074,8 @@ def main() -> None:
         run_reference(args)
     elif args.workload == "config4":
         run_config4(args)
+    elif args.workload == "config5":
+        run_config5(args)
     else:
         run_ours(args)
 

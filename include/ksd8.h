@@ -46,6 +46,10 @@
  *   ksd8_dspine_ln_bwd        the autograd backward of the same (LayerNorm, sigmoid gate)
  *   ksd8_transfer_rows        ksdraft/train/__init__.py:80-84, the transfer-space term per token
  *   ksd8_transfer_bwd         its gradient (the F.normalize backward) for a loss coefficient
+ *   ksd8_rosa_decode_build    no reference counterpart: the sorted key run behind
+ *                             ksd8_rosa_decode_step, built from a context's k bits
+ *   ksd8_rosa_decode_step     ksdraft/model/rosa.py:40-98 _match_payload_sign (+ :164 payload)
+ *                             answered for positions appended to a matched context
  */
 #ifndef KSD8_H_
 #define KSD8_H_
@@ -331,6 +335,45 @@ int ksd8_transfer_bwd(const void* p, int dtype, const float* e, const float* nor
                       const float* dot, int64_t m, int64_t d, float coef, const void* pgrad,
                       const float* first, int64_t t_len, void* dp, float* e_grad, int* status,
                       void* stream);
+
+/* ---- incremental Rosa matching (drafting) ----
+ *
+ * State of one (context, stream) row, all caller-allocated device memory:
+ *   q / k / v bit histories, (contexts * streams, nw) uint64, bit t of row r in
+ *   word t / 64 at bit t % 64 (the ksd8_rosa_pack_bits layout), zero beyond the
+ *   positions written;
+ *   the main run: sw (rows, cap) uint64 sorted key windows, sj (rows, cap)
+ *   uint16 their positions, blk (rows, cap / 64) uint16 max(position + 1) per
+ *   64 ranks; cap a multiple of 64.
+ * Keys 0 .. n_main - 1 are the matched context (main run = keys
+ * max_len - 1 .. n_main - 1; the earlier ones are compared directly), keys
+ * n_main .. t - 1 the delta since the last build, also compared directly.
+ * Results equal ksd8_rosa_match on the whole sequence when the sequence has at
+ * least max_len + 1 positions (the reference's cap min(62, T - 1) is then
+ * max_len = 62). */
+
+/* Sort the keys max_len - 1 .. n_keys - 1 of every row of kw into (sw, sj, blk);
+ * n_keys <= cap, smem-limited to n_keys - max_len + 1 <= 16384 keys. */
+int ksd8_rosa_decode_build(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_keys,
+                           int max_len, uint64_t* sw, uint16_t* sj, uint16_t* blk, int64_t cap,
+                           int* status, void* stream);
+
+/* Append k_new (1..32) positions t0 .. t0 + k_new - 1 to every row (bits =
+ * proj > 0 of the projections (contexts, k_new, streams), dtype F32 / BF16 /
+ * F16; positions >= t0 are overwritten, so t0 may also roll back to any
+ * length >= n_main; all three proj NULL: the bits are already in the
+ * histories) and write, for new position i, payload[s] * sign to
+ * out[c * out_cs + i * streams + s] and optionally the match length / latest
+ * endpoint to match_len / match_end[row * ml_rs + i] int32.  Returns
+ * KSD8_ERR_UNSUPPORTED when the delta n_main .. t0 + k_new - 2 outgrows the
+ * kernel's 34-word window (about 2000 keys): rebuild with n_keys = t0 first. */
+int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* proj_v, int dtype,
+                          int64_t contexts, int64_t streams, int64_t k_new, int64_t t0,
+                          int64_t n_main, int max_len, uint64_t* qw, uint64_t* kw, uint64_t* vw,
+                          int64_t nw, const uint64_t* sw, const uint16_t* sj,
+                          const uint16_t* blk, int64_t cap, const float* payload, void* out,
+                          int64_t out_cs, int out_dtype, int32_t* match_len, int32_t* match_end,
+                          int64_t ml_rs, int* status, void* stream);
 
 /* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);

@@ -56,6 +56,13 @@ int ksd8_dspine_ln_bwd_launch(const void*, const float*, const float*, const voi
                               const float*, float*, void*, void*, float*, int64_t, cudaStream_t);
 int ksd8_transfer_rows_launch(const void*, int, const float*, int64_t, int64_t, float*, float*,
                               float*, cudaStream_t);
+int ksd8_rosa_decode_build_launch(const uint64_t*, int64_t, int64_t, int64_t, int, uint64_t*,
+                                  uint16_t*, uint16_t*, int64_t, cudaStream_t);
+int ksd8_rosa_decode_step_launch(const void* const*, int, int64_t, int64_t, int64_t, int64_t,
+                                 int64_t, int, uint64_t* const*, int64_t, const uint64_t*,
+                                 const uint16_t*, const uint16_t*, int64_t, const float*, void*,
+                                 int64_t, int, int32_t*, int32_t*, int64_t, cudaStream_t);
+int ksd8_rosa_decode_limits(int64_t*, int64_t*, int64_t*);
 int ksd8_transfer_bwd_launch(const void*, int, const float*, const float*, const float*, int64_t,
                              int64_t, float, const void*, const float*, int64_t, void*, float*,
                              cudaStream_t);
@@ -607,4 +614,55 @@ int ksd8_transfer_bwd(const void* p, int dtype, const float* e, const float* nor
     return KSD8_ERR_ALIGN;
   return finish(ksd8_transfer_bwd_launch(p, dtype, e, norm, dot, m, d, coef, pgrad, first,
                                          first ? t_len : 1, dp, e_grad, S(stream)));
+}
+
+// ---- incremental Rosa matching (drafting) ----
+
+int ksd8_rosa_decode_build(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_keys,
+                           int max_len, uint64_t* sw, uint16_t* sj, uint16_t* blk, int64_t cap,
+                           int* status, void* stream) {
+  (void)status;
+  if (n_streams < 0 || nw < 0 || n_keys < 0 || cap <= 0 || cap % 64 != 0) return KSD8_ERR_SHAPE;
+  if (max_len < 1 || max_len > 64) return KSD8_ERR_ARG;
+  if (n_keys > nw * 64 || n_keys > cap || cap > 65536) return KSD8_ERR_SHAPE;
+  if (n_streams > 0 && (!kw || !sw || !sj || !blk)) return KSD8_ERR_ARG;
+  return finish(ksd8_rosa_decode_build_launch(kw, n_streams, nw, n_keys, max_len, sw, sj, blk,
+                                              cap, S(stream)));
+}
+
+int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* proj_v, int dtype,
+                          int64_t contexts, int64_t streams, int64_t k_new, int64_t t0,
+                          int64_t n_main, int max_len, uint64_t* qw, uint64_t* kw, uint64_t* vw,
+                          int64_t nw, const uint64_t* sw, const uint16_t* sj,
+                          const uint16_t* blk, int64_t cap, const float* payload, void* out,
+                          int64_t out_cs, int out_dtype, int32_t* match_len, int32_t* match_end,
+                          int64_t ml_rs, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype) || !valid_float_dtype(out_dtype)) return KSD8_ERR_DTYPE;
+  if (out_cs < k_new * streams || ((match_len || match_end) && ml_rs < k_new))
+    return KSD8_ERR_SHAPE;
+  int64_t max_new = 0, max_main = 0, max_dwords = 0;
+  ksd8_rosa_decode_limits(&max_new, &max_main, &max_dwords);
+  if (contexts < 0 || streams < 0 || k_new < 1 || k_new > max_new || t0 < 0 || n_main < 0 ||
+      n_main > t0 || cap <= 0 || cap % 64 != 0 || nw <= 0)
+    return KSD8_ERR_SHAPE;
+  if (max_len < 1 || max_len > 64) return KSD8_ERR_ARG;
+  if (t0 + k_new > nw * 64 || t0 + k_new > 65536 || cap > 65536) return KSD8_ERR_SHAPE;
+  const int64_t r0 = max_len - 1;
+  if (n_main - r0 > max_main || n_main > cap) return KSD8_ERR_UNSUPPORTED;
+  const int64_t dlo = n_main > r0 ? n_main : r0, dhi = t0 + k_new - 2;
+  if (dhi >= dlo) {
+    const int64_t w0 = dlo > 63 ? (dlo >> 6) - 1 : 0;
+    if ((dhi >> 6) - w0 + 1 > max_dwords) return KSD8_ERR_UNSUPPORTED;  // rebuild first
+  }
+  if ((proj_q == nullptr) != (proj_k == nullptr) || (proj_q == nullptr) != (proj_v == nullptr))
+    return KSD8_ERR_ARG;
+  if (contexts * streams > 0 && (!qw || !kw || !vw || !sw || !sj || !blk || !out))
+    return KSD8_ERR_ARG;
+  const void* proj[3] = {proj_q, proj_k, proj_v};
+  uint64_t* bits[3] = {qw, kw, vw};
+  return finish(ksd8_rosa_decode_step_launch(proj, dtype, contexts, streams, k_new, t0, n_main,
+                                             max_len, bits, nw, sw, sj, blk, cap, payload, out,
+                                             out_cs, out_dtype, match_len, match_end, ml_rs,
+                                             S(stream)));
 }

@@ -1,0 +1,368 @@
+"""Drafting with a KSDraft model on the INT8 tier.
+
+The reference describes a proposal API on the draft model,
+`propose(target_states, tokens, block_len, topk) -> candidates, logits, refined`
+(RESEARCH.md section B), but only implements whole-sequence forwards
+(KSDraftModel.forward, ksdraft/model/draft.py:58-82, with the int8 tier of
+ksdraft/model/int8_convert.py).  KSDraftDrafter keeps per-context state so
+that appending a block of positions costs only those positions:
+
+  prefill(tokens, teacher_states)   whole-context forward (C contexts x T0
+                                    positions), then the per-layer caches
+  propose(target_states, tokens, k) append a block (C x n positions, the
+                                    parallel draft block) and return the top-k
+                                    next-token candidates and logits at each
+                                    appended position
+
+The forward is the int8 tier's: Int8Linear W8A8 for the Rosa q/k/v/out and
+teacher projections, the all-INT8 KS3 cells, the DSpine injection and
+LayerNorms as float exceptions in the activation dtype, and the tied LM head
+W8A8 (the north star's vocab-sharded head).  What each appended position sees
+equals the whole-sequence forward of the extended context:
+
+  * Rosa time-shift mix: the previous position's ln_attn output is cached per
+    layer (rosa.py:128-133);
+  * Rosa matching: ksd8_rosa_decode_step answers the new positions against
+    every earlier key (bit histories plus a sorted run of the context's keys,
+    rebuilt when the appended delta outgrows the step kernel's window);
+  * DSpine: the previous position's predicted feature p is cached per layer
+    (spine.py:64-66); position 0 of a prefill takes the previous layer's
+    feature as in KSDraftModel.forward;
+  * everything else is per position.
+
+Data parallel serving: with a process group the contexts are split over the
+ranks for the 24 layers, the final hidden states are all-gathered, and every
+rank scores all rows against its vocabulary shard (VocabParallelHead); the
+per-shard top-k are merged by one all-gather.
+"""
+
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .. import _lib
+from ..kernels.gemm import _validate_and_pad, gemm_out
+from ..kernels.ks3_int8 import KS3Int8Cell, ks3_weights
+from ..kernels.quant import GROUP_SIZE, quantize_last_dim
+from ..train import injection
+from .head import VocabParallelHead
+from .rosa import pack_bits
+
+MAX_LEN = 62            # the reference's cap min(62, T - 1) once T >= 63
+DELTA_WORDS = 34        # k words of the appended delta the step kernel holds
+LN_EPS = 1e-5
+
+
+class RosaDecodeState:
+    """One layer's matcher state for `rows` = contexts x streams (row = c * S + s):
+    q / k / v bit histories and the sorted key run of the matched context."""
+
+    def __init__(self, contexts: int, streams: int, capacity: int, device):
+        if capacity % 64:
+            raise ValueError("capacity must be a multiple of 64 positions")
+        self.contexts, self.streams, self.capacity = contexts, streams, capacity
+        rows = contexts * streams
+        self.nw = capacity // 64
+        self.bits = [torch.zeros(rows, self.nw, dtype=torch.int64, device=device)
+                     for _ in range(3)]
+        self.sw = torch.empty(rows, capacity, dtype=torch.int64, device=device)
+        self.sj = torch.empty(rows, capacity, dtype=torch.int16, device=device)
+        self.blk = torch.zeros(rows, capacity // 64, dtype=torch.int16, device=device)
+        self.n_main = 0
+
+    def load_words(self, words, t_len: int) -> None:
+        """Bit histories from packed words (rows, ceil(t_len / 64)) of a whole context."""
+        if t_len > self.capacity:
+            raise ValueError(f"context of {t_len} positions exceeds capacity {self.capacity}")
+        for dst, src in zip(self.bits, words):
+            dst.zero_()
+            dst[:, :src.shape[1]].copy_(src)
+
+    def build(self, n_keys: int) -> None:
+        """Sort the keys of positions max_len - 1 .. n_keys - 1 into the main run."""
+        rows = self.contexts * self.streams
+        _lib.check(_lib.lib().ksd8_rosa_decode_build(
+            self.bits[1].data_ptr(), rows, self.nw, n_keys, MAX_LEN, self.sw.data_ptr(),
+            self.sj.data_ptr(), self.blk.data_ptr(), self.capacity, None,
+            _lib.stream_ptr(self.sw.device)), "rosa_decode_build")
+        self.n_main = n_keys
+
+    def needs_build(self, t0: int, k_new: int) -> bool:
+        """True when the delta keys of a step at t0 would not fit the step kernel."""
+        dlo = max(self.n_main, MAX_LEN - 1)
+        dhi = t0 + k_new - 2
+        if dhi < dlo:
+            return False
+        w0 = (dlo >> 6) - 1 if dlo > 63 else 0
+        return (dhi >> 6) - w0 + 1 > DELTA_WORDS
+
+    def _step(self, projs, t0: int, k_new: int, pay, out, out_cs: int, out_dt: int, ml, me,
+              ml_rs: int):
+        if self.needs_build(t0, k_new):
+            self.build(t0)
+        if t0 + k_new > self.capacity:
+            raise ValueError("decode state capacity exhausted")
+        C, S = self.contexts, self.streams
+        ptrs = (None, None, None) if projs is None else tuple(p.data_ptr() for p in projs)
+        dt = _lib.dtype_code(projs[0]) if projs is not None else 0
+        _lib.check(_lib.lib().ksd8_rosa_decode_step(
+            *ptrs, dt, C, S, k_new, t0, self.n_main, MAX_LEN,
+            *(b.data_ptr() for b in self.bits), self.nw, self.sw.data_ptr(), self.sj.data_ptr(),
+            self.blk.data_ptr(), self.capacity, pay.data_ptr(), out, out_cs, out_dt, ml, me,
+            ml_rs, None,
+            _lib.stream_ptr(self.sw.device)), "rosa_decode_step")
+
+    def step(self, projs, t0: int, payload: torch.Tensor, out: torch.Tensor,
+             match_len=None, match_end=None) -> None:
+        """Append the bits of projs (3 x (contexts, k_new, streams)) at t0 and write
+        payload * sign of the new positions into out (contexts, k_new, streams);
+        match_len / match_end (rows, k_new) int32 optional."""
+        C, k_new, S = projs[0].shape
+        self._step(projs, t0, k_new, payload.detach().float().contiguous(), out.data_ptr(),
+                   k_new * S, _lib.dtype_code(out), _lib.ptr(match_len), _lib.ptr(match_end),
+                   k_new)
+
+    def match_context(self, t_len: int, payload: torch.Tensor, out: torch.Tensor,
+                      match_len=None, match_end=None) -> None:
+        """Match a whole context already in the bit histories (load_words), 32
+        positions per launch with the main run rebuilt as it grows: out
+        (contexts, t_len, streams) payload * sign, match_len / match_end
+        (rows, t_len) int32 optional -- the sequence matcher's results, in
+        O(log T) per position whatever the bit statistics."""
+        S = self.streams
+        pay = payload.detach().float().contiguous()
+        self.n_main = 0
+        esz = out.element_size()
+        for t0 in range(0, t_len, 32):
+            k = min(32, t_len - t0)
+            ml = match_len.data_ptr() + 4 * t0 if match_len is not None else None
+            me = match_end.data_ptr() + 4 * t0 if match_end is not None else None
+            self._step(None, t0, k, pay, out.data_ptr() + esz * t0 * S, t_len * S,
+                       _lib.dtype_code(out), ml, me, t_len)
+
+
+def _int8_linear(w: torch.Tensor):
+    """GS128 codes of an nn.Linear weight (out, in): Int8Linear's weight pack."""
+    return quantize_last_dim(w.detach().float())
+
+
+def _linear_int8(x2: torch.Tensor, w, bias=None, out_dtype=torch.float32):
+    """Int8Linear.forward (linear.py:67-73): per-token GS128 codes of x, W8A8 GEMM,
+    fp32 bias in the epilogue."""
+    xq, xs = quantize_last_dim(x2)
+    xq, wq = _validate_and_pad(xq, xs, w[0], w[1], GROUP_SIZE)
+    return gemm_out(xq, xs, wq, w[1], out_dtype=out_dtype, bias=bias)
+
+
+class KSDraftDrafter:
+    """Serving-time INT8 draft model over `contexts` concurrent contexts.
+
+    state: {reference state-dict name: fp32 tensor} of a KSDraftModel
+    (ksdraft/model/draft.py, head tied to embedding.weight), e.g.
+    DraftTrainStep.parameter_dict() or a reference checkpoint.  shape: its
+    DraftShape.  capacity: positions per context the caches hold (prefill +
+    appended blocks).  group: process group to split the contexts over (the
+    vocabulary is sharded over the same ranks)."""
+
+    def __init__(self, state: dict, shape, device, *, contexts: int, capacity: int,
+                 act_dtype=torch.bfloat16, group=None):
+        injection.check_width(shape.d_model)
+        self.shape, self.dev, self.act = shape, torch.device(device), act_dtype
+        self.group = group
+        self.world = dist.get_world_size(group) if (group is not None or (
+            dist.is_available() and dist.is_initialized())) else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        if contexts % self.world:
+            raise ValueError(f"{contexts} contexts do not split over {self.world} ranks")
+        self.contexts = contexts
+        self.c_local = contexts // self.world
+        self.capacity = (capacity + 63) // 64 * 64
+        dev = self.dev
+        P = lambda n: torch.as_tensor(state[n]).to(dev, torch.float32)  # noqa: E731
+        with torch.no_grad():
+            self.E = P("embedding.weight").contiguous()
+            self.input_norm = (P("input_norm.weight"), P("input_norm.bias"))
+            self.output_norm = (P("output_norm.weight"), P("output_norm.bias"))
+            self.teacher = (_int8_linear(P("teacher_proj.weight"))
+                            if "teacher_proj.weight" in state else None)
+            self.layers = []
+            for l in range(shape.layers):
+                pre = f"blocks.{l}."
+                R = lambda n: P(pre + "rosa." + n)  # noqa: E731,B023
+                cell = KS3Int8Cell(ks3_weights(P(pre + "ffn.down.weight"), P(pre + "ffn.up.weight"),
+                                               P(pre + "ffn.coefficients"),
+                                               P(pre + "ffn.raw_scale"), P(pre + "ffn.raw_shift")),
+                                   nonlinear="int8", trainable=False)
+                W = {n: P(pre + "injection." + (n if n == "gate_bias" else n + ".weight"))
+                     for n in ("feature_down", "feature_up", "gate_q.down", "gate_q.up",
+                               "gate_p.down", "gate_p.up", "gate_bias", "inject.down",
+                               "inject.up")}
+                self.layers.append(SimpleNamespace(
+                    ln_attn=(P(pre + "ln_attn.weight").to(act_dtype),
+                             P(pre + "ln_attn.bias").to(act_dtype)),
+                    mixes=[torch.sigmoid(R(f"time_mix_{c}")).contiguous() for c in "qkv"],
+                    qkv=[_int8_linear(R(f"{c}_proj.weight")) for c in "qkv"],
+                    qkv_bias=[R(f"{c}_proj.bias").contiguous() for c in "qkv"],
+                    out=_int8_linear(R("out_proj.weight")),
+                    out_bias=R("out_proj.bias").contiguous(),
+                    payload=R("payload").contiguous(),
+                    iw=injection.InjectionWeights(W, act_dtype),
+                    ln_ffn=(P(pre + "ln_ffn.weight").contiguous(),
+                            P(pre + "ln_ffn.bias").contiguous()),
+                    cell=cell))
+            self.head = VocabParallelHead(self.E, group=group if self.world > 1 else None)
+        self.states = None
+        self.length = 0
+
+    # ---- forward -------------------------------------------------------------
+
+    def _layer(self, l: int, x: torch.Tensor, t0: int, p_first, prefill: bool,
+               probe: dict | None = None):
+        """One DraftBlock (block.py:34-42) on this rank's contexts: x (C, n, d) at
+        positions t0 .. t0 + n - 1.  Returns (x_out (C, n, d), p (C, n, d))."""
+        L = self.layers[l]
+        C, n, d = x.shape
+        S = self.shape.streams
+        dev, act = self.dev, self.act
+        lib = _lib.lib()
+        a = F.layer_norm(x, (d,), *L.ln_attn, LN_EPS)
+        # time-shift mix with the previous position's ln_attn output (zero before
+        # position 0): one leading row per context, whose own outputs are dropped
+        prev = torch.zeros(C, 1, d, dtype=act, device=dev) if prefill else self.cache_a[l][:, None]
+        ax = torch.cat([prev, a], 1).contiguous()
+        rows = C * (n + 1)
+        G = d // GROUP_SIZE
+        codes = [torch.empty(rows, d, dtype=torch.int8, device=dev) for _ in range(3)]
+        scales = [torch.empty(rows, G, dtype=torch.float16, device=dev) for _ in range(3)]
+        _lib.check(lib.ksd8_rosa_timemix_quantize(
+            ax.data_ptr(), _lib.dtype_code(ax), C, n + 1, d, *(m.data_ptr() for m in L.mixes),
+            codes[0].data_ptr(), scales[0].data_ptr(), codes[1].data_ptr(), scales[1].data_ptr(),
+            codes[2].data_ptr(), scales[2].data_ptr(), None, _lib.stream_ptr(dev)),
+            "rosa_timemix_quantize")
+        # q / k / v projections in fp32 (the promoted dtype of rosa.py:128-133)
+        projs = [gemm_out(codes[i], scales[i], *L.qkv[i], out_dtype=torch.float32,
+                          bias=L.qkv_bias[i]).view(C, n + 1, S)[:, 1:].contiguous()
+                 for i in range(3)]
+        del codes, scales, ax
+        mixed = torch.empty(C, n, S, dtype=act, device=dev)
+        st = self.states[l]
+        ml = me = None
+        if probe is not None:
+            ml = torch.empty(C * S, n, dtype=torch.int32, device=dev)
+            me = torch.empty_like(ml)
+        if prefill:
+            # the whole context through the decode matcher (O(log T) per position;
+            # the sequence matchers' shared-memory kernels stop at 4096 / 8192)
+            st.load_words([pack_bits(p, C, n, S, n * S, S, 1) for p in projs], n)
+            st.match_context(n, L.payload, mixed, ml, me)
+            st.build(n)
+        else:
+            st.step(projs, t0, L.payload, mixed, ml, me)
+        if probe is not None:
+            probe[l] = (ml, me, mixed)
+        r = _linear_int8(mixed.reshape(C * n, S), L.out, bias=L.out_bias, out_dtype=act)
+        h = x.reshape(C * n, d) + r
+        b, h2, p, _ = injection.forward(h, p_first, L.iw, *L.ln_ffn, C, n)
+        k = L.cell(b)
+        x_out = (h2 + k).view(C, n, d)
+        p = p.view(C, n, d)
+        self.cache_a[l] = a[:, -1].contiguous()
+        self.cache_p[l] = p[:, -1].contiguous()
+        return x_out, p
+
+    def _input(self, tokens: torch.Tensor, states: torch.Tensor | None) -> torch.Tensor:
+        """input_norm(E[tokens]) + teacher_proj(states) (draft.py:68-74), (C, n, d)."""
+        C, n = tokens.shape
+        d = self.shape.d_model
+        x = F.layer_norm(self.E[tokens.reshape(-1)].to(self.act), (d,),
+                         self.input_norm[0].to(self.act), self.input_norm[1].to(self.act),
+                         LN_EPS)
+        if states is not None:
+            if self.teacher is None:
+                raise ValueError("teacher_states passed but the model has no teacher_proj")
+            x = x + _linear_int8(states.reshape(C * n, -1), self.teacher, out_dtype=self.act)
+        return x.view(C, n, d)
+
+    def _local(self, t: torch.Tensor | None) -> torch.Tensor | None:
+        """This rank's contexts of a (contexts, ...) tensor, on the device."""
+        if t is None:
+            return None
+        if t.shape[0] != self.contexts:
+            raise ValueError(f"expected {self.contexts} contexts, got {t.shape[0]}")
+        t = t[self.rank * self.c_local:(self.rank + 1) * self.c_local]
+        return t.to(self.dev, non_blocking=True)
+
+    def _topk(self, xl: torch.Tensor, k: int):
+        """Head top-k of final hidden states xl (rows of this rank's contexts):
+        gathered over the ranks, scored against every vocabulary shard."""
+        d = self.shape.d_model
+        xf = F.layer_norm(xl, (d,), self.output_norm[0].to(self.act),
+                          self.output_norm[1].to(self.act), LN_EPS).reshape(-1, d)
+        if self.world > 1:
+            parts = [torch.empty_like(xf) for _ in range(self.world)]
+            dist.all_gather(parts, xf.contiguous(), group=self.group)
+            xf = torch.cat(parts)
+        return self.head.topk(xf, k)
+
+    def _check_tokens(self, tokens: torch.Tensor) -> None:
+        lo, hi = int(tokens.min()), int(tokens.max())
+        if lo < 0 or hi >= self.shape.vocab:
+            raise ValueError(f"token ids must lie in [0, {self.shape.vocab}); got [{lo}, {hi}]")
+
+    @torch.no_grad()
+    def prefill(self, tokens: torch.Tensor, teacher_states: torch.Tensor | None = None,
+                topk: int = 8, probe: dict | None = None):
+        """Whole-context forward of (contexts, T0) tokens (T0 > 62); builds the
+        caches and returns the top-k candidates (ids, logits) of every context's
+        next token, (contexts, k) each."""
+        self._check_tokens(tokens)
+        C, T0 = tokens.shape
+        if T0 <= MAX_LEN:
+            raise ValueError(f"prefill needs more than {MAX_LEN} positions (the Rosa cap "
+                             f"min(62, T - 1) is then fixed); got {T0}")
+        if T0 > self.capacity:
+            raise ValueError(f"{T0} positions exceed the capacity {self.capacity}")
+        tok = self._local(tokens)
+        sts = self._local(teacher_states)
+        S = self.shape.streams
+        self.states = [RosaDecodeState(self.c_local, S, self.capacity, self.dev)
+                       for _ in self.layers]
+        self.cache_a = [None] * len(self.layers)
+        self.cache_p = [None] * len(self.layers)
+        x = self._input(tok, sts)
+        p_first = None
+        for l in range(len(self.layers)):
+            x, p = self._layer(l, x, 0, p_first, True, probe)
+            p_first = p[:, 0]
+        self.length = T0
+        vals, ids = self._topk(x[:, -1:], topk)
+        return ids.view(C, topk), vals.view(C, topk)
+
+    @torch.no_grad()
+    def propose(self, target_states: torch.Tensor | None, tokens: torch.Tensor, topk: int = 8,
+                probe: dict | None = None):
+        """Append a block of n positions per context (tokens (contexts, n), n <= 32,
+        their teacher states (contexts, n, teacher_dim) or None) and draft from
+        it: returns (candidates (contexts, n, k) int64 vocab ids, logits
+        (contexts, n, k) fp32, None) -- the top-k next tokens after each
+        appended position; the third slot of the reference's signature
+        (refined candidates) has no counterpart in the reference code."""
+        if self.states is None:
+            raise RuntimeError("prefill() first")
+        self._check_tokens(tokens)
+        C, n = tokens.shape
+        if not 1 <= n <= 32:
+            raise ValueError(f"a block holds 1..32 positions; got {n}")
+        if self.length + n > self.capacity:
+            raise ValueError("the caches are full (capacity positions per context)")
+        t0 = self.length
+        x = self._input(self._local(tokens), self._local(target_states))
+        for l in range(len(self.layers)):
+            x, _ = self._layer(l, x, t0, self.cache_p[l], False, probe)
+        self.length = t0 + n
+        vals, ids = self._topk(x, topk)
+        return ids.view(C, n, topk), vals.view(C, n, topk), None

@@ -184,8 +184,11 @@ def clip_grad_norm(flat: torch.Tensor, max_norm: float, scratch: torch.Tensor,
 SM_RESERVE = int(os.environ.get("KSD8_SM_RESERVE", "16"))
 
 
-def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
-    """(rank, world, local_rank) from the torchrun environment; NCCL on GPUs."""
+def init_distributed(timeout_s: float = 120.0,
+                     nccl_max_ctas: int | None = None) -> tuple[int, int, int]:
+    """(rank, world, local_rank) from the torchrun environment; NCCL on GPUs,
+    limited to nccl_max_ctas CTAs (default: the SM reserve of the persistent
+    kernels)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -195,7 +198,7 @@ def init_distributed(timeout_s: float = 120.0) -> tuple[int, int, int]:
             torch.cuda.set_device(local)
             # NCCL's kernels then fit in the SMs the persistent kernels leave
             # free while a gradient reduction overlaps the backward
-            os.environ.setdefault("NCCL_MAX_CTAS", str(SM_RESERVE))
+            os.environ.setdefault("NCCL_MAX_CTAS", str(nccl_max_ctas or SM_RESERVE))
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
     return rank, world, local
 

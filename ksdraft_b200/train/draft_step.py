@@ -45,6 +45,7 @@ round trip.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -59,7 +60,13 @@ from ..kernels.quant import GROUP_SIZE, dequantize_last_dim, quantize_cols, quan
 from ..model.head import ce_grad, ce_grad_quant, ce_partials, combine_ce_partials
 from ..model.rosa import _default_max_len, match_words, pack_bits
 from . import injection
-from .dp import SM_RESERVE, allreduce_mean_async, wait_all
+from .dp import allreduce_mean_async, wait_all
+
+# SMs left to NCCL while a block's gradient reduction overlaps the backward.  The
+# config-4 backward is long (tens to hundreds of ms), so a few NCCL CTAs keep up
+# with it; on 2 B200s 8 (or 4) reserved SMs gave a 254 ms step, 16 gave 260 ms
+# (the KS3 backward's persistent GEMMs lose fewer SMs).
+DRAFT_SM_RESERVE = int(os.environ.get("KSD8_DRAFT_SM_RESERVE", "8"))
 
 
 @dataclass(frozen=True)
@@ -525,7 +532,7 @@ class DraftTrainStep:
         def reduce_span(span):
             works = allreduce_mean_async(span, self.group)
             if works and not overlapping[0]:
-                _lib.check(lib.ksd8_set_sm_reserve(SM_RESERVE), "set_sm_reserve")
+                _lib.check(lib.ksd8_set_sm_reserve(DRAFT_SM_RESERVE), "set_sm_reserve")
                 overlapping[0] = True
             pending.append(works)
 
