@@ -364,7 +364,10 @@ int ksd8_rosa_decode_build(const uint64_t* kw, int64_t n_streams, int64_t nw, in
  * length >= n_main; all three proj NULL: the bits are already in the
  * histories) and write, for new position i, payload[s] * sign to
  * out[c * out_cs + i * streams + s] and optionally the match length / latest
- * endpoint to match_len / match_end[row * ml_rs + i] int32.  Returns
+ * endpoint to match_len / match_end[row * ml_rs + i] int32.  pos (device
+ * int64 [t0, n_main], or NULL): the kernel reads t0 and n_main there instead
+ * (a CUDA graph replays the launch at every position); the host arguments must
+ * hold the same values when the launch is recorded or made.  Returns
  * KSD8_ERR_UNSUPPORTED when the delta n_main .. t0 + k_new - 2 outgrows the
  * kernel's 34-word window (about 2000 keys): rebuild with n_keys = t0 first. */
 int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* proj_v, int dtype,
@@ -373,7 +376,7 @@ int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* pr
                           int64_t nw, const uint64_t* sw, const uint16_t* sj,
                           const uint16_t* blk, int64_t cap, const float* payload, void* out,
                           int64_t out_cs, int out_dtype, int32_t* match_len, int32_t* match_end,
-                          int64_t ml_rs, int* status, void* stream);
+                          int64_t ml_rs, const int64_t* pos, int* status, void* stream);
 
 /* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);

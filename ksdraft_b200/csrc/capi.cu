@@ -61,7 +61,8 @@ int ksd8_rosa_decode_build_launch(const uint64_t*, int64_t, int64_t, int64_t, in
 int ksd8_rosa_decode_step_launch(const void* const*, int, int64_t, int64_t, int64_t, int64_t,
                                  int64_t, int, uint64_t* const*, int64_t, const uint64_t*,
                                  const uint16_t*, const uint16_t*, int64_t, const float*, void*,
-                                 int64_t, int, int32_t*, int32_t*, int64_t, cudaStream_t);
+                                 int64_t, int, int32_t*, int32_t*, int64_t, const int64_t*,
+                                 cudaStream_t);
 int ksd8_rosa_decode_limits(int64_t*, int64_t*, int64_t*);
 int ksd8_transfer_bwd_launch(const void*, int, const float*, const float*, const float*, int64_t,
                              int64_t, float, const void*, const float*, int64_t, void*, float*,
@@ -636,7 +637,7 @@ int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* pr
                           int64_t nw, const uint64_t* sw, const uint16_t* sj,
                           const uint16_t* blk, int64_t cap, const float* payload, void* out,
                           int64_t out_cs, int out_dtype, int32_t* match_len, int32_t* match_end,
-                          int64_t ml_rs, int* status, void* stream) {
+                          int64_t ml_rs, const int64_t* pos, int* status, void* stream) {
   (void)status;
   if (!valid_float_dtype(dtype) || !valid_float_dtype(out_dtype)) return KSD8_ERR_DTYPE;
   if (out_cs < k_new * streams || ((match_len || match_end) && ml_rs < k_new))
@@ -664,5 +665,5 @@ int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* pr
   return finish(ksd8_rosa_decode_step_launch(proj, dtype, contexts, streams, k_new, t0, n_main,
                                              max_len, bits, nw, sw, sj, blk, cap, payload, out,
                                              out_cs, out_dtype, match_len, match_end, ml_rs,
-                                             S(stream)));
+                                             pos, S(stream)));
 }

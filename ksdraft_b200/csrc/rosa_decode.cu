@@ -151,6 +151,7 @@ struct DecodeArgs {
                          // bits of the new positions are already in the histories
   int dtype;
   int64_t contexts, streams, k_new, t0, n_main;
+  const int64_t* pos;    // device [t0, n_main] overriding the two scalars (CUDA graphs)
   int max_len;
   uint64_t* bits[3];     // q, k, v bit histories (contexts * streams, nw)
   int64_t nw;
@@ -188,7 +189,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
   const unsigned full = 0xffffffffu;
   const int64_t c = st / a.streams, s = st % a.streams;
   const int K = (int)a.k_new;
-  const int64_t t0 = a.t0;
+  const int64_t t0 = a.pos ? a.pos[0] : a.t0;
+  const int64_t n_main = a.pos ? a.pos[1] : a.n_main;
   uint64_t* top = top_all[warp];
   uint64_t* dwords = dwords_all[warp];
 
@@ -228,14 +230,14 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
   const uint64_t* krow = a.bits[1] + st * a.nw;
   const uint64_t* vrow = a.bits[2] + st * a.nw;
   const int r0 = a.max_len > 0 ? a.max_len - 1 : 0;
-  const int64_t nk = a.n_main > r0 ? a.n_main - r0 : 0;     // main run size
+  const int64_t nk = n_main > r0 ? n_main - r0 : 0;     // main run size
   const int ntop = (int)((nk + DEC_BLK - 1) / DEC_BLK);
   const uint64_t* swr = a.sw + st * a.cap;
   const uint16_t* sjr = a.sj + st * a.cap;
   const uint16_t* blkr = a.blk + st * (a.cap / DEC_BLK);
   for (int b = lane; b < ntop; b += 32) top[b] = swr[(int64_t)b * DEC_BLK];
   // delta keys j in [dlo, t0 + K - 2]; their windows read words w0 .. of k
-  const int64_t dlo = max(a.n_main, (int64_t)r0);
+  const int64_t dlo = max(n_main, (int64_t)r0);
   const int64_t dhi = t0 + K - 2;
   const int64_t w0 = dlo > 63 ? (dlo >> 6) - 1 : 0;
   if (dhi >= dlo) {
@@ -382,7 +384,7 @@ int ksd8_rosa_decode_step_launch(const void* const* proj, int dtype, int64_t con
                                  const uint64_t* sw, const uint16_t* sj, const uint16_t* blk,
                                  int64_t cap, const float* payload, void* out, int64_t out_cs,
                                  int out_dtype, int32_t* match_len, int32_t* match_end,
-                                 int64_t ml_rs, cudaStream_t stream) {
+                                 int64_t ml_rs, const int64_t* pos, cudaStream_t stream) {
   DecodeArgs a;
   for (int q = 0; q < 3; ++q) {
     a.proj[q] = proj[q];
@@ -390,6 +392,7 @@ int ksd8_rosa_decode_step_launch(const void* const* proj, int dtype, int64_t con
   }
   a.dtype = dtype;
   a.contexts = contexts; a.streams = streams; a.k_new = k_new; a.t0 = t0; a.n_main = n_main;
+  a.pos = pos;
   a.max_len = max_len; a.nw = nw; a.sw = sw; a.sj = sj; a.blk = blk; a.cap = cap;
   a.payload = payload; a.out = out; a.out_cs = out_cs; a.out_dtype = out_dtype;
   a.match_len = match_len; a.match_end = match_end; a.ml_rs = ml_rs;

@@ -49,7 +49,7 @@ from ..kernels.gemm import _validate_and_pad, gemm_out
 from ..kernels.ks3_int8 import KS3Int8Cell, ks3_weights
 from ..kernels.quant import GROUP_SIZE, quantize_last_dim
 from ..train import injection
-from .head import VocabParallelHead
+from .head import VocabParallelHead, gather_topk, topk_rows
 from .rosa import pack_bits
 
 MAX_LEN = 62            # the reference's cap min(62, T - 1) once T >= 63
@@ -73,6 +73,7 @@ class RosaDecodeState:
         self.sj = torch.empty(rows, capacity, dtype=torch.int16, device=device)
         self.blk = torch.zeros(rows, capacity // 64, dtype=torch.int16, device=device)
         self.n_main = 0
+        self.pos = None        # device [t0, n_main] read by the step kernel (CUDA graphs)
 
     def load_words(self, words, t_len: int) -> None:
         """Bit histories from packed words (rows, ceil(t_len / 64)) of a whole context."""
@@ -101,8 +102,8 @@ class RosaDecodeState:
         return (dhi >> 6) - w0 + 1 > DELTA_WORDS
 
     def _step(self, projs, t0: int, k_new: int, pay, out, out_cs: int, out_dt: int, ml, me,
-              ml_rs: int):
-        if self.needs_build(t0, k_new):
+              ml_rs: int, prepared: bool = False):
+        if not prepared and self.needs_build(t0, k_new):
             self.build(t0)
         if t0 + k_new > self.capacity:
             raise ValueError("decode state capacity exhausted")
@@ -113,18 +114,19 @@ class RosaDecodeState:
             *ptrs, dt, C, S, k_new, t0, self.n_main, MAX_LEN,
             *(b.data_ptr() for b in self.bits), self.nw, self.sw.data_ptr(), self.sj.data_ptr(),
             self.blk.data_ptr(), self.capacity, pay.data_ptr(), out, out_cs, out_dt, ml, me,
-            ml_rs, None,
+            ml_rs, _lib.ptr(self.pos), None,
             _lib.stream_ptr(self.sw.device)), "rosa_decode_step")
 
     def step(self, projs, t0: int, payload: torch.Tensor, out: torch.Tensor,
-             match_len=None, match_end=None) -> None:
+             match_len=None, match_end=None, prepared: bool = False) -> None:
         """Append the bits of projs (3 x (contexts, k_new, streams)) at t0 and write
         payload * sign of the new positions into out (contexts, k_new, streams);
-        match_len / match_end (rows, k_new) int32 optional."""
+        match_len / match_end (rows, k_new) int32 optional.  prepared: the caller
+        has already rebuilt the main run if the step needed it."""
         C, k_new, S = projs[0].shape
         self._step(projs, t0, k_new, payload.detach().float().contiguous(), out.data_ptr(),
                    k_new * S, _lib.dtype_code(out), _lib.ptr(match_len), _lib.ptr(match_end),
-                   k_new)
+                   k_new, prepared)
 
     def match_context(self, t_len: int, payload: torch.Tensor, out: torch.Tensor,
                       match_len=None, match_end=None) -> None:
@@ -169,8 +171,12 @@ class KSDraftDrafter:
     vocabulary is sharded over the same ranks)."""
 
     def __init__(self, state: dict, shape, device, *, contexts: int, capacity: int,
-                 act_dtype=torch.bfloat16, group=None):
+                 act_dtype=torch.bfloat16, group=None, head_mode: str = "w8a8"):
         injection.check_width(shape.d_model)
+        if head_mode not in ("w8a8", "float"):
+            raise ValueError("head_mode is 'w8a8' (north star) or 'float' (the reference "
+                             "int8 tier's float head, int8_convert.py:8-12)")
+        self.head_mode = head_mode
         self.shape, self.dev, self.act = shape, torch.device(device), act_dtype
         self.group = group
         self.world = dist.get_world_size(group) if (group is not None or (
@@ -217,11 +223,13 @@ class KSDraftDrafter:
             self.head = VocabParallelHead(self.E, group=group if self.world > 1 else None)
         self.states = None
         self.length = 0
+        self.pos = torch.zeros(2, dtype=torch.int64, device=self.dev)
+        self._graph = None
 
     # ---- forward -------------------------------------------------------------
 
     def _layer(self, l: int, x: torch.Tensor, t0: int, p_first, prefill: bool,
-               probe: dict | None = None):
+               probe: dict | None = None, prepared: bool = False):
         """One DraftBlock (block.py:34-42) on this rank's contexts: x (C, n, d) at
         positions t0 .. t0 + n - 1.  Returns (x_out (C, n, d), p (C, n, d))."""
         L = self.layers[l]
@@ -261,7 +269,7 @@ class KSDraftDrafter:
             st.match_context(n, L.payload, mixed, ml, me)
             st.build(n)
         else:
-            st.step(projs, t0, L.payload, mixed, ml, me)
+            st.step(projs, t0, L.payload, mixed, ml, me, prepared)
         if probe is not None:
             probe[l] = (ml, me, mixed)
         r = _linear_int8(mixed.reshape(C * n, S), L.out, bias=L.out_bias, out_dtype=act)
@@ -270,8 +278,8 @@ class KSDraftDrafter:
         k = L.cell(b)
         x_out = (h2 + k).view(C, n, d)
         p = p.view(C, n, d)
-        self.cache_a[l] = a[:, -1].contiguous()
-        self.cache_p[l] = p[:, -1].contiguous()
+        self.cache_a[l].copy_(a[:, -1])
+        self.cache_p[l].copy_(p[:, -1])
         return x_out, p
 
     def _input(self, tokens: torch.Tensor, states: torch.Tensor | None) -> torch.Tensor:
@@ -306,6 +314,10 @@ class KSDraftDrafter:
             parts = [torch.empty_like(xf) for _ in range(self.world)]
             dist.all_gather(parts, xf.contiguous(), group=self.group)
             xf = torch.cat(parts)
+        if self.head_mode == "float":
+            logits = xf.float() @ self.head.weight.t()
+            v, i = topk_rows(logits, k, offset=self.head.vstart)
+            return gather_topk(v, i, k, self.group if self.world > 1 else None)
         return self.head.topk(xf, k)
 
     def _check_tokens(self, tokens: torch.Tensor) -> None:
@@ -331,8 +343,11 @@ class KSDraftDrafter:
         S = self.shape.streams
         self.states = [RosaDecodeState(self.c_local, S, self.capacity, self.dev)
                        for _ in self.layers]
-        self.cache_a = [None] * len(self.layers)
-        self.cache_p = [None] * len(self.layers)
+        d = self.shape.d_model
+        self.cache_a = [torch.empty(self.c_local, d, dtype=self.act, device=self.dev)
+                        for _ in self.layers]
+        self.cache_p = [torch.empty_like(c) for c in self.cache_a]
+        self._graph = None
         x = self._input(tok, sts)
         p_first = None
         for l in range(len(self.layers)):
@@ -341,6 +356,70 @@ class KSDraftDrafter:
         self.length = T0
         vals, ids = self._topk(x[:, -1:], topk)
         return ids.view(C, topk), vals.view(C, topk)
+
+    def _block(self, t0: int, tok, sts, topk: int, probe=None, prepared: bool = False):
+        """Forward of one appended block of this rank's contexts + the head top-k."""
+        x = self._input(tok, sts)
+        for l in range(len(self.layers)):
+            x, _ = self._layer(l, x, t0, self.cache_p[l], False, probe, prepared)
+        vals, ids = self._topk(x, topk)
+        return ids, vals
+
+    def _prepare(self, t0: int, n: int) -> None:
+        """Rebuild every layer's main run if a block at t0 would overflow the step
+        kernel's delta window, and publish [t0, n_main] for a graph replay."""
+        for st in self.states:
+            if st.needs_build(t0, n):
+                st.build(t0)
+        self.pos.copy_(torch.tensor([t0, self.states[0].n_main], dtype=torch.int64))
+
+    @torch.no_grad()
+    def capture(self, n: int, topk: int = 8, with_states: bool = True) -> None:
+        """Record propose() of an n-position block as one CUDA graph (the per-layer
+        launches of a decode step are small; replaying them removes the host
+        cost).  The step kernel reads the position from device memory, so one
+        recording serves every later block; main-run rebuilds stay outside the
+        graph.  Call after prefill(); propose() with the same n / topk / teacher
+        states presence replays it."""
+        if self.states is None:
+            raise RuntimeError("prefill() first")
+        C, dev = self.c_local, self.dev
+        t0 = self.length
+        if t0 + n > self.capacity:
+            raise ValueError("the caches are full (capacity positions per context)")
+        self._g_tok = torch.zeros(C, n, dtype=torch.int64, device=dev)
+        self._g_sts = (torch.zeros(C, n, self.shape.teacher_dim, dtype=self.act, device=dev)
+                       if with_states else None)
+        self._prepare(t0, n)
+        for st in self.states:
+            st.pos = self.pos
+        # one eager pass first (library workspaces, lazily built state), then the
+        # caches are restored: it appended placeholder bits at t0, which the
+        # replays overwrite
+        saved = [c.clone() for c in self.cache_a + self.cache_p]
+        from ..kernels.gemm import GemmTimer
+        timer, GemmTimer.active = GemmTimer.active, None   # a GEMM timer sees the graph only
+        try:
+            self._block(t0, self._g_tok, self._g_sts, topk, prepared=True)
+        finally:
+            GemmTimer.active = timer
+        for c, v in zip(self.cache_a + self.cache_p, saved):
+            c.copy_(v)
+        torch.cuda.synchronize(dev)
+        self._graph = torch.cuda.CUDAGraph()
+        launches0 = _lib.LAUNCHES
+        with torch.cuda.graph(self._graph, capture_error_mode="thread_local"):
+            self._g_out = self._block(t0, self._g_tok, self._g_sts, topk, prepared=True)
+        self.captured_launches = _lib.LAUNCHES - launches0     # ksd8 kernels per replay
+        self._g_key = (n, topk, with_states)
+        torch.cuda.synchronize(dev)
+
+    def release(self) -> None:
+        """Drop the recorded graph (and the collectives it holds)."""
+        self._graph = None
+        if self.states is not None:
+            for st in self.states:
+                st.pos = None
 
     @torch.no_grad()
     def propose(self, target_states: torch.Tensor | None, tokens: torch.Tensor, topk: int = 8,
@@ -360,9 +439,18 @@ class KSDraftDrafter:
         if self.length + n > self.capacity:
             raise ValueError("the caches are full (capacity positions per context)")
         t0 = self.length
-        x = self._input(self._local(tokens), self._local(target_states))
-        for l in range(len(self.layers)):
-            x, _ = self._layer(l, x, t0, self.cache_p[l], False, probe)
+        key = (n, topk, target_states is not None)
+        if self._graph is not None and probe is None and key == self._g_key:
+            self._prepare(t0, n)
+            self._g_tok.copy_(self._local(tokens))
+            if self._g_sts is not None:
+                self._g_sts.copy_(self._local(target_states))
+            self._graph.replay()
+            ids, vals = (t.clone() for t in self._g_out)
+        else:
+            if self._graph is not None:
+                self._prepare(t0, n)      # the recorded position must not go stale
+            ids, vals = self._block(t0, self._local(tokens), self._local(target_states), topk,
+                                    probe, prepared=self._graph is not None)
         self.length = t0 + n
-        vals, ids = self._topk(x, topk)
         return ids.view(C, n, topk), vals.view(C, n, topk), None

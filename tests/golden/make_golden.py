@@ -355,6 +355,30 @@ def gen_draft_step():
          **{"w." + k: v for k, v in weights.items()}, **grads)
 
 
+def gen_draft_eval():
+    """Whole-sequence evaluation forward of the draft_step model (same weights,
+    read back from draft_step.npz) on the reference's int8 tier (to_int8: W8A8
+    Rosa and teacher projections, INT8 KS3 cells, float head), the whole-context
+    semantics that drafting must reproduce: logits of the last 24 positions."""
+    from ksdraft.config import KSDraftConfig
+    from ksdraft.model import KSDraftModel
+    from ksdraft.model.int8_convert import to_int8
+    cfg = KSDraftConfig(vocab_size=512, layers=2, d_model=128, rosa_streams=128, ks3_charts=256)
+    model = KSDraftModel(cfg, teacher_dim=64)
+    src = np.load(HERE / "draft_step.npz")
+    sd = {k[2:]: torch.from_numpy(src[k]) for k in src.files if k.startswith("w.")}
+    sd["head.weight"] = sd["embedding.weight"]
+    model.load_state_dict(sd)
+    q = to_int8(model).eval()
+    g = torch.Generator().manual_seed(9)
+    base = torch.randint(0, 40, (2, 48), generator=g)
+    tokens = torch.cat([base, base[:, :40], torch.randint(0, 512, (2, 32), generator=g)], 1)
+    states = torch.randn(2, tokens.shape[1], 64, generator=g)
+    with torch.no_grad():
+        logits, _ = q(tokens, teacher_states=states)
+    save("draft_eval", tokens=tokens.numpy(), states=f32(states), logits_tail=f32(logits[:, -24:]))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("KSD8_REFERENCE"),
@@ -367,7 +391,7 @@ def main():
     torch.set_num_threads(8)
     topics = {"quant": gen_quant, "dither": gen_dither, "gemm": gen_gemm, "ks3_spine": gen_ks3,
               "ks3_layer": gen_ks3_layer, "rosa": gen_rosa, "tanh16": gen_tanh16,
-              "linear": gen_linear, "draft_step": gen_draft_step}
+              "linear": gen_linear, "draft_step": gen_draft_step, "draft_eval": gen_draft_eval}
     for name, fn in topics.items():
         if args.only is None or name in args.only:
             fn()

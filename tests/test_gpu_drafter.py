@@ -93,3 +93,67 @@ def test_drafter_argument_checks():
     d.prefill(tokens[:, :100], states[:, :100].to(torch.bfloat16))
     with pytest.raises(ValueError):
         d.propose(None, tokens[:, :33])                 # a block holds at most 32 positions
+
+
+def test_drafter_matches_reference_int8_eval(golden):
+    """The reference's own int8-tier evaluation forward (to_int8, float head) of
+    the draft_step model on 120 positions (tests/golden/draft_eval.npz): a
+    prefill of 96 positions and three appended blocks of 8 give, at every
+    appended position, the reference's top-5 candidates and their logits."""
+    from ksdraft_b200.model.drafter import KSDraftDrafter
+    from ksdraft_b200.train.draft_step import DraftShape
+    g = golden("draft_eval")
+    w = golden("draft_step")
+    state = {k[2:]: torch.from_numpy(v) for k, v in w.items() if k.startswith("w.")}
+    shape = DraftShape(vocab=512, layers=2, d_model=128, streams=128, charts=256,
+                       teacher_dim=64)
+    d = KSDraftDrafter(state, shape, "cuda", contexts=2, capacity=128,
+                       act_dtype=torch.float32, head_mode="float")
+    tokens = torch.from_numpy(g["tokens"])
+    states = torch.from_numpy(g["states"])
+    ref = torch.from_numpy(g["logits_tail"]).cuda()          # positions 96 .. 119
+    d.prefill(tokens[:, :96], states[:, :96])
+    worst, agree = 0.0, []
+    for b in range(3):
+        sl = slice(96 + 8 * b, 104 + 8 * b)
+        ids, vals, _ = d.propose(states[:, sl], tokens[:, sl], topk=5)
+        r = ref[:, 8 * b:8 * b + 8]
+        rv = torch.gather(r, 2, ids)                           # reference logits at our ids
+        worst = max(worst, ((vals - rv).norm() / rv.norm()).item())
+        agree.append((ids == r.topk(5, dim=-1).indices).float().mean().item())
+    print(f"drafter vs reference int8 eval: top-5 logits rel-L2 {worst:.2e}, "
+          f"top-5 ids agree {min(agree):.3f}")
+    assert worst < 2e-3
+    assert min(agree) > 0.95
+
+
+def test_graph_replay_equals_eager_across_rebuilds():
+    """propose() replayed from one recorded CUDA graph gives the eager result at
+    every block, including blocks after a main-run rebuild (taken outside the
+    graph, the position read from device memory)."""
+    from ksdraft_b200.model.drafter import KSDraftDrafter
+    shape, state = _model()
+    C, T0, n, blocks = 2, 96, 8, 280
+    tokens, states = _inputs(C, T0 + n * (blocks + 1), seed=5)
+    st = states.to(torch.bfloat16)
+    cap = T0 + n * (blocks + 1)
+    eager = KSDraftDrafter(state, shape, "cuda", contexts=C, capacity=cap)
+    graphed = KSDraftDrafter(state, shape, "cuda", contexts=C, capacity=cap)
+    for d in (eager, graphed):
+        d.prefill(tokens[:, :T0], st[:, :T0])
+    graphed.capture(n, topk=4)
+    n_main0 = graphed.states[0].n_main
+    worst, agree = 0.0, 1.0
+    for b in range(blocks):
+        sl = slice(T0 + b * n, T0 + (b + 1) * n)
+        ie, ve, _ = eager.propose(st[:, sl], tokens[:, sl], topk=4)
+        ig, vg, _ = graphed.propose(st[:, sl], tokens[:, sl], topk=4)
+        worst = max(worst, ((ve - vg).norm() / ve.norm()).item())
+        agree = min(agree, (ie[..., 0] == ig[..., 0]).float().mean().item())
+    print(f"graph vs eager over {blocks} blocks: top-4 logits rel {worst:.2e}, "
+          f"top-1 agree {agree:.3f}")
+    # the same kernels in the same order (cuBLAS may pick another algorithm for
+    # the low-rank bf16 GEMMs under capture: bf16 rounding level at most)
+    assert worst < 2e-2 and agree >= 0.95
+    assert graphed.states[0].n_main > n_main0      # at least one rebuild happened
+    graphed.release()
