@@ -603,7 +603,8 @@ def run_config4(args) -> None:
             if not use_graph:
                 gt = GemmTimer().__enter__()
             s.record()
-            run(tok_dev, ts_dev)
+            with torch.cuda.nvtx.range("c4_step"):    # launch-list filter for ncu --nvtx
+                run(tok_dev, ts_dev)
             e.record()
             torch.cuda.synchronize()
             if not use_graph:
@@ -768,7 +769,7 @@ def run_config5(args) -> None:
     captured = 0
     if use_graph:
         with gt:
-            drafter.capture(C5_BLOCK, C5_TOPK)
+            drafter.capture(C5_BLOCK, C5_TOPK, phase_marks=True)
         captured = drafter.captured_launches
     barrier()
     times, gemm = [], []
@@ -780,7 +781,8 @@ def run_config5(args) -> None:
             if not use_graph:
                 gt = GemmTimer().__enter__()
             s.record()
-            drafter.propose(*block(pos), topk=C5_TOPK)
+            with torch.cuda.nvtx.range("c5_step"):
+                drafter.propose(*block(pos), topk=C5_TOPK)
             e.record()
             torch.cuda.synchronize()
             if not use_graph:
@@ -822,6 +824,8 @@ def run_config5(args) -> None:
                     "h2d_bytes_per_step": C5_CONTEXTS * C5_BLOCK * (8 + C4_TEACHER * 2),
                     "d2h_bytes_per_step": C5_CONTEXTS * C5_BLOCK * C5_TOPK * 8},
             "gpu_launches": launches, "prefill_s": prefill_s, "cuda_graph": use_graph,
+            "phases_ms": ({k: round(v, 3) for k, v in drafter.phases().items()}
+                          if use_graph else None),
             "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     drafter.release()

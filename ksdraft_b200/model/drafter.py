@@ -225,6 +225,24 @@ class KSDraftDrafter:
         self.length = 0
         self.pos = torch.zeros(2, dtype=torch.int64, device=self.dev)
         self._graph = None
+        self.phase_marks = None   # a list to record (phase name, CUDA event) marks into
+        self._capturing = False
+
+    def _mark(self, name: str) -> None:
+        """Start phase `name` (device-side timing of a block's parts; inside a
+        recorded graph the events are graph nodes, re-recorded by every replay)."""
+        if self.phase_marks is not None:
+            ev = torch.cuda.Event(enable_timing=True, external=self._capturing)
+            ev.record()
+            self.phase_marks.append((name, ev))
+
+    def phases(self, marks=None) -> dict:
+        """ms per phase name over a list of marks (default: the recorded graph's)."""
+        marks = self._g_marks if marks is None else marks
+        out = {}
+        for (name, ev), (_, nxt) in zip(marks, marks[1:]):
+            out[name] = out.get(name, 0.0) + ev.elapsed_time(nxt)
+        return out
 
     # ---- forward -------------------------------------------------------------
 
@@ -237,6 +255,7 @@ class KSDraftDrafter:
         S = self.shape.streams
         dev, act = self.dev, self.act
         lib = _lib.lib()
+        self._mark("rosa_proj")
         a = F.layer_norm(x, (d,), *L.ln_attn, LN_EPS)
         # time-shift mix with the previous position's ln_attn output (zero before
         # position 0): one leading row per context, whose own outputs are dropped
@@ -256,6 +275,7 @@ class KSDraftDrafter:
                           bias=L.qkv_bias[i]).view(C, n + 1, S)[:, 1:].contiguous()
                  for i in range(3)]
         del codes, scales, ax
+        self._mark("rosa_match")
         mixed = torch.empty(C, n, S, dtype=act, device=dev)
         st = self.states[l]
         ml = me = None
@@ -272,9 +292,12 @@ class KSDraftDrafter:
             st.step(projs, t0, L.payload, mixed, ml, me, prepared)
         if probe is not None:
             probe[l] = (ml, me, mixed)
+        self._mark("rosa_out")
         r = _linear_int8(mixed.reshape(C * n, S), L.out, bias=L.out_bias, out_dtype=act)
         h = x.reshape(C * n, d) + r
+        self._mark("injection_ln")
         b, h2, p, _ = injection.forward(h, p_first, L.iw, *L.ln_ffn, C, n)
+        self._mark("ks3")
         k = L.cell(b)
         x_out = (h2 + k).view(C, n, d)
         p = p.view(C, n, d)
@@ -359,10 +382,13 @@ class KSDraftDrafter:
 
     def _block(self, t0: int, tok, sts, topk: int, probe=None, prepared: bool = False):
         """Forward of one appended block of this rank's contexts + the head top-k."""
+        self._mark("input")
         x = self._input(tok, sts)
         for l in range(len(self.layers)):
             x, _ = self._layer(l, x, t0, self.cache_p[l], False, probe, prepared)
+        self._mark("head_topk")
         vals, ids = self._topk(x, topk)
+        self._mark("end")
         return ids, vals
 
     def _prepare(self, t0: int, n: int) -> None:
@@ -374,7 +400,8 @@ class KSDraftDrafter:
         self.pos.copy_(torch.tensor([t0, self.states[0].n_main], dtype=torch.int64))
 
     @torch.no_grad()
-    def capture(self, n: int, topk: int = 8, with_states: bool = True) -> None:
+    def capture(self, n: int, topk: int = 8, with_states: bool = True,
+                phase_marks: bool = False) -> None:
         """Record propose() of an n-position block as one CUDA graph (the per-layer
         launches of a decode step are small; replaying them removes the host
         cost).  The step kernel reads the position from device memory, so one
@@ -399,17 +426,25 @@ class KSDraftDrafter:
         saved = [c.clone() for c in self.cache_a + self.cache_p]
         from ..kernels.gemm import GemmTimer
         timer, GemmTimer.active = GemmTimer.active, None   # a GEMM timer sees the graph only
+        marks, self.phase_marks = self.phase_marks, None
         try:
             self._block(t0, self._g_tok, self._g_sts, topk, prepared=True)
         finally:
             GemmTimer.active = timer
+            self.phase_marks = marks
         for c, v in zip(self.cache_a + self.cache_p, saved):
             c.copy_(v)
         torch.cuda.synchronize(dev)
         self._graph = torch.cuda.CUDAGraph()
         launches0 = _lib.LAUNCHES
-        with torch.cuda.graph(self._graph, capture_error_mode="thread_local"):
-            self._g_out = self._block(t0, self._g_tok, self._g_sts, topk, prepared=True)
+        marks, self.phase_marks = self.phase_marks, ([] if phase_marks else None)
+        self._capturing = True
+        try:
+            with torch.cuda.graph(self._graph, capture_error_mode="thread_local"):
+                self._g_out = self._block(t0, self._g_tok, self._g_sts, topk, prepared=True)
+        finally:
+            self._capturing = False
+            self._g_marks, self.phase_marks = self.phase_marks or [], marks
         self.captured_launches = _lib.LAUNCHES - launches0     # ksd8 kernels per replay
         self._g_key = (n, topk, with_states)
         torch.cuda.synchronize(dev)
