@@ -370,13 +370,31 @@ def gen_draft_eval():
     sd["head.weight"] = sd["embedding.weight"]
     model.load_state_dict(sd)
     q = to_int8(model).eval()
-    g = torch.Generator().manual_seed(9)
-    base = torch.randint(0, 40, (2, 48), generator=g)
-    tokens = torch.cat([base, base[:, :40], torch.randint(0, 512, (2, 32), generator=g)], 1)
-    states = torch.randn(2, tokens.shape[1], 64, generator=g)
-    with torch.no_grad():
-        logits, _ = q(tokens, teacher_states=states)
-    save("draft_eval", tokens=tokens.numpy(), states=f32(states), logits_tail=f32(logits[:, -24:]))
+    # Rosa bits are signs of fp32 projections: one within fp32 rounding of zero
+    # flips with the summation order (dequantise + fp32 matmul here, exact
+    # int32 groups on the GPU) and moves every later match of its stream.  The
+    # inputs are drawn until every q / k / v projection of every layer is
+    # clear of zero by 1e-5 of its tensor's mean magnitude (the two paths agree to
+    # 2.2e-6 of it).
+    projs = []
+    for blk in q.blocks:
+        for nm in ("q_proj", "k_proj", "v_proj"):
+            getattr(blk.rosa, nm).register_forward_hook(
+                lambda m, i, o: projs.append(o.detach()))
+    for seed in range(9, 200):
+        g = torch.Generator().manual_seed(seed)
+        base = torch.randint(0, 40, (2, 48), generator=g)
+        tokens = torch.cat([base, base[:, :40], torch.randint(0, 512, (2, 32), generator=g)], 1)
+        states = torch.randn(2, tokens.shape[1], 64, generator=g)
+        projs.clear()
+        with torch.no_grad():
+            logits, _ = q(tokens, teacher_states=states)
+        margin = min(float((p.abs() / p.abs().mean()).min()) for p in projs)
+        if margin > 1e-5:
+            break
+    print(f"draft_eval: seed {seed}, smallest |projection| / mean {margin:.2e}")
+    save("draft_eval", tokens=tokens.numpy(), states=f32(states), logits_tail=f32(logits[:, -24:]),
+         seed=np.int64(seed), margin=np.float32(margin))
 
 
 def main():

@@ -99,7 +99,12 @@ def test_drafter_matches_reference_int8_eval(golden):
     """The reference's own int8-tier evaluation forward (to_int8, float head) of
     the draft_step model on 120 positions (tests/golden/draft_eval.npz): a
     prefill of 96 positions and three appended blocks of 8 give, at every
-    appended position, the reference's top-5 candidates and their logits."""
+    appended position, the reference's top-5 candidates and their logits.
+    The fixture's inputs keep every Rosa projection at least 1e-5 of its mean
+    magnitude away from zero: a sign decided by fp32 summation order (the
+    reference dequantises and runs an fp32 matmul, the GEMM here sums exact
+    int32 groups; they agree to 2.2e-6 of the mean) would flip one bit and
+    every later match of its stream."""
     from ksdraft_b200.model.drafter import KSDraftDrafter
     from ksdraft_b200.train.draft_step import DraftShape
     g = golden("draft_eval")
