@@ -13,7 +13,12 @@ is fixed at 16 sequences, 16/N per GPU ("scaling": "strong");
 --per-gpu-batch K runs K sequences on every rank instead ("scaling": "weak").
 
 config2: one KS3 decoder layer INT8 fwd+bwd (+ DP all-reduce + AdamW) at 4096
-tokens per GPU (weak scaling), the round-1 workload, kept as a second line.
+tokens per GPU (weak scaling), kept as a second workload.
+
+config5: draft serving -- 64 contexts of 8192 Zipf(1.1) tokens prefilled (not
+timed), then each step appends a block of 8 positions to every context through
+the 24 layers and returns the top-8 candidates of the W8A8 head (contexts split
+over the GPUs, vocabulary sharded); value = 512 tokens per step / step time.
 
 `value`  tokens/s of the whole job with inputs resident in HBM, device-timed
          with CUDA events per step (L2 flushed between steps), max over ranks.
@@ -808,6 +813,15 @@ def run_config5(args) -> None:
         torch.cuda.synchronize()
         e2e.append(s.elapsed_time(e))
         pos += C5_BLOCK
+    # a main-run rebuild (every layer's keys re-sorted) comes every
+    # steps_per_rebuild blocks; its cost is reported beside the step time
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    drafter.rebuild()
+    e.record()
+    torch.cuda.synchronize()
+    rebuild_ms = s.elapsed_time(e)
     e2e_t = torch.tensor([sum(e2e)], device=dev)
     if world > 1:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
@@ -824,6 +838,10 @@ def run_config5(args) -> None:
                     "h2d_bytes_per_step": C5_CONTEXTS * C5_BLOCK * (8 + C4_TEACHER * 2),
                     "d2h_bytes_per_step": C5_CONTEXTS * C5_BLOCK * C5_TOPK * 8},
             "gpu_launches": launches, "prefill_s": prefill_s, "cuda_graph": use_graph,
+            "rebuild": {"ms": rebuild_ms, "every_steps": drafter.steps_per_rebuild(C5_BLOCK),
+                        "value_amortized": tok / ((total_ms + rebuild_ms * args.steps
+                                                   / drafter.steps_per_rebuild(C5_BLOCK))
+                                                  / 1e3)},
             "phases_ms": ({k: round(v, 3) for k, v in drafter.phases().items()}
                           if use_graph else None),
             "clocks": clocks.summary()}

@@ -449,6 +449,16 @@ class KSDraftDrafter:
         self._g_key = (n, topk, with_states)
         torch.cuda.synchronize(dev)
 
+    def rebuild(self) -> None:
+        """Sort every layer's keys up to the current length into its main run now
+        (propose() does it when a block would overflow the delta window)."""
+        for st in self.states:
+            st.build(self.length)
+
+    def steps_per_rebuild(self, n: int) -> int:
+        """Blocks of n positions appended between two main-run rebuilds."""
+        return max(1, ((DELTA_WORDS - 2) * 64) // n)
+
     def release(self) -> None:
         """Drop the recorded graph (and the collectives it holds)."""
         self._graph = None

@@ -37,13 +37,13 @@ def _full(bits3, B, T):
 
 
 @pytest.mark.parametrize("kind", ["fair", "runs", "periodic"])
-@pytest.mark.parametrize("k_new", [1, 8, 32])
+@pytest.mark.parametrize("k_new", [1, 8, 12, 32])
 def test_decode_matches_whole_sequence(kind, k_new):
     from ksdraft_b200.model.drafter import RosaDecodeState
     from ksdraft_b200.model.rosa import match_words, pack_bits
     gen = torch.Generator().manual_seed(sum(map(ord, kind)) * 100 + k_new)
     B, T0 = 3, 100
-    steps = 2600 // k_new if k_new > 1 else 150   # k_new 8 / 32 pass a main-run rebuild
+    steps = 2600 // k_new if k_new > 1 else 150   # k_new > 1 passes a main-run rebuild
     T = T0 + steps * k_new
     bits3 = [_bits(kind, B, T, gen).cuda() for _ in range(3)]
     ml_ref, me_ref, out_ref = _full(bits3, B, T)
