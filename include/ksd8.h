@@ -48,6 +48,8 @@
  *   ksd8_transfer_bwd         its gradient (the F.normalize backward) for a loss coefficient
  *   ksd8_rosa_decode_build    no reference counterpart: the sorted key run behind
  *                             ksd8_rosa_decode_step, built from a context's k bits
+ *   ksd8_rosa_decode_merge    no reference counterpart: the same run, grown by merging the
+ *                             keys appended since it was built
  *   ksd8_rosa_decode_step     ksdraft/model/rosa.py:40-98 _match_payload_sign (+ :164 payload)
  *                             answered for positions appended to a matched context
  */
@@ -357,6 +359,15 @@ int ksd8_transfer_bwd(const void* p, int dtype, const float* e, const float* nor
 int ksd8_rosa_decode_build(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_keys,
                            int max_len, uint64_t* sw, uint16_t* sj, uint16_t* blk, int64_t cap,
                            int* status, void* stream);
+
+/* The main run of keys max_len - 1 .. n_new - 1 from the run of keys
+ * max_len - 1 .. n_old - 1 in (sw_in, sj_in) (a copy: sw / sj are written)
+ * and the k bits of the keys appended since: those keys are sorted and merged
+ * in; blk is recomputed.  n_new - max(n_old, max_len - 1) <= 8192. */
+int ksd8_rosa_decode_merge(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_old,
+                           int64_t n_new, int max_len, const uint64_t* sw_in,
+                           const uint16_t* sj_in, uint64_t* sw, uint16_t* sj, uint16_t* blk,
+                           int64_t cap, int* status, void* stream);
 
 /* Append k_new (1..32) positions t0 .. t0 + k_new - 1 to every row (bits =
  * proj > 0 of the projections (contexts, k_new, streams), dtype F32 / BF16 /

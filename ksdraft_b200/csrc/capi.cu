@@ -64,6 +64,9 @@ int ksd8_rosa_decode_step_launch(const void* const*, int, int64_t, int64_t, int6
                                  int64_t, int, int32_t*, int32_t*, int64_t, const int64_t*,
                                  cudaStream_t);
 int ksd8_rosa_decode_limits(int64_t*, int64_t*, int64_t*);
+int ksd8_rosa_decode_merge_launch(const uint64_t*, int64_t, int64_t, int64_t, int64_t, int,
+                                  const uint64_t*, const uint16_t*, uint64_t*, uint16_t*,
+                                  uint16_t*, int64_t, cudaStream_t);
 int ksd8_transfer_bwd_launch(const void*, int, const float*, const float*, const float*, int64_t,
                              int64_t, float, const void*, const float*, int64_t, void*, float*,
                              cudaStream_t);
@@ -629,6 +632,22 @@ int ksd8_rosa_decode_build(const uint64_t* kw, int64_t n_streams, int64_t nw, in
   if (n_streams > 0 && (!kw || !sw || !sj || !blk)) return KSD8_ERR_ARG;
   return finish(ksd8_rosa_decode_build_launch(kw, n_streams, nw, n_keys, max_len, sw, sj, blk,
                                               cap, S(stream)));
+}
+
+int ksd8_rosa_decode_merge(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_old,
+                           int64_t n_new, int max_len, const uint64_t* sw_in,
+                           const uint16_t* sj_in, uint64_t* sw, uint16_t* sj, uint16_t* blk,
+                           int64_t cap, int* status, void* stream) {
+  (void)status;
+  if (n_streams < 0 || nw < 0 || n_old < 0 || n_new < n_old || cap <= 0 || cap % 64 != 0 ||
+      cap > 65536)
+    return KSD8_ERR_SHAPE;
+  if (max_len < 1 || max_len > 64) return KSD8_ERR_ARG;
+  if (n_new > nw * 64 || n_new > cap) return KSD8_ERR_SHAPE;
+  if (n_streams > 0 && (!kw || !sw_in || !sj_in || !sw || !sj || !blk)) return KSD8_ERR_ARG;
+  if (n_streams > 0 && (sw_in == sw || sj_in == sj)) return KSD8_ERR_ARG;   // out of place
+  return finish(ksd8_rosa_decode_merge_launch(kw, n_streams, nw, n_old, n_new, max_len, sw_in,
+                                              sj_in, sw, sj, blk, cap, S(stream)));
 }
 
 int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* proj_v, int dtype,

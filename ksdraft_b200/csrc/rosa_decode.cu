@@ -120,6 +120,98 @@ __global__ void __launch_bounds__(256) rosa_decode_build_kernel(const uint64_t* 
   }
 }
 
+// ---------------------------------------------------------------- merge
+//
+// Rebuild by merging: the keys appended since the last build, j in
+// [max(n_old, r0), n_new), are sorted in shared memory and merged with the old
+// main run (sw_in, sj_in: keys r0 .. n_old - 1): an old key moves up by the
+// number of new keys with a smaller window (a new key's position is larger,
+// so on equal windows the old key comes first), a new key lands at its own
+// rank plus the number of old keys with a window <= its own.  One CTA per
+// stream; O((n_old + nd) log nd) instead of re-sorting the whole run.
+__global__ void __launch_bounds__(256) rosa_decode_merge_kernel(
+    const uint64_t* __restrict__ kw, int64_t nw, int64_t n_old, int64_t n_new, int r0, int npd,
+    int64_t cap, const uint64_t* __restrict__ sw_in, const uint16_t* __restrict__ sj_in,
+    uint64_t* __restrict__ sw, uint16_t* __restrict__ sj, uint16_t* __restrict__ blk) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  uint64_t* W = reinterpret_cast<uint64_t*>(dsm);
+  uint32_t* J = reinterpret_cast<uint32_t*>(W + npd);
+  uint64_t* bits = reinterpret_cast<uint64_t*>(J + npd + (npd & 1));
+  const int64_t stream = blockIdx.x;
+  const int64_t nk_old = n_old > r0 ? n_old - r0 : 0;
+  const int64_t dlo = max(n_old, (int64_t)r0);
+  const int64_t nd = n_new > dlo ? n_new - dlo : 0;
+  const int64_t w0 = dlo > 63 ? (dlo >> 6) - 1 : 0;
+  const int64_t nwd = nd > 0 ? ((n_new - 1) >> 6) - w0 + 1 : 0;
+  for (int64_t i = threadIdx.x; i < nwd; i += blockDim.x) bits[i] = kw[stream * nw + w0 + i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < npd; i += blockDim.x) {
+    const bool real = i < nd;
+    uint64_t w = ~0ull;
+    if (real) {
+      const int64_t j = dlo + i;
+      const int64_t wi = (j >> 6) - w0;
+      const int sh = (int)(j & 63) + 1;
+      const uint64_t h = bits[wi];
+      const uint64_t l0 = (j >> 6) > 0 ? bits[wi - 1] : 0ull;
+      w = sh == 64 ? h : ((l0 >> sh) | (h << (64 - sh)));
+    }
+    W[i] = w;
+    J[i] = real ? (uint32_t)(dlo + i) : 0xFFFFFFFFu;
+  }
+  __syncthreads();
+  for (int k = 2; k <= npd; k <<= 1) {
+    for (int jj = k >> 1; jj > 0; jj >>= 1) {
+      for (int i = threadIdx.x; i < npd; i += blockDim.x) {
+        const int l = i ^ jj;
+        if (l > i) {
+          const bool up = (i & k) == 0;
+          const uint64_t wi = W[i], wl = W[l];
+          const uint32_t ji = J[i], jl = J[l];
+          if (key_less(wl, jl, wi, ji) == up) {
+            W[i] = wl; W[l] = wi;
+            J[i] = jl; J[l] = ji;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const uint64_t* swi = sw_in + stream * cap;
+  const uint16_t* sji = sj_in + stream * cap;
+  uint64_t* swo = sw + stream * cap;
+  uint16_t* sjo = sj + stream * cap;
+  for (int64_t r = threadIdx.x; r < nk_old; r += blockDim.x) {
+    const uint64_t w = swi[r];
+    int64_t a = 0, b = nd;   // new keys with a window < w
+    while (a < b) {
+      const int64_t mid = (a + b) >> 1;
+      if (W[mid] < w) a = mid + 1; else b = mid;
+    }
+    swo[r + a] = w;
+    sjo[r + a] = sji[r];
+  }
+  for (int64_t i = threadIdx.x; i < nd; i += blockDim.x) {
+    const uint64_t w = W[i];
+    int64_t a = 0, b = nk_old;   // old keys with a window <= w
+    while (a < b) {
+      const int64_t mid = (a + b) >> 1;
+      if (swi[mid] <= w) a = mid + 1; else b = mid;
+    }
+    swo[i + a] = w;
+    sjo[i + a] = (uint16_t)J[i];
+  }
+  __syncthreads();
+  const int64_t nk = nk_old + nd;
+  const int64_t nb = (nk + DEC_BLK - 1) / DEC_BLK;
+  for (int64_t bb = threadIdx.x; bb < nb; bb += blockDim.x) {
+    uint32_t m = 0;
+    const int64_t e = min(nk, (bb + 1) * DEC_BLK);
+    for (int64_t r = bb * DEC_BLK; r < e; ++r) m = max(m, (uint32_t)sjo[r] + 1u);
+    blk[stream * (cap / DEC_BLK) + bb] = (uint16_t)m;
+  }
+}
+
 // ---------------------------------------------------------------- step
 
 namespace {
@@ -423,6 +515,35 @@ int ksd8_rosa_decode_step_launch(const void* const* proj, int dtype, int64_t con
     rosa_decode_step_kernel<16><<<grid, DEC_WARPS * 32, 0, stream>>>(a);
   else
     rosa_decode_step_kernel<32><<<grid, DEC_WARPS * 32, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? KSD8_OK : KSD8_ERR_LAUNCH;
+}
+
+int ksd8_rosa_decode_merge_launch(const uint64_t* kw, int64_t n_streams, int64_t nw,
+                                  int64_t n_old, int64_t n_new, int max_len,
+                                  const uint64_t* sw_in, const uint16_t* sj_in, uint64_t* sw,
+                                  uint16_t* sj, uint16_t* blk, int64_t cap, cudaStream_t stream) {
+  if (n_streams == 0) return KSD8_OK;
+  const int r0 = max_len > 0 ? max_len - 1 : 0;
+  const int64_t dlo = n_old > r0 ? n_old : r0;
+  const int64_t nd = n_new > dlo ? n_new - dlo : 0;
+  int npd = 1;
+  while (npd < nd) npd <<= 1;
+  const int64_t w0 = dlo > 63 ? (dlo >> 6) - 1 : 0;
+  const int64_t nwd = nd > 0 ? ((n_new - 1) >> 6) - w0 + 1 : 0;
+  const size_t smem = (size_t)npd * 12 + 8 + (size_t)nwd * 8;
+  if (smem > 100 * 1024) return KSD8_ERR_UNSUPPORTED;
+  static unsigned attr_done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 32) return KSD8_ERR_UNSUPPORTED;
+  if (!(attr_done & (1u << dev))) {
+    if (cudaFuncSetAttribute(rosa_decode_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             100 * 1024) != cudaSuccess)
+      return KSD8_ERR_LAUNCH;
+    attr_done |= 1u << dev;
+  }
+  rosa_decode_merge_kernel<<<(unsigned)n_streams, 256, smem, stream>>>(
+      kw, nw, n_old, n_new, r0, npd, cap, sw_in, sj_in, sw, sj, blk);
   return cudaGetLastError() == cudaSuccess ? KSD8_OK : KSD8_ERR_LAUNCH;
 }
 

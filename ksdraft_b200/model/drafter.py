@@ -54,6 +54,7 @@ from .rosa import pack_bits
 
 MAX_LEN = 62            # the reference's cap min(62, T - 1) once T >= 63
 DELTA_WORDS = 34        # k words of the appended delta the step kernel holds
+MERGE_MAX = 8192        # appended keys one merge sorts in shared memory
 LN_EPS = 1e-5
 
 
@@ -84,12 +85,23 @@ class RosaDecodeState:
             dst[:, :src.shape[1]].copy_(src)
 
     def build(self, n_keys: int) -> None:
-        """Sort the keys of positions max_len - 1 .. n_keys - 1 into the main run."""
+        """Main run of the keys of positions max_len - 1 .. n_keys - 1: the keys
+        appended since the last build merged into the current run when there is
+        one (a copy of it is the merge's input), else all keys sorted."""
         rows = self.contexts * self.streams
-        _lib.check(_lib.lib().ksd8_rosa_decode_build(
-            self.bits[1].data_ptr(), rows, self.nw, n_keys, MAX_LEN, self.sw.data_ptr(),
-            self.sj.data_ptr(), self.blk.data_ptr(), self.capacity, None,
-            _lib.stream_ptr(self.sw.device)), "rosa_decode_build")
+        lib, stream = _lib.lib(), _lib.stream_ptr(self.sw.device)
+        n_old = self.n_main
+        if MAX_LEN - 1 < n_old <= n_keys and n_keys - n_old <= MERGE_MAX:
+            sw_in, sj_in = self.sw.clone(), self.sj.clone()
+            _lib.check(lib.ksd8_rosa_decode_merge(
+                self.bits[1].data_ptr(), rows, self.nw, n_old, n_keys, MAX_LEN,
+                sw_in.data_ptr(), sj_in.data_ptr(), self.sw.data_ptr(), self.sj.data_ptr(),
+                self.blk.data_ptr(), self.capacity, None, stream), "rosa_decode_merge")
+        else:
+            _lib.check(lib.ksd8_rosa_decode_build(
+                self.bits[1].data_ptr(), rows, self.nw, n_keys, MAX_LEN, self.sw.data_ptr(),
+                self.sj.data_ptr(), self.blk.data_ptr(), self.capacity, None, stream),
+                "rosa_decode_build")
         self.n_main = n_keys
 
     def needs_build(self, t0: int, k_new: int) -> bool:

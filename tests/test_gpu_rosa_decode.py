@@ -100,14 +100,14 @@ def test_decode_rollback_overwrites_appended_bits():
 @pytest.mark.parametrize("kind", ["fair", "runs"])
 def test_match_context_equals_sequence_matcher(kind):
     """The drafter's prefill path: a whole context matched 32 positions at a time
-    through the decode kernels (main-run rebuilds included)."""
+    through the decode kernels (a full main-run build and a merge included)."""
     from ksdraft_b200.model.drafter import RosaDecodeState
     from ksdraft_b200.model.rosa import pack_bits
     gen = torch.Generator().manual_seed(11 + len(kind))
-    B, T = 2, 3000
+    B, T = 2, 5000       # one full build, then one merge of the appended keys
     bits3 = [_bits(kind, B, T, gen).cuda() for _ in range(3)]
     ml_ref, me_ref, out_ref = _full(bits3, B, T)
-    st = RosaDecodeState(B, S, 3008, "cuda")
+    st = RosaDecodeState(B, S, 5056, "cuda")
     st.load_words([pack_bits(b, B, T, S, T * S, S, 1) for b in bits3], T)
     out = torch.empty(B, T, S, device="cuda")
     ml = torch.empty(B * S, T, dtype=torch.int32, device="cuda")
