@@ -376,7 +376,11 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
   }
 
   // 3. per query, the group's lanes together: the latest endpoint in [lo, hi)
-  //    of the main run, the early keys and the delta keys
+  //    of the main run, then the delta keys newest first (a key reaching the
+  //    query's cap ends the scan: no later key is left and none is longer),
+  //    then the early keys that can still be longer than the best so far
+  //    (length <= j + 1, and they lose ties to every later key)
+  const unsigned gmask = DEC_LANES == 32 ? full : (((1u << (DEC_LANES & 31)) - 1u) << gbase);
   int best = 0;
   int64_t bestj = -1;
   for (int i = 0; i < K; ++i) {
@@ -402,29 +406,51 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
         for (int64_t b = b0 + sub; b < b1; b += DEC_LANES) mx = max(mx, (uint32_t)blkr[b]);
       }
       bl = L;
-      bj = (int64_t)mx - 1;   // group maximum taken with the candidates below
+      bj = (int64_t)mx - 1;   // the group maximum is taken below
     }
-    if (active) {
-      // early keys j < min(r0, ti): length also capped at j + 1
-      for (int64_t j = sub; j < r0 && j < ti; j += DEC_LANES) {
-        const int l = min(lcp64(qwi, window_at(&kw0, j)), min(cq, (int)j + 1));
-        if (l > 0 && better(l, j, bl, bj)) { bl = l; bj = j; }
+    // delta keys dlo <= j <= ti - 1, newest first, DEC_LANES at a time; the loop
+    // runs until every group of the warp is done (full-warp ballots)
+    bool done = !active;
+    for (int64_t base = ti - 1; base >= dlo; base -= DEC_LANES) {
+      bool hit = false;
+      if (!done) {
+        const int64_t j = base - sub;
+        if (j >= dlo) {
+          const int64_t wi = (j >> 6) - w0;
+          const int sh = (int)(j & 63) + 1;
+          const uint64_t h = dwords[wi];
+          const uint64_t l0 = (j >> 6) > 0 ? dwords[wi - 1] : 0ull;
+          const uint64_t wk = sh == 64 ? h : ((l0 >> sh) | (h << (64 - sh)));
+          const int l = min(lcp64(qwi, wk), cq);
+          if (l > 0 && better(l, j, bl, bj)) { bl = l; bj = j; }
+          hit = l == cq;
+        }
       }
-      // delta keys dlo <= j <= ti - 1
-      for (int64_t j = dlo + sub; j <= ti - 1; j += DEC_LANES) {
-        const int64_t wi = (j >> 6) - w0;
-        const int sh = (int)(j & 63) + 1;
-        const uint64_t h = dwords[wi];
-        const uint64_t l0 = (j >> 6) > 0 ? dwords[wi - 1] : 0ull;
-        const uint64_t wk = sh == 64 ? h : ((l0 >> sh) | (h << (64 - sh)));
-        const int l = min(lcp64(qwi, wk), cq);
-        if (l > 0 && better(l, j, bl, bj)) { bl = l; bj = j; }
-      }
+      done = done || (__ballot_sync(full, hit) & gmask) != 0u;
+      if (__all_sync(full, done)) break;
     }
-    // group arg-best: longest, then latest (the main-run lanes all carry the
-    // same length, their maximum endpoint wins among them)
+    // the group's best so far: longest, then latest
     unsigned long long packed =
         bl > 0 ? (((unsigned long long)bl << 32) | (unsigned long long)(bj + 1)) : 0ull;
+#pragma unroll
+    for (int o = DEC_LANES / 2; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(full, packed, o);
+      packed = other > packed ? other : packed;
+    }
+    // early keys j < min(r0, ti): only j >= the best length can be longer
+    const int gbest = (int)(packed >> 32);
+    if (active) {
+      int el = 0;
+      int64_t ej = -1;
+      for (int64_t j = gbest + sub; j < r0 && j < ti; j += DEC_LANES) {
+        const int l = min(lcp64(qwi, window_at(&kw0, j)), min(cq, (int)j + 1));
+        if (l > gbest && better(l, j, el, ej)) { el = l; ej = j; }
+      }
+      if (el > 0) {
+        const unsigned long long e = ((unsigned long long)el << 32) | (unsigned long long)(ej + 1);
+        packed = e > packed ? e : packed;
+      }
+    }
 #pragma unroll
     for (int o = DEC_LANES / 2; o > 0; o >>= 1) {
       const unsigned long long other = __shfl_xor_sync(full, packed, o);
