@@ -33,6 +33,8 @@
  *                             of rosa.py:40 _match_payload_sign
  *   ksd8_rosa_match           ksdraft/model/rosa.py:40-98 _match_payload_sign (+ payload multiply of :164)
  *   ksd8_rosa_match_scratch   the same, adaptive matcher with caller scratch
+ *   ksd8_rosa_payload_bwd     the payload gradient of rosa.py:164 through the Int8Linear STE of
+ *                             out_proj (ksdraft/kernels/linear.py:88-94, incl. the scale term)
  *   ksd8_rosa_timemix_quantize ksdraft/model/rosa.py:128-133 _shifted followed by the per-token
  *                             quantisation of Int8Linear.forward (ksdraft/kernels/linear.py:69)
  *   ksd8_adamw_step           torch.optim.AdamW.step over fp32 masters (ksdraft/train/__init__.py:166)
@@ -337,6 +339,18 @@ int ksd8_transfer_bwd(const void* p, int dtype, const float* e, const float* nor
                       const float* dot, int64_t m, int64_t d, float coef, const void* pgrad,
                       const float* first, int64_t t_len, void* dp, float* e_grad, int* status,
                       void* stream);
+
+/* Training hard path, gradient of the Rosa payload: o = payload * sign (M, S)
+ * (the out_proj input, dtype F32 / BF16 / F16), its GS128 codes (M, S) int8,
+ * gx = dL/d(dequantised o) (M, S) fp32, sign (M, S) in o's dtype.  The
+ * Int8Linear STE input gradient do = gx + the GS128 scale term (elements tied
+ * at the group's amax: sign(o) fp16(sum gx * codes) / 127 / n_tied, inside the
+ * clamp range) is reduced to partials[p][s] = sum over the rows of chunk p of
+ * do * sign (n_parts chunks of ceil(M / n_parts) rows); the caller adds the
+ * rows.  streams a multiple of 128, at most 2048. */
+int ksd8_rosa_payload_bwd(const void* o, const int8_t* codes, const float* gx, const void* sign,
+                          int dtype, int64_t m, int64_t streams, float* partials,
+                          int64_t n_parts, int* status, void* stream);
 
 /* ---- incremental Rosa matching (drafting) ----
  *

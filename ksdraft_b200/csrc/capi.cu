@@ -64,6 +64,8 @@ int ksd8_rosa_decode_step_launch(const void* const*, int, int64_t, int64_t, int6
                                  int64_t, int, int32_t*, int32_t*, int64_t, const int64_t*,
                                  cudaStream_t);
 int ksd8_rosa_decode_limits(int64_t*, int64_t*, int64_t*);
+int ksd8_rosa_payload_bwd_launch(const void*, const int8_t*, const float*, const void*, int,
+                                 int64_t, int64_t, float*, int64_t, cudaStream_t);
 int ksd8_rosa_decode_merge_launch(const uint64_t*, int64_t, int64_t, int64_t, int64_t, int,
                                   const uint64_t*, const uint16_t*, uint64_t*, uint16_t*,
                                   uint16_t*, int64_t, cudaStream_t);
@@ -685,4 +687,18 @@ int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* pr
                                              max_len, bits, nw, sw, sj, blk, cap, payload, out,
                                              out_cs, out_dtype, match_len, match_end, ml_rs,
                                              pos, S(stream)));
+}
+
+int ksd8_rosa_payload_bwd(const void* o, const int8_t* codes, const float* gx, const void* sign,
+                          int dtype, int64_t m, int64_t streams, float* partials,
+                          int64_t n_parts, int* status, void* stream) {
+  (void)status;
+  if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
+  if (m < 0 || streams <= 0 || streams % 128 != 0 || streams > 2048) return KSD8_ERR_SHAPE;
+  if (n_parts <= 0 || n_parts > INT32_MAX || !partials) return KSD8_ERR_ARG;
+  if (m > 0 && (!o || !codes || !gx || !sign)) return KSD8_ERR_ARG;
+  if (m > 0 && ((reinterpret_cast<uintptr_t>(gx) & 15) || (reinterpret_cast<uintptr_t>(codes) & 3)))
+    return KSD8_ERR_ALIGN;
+  return finish(ksd8_rosa_payload_bwd_launch(o, codes, gx, sign, dtype, m, streams, partials,
+                                             n_parts, S(stream)));
 }

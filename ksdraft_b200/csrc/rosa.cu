@@ -829,9 +829,100 @@ __global__ void __launch_bounds__(32) grad_clip_coef_kernel(const float* partial
   }
 }
 
+// Backward of the Rosa output path into the payload (training hard path,
+// rosa.py:164-165 under the Int8Linear STE of out_proj, linear.py:88-94): with
+// gx = dL/d(dequantised out_proj input) (M, S) fp32, o = payload * sign (the
+// out_proj input) and its GS128 codes, the STE input gradient is
+//   do = gx + [|o| == amax_g] sign(o) fp16(sum_g gx * codes) / 127 / n_tied
+// (the scale gradient of quant.py:47-49, only inside the clamp range), and
+//   d payload[s] = sum_t do[t, s] * sign[t, s].
+// One warp per 128-stream group, a thread owns 4 streams; CTA rows
+// [blockIdx.x * rpc, +rpc); per-CTA column sums into partials (gridDim, S).
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__global__ void __launch_bounds__(512) rosa_payload_bwd_kernel(
+    const T* __restrict__ o, const int8_t* __restrict__ codes, const float* __restrict__ gx,
+    const T* __restrict__ sign, int64_t m, int S, int64_t rpc, float* __restrict__ partials) {
+  const int tid = threadIdx.x;
+  const int col = tid * 4;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int64_t r0 = (int64_t)blockIdx.x * rpc;
+  const int64_t r1 = min(m, r0 + rpc);
+  for (int64_t row = r0; row < r1; ++row) {
+    const int64_t off = row * S + col;
+    float ov[4], sv[4], gv[4], cv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ov[i] = to_f32(o[off + i]);
+      sv[i] = to_f32(sign[off + i]);
+    }
+    const float4 g4 = *reinterpret_cast<const float4*>(gx + off);
+    gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+    const char4 c4 = *reinterpret_cast<const char4*>(codes + off);
+    cv[0] = c4.x; cv[1] = c4.y; cv[2] = c4.z; cv[3] = c4.w;
+    float am = 0.f, dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      am = fmaxf(am, fabsf(ov[i]));
+      dot += gv[i] * cv[i];
+    }
+    am = warp_max(am);
+    dot = warp_sum(dot);
+    float nt = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) nt += fabsf(ov[i]) == am ? 1.f : 0.f;
+    nt = warp_sum(nt);
+    const float g16 = __half2float(__float2half_rn(dot));
+    const float s32 = am / 127.f;
+    const bool inside = s32 >= 5.9604644775390625e-08f && s32 <= 65504.f;
+    const float share = inside ? g16 / 127.f / nt : 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float sg = ov[i] > 0.f ? 1.f : (ov[i] < 0.f ? -1.f : 0.f);
+      const float d = gv[i] + (fabsf(ov[i]) == am ? sg * share : 0.f);
+      acc[i] += d * sv[i];
+    }
+  }
+  float* pp = partials + (int64_t)blockIdx.x * S + col;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) pp[i] = acc[i];
+}
+
 }  // namespace ksd8
 
 using namespace ksd8;
+
+int ksd8_rosa_payload_bwd_launch(const void* o, const int8_t* codes, const float* gx,
+                                 const void* sign, int dtype, int64_t m, int64_t streams,
+                                 float* partials, int64_t n_parts, cudaStream_t stream) {
+  if (m == 0) {
+    return cudaMemsetAsync(partials, 0, sizeof(float) * n_parts * streams, stream) == cudaSuccess
+               ? KSD8_OK : KSD8_ERR_LAUNCH;
+  }
+  const int64_t rpc = (m + n_parts - 1) / n_parts;
+  const unsigned threads = (unsigned)(streams / 4);
+  switch (dtype) {
+    case KSD8_F32:
+      rosa_payload_bwd_kernel<float><<<(unsigned)n_parts, threads, 0, stream>>>(
+          (const float*)o, codes, gx, (const float*)sign, m, (int)streams, rpc, partials);
+      break;
+    case KSD8_BF16:
+      rosa_payload_bwd_kernel<__nv_bfloat16><<<(unsigned)n_parts, threads, 0, stream>>>(
+          (const __nv_bfloat16*)o, codes, gx, (const __nv_bfloat16*)sign, m, (int)streams, rpc,
+          partials);
+      break;
+    case KSD8_F16:
+      rosa_payload_bwd_kernel<__half><<<(unsigned)n_parts, threads, 0, stream>>>(
+          (const __half*)o, codes, gx, (const __half*)sign, m, (int)streams, rpc, partials);
+      break;
+    default:
+      return KSD8_ERR_DTYPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? KSD8_OK : KSD8_ERR_LAUNCH;
+}
 
 int ksd8_adamw_multi_launch(int count, float* const* params, const void* const* grads, int gdt,
                             float* const* m, float* const* v, const int64_t* numels, float lr,
