@@ -32,9 +32,9 @@ namespace ksd8 {
 namespace {
 
 constexpr int DEC_BLK = 64;        // ranks per range-maximum block
-constexpr int DEC_WARPS = 4;       // warps per CTA in the step kernel
+constexpr int DEC_WARPS = 8;       // streams per CTA in the step kernel
 constexpr int DEC_MAX_NEW = 32;    // new positions per step
-constexpr int DEC_TOP_PER_WARP = 1024;  // sampled main-run windows in shared memory per warp
+constexpr int DEC_MAX_TOP = 512;   // sampled windows of the main run held in shared memory
 constexpr int DEC_DELTA_WORDS = 34;  // k words of the delta region held in shared memory
 
 // window of position t from bit words w (global or shared), bits before 0 are 0
@@ -272,31 +272,19 @@ __device__ __forceinline__ bool proj_positive(const void* p, int64_t i) {
   return as_float<T>(reinterpret_cast<const T*>(p)[i]) > 0.f;
 }
 
-// A warp serves 32 / LANES (context, stream) rows with LANES lanes each (LANES
-// the power of two >= k_new, at least 8): lane `sub` of a group owns the new
-// position t0 + sub for the searches, and the group's lanes share the scans of
-// each query.  Small blocks thus keep every lane of the searches busy.
-template <int LANES>
 __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(DecodeArgs a) {
-  constexpr int DEC_LANES = LANES, DEC_GROUPS = 32 / LANES;
-  constexpr int TOP = DEC_TOP_PER_WARP / DEC_GROUPS;   // sampled windows per row
-  __shared__ uint64_t top_all[DEC_WARPS][DEC_GROUPS][TOP];
-  __shared__ uint64_t dwords_all[DEC_WARPS][DEC_GROUPS][DEC_DELTA_WORDS];
+  __shared__ uint64_t top_all[DEC_WARPS][DEC_MAX_TOP];
+  __shared__ uint64_t dwords_all[DEC_WARPS][DEC_DELTA_WORDS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int grp = lane / DEC_LANES, sub = lane % DEC_LANES, gbase = grp * DEC_LANES;
-  const int64_t rows = a.contexts * a.streams;
-  const int64_t st0 = ((int64_t)blockIdx.x * DEC_WARPS + warp) * DEC_GROUPS;
-  if (st0 >= rows) return;  // whole warp; no CTA barrier below
-  const int64_t st = st0 + grp;
-  const bool active = st < rows;   // idle groups still take part in the shuffles
+  const int64_t st = (int64_t)blockIdx.x * DEC_WARPS + warp;
+  if (st >= a.contexts * a.streams) return;  // whole warp; no CTA barrier below
   const unsigned full = 0xffffffffu;
-  const int64_t c = active ? st / a.streams : 0, s = active ? st % a.streams : 0;
+  const int64_t c = st / a.streams, s = st % a.streams;
   const int K = (int)a.k_new;
   const int64_t t0 = a.pos ? a.pos[0] : a.t0;
   const int64_t n_main = a.pos ? a.pos[1] : a.n_main;
-  uint64_t* top = top_all[warp][grp];
-  uint64_t* dwords = dwords_all[warp][grp];
-  const int64_t row = active ? st : 0;
+  uint64_t* top = top_all[warp];
+  uint64_t* dwords = dwords_all[warp];
 
   // 1. append the new bits (proj > 0, rosa.py:156-158) at positions t0 .. t0 + K - 1
   const bool append = a.proj[0] != nullptr;
@@ -304,24 +292,23 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
 #pragma unroll
   for (int q = 0; q < 3; ++q) {
     bool bit = false;
-    if (append && active && sub < K) {
-      const int64_t i = (c * a.k_new + sub) * a.streams + s;
+    if (append && lane < K) {
+      const int64_t i = (c * a.k_new + lane) * a.streams + s;
       switch (a.dtype) {
         case KSD8_F32: bit = proj_positive<float>(a.proj[q], i); break;
         case KSD8_BF16: bit = proj_positive<__nv_bfloat16>(a.proj[q], i); break;
         default: bit = proj_positive<__half>(a.proj[q], i); break;
       }
     }
-    m[q] = DEC_LANES == 32 ? __ballot_sync(full, bit)
-                           : (__ballot_sync(full, bit) >> gbase) & ((1u << (DEC_LANES & 31)) - 1u);
+    m[q] = __ballot_sync(full, bit);
   }
-  if (append && active && sub == 0) {
+  if (append && lane == 0) {
     const int64_t wi = t0 >> 6;
     const int off = (int)(t0 & 63);
-    const uint64_t M = (1ull << K) - 1ull;
+    const uint64_t M = (K == 64) ? ~0ull : ((1ull << K) - 1ull);
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
-      uint64_t* w = a.bits[q] + row * a.nw;
+      uint64_t* w = a.bits[q] + st * a.nw;
       w[wi] = (w[wi] & ~(M << off)) | ((uint64_t)m[q] << off);
       if (off + K > 64) {
         const int rs = 64 - off;
@@ -331,32 +318,31 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
   }
   __syncwarp();
 
-  const uint64_t* qrow = a.bits[0] + row * a.nw;
-  const uint64_t* krow = a.bits[1] + row * a.nw;
-  const uint64_t* vrow = a.bits[2] + row * a.nw;
+  const uint64_t* qrow = a.bits[0] + st * a.nw;
+  const uint64_t* krow = a.bits[1] + st * a.nw;
+  const uint64_t* vrow = a.bits[2] + st * a.nw;
   const int r0 = a.max_len > 0 ? a.max_len - 1 : 0;
   const int64_t nk = n_main > r0 ? n_main - r0 : 0;     // main run size
   const int ntop = (int)((nk + DEC_BLK - 1) / DEC_BLK);
-  const uint64_t* swr = a.sw + row * a.cap;
-  const uint16_t* sjr = a.sj + row * a.cap;
-  const uint16_t* blkr = a.blk + row * (a.cap / DEC_BLK);
-  if (active)
-    for (int b = sub; b < ntop; b += DEC_LANES) top[b] = swr[(int64_t)b * DEC_BLK];
+  const uint64_t* swr = a.sw + st * a.cap;
+  const uint16_t* sjr = a.sj + st * a.cap;
+  const uint16_t* blkr = a.blk + st * (a.cap / DEC_BLK);
+  for (int b = lane; b < ntop; b += 32) top[b] = swr[(int64_t)b * DEC_BLK];
   // delta keys j in [dlo, t0 + K - 2]; their windows read words w0 .. of k
   const int64_t dlo = max(n_main, (int64_t)r0);
   const int64_t dhi = t0 + K - 2;
   const int64_t w0 = dlo > 63 ? (dlo >> 6) - 1 : 0;
-  if (active && dhi >= dlo) {
+  if (dhi >= dlo) {
     const int64_t nwd = (dhi >> 6) - w0 + 1;
-    for (int64_t i = sub; i < nwd; i += DEC_LANES) dwords[i] = krow[w0 + i];
+    for (int64_t i = lane; i < nwd; i += 32) dwords[i] = krow[w0 + i];
   }
   const uint64_t kw0 = krow[0];  // every early key's window lies in word 0
   __syncwarp();
 
   // 2. main run, one query per lane: longest match at the sorted neighbours,
   //    then the rank interval sharing that prefix
-  const int64_t t = t0 + sub;
-  const bool valid = active && sub < K;
+  const int64_t t = t0 + lane;
+  const bool valid = lane < K;
   const uint64_t wq = valid ? window_at(qrow, t) : 0ull;
   const int capq = valid ? (int)min((int64_t)a.max_len, t) : 0;
   int Lm = 0;
@@ -375,90 +361,62 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
     }
   }
 
-  // 3. per query, the group's lanes together: the latest endpoint in [lo, hi)
-  //    of the main run, then the delta keys newest first (a key reaching the
-  //    query's cap ends the scan: no later key is left and none is longer),
-  //    then the early keys that can still be longer than the best so far
-  //    (length <= j + 1, and they lose ties to every later key)
-  const unsigned gmask = DEC_LANES == 32 ? full : (((1u << (DEC_LANES & 31)) - 1u) << gbase);
+  // 3. per query, the warp together: the latest endpoint in [lo, hi) of the
+  //    main run, the early keys and the delta keys
   int best = 0;
   int64_t bestj = -1;
   for (int i = 0; i < K; ++i) {
-    const int src = gbase + i;
-    const int L = __shfl_sync(full, Lm, src);
-    const int64_t ilo = __shfl_sync(full, lo, src), ihi = __shfl_sync(full, hi, src);
-    const uint64_t qwi = __shfl_sync(full, wq, src);
-    const int cq = __shfl_sync(full, capq, src);
+    const int L = __shfl_sync(full, Lm, i);
+    const int64_t ilo = __shfl_sync(full, lo, i), ihi = __shfl_sync(full, hi, i);
+    const uint64_t qwi = __shfl_sync(full, wq, i);
+    const int cq = __shfl_sync(full, capq, i);
     const int64_t ti = t0 + i;
     int bl = 0;
     int64_t bj = -1;
-    if (active && L > 0) {
+    if (L > 0) {
       // max of j + 1 over ranks [ilo, ihi): partial blocks and whole blocks
       uint32_t mx = 0;
       const int64_t b0 = (ilo + DEC_BLK - 1) / DEC_BLK, b1 = ihi / DEC_BLK;
       if (b0 >= b1) {
-        for (int64_t r = ilo + sub; r < ihi; r += DEC_LANES) mx = max(mx, (uint32_t)sjr[r] + 1u);
+        for (int64_t r = ilo + lane; r < ihi; r += 32) mx = max(mx, (uint32_t)sjr[r] + 1u);
       } else {
-        for (int64_t r = ilo + sub; r < b0 * DEC_BLK; r += DEC_LANES)
+        for (int64_t r = ilo + lane; r < b0 * DEC_BLK; r += 32)
           mx = max(mx, (uint32_t)sjr[r] + 1u);
-        for (int64_t r = b1 * DEC_BLK + sub; r < ihi; r += DEC_LANES)
+        for (int64_t r = b1 * DEC_BLK + lane; r < ihi; r += 32)
           mx = max(mx, (uint32_t)sjr[r] + 1u);
-        for (int64_t b = b0 + sub; b < b1; b += DEC_LANES) mx = max(mx, (uint32_t)blkr[b]);
+        for (int64_t b = b0 + lane; b < b1; b += 32) mx = max(mx, (uint32_t)blkr[b]);
       }
+      mx = __reduce_max_sync(full, mx);
       bl = L;
-      bj = (int64_t)mx - 1;   // the group maximum is taken below
+      bj = (int64_t)mx - 1;
     }
-    // delta keys dlo <= j <= ti - 1, newest first, DEC_LANES at a time; the loop
-    // runs until every group of the warp is done (full-warp ballots)
-    bool done = !active;
-    for (int64_t base = ti - 1; base >= dlo; base -= DEC_LANES) {
-      bool hit = false;
-      if (!done) {
-        const int64_t j = base - sub;
-        if (j >= dlo) {
-          const int64_t wi = (j >> 6) - w0;
-          const int sh = (int)(j & 63) + 1;
-          const uint64_t h = dwords[wi];
-          const uint64_t l0 = (j >> 6) > 0 ? dwords[wi - 1] : 0ull;
-          const uint64_t wk = sh == 64 ? h : ((l0 >> sh) | (h << (64 - sh)));
-          const int l = min(lcp64(qwi, wk), cq);
-          if (l > 0 && better(l, j, bl, bj)) { bl = l; bj = j; }
-          hit = l == cq;
-        }
-      }
-      done = done || (__ballot_sync(full, hit) & gmask) != 0u;
-      if (__all_sync(full, done)) break;
+    // early keys j < min(r0, ti): length also capped at j + 1
+    for (int64_t j = lane; j < r0 && j < ti; j += 32) {
+      const int l = min(lcp64(qwi, window_at(&kw0, j)), min(cq, (int)j + 1));
+      if (l > 0 && better(l, j, bl, bj)) { bl = l; bj = j; }
     }
-    // the group's best so far: longest, then latest
-    unsigned long long packed =
+    // delta keys dlo <= j <= ti - 1
+    for (int64_t j = dlo + lane; j <= ti - 1; j += 32) {
+      const int64_t wi = (j >> 6) - w0;
+      const int sh = (int)(j & 63) + 1;
+      const uint64_t h = dwords[wi];
+      const uint64_t l0 = (j >> 6) > 0 ? dwords[wi - 1] : 0ull;
+      const uint64_t wk = sh == 64 ? h : ((l0 >> sh) | (h << (64 - sh)));
+      const int l = min(lcp64(qwi, wk), cq);
+      if (l > 0 && better(l, j, bl, bj)) { bl = l; bj = j; }
+    }
+    // warp arg-best: longest, then latest
+    const unsigned long long packed =
         bl > 0 ? (((unsigned long long)bl << 32) | (unsigned long long)(bj + 1)) : 0ull;
+    unsigned long long top_packed = packed;
 #pragma unroll
-    for (int o = DEC_LANES / 2; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(full, packed, o);
-      packed = other > packed ? other : packed;
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(full, top_packed, o);
+      top_packed = other > top_packed ? other : top_packed;
     }
-    // early keys j < min(r0, ti): only j >= the best length can be longer
-    const int gbest = (int)(packed >> 32);
-    if (active) {
-      int el = 0;
-      int64_t ej = -1;
-      for (int64_t j = gbest + sub; j < r0 && j < ti; j += DEC_LANES) {
-        const int l = min(lcp64(qwi, window_at(&kw0, j)), min(cq, (int)j + 1));
-        if (l > gbest && better(l, j, el, ej)) { el = l; ej = j; }
-      }
-      if (el > 0) {
-        const unsigned long long e = ((unsigned long long)el << 32) | (unsigned long long)(ej + 1);
-        packed = e > packed ? e : packed;
-      }
-    }
-#pragma unroll
-    for (int o = DEC_LANES / 2; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(full, packed, o);
-      packed = other > packed ? other : packed;
-    }
-    if (sub == i) {
-      best = (int)(packed >> 32);
-      bestj = packed ? (int64_t)(packed & 0xFFFFFFFFull) - 1 : -1;
+    if (lane == i) {
+      best = (int)(top_packed >> 32);
+      bestj = top_packed ? (int64_t)(top_packed & 0xFFFFFFFFull) - 1 : -1;
     }
   }
 
@@ -470,15 +428,15 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
       sign = ((vrow[succ >> 6] >> (succ & 63)) & 1ull) ? 1.f : -1.f;
     }
     const float o = (a.payload ? a.payload[s] : 1.f) * sign;
-    const int64_t oo = c * a.out_cs + sub * a.streams + s;
+    const int64_t oo = c * a.out_cs + lane * a.streams + s;
     if (a.out_dtype == KSD8_F32)
       reinterpret_cast<float*>(a.out)[oo] = o;
     else if (a.out_dtype == KSD8_BF16)
       reinterpret_cast<__nv_bfloat16*>(a.out)[oo] = __float2bfloat16_rn(o);
     else
       reinterpret_cast<__half*>(a.out)[oo] = __float2half_rn(o);
-    if (a.match_len) a.match_len[st * a.ml_rs + sub] = best;
-    if (a.match_end) a.match_end[st * a.ml_rs + sub] = (int32_t)bestj;
+    if (a.match_len) a.match_len[st * a.ml_rs + lane] = best;
+    if (a.match_end) a.match_end[st * a.ml_rs + lane] = (int32_t)bestj;
   }
 }
 
@@ -532,15 +490,8 @@ int ksd8_rosa_decode_step_launch(const void* const* proj, int dtype, int64_t con
   a.match_len = match_len; a.match_end = match_end; a.ml_rs = ml_rs;
   const int64_t n = contexts * streams;
   if (n == 0 || k_new == 0) return KSD8_OK;
-  const int lanes = k_new <= 8 ? 8 : (k_new <= 16 ? 16 : 32);
-  const int64_t per_cta = (int64_t)DEC_WARPS * (32 / lanes);
-  const unsigned grid = (unsigned)((n + per_cta - 1) / per_cta);
-  if (lanes == 8)
-    rosa_decode_step_kernel<8><<<grid, DEC_WARPS * 32, 0, stream>>>(a);
-  else if (lanes == 16)
-    rosa_decode_step_kernel<16><<<grid, DEC_WARPS * 32, 0, stream>>>(a);
-  else
-    rosa_decode_step_kernel<32><<<grid, DEC_WARPS * 32, 0, stream>>>(a);
+  rosa_decode_step_kernel<<<(unsigned)((n + DEC_WARPS - 1) / DEC_WARPS), DEC_WARPS * 32, 0,
+                            stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? KSD8_OK : KSD8_ERR_LAUNCH;
 }
 
@@ -576,7 +527,7 @@ int ksd8_rosa_decode_merge_launch(const uint64_t* kw, int64_t n_streams, int64_t
 // host-side limits of the step kernel (shared with the C ABI checks)
 int ksd8_rosa_decode_limits(int64_t* max_new, int64_t* max_main, int64_t* max_delta_words) {
   *max_new = DEC_MAX_NEW;
-  *max_main = (int64_t)(DEC_TOP_PER_WARP / 4) * DEC_BLK;   // rows of 8 lanes: 4 per warp
+  *max_main = (int64_t)DEC_MAX_TOP * DEC_BLK;
   *max_delta_words = DEC_DELTA_WORDS;
   return KSD8_OK;
 }
