@@ -55,7 +55,6 @@ import torch.nn.functional as F
 from .. import _lib
 from ..kernels.gemm import _validate_and_pad, gemm_out
 from ..kernels.ks3_int8 import KS3Int8Cell, ks3_backward, ks3_train_forward, ks3_weights
-from ..kernels.linear import ste_input_grad
 from ..kernels.quant import GROUP_SIZE, dequantize_last_dim, quantize_cols, quantize_last_dim
 from ..model.head import ce_grad, ce_grad_quant, ce_partials, combine_ce_partials
 from ..model.rosa import _default_max_len, match_words, pack_bits
@@ -418,9 +417,16 @@ class DraftTrainStep:
             torch.matmul(dr32.t(), xd, out=self.flat.g(pre + "out_proj.weight"))
             gx = dr32 @ dequantize_last_dim(wq, ws)                 # (M, S)
         torch.sum(dr32, 0, out=self.flat.g(pre + "out_proj.bias"))
-        do = ste_input_grad(o.float(), oq, gx)
-        # o = (payload * sign).to(act): d payload[s] = sum over tokens of do * sign
-        torch.sum(do * sign.reshape(B * T, S).float(), 0, out=self.flat.g(pre + "payload"))
+        # o = (payload * sign).to(act): d payload[s] = sum over tokens of do * sign,
+        # do = the STE input gradient of gx (incl. the GS128 scale term), one kernel
+        M = B * T
+        n_parts = max(1, min(M, 4 * torch.cuda.get_device_properties(self.dev)
+                                 .multi_processor_count))
+        parts = torch.empty(n_parts, S, dtype=torch.float32, device=self.dev)
+        _lib.check(_lib.lib().ksd8_rosa_payload_bwd(
+            o.data_ptr(), oq.data_ptr(), gx.data_ptr(), sign.data_ptr(), _lib.dtype_code(o), M, S,
+            parts.data_ptr(), n_parts, None, _lib.stream_ptr(self.dev)), "rosa_payload_bwd")
+        torch.sum(parts, 0, out=self.flat.g(pre + "payload"))
 
     def _dspine_weights(self, layer: int):
         return {n: self.flat.p(f"blocks.{layer}.{_dspine_name(n)}") for n in DSPINE}
