@@ -17,7 +17,7 @@ def test_payload_grad_matches_ste_formula(act):
     g = torch.Generator().manual_seed(3)
     M, S = 1000, 256
     payload = 1.0 + 0.2 * torch.randn(S, generator=g)
-    payload[5] = payload[9] = payload[100]          # ties at a group's maximum
+    payload[5] = payload[9] = payload[100] = 3.0     # three elements tied at the group maximum
     payload[130] = -payload[140].abs() - 2.0        # a negative group maximum
     sign = torch.where(torch.rand(M, S, generator=g) > 0.5, 1.0, -1.0)
     o = (payload * sign).to(act).cuda()
