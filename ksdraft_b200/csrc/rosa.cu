@@ -21,6 +21,8 @@
 // latest one, so only strictly longer matches replace the current best;
 // a lane stops once best == min(max_len, t) and the warp stops when no lane
 // can still improve (remaining j are too short: length <= j+1).
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace ksd8 {
@@ -472,6 +474,20 @@ __device__ __forceinline__ int rs_lower_bound(const uint64_t* sw, int np, uint64
   return (pos == np - 1 && sw[pos] < key) ? np : pos;
 }
 
+// rs_lower_bound of two keys at once: the two searches are independent, so
+// their shared-memory loads overlap
+__device__ __forceinline__ void rs_lower_bound2(const uint64_t* sw, int np, uint64_t k1,
+                                                uint64_t k2, int& r1, int& r2) {
+  int p1 = 0, p2 = 0;
+  for (int step = np >> 1; step > 0; step >>= 1) {
+    const uint64_t a = sw[p1 + step - 1], b = sw[p2 + step - 1];
+    if (a < k1) p1 += step;
+    if (b < k2) p2 += step;
+  }
+  r1 = (p1 == np - 1 && sw[p1] < k1) ? np : p1;
+  r2 = (p2 == np - 1 && sw[p2] < k2) ? np : p2;
+}
+
 // largest inserted rank < r (-1 if none); bitmap words bm (32 bits), summary sm[2]
 __device__ __forceinline__ int rs_pred(const uint32_t* bm, const uint64_t* sm, int r) {
   if (r <= 0) return -1;
@@ -552,19 +568,19 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchA
     SJ[i] = real ? (uint16_t)(r0 + i) : (uint16_t)0xFFFFu;
   }
   __syncwarp();
-  // bitonic sort of (SW, SJ) ascending
+  // bitonic sort of (SW, SJ) ascending; each lane takes compare-exchange pairs
+  // (i, i + jj), i with bit jj clear, so no lane idles on the upper halves
   for (int k = 2; k <= np; k <<= 1) {
     for (int jj = k >> 1; jj > 0; jj >>= 1) {
-      for (int i = lane; i < np; i += 32) {
-        const int l = i ^ jj;
-        if (l > i) {
-          const bool up = (i & k) == 0;
-          const uint64_t wi = SW[i], wl = SW[l];
-          const uint16_t ji = SJ[i], jl = SJ[l];
-          if (rs_less(wl, jl, wi, ji) == up) {
-            SW[i] = wl; SW[l] = wi;
-            SJ[i] = jl; SJ[l] = ji;
-          }
+      for (int pr = lane; pr < (np >> 1); pr += 32) {
+        const int i = ((pr & ~(jj - 1)) << 1) | (pr & (jj - 1));
+        const int l = i | jj;
+        const bool up = (i & k) == 0;
+        const uint64_t wi = SW[i], wl = SW[l];
+        const uint16_t ji = SJ[i], jl = SJ[l];
+        if (rs_less(wl, jl, wi, ji) == up) {
+          SW[i] = wl; SW[l] = wi;
+          SJ[i] = jl; SJ[l] = ji;
         }
       }
       __syncwarp();
@@ -598,8 +614,9 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchA
       if (L > 0) {
         const uint64_t pre = L >= 64 ? wq : (wq >> (64 - L)) << (64 - L);
         const uint64_t last = L >= 64 ? wq : pre | (~0ull >> L);
-        const int lo = rs_lower_bound(SW, np, pre);
-        const int hi = last == ~0ull ? np : rs_lower_bound(SW, np, last + 1);  // exclusive
+        int lo, hi;   // [lo, hi): the ranks sharing the top L bits
+        rs_lower_bound2(SW, np, pre, last == ~0ull ? last : last + 1, lo, hi);
+        if (last == ~0ull) hi = np;
         int res = 0;
         for (int l = lo + np, h = hi + np; l < h; l >>= 1, h >>= 1) {
           if (l & 1) res = max(res, (int)seg[l++]);
@@ -1033,6 +1050,18 @@ static int launch_chunk(const MatchArgs& a, int64_t t_len, int dev, int algo,
 #define KSD8_ROSA_REDO_BUDGET 4
 #endif
 
+// Chain steps per position (average, after the first 96 positions) that the
+// chunked matcher spends on a stream before handing it to the sorted-key one;
+// KSD8_ROSA_REDO_BUDGET in the environment overrides the compiled default.
+static int redo_budget() {
+  static const int b = [] {
+    const char* e = std::getenv("KSD8_ROSA_REDO_BUDGET");
+    const int v = e ? std::atoi(e) : 0;
+    return v > 0 ? v : KSD8_ROSA_REDO_BUDGET;
+  }();
+  return b;
+}
+
 int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
                            int64_t batch, int64_t streams, int64_t t_len, int max_len,
                            const float* payload, void* out, int out_dtype, int64_t ob, int64_t ot,
@@ -1065,7 +1094,7 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
     // adaptive: chunked prefix tables, degenerate streams redone by the sorted kernel
     if (cudaMemsetAsync(redo, 0, sizeof(int32_t), stream) != cudaSuccess) return KSD8_ERR_LAUNCH;
     a.redo = redo;
-    a.redo_budget = KSD8_ROSA_REDO_BUDGET;
+    a.redo_budget = redo_budget();
   }
   if (algo == 3 || a.redo) {
     if (sorted_ok) {
