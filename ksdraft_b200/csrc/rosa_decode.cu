@@ -92,16 +92,15 @@ __global__ void __launch_bounds__(256) rosa_decode_build_kernel(const uint64_t* 
   __syncthreads();
   for (int k = 2; k <= np; k <<= 1) {
     for (int jj = k >> 1; jj > 0; jj >>= 1) {
-      for (int i = threadIdx.x; i < np; i += blockDim.x) {
-        const int l = i ^ jj;
-        if (l > i) {
-          const bool up = (i & k) == 0;
-          const uint64_t wi = W[i], wl = W[l];
-          const uint32_t ji = J[i], jl = J[l];
-          if (key_less(wl, jl, wi, ji) == up) {
-            W[i] = wl; W[l] = wi;
-            J[i] = jl; J[l] = ji;
-          }
+      for (int pr = threadIdx.x; pr < (np >> 1); pr += blockDim.x) {   // pairs (i, i + jj)
+        const int i = ((pr & ~(jj - 1)) << 1) | (pr & (jj - 1));
+        const int l = i | jj;
+        const bool up = (i & k) == 0;
+        const uint64_t wi = W[i], wl = W[l];
+        const uint32_t ji = J[i], jl = J[l];
+        if (key_less(wl, jl, wi, ji) == up) {
+          W[i] = wl; W[l] = wi;
+          J[i] = jl; J[l] = ji;
         }
       }
       __syncthreads();
@@ -162,16 +161,15 @@ __global__ void __launch_bounds__(256) rosa_decode_merge_kernel(
   __syncthreads();
   for (int k = 2; k <= npd; k <<= 1) {
     for (int jj = k >> 1; jj > 0; jj >>= 1) {
-      for (int i = threadIdx.x; i < npd; i += blockDim.x) {
-        const int l = i ^ jj;
-        if (l > i) {
-          const bool up = (i & k) == 0;
-          const uint64_t wi = W[i], wl = W[l];
-          const uint32_t ji = J[i], jl = J[l];
-          if (key_less(wl, jl, wi, ji) == up) {
-            W[i] = wl; W[l] = wi;
-            J[i] = jl; J[l] = ji;
-          }
+      for (int pr = threadIdx.x; pr < (npd >> 1); pr += blockDim.x) {   // pairs (i, i + jj)
+        const int i = ((pr & ~(jj - 1)) << 1) | (pr & (jj - 1));
+        const int l = i | jj;
+        const bool up = (i & k) == 0;
+        const uint64_t wi = W[i], wl = W[l];
+        const uint32_t ji = J[i], jl = J[l];
+        if (key_less(wl, jl, wi, ji) == up) {
+          W[i] = wl; W[l] = wi;
+          J[i] = jl; J[l] = ji;
         }
       }
       __syncthreads();
