@@ -977,6 +977,22 @@ def profile_case_fn(case: str, dev):
         out = torch.empty(B, T, S, dtype=torch.bfloat16, device=dev)
         fn = lambda: match_words(*words, B, S, T, 62, out=out,  # noqa: E731
                                  strides=(T * S, S, 1))
+    elif case == "decode_step":
+        # config 5's incremental match of one layer: 64 contexts x 512 streams
+        # matched up to 8192 positions (fair bits), then blocks of 8 appended
+        from ksdraft_b200.model.drafter import RosaDecodeState
+        from ksdraft_b200.model.rosa import pack_bits
+        C, S, T0, k = 64, 512, 8192, 8
+        bits = [(torch.rand(C, T0, S, device=dev, generator=g) > 0.5).to(torch.int8)
+                for _ in range(3)]
+        st = RosaDecodeState(C, S, T0 + 512, dev)
+        st.load_words([pack_bits(b, C, T0, S, T0 * S, S, 1) for b in bits], T0)
+        del bits
+        st.build(T0)
+        projs = [torch.randn(C, k, S, device=dev, generator=g) for _ in range(3)]
+        pay = torch.ones(S, device=dev)
+        out = torch.empty(C, k, S, dtype=torch.bfloat16, device=dev)
+        fn = lambda: st.step(projs, T0, pay, out)  # noqa: E731  (re-appends the same block)
     elif case == "rosa_mixer":
         # config 3 end to end: RosaMixer(1536, 512) after to_int8 (Int8Linear q/k/v/out
         # projections N(0, 0.02)), evaluation forward on x = E[ids], E bf16 N(0, 1)
