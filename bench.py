@@ -1,4 +1,4 @@
-"""Benchmark: the KSDraft INT8 training step (BASELINE config 4 by default).
+"""Benchmark: the KSDraft INT8 training step (benchmark config 4 by default).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
                     [--workload config4|config2]
@@ -59,7 +59,7 @@ DITHER = 0.5
 
 def config4(n: int, per_gpu: int | None = None) -> dict:
     per_gpu = C4_BATCH // n if per_gpu is None else per_gpu
-    return {"workload": "BASELINE config 4: full KSDraft INT8 training step, 24 layers, "
+    return {"workload": "benchmark config 4: full KSDraft INT8 training step, 24 layers, "
                         "d_model=1536, vocab=150144, 512 Rosa streams, 5888 KS3 charts, "
                         + (f"batch {per_gpu} x 2048 tokens per GPU" if per_gpu * n != C4_BATCH
                            else f"global batch {C4_BATCH} x 2048 tokens ({per_gpu} per GPU)")
@@ -73,7 +73,7 @@ def config4(n: int, per_gpu: int | None = None) -> dict:
 
 
 def config(n: int) -> dict:
-    return {"workload": "BASELINE config 2: one KS3 decoder layer INT8 fwd+bwd (+DP all-reduce "
+    return {"workload": "benchmark config 2: one KS3 decoder layer INT8 fwd+bwd (+DP all-reduce "
                         "+ AdamW), d_model=1536, charts=5888, 4096 tokens/GPU",
             "model": "KSDraft KS3 decoder layer (d_model=1536, charts=5888)",
             "global_batch": BATCH * n, "seq_len": SEQ, "tokens_per_gpu": TOKENS,
@@ -549,7 +549,7 @@ def _roofline_from_gemms(gemm, peaks) -> tuple[dict, dict]:
 
 
 def run_config4(args) -> None:
-    """BASELINE config 4 on N GPUs (one process each): the full training step."""
+    """benchmark config 4 on N GPUs (one process each): the full training step."""
     import torch
     import torch.distributed as dist
 
@@ -697,7 +697,7 @@ def run_config4(args) -> None:
 
 
 def config5(n: int) -> dict:
-    return {"workload": "BASELINE config 5: KSDraft INT8 draft serving, 64 concurrent contexts "
+    return {"workload": "benchmark config 5: KSDraft INT8 draft serving, 64 concurrent contexts "
                         "of 8192 Zipf(1.1) tokens with bf16 N(0,1) teacher states, blocks of 8 "
                         "appended positions per context per step through 24 layers at "
                         "d_model=1536, top-8 candidates from the W8A8 GS128 LM head (vocab "
@@ -711,7 +711,7 @@ def config5(n: int) -> dict:
 
 
 def run_config5(args) -> None:
-    """BASELINE config 5 on N GPUs: prefill the contexts (untimed), then time
+    """benchmark config 5 on N GPUs: prefill the contexts (untimed), then time
     `steps` propose() calls of one 8-position block per context."""
     import torch
     import torch.distributed as dist
@@ -884,7 +884,7 @@ def profile_case_fn(case: str, dev):
     from ksdraft_b200.kernels.quant import quantize_cols, quantize_last_dim
     g = torch.Generator(device=dev).manual_seed(0)
     if case == "gemm_config1":
-        # A (256, 1536) N(0,1), W (1536, 1536) N(0,0.02), GS128, fp32 out
+        # benchmark config 1: A (256, 1536) N(0,1), W (1536, 1536) N(0,0.02), GS128, fp32 out
         a = torch.randn(256, D_MODEL, device=dev, generator=g)
         w = torch.randn(D_MODEL, D_MODEL, device=dev, generator=g) * 0.02
         ac, as_ = quantize_last_dim(a)
@@ -1056,7 +1056,7 @@ def time_on_device(fn, iters: int) -> float:
 
 
 def side_measurements(dev) -> dict:
-    """1-GPU figures of the other BASELINE configurations, measured after the
+    """1-GPU figures of the other benchmark configurations, measured after the
     main line (outside its timed region): config 1 (W8A8 GEMM fwd), config 3
     (Rosa stream matcher, B 4 x T 4096 x 512 streams) and the LM head
     (4096 tokens x vocab 150144 on one GPU, forward + backward)."""

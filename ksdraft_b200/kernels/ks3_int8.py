@@ -63,7 +63,7 @@ def ks3_weights(down: torch.Tensor, up: torch.Tensor, coefficients: torch.Tensor
 def init_ks3_weights(d_model: int, charts: int, *, generator: torch.Generator | None = None,
                      device=None, std: float = 0.02, coeff_std: float = 0.05) -> SimpleNamespace:
     """Seeded synthetic KS3 weights for benches and tests: projections N(0, std)
-    (the BASELINE configs' weight init), spine coefficients N(0, coeff_std),
+    (the benchmark configs' weight init), spine coefficients N(0, coeff_std),
     warp raw scale 0.75 and raw shift 0.  Drawn on `generator`'s device."""
     gdev = generator.device if generator is not None else torch.device("cpu")
 

@@ -1,4 +1,4 @@
-"""Drafting with a KSDraft model on the INT8 tier.
+"""Drafting with a KSDraft model on the INT8 tier (benchmark config 5).
 
 The reference describes a proposal API on the draft model,
 `propose(target_states, tokens, block_len, topk) -> candidates, logits, refined`

@@ -70,7 +70,7 @@ DRAFT_SM_RESERVE = int(os.environ.get("KSD8_DRAFT_SM_RESERVE", "8"))
 
 @dataclass(frozen=True)
 class DraftShape:
-    """Model dimensions (defaults: configs/flint.yaml's decided draft)."""
+    """Model dimensions (defaults: configs/flint.yaml's decided draft, benchmark config 4)."""
     vocab: int = 150144
     layers: int = 24
     d_model: int = 1536
@@ -174,7 +174,7 @@ class FlatParams:
 
 
 def init_draft_params(shape: DraftShape, device, seed: int = 0, std: float = 0.02):
-    """Seeded synthetic weights (N(0, 0.02), quantised GS128 on
+    """Seeded synthetic weights (benchmark config 4: N(0, 0.02), quantised GS128 on
     use; LayerNorms at weight 1 / bias 0; Rosa payload 1, time mixes 0; KS3 spine
     coefficients N(0, 0.05), warp raw scale 0.75, raw shift 0).  Returns
     (FlatParams, frozen {name: tensor})."""

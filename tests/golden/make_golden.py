@@ -87,7 +87,7 @@ def gen_gemm():
     from ksdraft.kernels.gemm import w8a8_gemm
     from ksdraft.kernels.quant import quantize_last_dim
     out = {}
-    # seed 0, A ~ N(0,1) [256,1536], W ~ N(0,0.02) [1536,1536]
+    # benchmark config 1: seed 0, A ~ N(0,1) [256,1536], W ~ N(0,0.02) [1536,1536]
     torch.manual_seed(0)
     A = torch.randn(256, 1536)
     W = torch.randn(1536, 1536) * 0.02

@@ -1,4 +1,4 @@
-"""GPU: drafting (BASELINE config 5 path, ksdraft_b200/model/drafter.py).
+"""GPU: drafting (benchmark config 5 path, ksdraft_b200/model/drafter.py).
 
 Appending blocks to prefilled contexts must give what a whole-sequence int8
 forward of the extended contexts gives (KSDraftModel.forward semantics,
