@@ -1047,12 +1047,14 @@ static int launch_chunk(const MatchArgs& a, int64_t t_len, int dev, int algo,
 }
 
 #ifndef KSD8_ROSA_REDO_BUDGET
-#define KSD8_ROSA_REDO_BUDGET 4
+#define KSD8_ROSA_REDO_BUDGET 8
 #endif
 
 // Chain steps per position (average, after the first 96 positions) that the
 // chunked matcher spends on a stream before handing it to the sorted-key one;
 // KSD8_ROSA_REDO_BUDGET in the environment overrides the compiled default.
+// Config-4 step, Rosa forward of the 24 layers: 149.8 / 151.2 / 140.2 / 156.4 /
+// 184.6 ms at budgets 2 / 4 / 8 / 16 / 32.
 static int redo_budget() {
   static const int b = [] {
     const char* e = std::getenv("KSD8_ROSA_REDO_BUDGET");
