@@ -215,8 +215,10 @@ __global__ void __launch_bounds__(256) rosa_decode_merge_kernel(
 namespace {
 
 // first rank r in [0, nk) with SW[r] >= key (nk when none): the sampled
-// windows top[b] = SW[b * DEC_BLK] (shared memory) pick the block, a binary
-// search of the block's global windows finishes
+// windows top[b] = SW[b * DEC_BLK] (shared memory) pick the block, then two
+// rounds of independent global loads finish it -- the block's 7 inner samples
+// SW[base + 8i] pick the run of 8, whose 7 remaining windows give the rank --
+// instead of a 6-step dependent binary search of the block.
 __device__ __forceinline__ int64_t main_lower_bound(const uint64_t* top, int ntop,
                                                     const uint64_t* swr, int64_t nk,
                                                     uint64_t key) {
@@ -226,12 +228,29 @@ __device__ __forceinline__ int64_t main_lower_bound(const uint64_t* top, int nto
     if (top[mid] < key) lo = mid + 1; else hi = mid;
   }
   if (lo == 0) return 0;
-  int64_t a = (int64_t)(lo - 1) * DEC_BLK + 1, b = min(nk, (int64_t)lo * DEC_BLK);
-  while (a < b) {
-    const int64_t mid = (a + b) >> 1;
-    if (swr[mid] < key) a = mid + 1; else b = mid;
+  // SW[base] < key; the answer lies in [base + 1, end]
+  const int64_t base = (int64_t)(lo - 1) * DEC_BLK;
+  const int64_t end = min(nk, (int64_t)lo * DEC_BLK);
+  static_assert(DEC_BLK == 64, "two rounds of 8");
+  uint64_t v[7];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) {
+    const int64_t r = base + 8 * (i + 1);
+    v[i] = r < end ? swr[r] : ~0ull;
   }
-  return a;
+  int sub = 0;  // samples SW[base + 8i] < key, i = 1 .. 7 (a prefix: the run is sorted)
+#pragma unroll
+  for (int i = 0; i < 7; ++i) sub += (base + 8 * (i + 1) < end && v[i] < key) ? 1 : 0;
+  const int64_t b8 = base + 8 * sub;  // SW[b8] < key
+#pragma unroll
+  for (int i = 0; i < 7; ++i) {
+    const int64_t r = b8 + 1 + i;
+    v[i] = r < end ? swr[r] : ~0ull;
+  }
+  int cnt = 0;
+#pragma unroll
+  for (int i = 0; i < 7; ++i) cnt += (b8 + 1 + i < end && v[i] < key) ? 1 : 0;
+  return b8 + 1 + cnt;
 }
 
 }  // namespace
