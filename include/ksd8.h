@@ -347,7 +347,8 @@ int ksd8_transfer_bwd(const void* p, int dtype, const float* e, const float* nor
  * at the group's amax: sign(o) fp16(sum gx * codes) / 127 / n_tied, inside the
  * clamp range) is reduced to partials[p][s] = sum over the rows of chunk p of
  * do * sign (n_parts chunks of ceil(M / n_parts) rows); the caller adds the
- * rows.  streams a multiple of 128, at most 2048. */
+ * rows.  streams a multiple of 4, at most 2048 (the last GS128 group is
+ * zero-padded when streams % 128 != 0, as the quantiser pads). */
 int ksd8_rosa_payload_bwd(const void* o, const int8_t* codes, const float* gx, const void* sign,
                           int dtype, int64_t m, int64_t streams, float* partials,
                           int64_t n_parts, int* status, void* stream);
@@ -360,7 +361,8 @@ int ksd8_rosa_payload_bwd(const void* o, const int8_t* codes, const float* gx, c
  *   positions written;
  *   the main run: sw (rows, cap) uint64 sorted key windows, sj (rows, cap)
  *   uint16 their positions, blk (rows, cap / 64) uint16 max(position + 1) per
- *   64 ranks; cap a multiple of 64.
+ *   64 ranks, smp (rows, cap / 64 + cap / 8) uint64 its sample index (the
+ *   windows of every 64th rank, then of every 8th rank); cap a multiple of 64.
  * Keys 0 .. n_main - 1 are the matched context (main run = keys
  * max_len - 1 .. n_main - 1; the earlier ones are compared directly), keys
  * n_main .. t - 1 the delta since the last build, also compared directly.
@@ -368,20 +370,20 @@ int ksd8_rosa_payload_bwd(const void* o, const int8_t* codes, const float* gx, c
  * least max_len + 1 positions (the reference's cap min(62, T - 1) is then
  * max_len = 62). */
 
-/* Sort the keys max_len - 1 .. n_keys - 1 of every row of kw into (sw, sj, blk);
- * n_keys <= cap, smem-limited to n_keys - max_len + 1 <= 16384 keys. */
+/* Sort the keys max_len - 1 .. n_keys - 1 of every row of kw into (sw, sj, blk,
+ * smp); n_keys <= cap, smem-limited to n_keys - max_len + 1 <= 16384 keys. */
 int ksd8_rosa_decode_build(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_keys,
-                           int max_len, uint64_t* sw, uint16_t* sj, uint16_t* blk, int64_t cap,
-                           int* status, void* stream);
+                           int max_len, uint64_t* sw, uint16_t* sj, uint16_t* blk,
+                           uint64_t* smp, int64_t cap, int* status, void* stream);
 
 /* The main run of keys max_len - 1 .. n_new - 1 from the run of keys
  * max_len - 1 .. n_old - 1 in (sw_in, sj_in) (a copy: sw / sj are written)
  * and the k bits of the keys appended since: those keys are sorted and merged
- * in; blk is recomputed.  n_new - max(n_old, max_len - 1) <= 8192. */
+ * in; blk and smp are recomputed.  n_new - max(n_old, max_len - 1) <= 8192. */
 int ksd8_rosa_decode_merge(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_old,
                            int64_t n_new, int max_len, const uint64_t* sw_in,
                            const uint16_t* sj_in, uint64_t* sw, uint16_t* sj, uint16_t* blk,
-                           int64_t cap, int* status, void* stream);
+                           uint64_t* smp, int64_t cap, int* status, void* stream);
 
 /* Append k_new (1..32) positions t0 .. t0 + k_new - 1 to every row (bits =
  * proj > 0 of the projections (contexts, k_new, streams), dtype F32 / BF16 /
@@ -399,9 +401,10 @@ int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* pr
                           int64_t contexts, int64_t streams, int64_t k_new, int64_t t0,
                           int64_t n_main, int max_len, uint64_t* qw, uint64_t* kw, uint64_t* vw,
                           int64_t nw, const uint64_t* sw, const uint16_t* sj,
-                          const uint16_t* blk, int64_t cap, const float* payload, void* out,
-                          int64_t out_cs, int out_dtype, int32_t* match_len, int32_t* match_end,
-                          int64_t ml_rs, const int64_t* pos, int* status, void* stream);
+                          const uint16_t* blk, const uint64_t* smp, int64_t cap,
+                          const float* payload, void* out, int64_t out_cs, int out_dtype,
+                          int32_t* match_len, int32_t* match_end, int64_t ml_rs,
+                          const int64_t* pos, int* status, void* stream);
 
 /* Philox4x32-10 uniform stream used by the dither: out[i] = (word(seed, offset+i) >> 8) * 2^-24. */
 int ksd8_philox_uniform(uint64_t seed, uint64_t offset, int64_t n, float* out, void* stream);

@@ -66,10 +66,11 @@ SIGNATURES: dict[str, list] = {
     "ksd8_transfer_rows": [vp, i32, vp, i64, i64, vp, vp, vp, vp, vp],
     "ksd8_transfer_bwd": [vp, i32, vp, vp, vp, i64, i64, f32, vp, vp, i64, vp, vp, vp, vp],
     "ksd8_rosa_payload_bwd": [vp, vp, vp, vp, i32, i64, i64, vp, i64, vp, vp],
-    "ksd8_rosa_decode_build": [vp, i64, i64, i64, i32, vp, vp, vp, i64, vp, vp],
-    "ksd8_rosa_decode_merge": [vp, i64, i64, i64, i64, i32, vp, vp, vp, vp, vp, i64, vp, vp],
+    "ksd8_rosa_decode_build": [vp, i64, i64, i64, i32, vp, vp, vp, vp, i64, vp, vp],
+    "ksd8_rosa_decode_merge": [vp, i64, i64, i64, i64, i32, vp, vp, vp, vp, vp, vp, i64, vp,
+                               vp],
     "ksd8_rosa_decode_step": [vp, vp, vp, i32, i64, i64, i64, i64, i64, i32, vp, vp, vp, i64,
-                              vp, vp, vp, i64, vp, vp, i64, i32, vp, vp, i64, vp, vp, vp],
+                              vp, vp, vp, vp, i64, vp, vp, i64, i32, vp, vp, i64, vp, vp, vp],
     "ksd8_rosa_set_algorithm": [i32],
     "ksd8_set_sm_reserve": [i32],
     "ksd8_get_sm_reserve": [],

@@ -57,10 +57,11 @@ int ksd8_dspine_ln_bwd_launch(const void*, const float*, const float*, const voi
 int ksd8_transfer_rows_launch(const void*, int, const float*, int64_t, int64_t, float*, float*,
                               float*, cudaStream_t);
 int ksd8_rosa_decode_build_launch(const uint64_t*, int64_t, int64_t, int64_t, int, uint64_t*,
-                                  uint16_t*, uint16_t*, int64_t, cudaStream_t);
+                                  uint16_t*, uint16_t*, uint64_t*, int64_t, cudaStream_t);
 int ksd8_rosa_decode_step_launch(const void* const*, int, int64_t, int64_t, int64_t, int64_t,
                                  int64_t, int, uint64_t* const*, int64_t, const uint64_t*,
-                                 const uint16_t*, const uint16_t*, int64_t, const float*, void*,
+                                 const uint16_t*, const uint16_t*, const uint64_t*, int64_t,
+                                 const float*, void*,
                                  int64_t, int, int32_t*, int32_t*, int64_t, const int64_t*,
                                  cudaStream_t);
 int ksd8_rosa_decode_limits(int64_t*, int64_t*, int64_t*);
@@ -68,7 +69,7 @@ int ksd8_rosa_payload_bwd_launch(const void*, const int8_t*, const float*, const
                                  int64_t, int64_t, float*, int64_t, cudaStream_t);
 int ksd8_rosa_decode_merge_launch(const uint64_t*, int64_t, int64_t, int64_t, int64_t, int,
                                   const uint64_t*, const uint16_t*, uint64_t*, uint16_t*,
-                                  uint16_t*, int64_t, cudaStream_t);
+                                  uint16_t*, uint64_t*, int64_t, cudaStream_t);
 int ksd8_transfer_bwd_launch(const void*, int, const float*, const float*, const float*, int64_t,
                              int64_t, float, const void*, const float*, int64_t, void*, float*,
                              cudaStream_t);
@@ -625,40 +626,42 @@ int ksd8_transfer_bwd(const void* p, int dtype, const float* e, const float* nor
 // ---- incremental Rosa matching (drafting) ----
 
 int ksd8_rosa_decode_build(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_keys,
-                           int max_len, uint64_t* sw, uint16_t* sj, uint16_t* blk, int64_t cap,
-                           int* status, void* stream) {
+                           int max_len, uint64_t* sw, uint16_t* sj, uint16_t* blk,
+                           uint64_t* smp, int64_t cap, int* status, void* stream) {
   (void)status;
   if (n_streams < 0 || nw < 0 || n_keys < 0 || cap <= 0 || cap % 64 != 0) return KSD8_ERR_SHAPE;
   if (max_len < 1 || max_len > 64) return KSD8_ERR_ARG;
   if (n_keys > nw * 64 || n_keys > cap || cap > 65536) return KSD8_ERR_SHAPE;
-  if (n_streams > 0 && (!kw || !sw || !sj || !blk)) return KSD8_ERR_ARG;
+  if (n_streams > 0 && (!kw || !sw || !sj || !blk || !smp)) return KSD8_ERR_ARG;
   return finish(ksd8_rosa_decode_build_launch(kw, n_streams, nw, n_keys, max_len, sw, sj, blk,
-                                              cap, S(stream)));
+                                              smp, cap, S(stream)));
 }
 
 int ksd8_rosa_decode_merge(const uint64_t* kw, int64_t n_streams, int64_t nw, int64_t n_old,
                            int64_t n_new, int max_len, const uint64_t* sw_in,
                            const uint16_t* sj_in, uint64_t* sw, uint16_t* sj, uint16_t* blk,
-                           int64_t cap, int* status, void* stream) {
+                           uint64_t* smp, int64_t cap, int* status, void* stream) {
   (void)status;
   if (n_streams < 0 || nw < 0 || n_old < 0 || n_new < n_old || cap <= 0 || cap % 64 != 0 ||
       cap > 65536)
     return KSD8_ERR_SHAPE;
   if (max_len < 1 || max_len > 64) return KSD8_ERR_ARG;
   if (n_new > nw * 64 || n_new > cap) return KSD8_ERR_SHAPE;
-  if (n_streams > 0 && (!kw || !sw_in || !sj_in || !sw || !sj || !blk)) return KSD8_ERR_ARG;
+  if (n_streams > 0 && (!kw || !sw_in || !sj_in || !sw || !sj || !blk || !smp))
+    return KSD8_ERR_ARG;
   if (n_streams > 0 && (sw_in == sw || sj_in == sj)) return KSD8_ERR_ARG;   // out of place
   return finish(ksd8_rosa_decode_merge_launch(kw, n_streams, nw, n_old, n_new, max_len, sw_in,
-                                              sj_in, sw, sj, blk, cap, S(stream)));
+                                              sj_in, sw, sj, blk, smp, cap, S(stream)));
 }
 
 int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* proj_v, int dtype,
                           int64_t contexts, int64_t streams, int64_t k_new, int64_t t0,
                           int64_t n_main, int max_len, uint64_t* qw, uint64_t* kw, uint64_t* vw,
                           int64_t nw, const uint64_t* sw, const uint16_t* sj,
-                          const uint16_t* blk, int64_t cap, const float* payload, void* out,
-                          int64_t out_cs, int out_dtype, int32_t* match_len, int32_t* match_end,
-                          int64_t ml_rs, const int64_t* pos, int* status, void* stream) {
+                          const uint16_t* blk, const uint64_t* smp, int64_t cap,
+                          const float* payload, void* out, int64_t out_cs, int out_dtype,
+                          int32_t* match_len, int32_t* match_end, int64_t ml_rs,
+                          const int64_t* pos, int* status, void* stream) {
   (void)status;
   if (!valid_float_dtype(dtype) || !valid_float_dtype(out_dtype)) return KSD8_ERR_DTYPE;
   if (out_cs < k_new * streams || ((match_len || match_end) && ml_rs < k_new))
@@ -679,12 +682,13 @@ int ksd8_rosa_decode_step(const void* proj_q, const void* proj_k, const void* pr
   }
   if ((proj_q == nullptr) != (proj_k == nullptr) || (proj_q == nullptr) != (proj_v == nullptr))
     return KSD8_ERR_ARG;
-  if (contexts * streams > 0 && (!qw || !kw || !vw || !sw || !sj || !blk || !out))
+  if (contexts * streams > 0 && (!qw || !kw || !vw || !sw || !sj || !blk || !smp || !out))
     return KSD8_ERR_ARG;
   const void* proj[3] = {proj_q, proj_k, proj_v};
   uint64_t* bits[3] = {qw, kw, vw};
   return finish(ksd8_rosa_decode_step_launch(proj, dtype, contexts, streams, k_new, t0, n_main,
-                                             max_len, bits, nw, sw, sj, blk, cap, payload, out,
+                                             max_len, bits, nw, sw, sj, blk, smp, cap, payload,
+                                             out,
                                              out_cs, out_dtype, match_len, match_end, ml_rs,
                                              pos, S(stream)));
 }
@@ -694,7 +698,7 @@ int ksd8_rosa_payload_bwd(const void* o, const int8_t* codes, const float* gx, c
                           int64_t n_parts, int* status, void* stream) {
   (void)status;
   if (!valid_float_dtype(dtype)) return KSD8_ERR_DTYPE;
-  if (m < 0 || streams <= 0 || streams % 128 != 0 || streams > 2048) return KSD8_ERR_SHAPE;
+  if (m < 0 || streams <= 0 || streams % 4 != 0 || streams > 2048) return KSD8_ERR_SHAPE;
   if (n_parts <= 0 || n_parts > INT32_MAX || !partials) return KSD8_ERR_ARG;
   if (m > 0 && (!o || !codes || !gx || !sign)) return KSD8_ERR_ARG;
   if (m > 0 && ((reinterpret_cast<uintptr_t>(gx) & 15) || (reinterpret_cast<uintptr_t>(codes) & 3)))

@@ -853,7 +853,8 @@ __global__ void __launch_bounds__(32) grad_clip_coef_kernel(const float* partial
 //   do = gx + [|o| == amax_g] sign(o) fp16(sum_g gx * codes) / 127 / n_tied
 // (the scale gradient of quant.py:47-49, only inside the clamp range), and
 //   d payload[s] = sum_t do[t, s] * sign[t, s].
-// One warp per 128-stream group, a thread owns 4 streams; CTA rows
+// One warp per 128-stream group (the last one zero-padded when S % 128 != 0,
+// as quantize_last_dim pads), a thread owns 4 streams; CTA rows
 // [blockIdx.x * rpc, +rpc); per-CTA column sums into partials (gridDim, S).
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
@@ -868,18 +869,22 @@ __global__ void __launch_bounds__(512) rosa_payload_bwd_kernel(
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   const int64_t r0 = (int64_t)blockIdx.x * rpc;
   const int64_t r1 = min(m, r0 + rpc);
+  const bool live = col < S;  // S % 4 == 0: a thread's 4 streams are all real or all padding
   for (int64_t row = r0; row < r1; ++row) {
     const int64_t off = row * S + col;
-    float ov[4], sv[4], gv[4], cv[4];
+    float ov[4] = {0.f, 0.f, 0.f, 0.f}, sv[4] = {0.f, 0.f, 0.f, 0.f};
+    float gv[4] = {0.f, 0.f, 0.f, 0.f}, cv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (live) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      ov[i] = to_f32(o[off + i]);
-      sv[i] = to_f32(sign[off + i]);
+      for (int i = 0; i < 4; ++i) {
+        ov[i] = to_f32(o[off + i]);
+        sv[i] = to_f32(sign[off + i]);
+      }
+      const float4 g4 = *reinterpret_cast<const float4*>(gx + off);
+      gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+      const char4 c4 = *reinterpret_cast<const char4*>(codes + off);
+      cv[0] = c4.x; cv[1] = c4.y; cv[2] = c4.z; cv[3] = c4.w;
     }
-    const float4 g4 = *reinterpret_cast<const float4*>(gx + off);
-    gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
-    const char4 c4 = *reinterpret_cast<const char4*>(codes + off);
-    cv[0] = c4.x; cv[1] = c4.y; cv[2] = c4.z; cv[3] = c4.w;
     float am = 0.f, dot = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -903,9 +908,11 @@ __global__ void __launch_bounds__(512) rosa_payload_bwd_kernel(
       acc[i] += d * sv[i];
     }
   }
-  float* pp = partials + (int64_t)blockIdx.x * S + col;
+  if (live) {
+    float* pp = partials + (int64_t)blockIdx.x * S + col;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) pp[i] = acc[i];
+    for (int i = 0; i < 4; ++i) pp[i] = acc[i];
+  }
 }
 
 }  // namespace ksd8
@@ -920,7 +927,7 @@ int ksd8_rosa_payload_bwd_launch(const void* o, const int8_t* codes, const float
                ? KSD8_OK : KSD8_ERR_LAUNCH;
   }
   const int64_t rpc = (m + n_parts - 1) / n_parts;
-  const unsigned threads = (unsigned)(streams / 4);
+  const unsigned threads = (unsigned)((streams + 127) / 128 * 32);  // whole warps per group
   switch (dtype) {
     case KSD8_F32:
       rosa_payload_bwd_kernel<float><<<(unsigned)n_parts, threads, 0, stream>>>(

@@ -36,6 +36,16 @@ constexpr int DEC_WARPS = 8;       // streams per CTA in the step kernel
 constexpr int DEC_MAX_NEW = 32;    // new positions per step
 constexpr int DEC_MAX_TOP = 512;   // sampled windows of the main run held in shared memory
 constexpr int DEC_DELTA_WORDS = 34;  // k words of the delta region held in shared memory
+constexpr int DEC_SUB = 8;         // ranks per inner sample
+
+// Sample index of a main run, per row (stride dec_smp_stride(cap) uint64):
+// [0, cap / DEC_BLK): the windows of ranks 0, DEC_BLK, 2 DEC_BLK, ...;
+// then [cap / DEC_BLK, + cap / DEC_SUB): the windows of ranks 0, DEC_SUB, ...
+// Both contiguous, so the step kernel's per-row sample load and the inner
+// samples of a block are whole sectors.
+__host__ __device__ constexpr int64_t dec_smp_stride(int64_t cap) {
+  return cap / DEC_BLK + cap / DEC_SUB;
+}
 
 // window of position t from bit words w (global or shared), bits before 0 are 0
 __device__ __forceinline__ uint64_t window_at(const uint64_t* w, int64_t t) {
@@ -74,7 +84,8 @@ __global__ void __launch_bounds__(256) rosa_decode_build_kernel(const uint64_t* 
                                                                 int r0, int np, int64_t cap,
                                                                 uint64_t* __restrict__ sw,
                                                                 uint16_t* __restrict__ sj,
-                                                                uint16_t* __restrict__ blk) {
+                                                                uint16_t* __restrict__ blk,
+                                                                uint64_t* __restrict__ smp) {
   extern __shared__ __align__(16) uint8_t dsm[];
   uint64_t* W = reinterpret_cast<uint64_t*>(dsm);
   uint32_t* J = reinterpret_cast<uint32_t*>(W + np);
@@ -110,6 +121,12 @@ __global__ void __launch_bounds__(256) rosa_decode_build_kernel(const uint64_t* 
     sw[stream * cap + r] = W[r];
     sj[stream * cap + r] = (uint16_t)J[r];
   }
+  {
+    uint64_t* sr = smp + stream * dec_smp_stride(cap);
+    for (int64_t b = threadIdx.x; b * DEC_BLK < nk; b += blockDim.x) sr[b] = W[b * DEC_BLK];
+    for (int64_t q = threadIdx.x; q * DEC_SUB < nk; q += blockDim.x)
+      sr[cap / DEC_BLK + q] = W[q * DEC_SUB];
+  }
   const int64_t nb = (nk + DEC_BLK - 1) / DEC_BLK;
   for (int64_t b = threadIdx.x; b < nb; b += blockDim.x) {
     uint32_t m = 0;
@@ -131,7 +148,8 @@ __global__ void __launch_bounds__(256) rosa_decode_build_kernel(const uint64_t* 
 __global__ void __launch_bounds__(256) rosa_decode_merge_kernel(
     const uint64_t* __restrict__ kw, int64_t nw, int64_t n_old, int64_t n_new, int r0, int npd,
     int64_t cap, const uint64_t* __restrict__ sw_in, const uint16_t* __restrict__ sj_in,
-    uint64_t* __restrict__ sw, uint16_t* __restrict__ sj, uint16_t* __restrict__ blk) {
+    uint64_t* __restrict__ sw, uint16_t* __restrict__ sj, uint16_t* __restrict__ blk,
+    uint64_t* __restrict__ smp) {
   extern __shared__ __align__(16) uint8_t dsm[];
   uint64_t* W = reinterpret_cast<uint64_t*>(dsm);
   uint32_t* J = reinterpret_cast<uint32_t*>(W + npd);
@@ -201,6 +219,12 @@ __global__ void __launch_bounds__(256) rosa_decode_merge_kernel(
   }
   __syncthreads();
   const int64_t nk = nk_old + nd;
+  {
+    uint64_t* sr = smp + stream * dec_smp_stride(cap);
+    for (int64_t b = threadIdx.x; b * DEC_BLK < nk; b += blockDim.x) sr[b] = swo[b * DEC_BLK];
+    for (int64_t q = threadIdx.x; q * DEC_SUB < nk; q += blockDim.x)
+      sr[cap / DEC_BLK + q] = swo[q * DEC_SUB];
+  }
   const int64_t nb = (nk + DEC_BLK - 1) / DEC_BLK;
   for (int64_t bb = threadIdx.x; bb < nb; bb += blockDim.x) {
     uint32_t m = 0;
@@ -214,14 +238,14 @@ __global__ void __launch_bounds__(256) rosa_decode_merge_kernel(
 
 namespace {
 
-// first rank r in [0, nk) with SW[r] >= key (nk when none): the sampled
-// windows top[b] = SW[b * DEC_BLK] (shared memory) pick the block, then two
-// rounds of independent global loads finish it -- the block's 7 inner samples
-// SW[base + 8i] pick the run of 8, whose 7 remaining windows give the rank --
-// instead of a 6-step dependent binary search of the block.
+// first rank r in [0, nk) with SW[r] >= key (nk when none): the block
+// samples top[b] = SW[b * DEC_BLK] (shared memory) pick the block, its 7 inner
+// samples SW[base + 8i] (contiguous in the sample index, sub) pick the run of
+// 8, whose 7 remaining windows give the rank: two rounds of independent loads
+// of 56 contiguous bytes each.
 __device__ __forceinline__ int64_t main_lower_bound(const uint64_t* top, int ntop,
-                                                    const uint64_t* swr, int64_t nk,
-                                                    uint64_t key) {
+                                                    const uint64_t* sub, const uint64_t* swr,
+                                                    int64_t nk, uint64_t key) {
   int lo = 0, hi = ntop;
   while (lo < hi) {
     const int mid = (lo + hi) >> 1;
@@ -231,17 +255,17 @@ __device__ __forceinline__ int64_t main_lower_bound(const uint64_t* top, int nto
   // SW[base] < key; the answer lies in [base + 1, end]
   const int64_t base = (int64_t)(lo - 1) * DEC_BLK;
   const int64_t end = min(nk, (int64_t)lo * DEC_BLK);
-  static_assert(DEC_BLK == 64, "two rounds of 8");
+  static_assert(DEC_BLK == 8 * DEC_SUB && DEC_SUB == 8, "two rounds of 8");
   uint64_t v[7];
 #pragma unroll
   for (int i = 0; i < 7; ++i) {
-    const int64_t r = base + 8 * (i + 1);
-    v[i] = r < end ? swr[r] : ~0ull;
+    const int64_t r = base + DEC_SUB * (i + 1);
+    v[i] = r < end ? sub[r / DEC_SUB] : ~0ull;
   }
-  int sub = 0;  // samples SW[base + 8i] < key, i = 1 .. 7 (a prefix: the run is sorted)
+  int c = 0;  // inner samples < key, i = 1 .. 7 (a prefix: the run is sorted)
 #pragma unroll
-  for (int i = 0; i < 7; ++i) sub += (base + 8 * (i + 1) < end && v[i] < key) ? 1 : 0;
-  const int64_t b8 = base + 8 * sub;  // SW[b8] < key
+  for (int i = 0; i < 7; ++i) c += (base + DEC_SUB * (i + 1) < end && v[i] < key) ? 1 : 0;
+  const int64_t b8 = base + DEC_SUB * c;  // SW[b8] < key
 #pragma unroll
   for (int i = 0; i < 7; ++i) {
     const int64_t r = b8 + 1 + i;
@@ -267,6 +291,7 @@ struct DecodeArgs {
   const uint64_t* sw;    // main run windows (contexts * streams, cap)
   const uint16_t* sj;    // main run positions
   const uint16_t* blk;   // max(j + 1) per DEC_BLK ranks (contexts * streams, cap / DEC_BLK)
+  const uint64_t* smp;   // sample index (contexts * streams, dec_smp_stride(cap))
   int64_t cap;
   const float* payload;  // (streams) or null
   void* out;             // out[c * out_cs + i * streams + s] for new position i
@@ -344,7 +369,9 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
   const uint64_t* swr = a.sw + st * a.cap;
   const uint16_t* sjr = a.sj + st * a.cap;
   const uint16_t* blkr = a.blk + st * (a.cap / DEC_BLK);
-  for (int b = lane; b < ntop; b += 32) top[b] = swr[(int64_t)b * DEC_BLK];
+  const uint64_t* smr = a.smp + st * dec_smp_stride(a.cap);
+  const uint64_t* subr = smr + a.cap / DEC_BLK;
+  for (int b = lane; b < ntop; b += 32) top[b] = smr[b];
   // delta keys j in [dlo, t0 + K - 2]; their windows read words w0 .. of k
   const int64_t dlo = max(n_main, (int64_t)r0);
   const int64_t dhi = t0 + K - 2;
@@ -365,7 +392,7 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
   int Lm = 0;
   int64_t lo = 0, hi = 0;
   if (valid && nk > 0 && capq > 0) {
-    const int64_t r = main_lower_bound(top, ntop, swr, nk, wq);
+    const int64_t r = main_lower_bound(top, ntop, subr, swr, nk, wq);
     int lraw = 0;
     if (r > 0) lraw = lcp64(wq, swr[r - 1]);
     if (r < nk) lraw = max(lraw, lcp64(wq, swr[r]));
@@ -373,8 +400,8 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
     if (Lm > 0) {
       const uint64_t pre = Lm >= 64 ? wq : (wq >> (64 - Lm)) << (64 - Lm);
       const uint64_t last = Lm >= 64 ? wq : pre | (~0ull >> Lm);
-      lo = main_lower_bound(top, ntop, swr, nk, pre);
-      hi = last == ~0ull ? nk : main_lower_bound(top, ntop, swr, nk, last + 1);
+      lo = main_lower_bound(top, ntop, subr, swr, nk, pre);
+      hi = last == ~0ull ? nk : main_lower_bound(top, ntop, subr, swr, nk, last + 1);
     }
   }
 
@@ -463,7 +490,8 @@ using namespace ksd8;
 
 int ksd8_rosa_decode_build_launch(const uint64_t* kw, int64_t n_streams, int64_t nw,
                                   int64_t n_keys, int max_len, uint64_t* sw, uint16_t* sj,
-                                  uint16_t* blk, int64_t cap, cudaStream_t stream) {
+                                  uint16_t* blk, uint64_t* smp, int64_t cap,
+                                  cudaStream_t stream) {
   if (n_streams == 0) return KSD8_OK;
   const int r0 = max_len > 0 ? max_len - 1 : 0;
   const int64_t nk = n_keys > r0 ? n_keys - r0 : 0;
@@ -483,7 +511,7 @@ int ksd8_rosa_decode_build_launch(const uint64_t* kw, int64_t n_streams, int64_t
     attr_done |= 1u << dev;
   }
   rosa_decode_build_kernel<<<(unsigned)n_streams, 256, smem, stream>>>(kw, nw, n_keys, r0, np,
-                                                                       cap, sw, sj, blk);
+                                                                       cap, sw, sj, blk, smp);
   return cudaGetLastError() == cudaSuccess ? KSD8_OK : KSD8_ERR_LAUNCH;
 }
 
@@ -491,7 +519,7 @@ int ksd8_rosa_decode_step_launch(const void* const* proj, int dtype, int64_t con
                                  int64_t streams, int64_t k_new, int64_t t0, int64_t n_main,
                                  int max_len, uint64_t* const* bits, int64_t nw,
                                  const uint64_t* sw, const uint16_t* sj, const uint16_t* blk,
-                                 int64_t cap, const float* payload, void* out, int64_t out_cs,
+                                 const uint64_t* smp, int64_t cap, const float* payload, void* out, int64_t out_cs,
                                  int out_dtype, int32_t* match_len, int32_t* match_end,
                                  int64_t ml_rs, const int64_t* pos, cudaStream_t stream) {
   DecodeArgs a;
@@ -502,7 +530,7 @@ int ksd8_rosa_decode_step_launch(const void* const* proj, int dtype, int64_t con
   a.dtype = dtype;
   a.contexts = contexts; a.streams = streams; a.k_new = k_new; a.t0 = t0; a.n_main = n_main;
   a.pos = pos;
-  a.max_len = max_len; a.nw = nw; a.sw = sw; a.sj = sj; a.blk = blk; a.cap = cap;
+  a.max_len = max_len; a.nw = nw; a.sw = sw; a.sj = sj; a.blk = blk; a.smp = smp; a.cap = cap;
   a.payload = payload; a.out = out; a.out_cs = out_cs; a.out_dtype = out_dtype;
   a.match_len = match_len; a.match_end = match_end; a.ml_rs = ml_rs;
   const int64_t n = contexts * streams;
@@ -515,7 +543,8 @@ int ksd8_rosa_decode_step_launch(const void* const* proj, int dtype, int64_t con
 int ksd8_rosa_decode_merge_launch(const uint64_t* kw, int64_t n_streams, int64_t nw,
                                   int64_t n_old, int64_t n_new, int max_len,
                                   const uint64_t* sw_in, const uint16_t* sj_in, uint64_t* sw,
-                                  uint16_t* sj, uint16_t* blk, int64_t cap, cudaStream_t stream) {
+                                  uint16_t* sj, uint16_t* blk, uint64_t* smp, int64_t cap,
+                                  cudaStream_t stream) {
   if (n_streams == 0) return KSD8_OK;
   const int r0 = max_len > 0 ? max_len - 1 : 0;
   const int64_t dlo = n_old > r0 ? n_old : r0;
@@ -537,7 +566,7 @@ int ksd8_rosa_decode_merge_launch(const uint64_t* kw, int64_t n_streams, int64_t
     attr_done |= 1u << dev;
   }
   rosa_decode_merge_kernel<<<(unsigned)n_streams, 256, smem, stream>>>(
-      kw, nw, n_old, n_new, r0, npd, cap, sw_in, sj_in, sw, sj, blk);
+      kw, nw, n_old, n_new, r0, npd, cap, sw_in, sj_in, sw, sj, blk, smp);
   return cudaGetLastError() == cudaSuccess ? KSD8_OK : KSD8_ERR_LAUNCH;
 }
 

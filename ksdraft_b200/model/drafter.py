@@ -73,6 +73,9 @@ class RosaDecodeState:
         self.sw = torch.empty(rows, capacity, dtype=torch.int64, device=device)
         self.sj = torch.empty(rows, capacity, dtype=torch.int16, device=device)
         self.blk = torch.zeros(rows, capacity // 64, dtype=torch.int16, device=device)
+        # sample index: windows of every 64th, then every 8th rank of the run
+        self.smp = torch.zeros(rows, capacity // 64 + capacity // 8, dtype=torch.int64,
+                               device=device)
         self.n_main = 0
         self.pos = None        # device [t0, n_main] read by the step kernel (CUDA graphs)
 
@@ -96,11 +99,13 @@ class RosaDecodeState:
             _lib.check(lib.ksd8_rosa_decode_merge(
                 self.bits[1].data_ptr(), rows, self.nw, n_old, n_keys, MAX_LEN,
                 sw_in.data_ptr(), sj_in.data_ptr(), self.sw.data_ptr(), self.sj.data_ptr(),
-                self.blk.data_ptr(), self.capacity, None, stream), "rosa_decode_merge")
+                self.blk.data_ptr(), self.smp.data_ptr(), self.capacity, None, stream),
+                "rosa_decode_merge")
         else:
             _lib.check(lib.ksd8_rosa_decode_build(
                 self.bits[1].data_ptr(), rows, self.nw, n_keys, MAX_LEN, self.sw.data_ptr(),
-                self.sj.data_ptr(), self.blk.data_ptr(), self.capacity, None, stream),
+                self.sj.data_ptr(), self.blk.data_ptr(), self.smp.data_ptr(), self.capacity,
+                None, stream),
                 "rosa_decode_build")
         self.n_main = n_keys
 
@@ -125,7 +130,8 @@ class RosaDecodeState:
         _lib.check(_lib.lib().ksd8_rosa_decode_step(
             *ptrs, dt, C, S, k_new, t0, self.n_main, MAX_LEN,
             *(b.data_ptr() for b in self.bits), self.nw, self.sw.data_ptr(), self.sj.data_ptr(),
-            self.blk.data_ptr(), self.capacity, pay.data_ptr(), out, out_cs, out_dt, ml, me,
+            self.blk.data_ptr(), self.smp.data_ptr(), self.capacity, pay.data_ptr(), out,
+            out_cs, out_dt, ml, me,
             ml_rs, _lib.ptr(self.pos), None,
             _lib.stream_ptr(self.sw.device)), "rosa_decode_step")
 

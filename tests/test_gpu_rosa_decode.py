@@ -121,10 +121,10 @@ def test_decode_rejects_bad_arguments():
     lib = _lib.lib()
     # k_new outside 1..32, n_main beyond t0: shape errors before any launch
     rc = lib.ksd8_rosa_decode_step(None, None, None, 0, 1, 1, 33, 0, 0, 62, None, None, None, 1,
-                                   None, None, None, 64, None, None, 33, 0, None, None, 33, None,
-                                   None, None)
+                                   None, None, None, None, 64, None, None, 33, 0, None, None, 33,
+                                   None, None, None)
     assert rc == 1
     rc = lib.ksd8_rosa_decode_step(None, None, None, 0, 1, 1, 8, 10, 11, 62, None, None, None, 1,
-                                   None, None, None, 64, None, None, 8, 0, None, None, 8, None,
-                                   None, None)
+                                   None, None, None, None, 64, None, None, 8, 0, None, None, 8,
+                                   None, None, None)
     assert rc == 1

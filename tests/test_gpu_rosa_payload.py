@@ -9,16 +9,17 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("act", [torch.float32, torch.bfloat16])
-def test_payload_grad_matches_ste_formula(act):
+@pytest.mark.parametrize("act,S", [(torch.float32, 256), (torch.bfloat16, 256),
+                                   (torch.float32, 64), (torch.bfloat16, 320)])
+def test_payload_grad_matches_ste_formula(act, S):
     from ksdraft_b200 import _lib
     from ksdraft_b200.kernels.linear import ste_input_grad
     from ksdraft_b200.kernels.quant import quantize_last_dim
     g = torch.Generator().manual_seed(3)
-    M, S = 1000, 256
+    M = 1000      # S % 128 != 0: the last group is zero-padded (quant.py:40-44)
     payload = 1.0 + 0.2 * torch.randn(S, generator=g)
-    payload[5] = payload[9] = payload[100] = 3.0     # three elements tied at the group maximum
-    payload[130] = -payload[140].abs() - 2.0        # a negative group maximum
+    payload[5] = payload[9] = payload[min(100, S - 1)] = 3.0   # three tied at the group maximum
+    payload[S - 60] = -payload[S - 50].abs() - 2.0  # a negative group maximum
     sign = torch.where(torch.rand(M, S, generator=g) > 0.5, 1.0, -1.0)
     o = (payload * sign).to(act).cuda()
     sign = sign.to(act).cuda()
