@@ -732,7 +732,12 @@ def run_config5(args) -> None:
     state = {n: flat.p(n) for n in flat.names}
     state.update(frozen)
     group = dist.group.WORLD if world > 1 else None
-    n_steps = args.warmup + 2 * args.steps
+    # the delta keys the step kernel compares directly grow from 0 to ~2000
+    # between two main-run rebuilds: untimed blocks after the warm-up bring the
+    # timed ones to the middle of that cycle, whose step time is the average
+    advance = max(0, KSDraftDrafter.steps_per_rebuild(C5_BLOCK) // 2 - args.warmup
+                  - args.steps // 2)
+    n_steps = args.warmup + advance + 2 * args.steps
     cap = C5_CONTEXT_LEN + n_steps * C5_BLOCK
     drafter = KSDraftDrafter(state, shape, dev, contexts=C5_CONTEXTS, capacity=cap,
                              group=group)
@@ -769,6 +774,9 @@ def run_config5(args) -> None:
     ids_dev = ids.to(dev)
     states_dev = states.to(dev)
     for _ in range(args.warmup):
+        drafter.propose(*block(pos), topk=C5_TOPK)
+        pos += C5_BLOCK
+    for _ in range(advance):
         drafter.propose(*block(pos), topk=C5_TOPK)
         pos += C5_BLOCK
     # the block's ~750 small launches replay as one CUDA graph (position read on
@@ -843,6 +851,7 @@ def run_config5(args) -> None:
                     "d2h_bytes_per_step": C5_CONTEXTS * C5_BLOCK * C5_TOPK * 8},
             "gpu_launches": launches, "prefill_s": prefill_s, "cuda_graph": use_graph,
             "rebuild": {"ms": rebuild_ms, "every_steps": drafter.steps_per_rebuild(C5_BLOCK),
+                        "timed_blocks_after_build": args.warmup + advance,
                         "value_amortized": tok / ((total_ms + rebuild_ms * args.steps
                                                    / drafter.steps_per_rebuild(C5_BLOCK))
                                                   / 1e3)},
@@ -977,9 +986,11 @@ def profile_case_fn(case: str, dev):
         out = torch.empty(B, T, S, dtype=torch.bfloat16, device=dev)
         fn = lambda: match_words(*words, B, S, T, 62, out=out,  # noqa: E731
                                  strides=(T * S, S, 1))
-    elif case == "decode_step":
+    elif case in ("decode_step", "decode_step_delta"):
         # config 5's incremental match of one layer: 64 contexts x 512 streams
-        # matched up to 8192 positions (fair bits), then blocks of 8 appended
+        # matched up to 8192 positions (fair bits), then blocks of 8 appended;
+        # decode_step_delta: the main run ends 1024 positions earlier (the
+        # middle of a rebuild cycle: 1024 delta keys compared directly)
         from ksdraft_b200.model.drafter import RosaDecodeState
         from ksdraft_b200.model.rosa import pack_bits
         C, S, T0, k = 64, 512, 8192, 8
@@ -988,7 +999,7 @@ def profile_case_fn(case: str, dev):
         st = RosaDecodeState(C, S, T0 + 512, dev)
         st.load_words([pack_bits(b, C, T0, S, T0 * S, S, 1) for b in bits], T0)
         del bits
-        st.build(T0)
+        st.build(T0 - 1024 if case == "decode_step_delta" else T0)
         projs = [torch.randn(C, k, S, device=dev, generator=g) for _ in range(3)]
         pay = torch.ones(S, device=dev)
         out = torch.empty(C, k, S, dtype=torch.bfloat16, device=dev)

@@ -405,64 +405,103 @@ __global__ void __launch_bounds__(DEC_WARPS * 32) rosa_decode_step_kernel(Decode
     }
   }
 
-  // 3. per query, the warp together: the latest endpoint in [lo, hi) of the
-  //    main run, the early keys and the delta keys
-  int best = 0;
-  int64_t bestj = -1;
+  // 3a. per query, the warp together: the latest endpoint in [lo, hi) of the
+  //     main run (partial blocks and block maxima).  Candidates are packed as
+  //     (length << 32) | (j + 1): the larger packed value is the longer match,
+  //     then the later endpoint.
+  unsigned long long mine = 0ull;  // lane i: the best candidate of query i so far
   for (int i = 0; i < K; ++i) {
     const int L = __shfl_sync(full, Lm, i);
+    if (L == 0) continue;  // uniform across the warp
     const int64_t ilo = __shfl_sync(full, lo, i), ihi = __shfl_sync(full, hi, i);
-    const uint64_t qwi = __shfl_sync(full, wq, i);
-    const int cq = __shfl_sync(full, capq, i);
-    const int64_t ti = t0 + i;
-    int bl = 0;
-    int64_t bj = -1;
-    if (L > 0) {
-      // max of j + 1 over ranks [ilo, ihi): partial blocks and whole blocks
-      uint32_t mx = 0;
-      const int64_t b0 = (ilo + DEC_BLK - 1) / DEC_BLK, b1 = ihi / DEC_BLK;
-      if (b0 >= b1) {
-        for (int64_t r = ilo + lane; r < ihi; r += 32) mx = max(mx, (uint32_t)sjr[r] + 1u);
-      } else {
-        for (int64_t r = ilo + lane; r < b0 * DEC_BLK; r += 32)
-          mx = max(mx, (uint32_t)sjr[r] + 1u);
-        for (int64_t r = b1 * DEC_BLK + lane; r < ihi; r += 32)
-          mx = max(mx, (uint32_t)sjr[r] + 1u);
-        for (int64_t b = b0 + lane; b < b1; b += 32) mx = max(mx, (uint32_t)blkr[b]);
+    uint32_t mx = 0;
+    const int64_t b0 = (ilo + DEC_BLK - 1) / DEC_BLK, b1 = ihi / DEC_BLK;
+    if (b0 >= b1) {
+      for (int64_t r = ilo + lane; r < ihi; r += 32) mx = max(mx, (uint32_t)sjr[r] + 1u);
+    } else {
+      for (int64_t r = ilo + lane; r < b0 * DEC_BLK; r += 32)
+        mx = max(mx, (uint32_t)sjr[r] + 1u);
+      for (int64_t r = b1 * DEC_BLK + lane; r < ihi; r += 32)
+        mx = max(mx, (uint32_t)sjr[r] + 1u);
+      for (int64_t b = b0 + lane; b < b1; b += 32) mx = max(mx, (uint32_t)blkr[b]);
+    }
+    mx = __reduce_max_sync(full, mx);
+    if (lane == i) mine = ((unsigned long long)L << 32) | mx;
+  }
+
+  // 3b. early keys (j < r0: also capped at j + 1) and delta keys (dlo <= j <=
+  //     t - 1), bit-parallel over the 64 keys of a k word: the keys whose
+  //     windows agree with the query window in the top l bits are a bit mask
+  //     M_l = M_{l-1} & (k shifted by l == q[t - l]), so a word costs one
+  //     and-step per matched bit (about log2 of the keys scanned), and the
+  //     latest key of the longest match is the highest bit of the last
+  //     non-empty mask.  8 queries at a time, 4 lanes per query taking every
+  //     4th word; item -1 of a query is the early-key word.
+  for (int c0 = 0; c0 < K; c0 += 8) {
+    const int ql = lane >> 2, sub = lane & 3;
+    const int qi = c0 + ql;                     // this lane's query
+    const bool qok = qi < K;
+    const uint64_t qv = __shfl_sync(full, wq, qok ? qi : 0);
+    const int qcap_src = __shfl_sync(full, capq, qok ? qi : 0);
+    const int qcap = qok ? qcap_src : 0;
+    const int64_t tq = t0 + qi;
+    unsigned long long pk = 0ull;
+    if (qok && qcap > 0) {
+      const int64_t wlo = dlo >> 6, whi = (tq - 1) >> 6;   // delta words of this query
+      for (int64_t w = wlo - 1 + sub; w <= whi; w += 4) {
+        uint64_t kwd, kprev, M;
+        bool early;
+        int64_t jb;
+        if (w == wlo - 1) {                      // the early keys j < min(r0, t)
+          const int64_t ne = min((int64_t)r0, tq);
+          if (ne <= 0) continue;
+          kwd = kw0;
+          kprev = 0ull;
+          M = ne >= 64 ? ~0ull : ((1ull << ne) - 1ull);
+          early = true;
+          jb = 0;
+        } else {
+          if (tq - 1 < dlo) continue;            // no delta keys for this query
+          kwd = dwords[w - w0];
+          kprev = w > 0 ? dwords[w - 1 - w0] : 0ull;
+          const int64_t lo_b = max(dlo - (w << 6), (int64_t)0);
+          const int64_t hi_b = min(tq - 1 - (w << 6), (int64_t)63);
+          if (lo_b > hi_b) continue;
+          M = (~0ull << lo_b) & (~0ull >> (63 - hi_b));
+          early = false;
+          jb = w << 6;
+        }
+        int len = 0;
+        while (len < qcap) {
+          const uint64_t sh = len ? ((kwd << len) | (kprev >> (64 - len))) : kwd;
+          uint64_t e = ((qv >> (63 - len)) & 1ull) ? sh : ~sh;
+          if (early) e &= ~0ull << len;          // length <= j + 1
+          const uint64_t m2 = M & e;
+          if (!m2) break;
+          M = m2;
+          ++len;
+        }
+        if (len > 0) {
+          const unsigned long long c =
+              ((unsigned long long)len << 32) | (unsigned long long)(jb + 63 - __clzll((long long)M) + 1);
+          pk = c > pk ? c : pk;
+        }
       }
-      mx = __reduce_max_sync(full, mx);
-      bl = L;
-      bj = (int64_t)mx - 1;
     }
-    // early keys j < min(r0, ti): length also capped at j + 1
-    for (int64_t j = lane; j < r0 && j < ti; j += 32) {
-      const int l = min(lcp64(qwi, window_at(&kw0, j)), min(cq, (int)j + 1));
-      if (l > 0 && better(l, j, bl, bj)) { bl = l; bj = j; }
-    }
-    // delta keys dlo <= j <= ti - 1
-    for (int64_t j = dlo + lane; j <= ti - 1; j += 32) {
-      const int64_t wi = (j >> 6) - w0;
-      const int sh = (int)(j & 63) + 1;
-      const uint64_t h = dwords[wi];
-      const uint64_t l0 = (j >> 6) > 0 ? dwords[wi - 1] : 0ull;
-      const uint64_t wk = sh == 64 ? h : ((l0 >> sh) | (h << (64 - sh)));
-      const int l = min(lcp64(qwi, wk), cq);
-      if (l > 0 && better(l, j, bl, bj)) { bl = l; bj = j; }
-    }
-    // warp arg-best: longest, then latest
-    const unsigned long long packed =
-        bl > 0 ? (((unsigned long long)bl << 32) | (unsigned long long)(bj + 1)) : 0ull;
-    unsigned long long top_packed = packed;
+    // the 4 lanes of a query, then its owner lane
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(full, top_packed, o);
-      top_packed = other > top_packed ? other : top_packed;
+    for (int o = 1; o <= 2; o <<= 1) {
+      const unsigned long long other = __shfl_xor_sync(full, pk, o);
+      pk = other > pk ? other : pk;
     }
-    if (lane == i) {
-      best = (int)(top_packed >> 32);
-      bestj = top_packed ? (int64_t)(top_packed & 0xFFFFFFFFull) - 1 : -1;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const unsigned long long v = __shfl_sync(full, pk, 4 * q);
+      if (lane == c0 + q && v > mine) mine = v;
     }
   }
+  const int best = (int)(mine >> 32);
+  const int64_t bestj = mine ? (int64_t)(mine & 0xFFFFFFFFull) - 1 : -1;
 
   // 4. sign from v[j + 1], payload, outputs
   if (valid) {

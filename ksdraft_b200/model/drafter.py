@@ -473,7 +473,8 @@ class KSDraftDrafter:
         for st in self.states:
             st.build(self.length)
 
-    def steps_per_rebuild(self, n: int) -> int:
+    @staticmethod
+    def steps_per_rebuild(n: int) -> int:
         """Blocks of n positions appended between two main-run rebuilds."""
         return max(1, ((DELTA_WORDS - 2) * 64) // n)
 
