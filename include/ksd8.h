@@ -246,10 +246,13 @@ int ksd8_rosa_match_scratch(const uint64_t* qw, const uint64_t* kw, const uint64
                             int32_t* scratch, int64_t scratch_len, int* status, void* stream);
 
 /* Matcher kernel behind ksd8_rosa_match (process-wide, identical results):
- * 0 = prefix tables processed 32 positions per warp step (default), 1 = prefix
- * tables one position per step, 2 = window scan (always used for T >= 8192),
- * 3 = sorted key windows with a max segment tree (O(log T) per position on any
- * bit statistics; T <= 4096 + max_len - 1, else as 0). */
+ * 0 = prefix tables processed 32 positions per warp step, degenerate streams
+ * redone by sorted keys (default), 1 = prefix tables one position per step, 2 =
+ * window scan, 3 = sorted key windows with a max segment tree (O(log T) per
+ * position on any bit statistics; T <= 4096 + max_len - 1, else as 0), 4 =
+ * bit-parallel over the k words (64 keys per mask step, O(T / 64 x matched
+ * bits) per position).  T >= 8192 takes the bit-parallel kernel (the window
+ * scan under 2). */
 int ksd8_rosa_set_algorithm(int algo);
 
 /* Rosa time-shift mix + per-token GS quantisation of the three projection

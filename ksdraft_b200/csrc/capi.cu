@@ -454,7 +454,7 @@ int ksd8_topk_rows(const void* vals, int dtype, const int64_t* idx, int64_t m, i
 }
 
 int ksd8_rosa_set_algorithm(int algo) {
-  if (algo < 0 || algo > 3) return KSD8_ERR_ARG;
+  if (algo < 0 || algo > 4) return KSD8_ERR_ARG;
   ksd8_rosa_algorithm(algo);
   return KSD8_OK;
 }

@@ -685,6 +685,106 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchA
   }
 }
 
+// ---------------------------------------------------------------- bit-parallel matcher
+//
+// Exact, O(T / 64 x matched bits) per position and no per-stream index: for
+// query t, the keys of one k word (64 consecutive positions j) whose windows
+// agree with Wq(t) in the top l bits form a bit mask M_l = M_{l-1} & E_l,
+// where E_l marks k[j - l] == q[t - l] (the k word shifted up by l, the bits
+// below position 0 reading 0).  The loop narrows M until it empties or
+// reaches the cap: the surviving keys all have that length, the highest bit
+// is the latest of them.  Words are taken latest first, so an earlier word
+// only replaces a strictly longer match; the search stops at the cap.  In
+// word 0 a key j is also capped at j + 1 (E_l keeps only j >= l).  One warp
+// per stream, lane = query, 3 x ceil(T / 64) words of shared memory per warp.
+__device__ __forceinline__ int bits_word_match(uint64_t kwd, uint64_t kprev, uint64_t M,
+                                               uint64_t wq, int cap, bool first_word,
+                                               uint64_t& mout) {
+  int len = 0;
+  while (len < cap) {
+    const uint64_t sh = len ? ((kwd << len) | (kprev >> (64 - len))) : kwd;
+    uint64_t e = ((wq >> (63 - len)) & 1ull) ? sh : ~sh;
+    if (first_word) e &= ~0ull << len;  // length <= j + 1
+    const uint64_t m2 = M & e;
+    if (!m2) break;
+    M = m2;
+    ++len;
+  }
+  mout = M;
+  return len;
+}
+
+__global__ void __launch_bounds__(256) rosa_match_bits_kernel(MatchArgs a) {
+  extern __shared__ __align__(16) uint64_t rbw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int64_t stream = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (a.redo_pass) {  // only the streams the chunked kernel handed over
+    if (stream >= a.redo[0]) return;
+    stream = a.redo[1 + stream];
+  }
+  if (stream >= a.batch * a.streams) return;  // the whole warp: no CTA barrier below
+  const int64_t T = a.t_len;
+  const int nw = (int)((T + 63) / 64);
+  const int ml = a.max_len;
+  uint64_t* sq = rbw + (size_t)warp * 3 * nw;
+  uint64_t* sk = sq + nw;
+  uint64_t* sv = sk + nw;
+  for (int i = lane; i < nw; i += 32) {
+    sq[i] = a.qw[stream * nw + i];
+    sk[i] = a.kw[stream * nw + i];
+    sv[i] = a.vw[stream * nw + i];
+  }
+  __syncwarp();
+  const int64_t b = stream / a.streams, s = stream % a.streams;
+  const float pay = a.payload ? a.payload[s] : 1.f;
+  for (int64_t t0 = 0; t0 < T; t0 += 32) {
+    const int64_t t = t0 + lane;
+    if (t >= T) break;
+    const uint64_t wq = window_sm(sq, t);
+    const int cap = (int)min((int64_t)ml, t);
+    int best = 0;
+    int64_t bestj = -1;
+    if (cap > 0) {
+      // keys j <= t - 1, word by word from the latest
+      const int64_t wl = (t - 1) >> 6;
+      uint64_t M = ~0ull >> (63 - (int)((t - 1) & 63));   // j <= t - 1 in the latest word
+      for (int64_t w = wl; w >= 1; --w) {
+        uint64_t mo;
+        const int len = bits_word_match(sk[w], sk[w - 1], M, wq, cap, false, mo);
+        if (len > best) {
+          best = len;
+          bestj = (w << 6) + 63 - __clzll((long long)mo);
+          if (best == cap) break;
+        }
+        M = ~0ull;
+      }
+      if (best < cap) {
+        uint64_t mo;
+        const int len = bits_word_match(sk[0], 0ull, wl == 0 ? M : ~0ull, wq, cap, true, mo);
+        if (len > best) {
+          best = len;
+          bestj = 63 - __clzll((long long)mo);
+        }
+      }
+    }
+    float sign = -1.f;
+    if (bestj >= 0) {
+      const int64_t succ = bestj + 1;
+      sign = ((sv[succ >> 6] >> (succ & 63)) & 1ull) ? 1.f : -1.f;
+    }
+    const float o = pay * sign;
+    const int64_t oo = b * a.ob + t * a.ot + s * a.os;
+    if (a.out_dtype == KSD8_F32)
+      reinterpret_cast<float*>(a.out)[oo] = o;
+    else if (a.out_dtype == KSD8_BF16)
+      reinterpret_cast<__nv_bfloat16*>(a.out)[oo] = __float2bfloat16_rn(o);
+    else
+      reinterpret_cast<__half*>(a.out)[oo] = __float2half_rn(o);
+    if (a.match_len) a.match_len[stream * a.t_len + t] = best;
+    if (a.match_end) a.match_end[stream * a.t_len + t] = (int32_t)bestj;
+  }
+}
+
 struct TimemixArgs {
   const void* x;
   int64_t batch, t_len, d;
@@ -1013,15 +1113,47 @@ int ksd8_rosa_pack_bits_launch(const void* x, int x_dtype, int64_t batch, int64_
   return KSD8_OK;
 }
 
-// Matcher selection (process-wide): 0 = chunked prefix tables (default),
-// 1 = one position per step prefix tables, 2 = window scan, 3 = sorted keys
-// (streams up to 4096 + max_len - 1 positions, else as 0).  Streams of 8192 or
-// more positions always take the window scan.  algo < 0 only reads.
+// Matcher selection (process-wide): 0 = chunked prefix tables with the
+// degenerate streams redone by the sorted-key kernel (default), 1 = one
+// position per step prefix tables, 2 = window scan, 3 = sorted keys (streams
+// up to 4096 + max_len - 1 positions, else as 0), 4 = bit-parallel for every
+// stream.  Streams of 8192 or more positions take the bit-parallel kernel
+// (the window scan under 2).  algo < 0 only reads.
+// Config-4 layer (16 x 2048 positions x 512 streams): fair bits 2.28 ms
+// (0) / 6.59 (3) / 3.60 (4); bits in runs of ~10 (deep layers) 7.30 / 6.42 /
+// 7.59 ms; the bit-parallel kernel as the redo pass of 0 gave 8.47 ms there.
+// 512 streams of 8192 / 16384 positions, window scan vs bit-parallel: fair
+// bits 21.7 / 13.0 and 115.9 / 51.1 ms, runs 21.5 / 27.1 and 115.6 / 107.8 ms.
 int ksd8_rosa_algorithm(int algo) {
   static int g_algo = 0;
-  if (algo >= 0 && algo <= 3) g_algo = algo;
+  if (algo >= 0 && algo <= 4) g_algo = algo;
   return g_algo;
 }
+
+// The bit-parallel matcher over the given streams (all, or the redo list).
+static int launch_bits(const MatchArgs& a, int64_t n, cudaStream_t stream) {
+  const int nw = (int)((a.t_len + 63) / 64);
+  const size_t per_warp = (size_t)3 * nw * 8;
+  int nwarps = 8;
+  while (nwarps > 1 && (size_t)nwarps * per_warp > 227 * 1024) nwarps >>= 1;
+  const size_t smem = (size_t)nwarps * per_warp;
+  if (smem > 227 * 1024) return KSD8_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024) {
+    static unsigned attr = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 32) return KSD8_ERR_UNSUPPORTED;
+    if (!(attr & (1u << dev))) {
+      if (cudaFuncSetAttribute(rosa_match_bits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               227 * 1024) != cudaSuccess)
+        return KSD8_ERR_LAUNCH;
+      attr |= 1u << dev;
+    }
+  }
+  rosa_match_bits_kernel<<<(unsigned)((n + nwarps - 1) / nwarps), nwarps * 32, smem, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? KSD8_OK : KSD8_ERR_LAUNCH;
+}
+
 
 // The prefix-table matchers (chunked, or one position per step for algo 1).
 static int launch_chunk(const MatchArgs& a, int64_t t_len, int dev, int algo,
@@ -1105,6 +1237,7 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
     a.redo = redo;
     a.redo_budget = redo_budget();
   }
+  if (algo == 4) return launch_bits(a, batch * streams, stream);
   if (algo == 3 || a.redo) {
     if (sorted_ok) {
       const size_t head = ((size_t)np * 12 + (size_t)t_len * 2 + 15) / 16 * 16;
@@ -1140,6 +1273,7 @@ int ksd8_rosa_match_launch(const uint64_t* qw, const uint64_t* kw, const uint64_
     a.redo = nullptr;
   }
   if (t_len < RP_TMAX && algo != 2) return launch_chunk(a, t_len, dev, algo, stream);
+  if (algo != 2) return launch_bits(a, batch * streams, stream);
   int threads = 512;
   if (t_len <= 256) threads = 256;
   rosa_match_kernel<<<(unsigned)(batch * streams), threads, smem, stream>>>(a);

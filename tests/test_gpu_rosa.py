@@ -39,7 +39,7 @@ def _streams(rng, S, T, repeat_frac=0.3):
 
 @pytest.mark.parametrize("S,T", [(8, 1), (8, 2), (16, 33), (16, 64), (16, 65), (12, 300),
                                  (6, 1000), (3, 4096), (64, 2048),
-                                 (2, 8300)])   # T >= 8192: the brute-force kernel
+                                 (2, 8300)])   # T >= 8192: the bit-parallel kernel
 def test_match_indices_vs_oracle(oracle, S, T):
     from ksdraft_b200.model.rosa import match_payload_sign_with_indices
     rng = np.random.default_rng(S * 1000 + T)
@@ -62,16 +62,17 @@ def rosa_algorithm():
     use(0)
 
 
-@pytest.mark.parametrize("algo", [0, 1, 2, 3])
+@pytest.mark.parametrize("algo", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("S,T,max_len", [(16, 31, None), (16, 32, None), (16, 97, None),
                                          (40, 700, None), (8, 2048, None), (8, 700, 5),
                                          (8, 700, 12), (8, 700, 13), (5, 3000, 40),
                                          (4, 4157, None), (6, 300, 64), (6, 200, 1)])
 def test_match_kernels_agree_with_oracle(oracle, rosa_algorithm, algo, S, T, max_len):
     """Every matcher kernel (chunked prefix tables, per-position prefix tables,
-    window scan) gives the oracle's signs, lengths and endpoints, across chunk
-    boundaries, around the 12-level table depth and with explicit caps; highly
-    repetitive streams make many prefix collisions inside one 32-position chunk."""
+    window scan, sorted keys, bit-parallel) gives the oracle's signs, lengths
+    and endpoints, across chunk boundaries, around the 12-level table depth and
+    with explicit caps; highly repetitive streams make many prefix collisions
+    inside one 32-position chunk."""
     from ksdraft_b200.model.rosa import match_payload_sign_with_indices
     rosa_algorithm(algo)
     rng = np.random.default_rng(S * 7 + T)
