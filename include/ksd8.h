@@ -54,6 +54,7 @@
  *                             keys appended since it was built
  *   ksd8_rosa_decode_step     ksdraft/model/rosa.py:40-98 _match_payload_sign (+ :164 payload)
  *                             answered for positions appended to a matched context
+ *   ksd8_rosa_credits         ksdraft/kernels/rosa_credit_gpu.py:25-48 _chunk_credits
  */
 #ifndef KSD8_H_
 #define KSD8_H_
@@ -254,6 +255,21 @@ int ksd8_rosa_match_scratch(const uint64_t* qw, const uint64_t* kw, const uint64
  * bits) per position).  T >= 8192 takes the bit-parallel kernel (the window
  * scan under 2). */
 int ksd8_rosa_set_algorithm(int algo);
+
+/* Counterfactual credits of the hard Rosa core, ksdraft/kernels/rosa_credit_gpu.py:25-48
+ * (HardRosaGPU.backward's _chunk_credits; the reference stops at T <= 63):
+ * for stream r and every position p, credit_X[r * T + p] = sum over t of
+ * (sign'(t) - sign(t)) * grad[r * T + t], sign' the match signs (rosa.py:40-98,
+ * cap max_len) with bit X[p] flipped, X = q, k, v; grad (streams, T) fp32 =
+ * dL/d sign; bits as ksd8_rosa_pack_bits packs them.  Exact: only the
+ * positions a flip can change are re-matched.  Work grows as T^2 per stream
+ * (about 64 key comparisons per (flip, later position)); t_len <=
+ * KSD8_ROSA_CREDITS_TMAX. */
+#define KSD8_ROSA_CREDITS_TMAX 16384
+int ksd8_rosa_credits(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
+                      int64_t streams, int64_t t_len, int max_len, const float* grad,
+                      float* credit_q, float* credit_k, float* credit_v, int* status,
+                      void* stream);
 
 /* Rosa time-shift mix + per-token GS quantisation of the three projection
  * inputs: x (B, T, d) bf16/f32; mix_q/k/v (d) fp32 = sigmoid(time_mix_*);

@@ -48,6 +48,7 @@ SIGNATURES: dict[str, list] = {
     "ksd8_ks3_vjp_reduce": [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp],
     "ksd8_ks3_vjp_reduce_f32": [vp, i64, i64, vp, vp, vp, vp, vp, vp, vp],
     "ksd8_rosa_pack_bits": [vp, i32, i64, i64, i64, i64, i64, i64, vp, vp, vp],
+    "ksd8_rosa_credits": [vp, vp, vp, i64, i64, i32, vp, vp, vp, vp, vp, vp],
     "ksd8_rosa_match": [vp, vp, vp, i64, i64, i64, i32, vp, vp, i32, i64, i64, i64, vp, vp, vp,
                         vp],
     "ksd8_rosa_match_scratch": [vp, vp, vp, i64, i64, i64, i32, vp, vp, i32, i64, i64, i64, vp,

@@ -30,6 +30,8 @@ int ksd8_ks3_vjp_reduce_launch(const float*, int64_t, int64_t, const float*, con
                                void*, void*, int*, cudaStream_t, float*, float*, float*);
 int ksd8_rosa_pack_bits_launch(const void*, int, int64_t, int64_t, int64_t, int64_t, int64_t,
                                int64_t, uint64_t*, cudaStream_t);
+int ksd8_rosa_credits_launch(const uint64_t*, const uint64_t*, const uint64_t*, int64_t, int64_t,
+                             int, const float*, float*, float*, float*, cudaStream_t);
 int ksd8_rosa_match_launch(const uint64_t*, const uint64_t*, const uint64_t*, int64_t, int64_t,
                            int64_t, int, const float*, void*, int, int64_t, int64_t, int64_t,
                            int32_t*, int32_t*, cudaStream_t, int32_t*);
@@ -326,6 +328,20 @@ int ksd8_rosa_match_scratch(const uint64_t* qw, const uint64_t* kw, const uint64
   return finish(ksd8_rosa_match_launch(qw, kw, vw, batch, streams, t_len, max_len, payload, out,
                                        out_dtype, ob, ot, os, match_len, match_end, S(stream),
                                        scratch));
+}
+
+int ksd8_rosa_credits(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
+                      int64_t streams, int64_t t_len, int max_len, const float* grad,
+                      float* credit_q, float* credit_k, float* credit_v, int* status,
+                      void* stream) {
+  (void)status;
+  if (streams < 0 || t_len < 0) return KSD8_ERR_SHAPE;
+  if (max_len < 0 || max_len > 64) return KSD8_ERR_ARG;
+  if (t_len > KSD8_ROSA_CREDITS_TMAX) return KSD8_ERR_UNSUPPORTED;
+  if (streams * t_len > 0 && (!qw || !kw || !vw || !grad || !credit_q || !credit_k || !credit_v))
+    return KSD8_ERR_ARG;
+  return finish(ksd8_rosa_credits_launch(qw, kw, vw, streams, t_len, max_len, grad, credit_q,
+                                         credit_k, credit_v, S(stream)));
 }
 
 int ksd8_rosa_timemix_quantize(const void* x, int x_dtype, int64_t batch, int64_t t_len,

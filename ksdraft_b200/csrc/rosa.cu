@@ -1015,6 +1015,187 @@ __global__ void __launch_bounds__(512) rosa_payload_bwd_kernel(
   }
 }
 
+// ---------------------------------------------------------------- counterfactual credits
+//
+// HardRosaGPU's backward (ksdraft/kernels/rosa_credit_gpu.py:25-48): for every
+// q, k and v bit of a stream, flip it, re-match the whole window and sum
+// (sign' - sign) * grad over the positions, grad = dL/d sign.  The reference
+// builds all 3T perturbed streams and re-matches each in full (T <= 63); here
+// only what a flip can change is recomputed, exactly:
+//   v[p]  the sign of the positions whose match ends at p - 1 (closed form);
+//   q[p]  the queries t in [p, p + 61] whose window has bit p at depth
+//         l = t - p <= their match length (a shallower bit cannot change a
+//         capped match): one full re-match each;
+//   k[p]  the keys j in [p, p + 63] (their windows hold k[p] at depth j - p).
+//         For a query t > p whose best key is not one of them, or is one whose
+//         capped length does not drop, the new answer is the better of the old
+//         one and the 64 changed keys; otherwise one full re-match with k[p]
+//         flipped.  A query whose best key is later than every changed key and
+//         already at the cap cannot change.
+// One CTA per stream: 8 warps share the stream's words, gradients and base
+// matches in shared memory; warp w takes the flips p = w, w + 8, ...
+struct CreditArgs {
+  const uint64_t* qw;
+  const uint64_t* kw;
+  const uint64_t* vw;
+  const float* grad;   // (rows, T) dL/d sign
+  float* cq;           // (rows, T) credits of the q, k, v bits
+  float* ck;
+  float* cv;
+  int64_t rows, t_len;
+  int max_len;
+};
+
+constexpr int CR_WARPS = 8;
+
+// longest capped match of query window wq at t against keys j <= t - 1, the
+// latest among the longest (bit-parallel per k word, as rosa_match_bits_kernel);
+// fp >= 0: the k bit at position fp reads flipped
+__device__ __forceinline__ int credit_match(const uint64_t* sk, int64_t t, uint64_t wq, int cap,
+                                            int64_t fp, int64_t& bestj) {
+  int best = 0;
+  bestj = -1;
+  if (cap <= 0) return 0;
+  const int64_t fw = fp >= 0 ? (fp >> 6) : -1;
+  const uint64_t fm = fp >= 0 ? (1ull << (fp & 63)) : 0ull;
+  auto kword = [&](int64_t w) -> uint64_t { return sk[w] ^ (w == fw ? fm : 0ull); };
+  const int64_t wl = (t - 1) >> 6;
+  uint64_t M = ~0ull >> (63 - (int)((t - 1) & 63));
+  for (int64_t w = wl; w >= 1; --w) {
+    uint64_t mo;
+    const int len = bits_word_match(kword(w), kword(w - 1), M, wq, cap, false, mo);
+    if (len > best) {
+      best = len;
+      bestj = (w << 6) + 63 - __clzll((long long)mo);
+      if (best == cap) return best;
+    }
+    M = ~0ull;
+  }
+  uint64_t mo;
+  const int len = bits_word_match(kword(0), 0ull, wl == 0 ? M : ~0ull, wq, cap, true, mo);
+  if (len > best) {
+    best = len;
+    bestj = 63 - __clzll((long long)mo);
+  }
+  return best;
+}
+
+__device__ __forceinline__ float credit_sign(const uint64_t* sv, int64_t j) {
+  if (j < 0) return -1.f;
+  const int64_t s = j + 1;
+  return ((sv[s >> 6] >> (s & 63)) & 1ull) ? 1.f : -1.f;
+}
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void __launch_bounds__(CR_WARPS * 32) rosa_credits_kernel(CreditArgs a) {
+  extern __shared__ __align__(16) uint8_t crs[];
+  const int64_t row = blockIdx.x;
+  const int T = (int)a.t_len;
+  const int nw = (T + 63) / 64;
+  const int ml = a.max_len;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* sq = reinterpret_cast<uint64_t*>(crs);
+  uint64_t* sk = sq + nw;
+  uint64_t* sv = sk + nw;
+  uint64_t* cw_all = sv + nw;                                   // [CR_WARPS][64] changed windows
+  float* g = reinterpret_cast<float*>(cw_all + CR_WARPS * 64);  // [T]
+  int16_t* bj = reinterpret_cast<int16_t*>(g + T);              // [T] base endpoints
+  int8_t* bl = reinterpret_cast<int8_t*>(bj + T);               // [T] base lengths
+  for (int i = threadIdx.x; i < nw; i += blockDim.x) {
+    sq[i] = a.qw[row * nw + i];
+    sk[i] = a.kw[row * nw + i];
+    sv[i] = a.vw[row * nw + i];
+  }
+  for (int i = threadIdx.x; i < T; i += blockDim.x) g[i] = a.grad[row * T + i];
+  __syncthreads();
+  // base matches
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    int64_t j;
+    const int len = credit_match(sk, t, window_sm(sq, t), min(ml, t), -1, j);
+    bl[t] = (int8_t)len;
+    bj[t] = (int16_t)j;
+  }
+  __syncthreads();
+  // v[p]: positions whose match ends at p - 1 read their sign from v[p]
+  for (int p = threadIdx.x; p < T; p += blockDim.x) {
+    float c = 0.f;
+    const float s = ((sv[p >> 6] >> (p & 63)) & 1ull) ? 1.f : -1.f;
+    for (int t = 0; t < T; ++t)
+      if (bj[t] >= 0 && bj[t] + 1 == p) c += (-2.f * s) * g[t];
+    a.cv[row * T + p] = c;
+  }
+  // q[p]: queries t = p .. p + 61 whose window holds bit p at depth <= their length
+  for (int p = warp; p < T; p += CR_WARPS) {
+    float c = 0.f;
+#pragma unroll
+    for (int r = 0; r < 64; r += 32) {
+      const int t = p + r + lane;
+      const int l = r + lane;
+      if (t < T) {
+        const int cap = min(ml, t);
+        if (l < cap && l <= bl[t]) {
+          const uint64_t wq = window_sm(sq, t) ^ (1ull << (63 - l));
+          int64_t nj;
+          credit_match(sk, t, wq, cap, -1, nj);
+          c += (credit_sign(sv, nj) - credit_sign(sv, bj[t])) * g[t];
+        }
+      }
+    }
+    c = warp_sum_f(c);
+    if (lane == 0) a.cq[row * T + p] = c;
+  }
+  // k[p]: keys p .. p + 63 change
+  uint64_t* cw = cw_all + warp * 64;
+  for (int p = warp; p < T; p += CR_WARPS) {
+#pragma unroll
+    for (int r = 0; r < 64; r += 32) {
+      const int j = p + r + lane;
+      cw[r + lane] = j < T ? (window_sm(sk, j) ^ (1ull << (63 - (r + lane)))) : 0ull;
+    }
+    __syncwarp();
+    float c = 0.f;
+    for (int t = p + 1 + lane; t < T; t += 32) {
+      const int cap = min(ml, t);
+      const int best = bl[t];
+      const int64_t bestj = bj[t];
+      if (best == cap && bestj > p + 63) continue;   // a later key already at the cap
+      const uint64_t wq = window_sm(sq, t);
+      int nb = best;
+      int64_t nbj = bestj;
+      bool full = false;
+      if (bestj >= p && bestj <= p + 63) {
+        const uint64_t x = wq ^ cw[bestj - p];
+        const int raw = x ? __clzll((long long)x) : 64;
+        full = min(raw, min(cap, (int)bestj + 1)) < best;
+      }
+      if (full) {
+        nb = credit_match(sk, t, wq, cap, p, nbj);
+      } else {
+        const int hi = min(63, t - 1 - p);
+        for (int i = 0; i <= hi; ++i) {
+          const int64_t j = p + i;
+          const uint64_t x = wq ^ cw[i];
+          int len = x ? __clzll((long long)x) : 64;
+          len = min(len, min(cap, (int)j + 1));
+          if (len > nb || (len == nb && len > 0 && j > nbj)) {
+            nb = len;
+            nbj = j;
+          }
+        }
+      }
+      c += (credit_sign(sv, nbj) - credit_sign(sv, bestj)) * g[t];
+    }
+    c = warp_sum_f(c);
+    if (lane == 0) a.ck[row * T + p] = c;
+    __syncwarp();   // cw is rewritten for the next p
+  }
+}
+
 }  // namespace ksd8
 
 using namespace ksd8;
@@ -1317,4 +1498,35 @@ int ksd8_adamw_launch(float* p, const void* g, int gdt, float* m, float* v, int6
   adamw_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p, g, gdt, m, v, n, lr, b1, b2, eps, wd, bc1,
                                                       sqrtf(bc2), gscale);
   return KSD8_OK;
+}
+
+// shared memory of rosa_credits_kernel for a stream of t_len positions
+static size_t credits_smem(int64_t t_len) {
+  const int64_t nw = (t_len + 63) / 64;
+  return (size_t)(3 * nw + CR_WARPS * 64) * 8 + (size_t)t_len * (4 + 2 + 1) + 16;
+}
+
+int ksd8_rosa_credits_launch(const uint64_t* qw, const uint64_t* kw, const uint64_t* vw,
+                             int64_t rows, int64_t t_len, int max_len, const float* grad,
+                             float* cq, float* ck, float* cv, cudaStream_t stream) {
+  if (rows == 0 || t_len == 0) return KSD8_OK;
+  const size_t smem = credits_smem(t_len);
+  if (smem > 227 * 1024) return KSD8_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024) {
+    static unsigned attr = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 32) return KSD8_ERR_UNSUPPORTED;
+    if (!(attr & (1u << dev))) {
+      if (cudaFuncSetAttribute(rosa_credits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               227 * 1024) != cudaSuccess)
+        return KSD8_ERR_LAUNCH;
+      attr |= 1u << dev;
+    }
+  }
+  CreditArgs a;
+  a.qw = qw; a.kw = kw; a.vw = vw; a.grad = grad; a.cq = cq; a.ck = ck; a.cv = cv;
+  a.rows = rows; a.t_len = t_len; a.max_len = max_len;
+  rosa_credits_kernel<<<(unsigned)rows, CR_WARPS * 32, smem, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? KSD8_OK : KSD8_ERR_LAUNCH;
 }

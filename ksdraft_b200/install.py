@@ -6,13 +6,14 @@
 
 Whole modules are replaced where this package mirrors every public name of
 the reference module (ksdraft/kernels/{quant,gemm,linear,ks3_int8,
-ks3_triton}.py): their entries in `sys.modules` point at the mirrors, so the
-reference's own `from .quant import ...` statements bind the B200 functions.
+ks3_triton,rosa_credit_gpu}.py): their entries in `sys.modules` point at the
+mirrors, so the reference's own `from .quant import ...` statements (and
+RosaMixer's `from ..kernels.rosa_credit_gpu import HardRosaGPU`) bind the B200
+code.
 Where the reference module holds more than the hot path, single functions
 are patched instead:
   ksdraft/model/rosa.py:40      _match_payload_sign (RosaMixer.forward looks
                                 it up at call time, rosa.py:161)
-  ksdraft/kernels/rosa_credit_gpu.py:23  the same function as HardRosaGPU binds it
   ksdraft/train/stages.py:27    quantize_last_dim_dithered
 """
 
@@ -22,11 +23,9 @@ import importlib
 import importlib.util
 import sys
 
-KERNEL_MODULES = ("quant", "gemm", "linear", "ks3_int8", "ks3_triton")
+KERNEL_MODULES = ("quant", "gemm", "linear", "ks3_int8", "ks3_triton", "rosa_credit_gpu")
 PATCHED_FUNCTIONS = (
     ("model.rosa", "_match_payload_sign", "ksdraft_b200.model.rosa"),
-    # bound by name at import (rosa_credit_gpu.py:23): HardRosaGPU's re-matches
-    ("kernels.rosa_credit_gpu", "_match_payload_sign", "ksdraft_b200.model.rosa"),
     ("train.stages", "quantize_last_dim_dithered", "ksdraft_b200.train.stages"),
 )
 

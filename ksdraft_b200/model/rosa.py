@@ -147,11 +147,15 @@ class RosaMixer(nn.Module):
         _lib.require_cuda(x)
         if self._fused_int8_eval():
             return rosa_forward_int8(self, x)
-        # Training takes the reference's hard path (rosa.py:154-165, the path it
-        # runs when no credit engine is present): gradients reach the payload
-        # scales and the output projection only; the counterfactual credits of
-        # HardRosaGPU (T <= 63) are not part of this build.
         q_in, k_in, v_in = self._shifted(x)
+        if self.training:
+            # the reference's CUDA training path (rosa.py:141-145): the hard core
+            # through HardRosaGPU, whose counterfactual credits give the q / k / v
+            # projections gradients (ValueError beyond its window, as there)
+            from ..kernels.rosa_credit_gpu import HardRosaGPU
+            hard = HardRosaGPU.apply(self.q_proj(q_in), self.k_proj(k_in), self.v_proj(v_in),
+                                     self.payload)
+            return self.out_proj(hard.to(x.dtype))
         qbits = (self.q_proj(q_in) > 0).to(torch.int8)
         kbits = (self.k_proj(k_in) > 0).to(torch.int8)
         vbits = (self.v_proj(v_in) > 0).to(torch.int8)

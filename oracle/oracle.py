@@ -408,6 +408,27 @@ def rosa_match(q, k, v, max_match_len=None, method="bruteforce"):
     return sign, L, E
 
 
+def rosa_credits(q, k, v, grad, max_match_len=None):
+    """Counterfactual credits of ksdraft/kernels/rosa_credit_gpu.py:25-48
+    (_chunk_credits), by brute force: for every stream and every q / k / v bit,
+    the whole stream re-matched with that bit flipped (rosa_match, dp), and
+    credit = sum_t (sign' - sign) * grad.  q, k, v (S, T) int8 bits, grad (S, T)
+    fp32 = dL/d sign.  Returns (cq, ck, cv), each (S, T) float64."""
+    q, k, v = (_c(b, np.int8) for b in (q, k, v))
+    grad = np.asarray(grad, np.float64)
+    S, T = q.shape
+    out = [np.zeros((S, T), np.float64) for _ in range(3)]
+    base, _, _ = rosa_match(q, k, v, max_match_len, method="dp")
+    idx = np.arange(T)
+    for s in range(S):
+        for which in range(3):
+            pert = [np.repeat(x[s][None, :], T, 0) for x in (q, k, v)]   # (T, T): row p flips bit p
+            pert[which][idx, idx] ^= 1
+            sp, _, _ = rosa_match(*pert, max_match_len, method="dp")
+            out[which][s] = ((sp.astype(np.float64) - base[s][None, :]) * grad[s][None, :]).sum(1)
+    return tuple(out)
+
+
 def _bf16(a: np.ndarray) -> np.ndarray:
     """Round fp32 values to bfloat16 (round to nearest even), returned as fp32."""
     u = np.ascontiguousarray(a, np.float32).view(np.uint32)

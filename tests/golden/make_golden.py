@@ -397,6 +397,35 @@ def gen_draft_eval():
          seed=np.int64(seed), margin=np.float32(margin))
 
 
+def gen_rosa_credits():
+    """HardRosaGPU (ksdraft/kernels/rosa_credit_gpu.py:51-112, torch ops, run on
+    the CPU here) forward and backward: the hard output and the gradients of
+    q / k / v (counterfactual credits through the Bernoulli map) and payload,
+    on random projections (tests/test_rosa_credit_gpu.py:12-19 regime) and on
+    projections whose signs come in long runs (long matches, the 62-bit cap)."""
+    from ksdraft.kernels.rosa_credit_gpu import HardRosaGPU
+    out = {}
+    g = torch.Generator().manual_seed(21)
+    cases = {"small": (2, 16, 8, False), "runs": (1, 63, 6, True), "mid": (2, 40, 5, False)}
+    for name, (B, T, S, runs) in cases.items():
+        q, k, v = (torch.randn(B, T, S, generator=g) * 2 for _ in range(3))
+        if runs:   # signs flip with probability 0.1 per position
+            for x in (q, k, v):
+                flips = (torch.rand(B, T, S, generator=g) < 0.1).to(torch.int64)
+                sgn = 1.0 - 2.0 * (torch.cumsum(flips, 1) % 2).float()
+                x.copy_(x.abs() * sgn)
+        payload = torch.randn(S, generator=g).abs() + 0.5
+        gy = torch.randn(B, T, S, generator=g)
+        leaves = [t.clone().requires_grad_(True) for t in (q, k, v, payload)]
+        y = HardRosaGPU.apply(*leaves)
+        y.backward(gy)
+        out.update({f"{name}_q": f32(q), f"{name}_k": f32(k), f"{name}_v": f32(v),
+                    f"{name}_payload": f32(payload), f"{name}_gy": f32(gy), f"{name}_y": f32(y),
+                    f"{name}_gq": f32(leaves[0].grad), f"{name}_gk": f32(leaves[1].grad),
+                    f"{name}_gv": f32(leaves[2].grad), f"{name}_gp": f32(leaves[3].grad)})
+    save("rosa_credits", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("KSD8_REFERENCE"),
@@ -409,7 +438,8 @@ def main():
     torch.set_num_threads(8)
     topics = {"quant": gen_quant, "dither": gen_dither, "gemm": gen_gemm, "ks3_spine": gen_ks3,
               "ks3_layer": gen_ks3_layer, "rosa": gen_rosa, "tanh16": gen_tanh16,
-              "linear": gen_linear, "draft_step": gen_draft_step, "draft_eval": gen_draft_eval}
+              "linear": gen_linear, "draft_step": gen_draft_step, "draft_eval": gen_draft_eval,
+              "rosa_credits": gen_rosa_credits}
     for name, fn in topics.items():
         if args.only is None or name in args.only:
             fn()

@@ -166,27 +166,25 @@ def test_rosa_mixer_int8_eval_vs_oracle(oracle):
     np.testing.assert_array_equal(y.float().cpu().numpy(), y_o)
 
 
-def test_rosa_mixer_training_hard_path():
-    """Training mode takes the reference's hard path (rosa.py:154-165): gradients
-    reach payload and out_proj only, equal to autograd of the composition."""
-    from ksdraft_b200.model.rosa import _match_payload_sign
+def test_rosa_mixer_training_credits():
+    """Training mode takes the reference's CUDA path (rosa.py:141-145): the hard
+    core through HardRosaGPU, so the q / k / v projections receive the
+    counterfactual credits; equal to autograd of the explicit composition."""
+    import copy
+    from ksdraft_b200.kernels.rosa_credit_gpu import HardRosaGPU
     B, T, d, S = 2, 200, 256, 128
     m = _mixer(d, S, 3).train()
+    ref = copy.deepcopy(m)
     x = torch.randn(B, T, d, device="cuda")
+    gy = torch.randn(B, T, d, device="cuda")
     y = m(x)
-    gy = torch.randn_like(y)
     y.backward(gy)
-    with torch.no_grad():
-        q_in, k_in, v_in = m._shifted(x)
-        bits = [(getattr(m, f"{c}_proj")(i) > 0).to(torch.int8).permute(0, 2, 1)
-                for c, i in zip("qkv", (q_in, k_in, v_in))]
-        sign = _match_payload_sign(*bits)
-    pay = m.payload.detach().clone().requires_grad_(True)
-    wo = m.out_proj.weight.detach().clone().requires_grad_(True)
-    bo = m.out_proj.bias.detach().clone().requires_grad_(True)
-    yr = torch.nn.functional.linear((pay[None, :, None] * sign).permute(0, 2, 1), wo, bo)
+    q_in, k_in, v_in = ref._shifted(x)
+    hard = HardRosaGPU.apply(ref.q_proj(q_in), ref.k_proj(k_in), ref.v_proj(v_in), ref.payload)
+    yr = ref.out_proj(hard.to(x.dtype))
     yr.backward(gy)
-    assert torch.allclose(y, yr, rtol=1e-5, atol=1e-6)
-    assert torch.allclose(m.payload.grad, pay.grad, rtol=1e-4, atol=1e-5)
-    assert torch.allclose(m.out_proj.weight.grad, wo.grad, rtol=1e-4, atol=1e-5)
-    assert m.q_proj.weight.grad is None and m.time_mix_q.grad is None
+    assert torch.equal(y, yr)
+    for (n, p_), (_, pr) in zip(m.named_parameters(), ref.named_parameters()):
+        assert p_.grad is not None and torch.isfinite(p_.grad).all(), n
+        assert torch.equal(p_.grad, pr.grad), n
+    assert m.q_proj.weight.grad.abs().sum() > 0          # the credits reach the projections

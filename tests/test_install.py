@@ -22,7 +22,7 @@ FILES = {
     "ksdraft/kernels/linear.py": "Int8Linear = 'reference'\n",
     "ksdraft/kernels/ks3_int8.py": "KS3Int8Cell = 'reference'\n",
     "ksdraft/kernels/ks3_triton.py": "project_fused = 'reference'\n",
-    "ksdraft/kernels/rosa_credit_gpu.py": "from ..model.rosa import _match_payload_sign\n",
+    "ksdraft/kernels/rosa_credit_gpu.py": "MAX_WINDOW = 63\nHardRosaGPU = 'reference'\n",
     "ksdraft/model/__init__.py": "",
     "ksdraft/model/rosa.py":
         "_match_payload_sign = 'reference'\n"
@@ -73,7 +73,8 @@ def test_install_rebinds_modules_and_functions(tmp_path):
         assert stages.quantize_last_dim_dithered is s.quantize_last_dim_dithered
         assert stages.wtv_loss() == 'kept'                             # rest untouched
         import ksdraft.kernels.rosa_credit_gpu as cg
-        assert cg._match_payload_sign is r._match_payload_sign         # bound by name
+        import ksdraft_b200.kernels.rosa_credit_gpu as mine
+        assert cg is mine and cg.HardRosaGPU is mine.HardRosaGPU      # the whole module
         print(len(done))
     """))
     assert out.strip() == "8"

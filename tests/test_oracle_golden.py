@@ -264,3 +264,32 @@ def test_int8_linear_ste_matches_reference(golden, oracle):
         wq, ws = oracle.quantize_rows_c(g[f"c{i}_w"])
         plain = g[f"c{i}_gy"] @ oracle.dequantize_last_dim(wq, ws)
         assert _rel(plain, g[f"c{i}_dx"]) > 0.1
+
+
+def _credit_grads(oracle, g, name):
+    """q / k / v gradients of HardRosaGPU (rosa_credit_gpu.py:79-112) from the
+    oracle's brute-force credits, in the reference's float32 arithmetic."""
+    q, k, v = (g[f"{name}_{c}"] for c in "qkv")
+    B, T, S = q.shape
+    gy, payload = g[f"{name}_gy"], g[f"{name}_payload"]
+    bits = [(x > 0).astype(np.int8).transpose(0, 2, 1).reshape(B * S, T) for x in (q, k, v)]
+    gs = (gy.transpose(0, 2, 1) * payload[None, :, None]).astype(np.float32).reshape(B * S, T)
+    cr = oracle.rosa_credits(*bits, gs)
+    out = []
+    for c, b, pre in zip(cr, bits, (q, k, v)):
+        delta = (c * (1 - 2 * b.astype(np.float64))).astype(np.float32).reshape(B, S, T)
+        s = 1.0 / (1.0 + np.exp(-pre.astype(np.float64)))
+        out.append(delta.transpose(0, 2, 1) * (s * (1 - s)).astype(np.float32))
+    return out
+
+
+@pytest.mark.parametrize("name", ["small", "runs", "mid"])
+def test_rosa_credits_match_reference(golden, oracle, name):
+    """The oracle's brute-force counterfactual credits, mapped through the
+    Bernoulli factor, give the q / k / v gradients of the reference's own
+    HardRosaGPU (tests/golden/rosa_credits.npz, run on the CPU)."""
+    g = golden("rosa_credits")
+    for got, c in zip(_credit_grads(oracle, g, name), "qkv"):
+        ref = g[f"{name}_g{c}"]
+        err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
+        assert err < 1e-5, (name, c, err)
