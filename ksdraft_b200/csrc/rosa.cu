@@ -821,47 +821,105 @@ struct TimemixArgs {
   __half* scales[3];
 };
 
-// One warp per (token, 128-wide group); lane owns 4 consecutive features.
+// One warp per (128-wide group, run of TM_TOKENS consecutive tokens); a lane
+// owns 4 consecutive features.  The mix factors stay in registers for the
+// run, a token's row is the next token's `prev` (one load per element), and
+// the codes come from the packed four-code path (gs_code4_normal: one
+// multiply by RN(1/scale) and the 1.5 * 2^23 shifter, the IEEE division only
+// near a rounding tie), as in the row quantiser.
+constexpr int TM_TOKENS = 16;
+
+template <typename T>
+__device__ __forceinline__ void load4f(const T* p, bool full, int n, float (&o)[4]) {
+  if constexpr (sizeof(T) == 4) {
+    if (full) {
+      const float4 v = *reinterpret_cast<const float4*>(p);
+      o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+      return;
+    }
+  } else {
+    if (full) {
+      const uint2 v = *reinterpret_cast<const uint2*>(p);
+      const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = (float)h[i];
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = i < n ? (float)p[i] : 0.f;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) rosa_timemix_quant_kernel(TimemixArgs a) {
   const int64_t groups = (a.d + 127) / 128;
   const int64_t tokens = a.batch * a.t_len;
-  const int64_t total = tokens * groups;
+  const int64_t runs = (tokens + TM_TOKENS - 1) / TM_TOKENS;
+  const int64_t total = groups * runs;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const T* x = reinterpret_cast<const T*>(a.x);
+  // vector loads need 4 whole features in range and 16-/8-byte aligned rows
+  const bool vec = (a.d % 4) == 0 && (reinterpret_cast<uintptr_t>(a.x) % (4 * sizeof(T))) == 0;
   for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total;
        w += nwarps) {
-    const int64_t tok = w / groups, g = w - tok * groups;
-    const int64_t t = tok % a.t_len;
+    const int64_t g = w % groups, run = w / groups;
     const int64_t c = g * 128 + lane * 4;
-    float cur[4], prev[4], diff[4];
+    const int n = (int)max((int64_t)0, min((int64_t)4, a.d - c));
+    const bool full = vec && n == 4;
+    float mix[3][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const bool in = c + i < a.d;
-      cur[i] = in ? (float)x[tok * a.d + c + i] : 0.f;
-      prev[i] = (in && t > 0) ? (float)x[(tok - 1) * a.d + c + i] : 0.f;
-      // (x - prev) is evaluated in x's dtype
-      if constexpr (sizeof(T) == 2) diff[i] = (float)(T)(cur[i] - prev[i]);
-      else diff[i] = cur[i] - prev[i];
-    }
+    for (int p = 0; p < 3; ++p)
 #pragma unroll
-    for (int p = 0; p < 3; ++p) {
-      float v[4];
+      for (int i = 0; i < 4; ++i) mix[p][i] = i < n ? a.mix[p][c + i] : 0.f;
+    const int64_t tok0 = run * TM_TOKENS;
+    const int64_t tok1 = min(tokens, tok0 + TM_TOKENS);
+    float prev[4] = {0.f, 0.f, 0.f, 0.f};
+    if (tok0 % a.t_len != 0 && n > 0) load4f(x + (tok0 - 1) * a.d + c, full, n, prev);
+    for (int64_t tok = tok0; tok < tok1; ++tok) {
+      if (tok % a.t_len == 0) {  // a sequence starts: prev is the zero padding
+#pragma unroll
+        for (int i = 0; i < 4; ++i) prev[i] = 0.f;
+      }
+      float cur[4] = {0.f, 0.f, 0.f, 0.f};
+      if (n > 0) load4f(x + tok * a.d + c, full, n, cur);
+      float diff[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float mix = (c + i < a.d) ? a.mix[p][c + i] : 0.f;
-        v[i] = __fadd_rn(prev[i], __fmul_rn(diff[i], mix));
+        // (x - prev) is evaluated in x's dtype
+        if constexpr (sizeof(T) == 2) diff[i] = (float)(T)(cur[i] - prev[i]);
+        else diff[i] = cur[i] - prev[i];
       }
-      float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-      m = warp_max(m);
-      __half sh;
-      const float scale = gs_scale(m, &sh);
-      int8_t* out = a.codes[p] + tok * a.d + c;
+      // the three projection inputs, their group maxima reduced together
+      float vv[3][4], mm[3];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (c + i < a.d) out[i] = (int8_t)gs_code(v[i], scale);
-      if (lane == 0) a.scales[p][tok * groups + g] = sh;
+      for (int p = 0; p < 3; ++p) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) vv[p][i] = __fadd_rn(prev[i], __fmul_rn(diff[i], mix[p][i]));
+        mm[p] = fmaxf(fmaxf(fabsf(vv[p][0]), fabsf(vv[p][1])), fmaxf(fabsf(vv[p][2]), fabsf(vv[p][3])));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int p = 0; p < 3; ++p) mm[p] = fmaxf(mm[p], __shfl_xor_sync(0xffffffffu, mm[p], o));
+#pragma unroll
+      for (int p = 0; p < 3; ++p) {
+        const float (&v)[4] = vv[p];
+        const float m = mm[p];
+        __half sh;
+        const float scale = gs_scale_fast(m, &sh);
+        int8_t* out = a.codes[p] + tok * a.d + c;
+        if (n == 4 && gs_scale_is_normal(m, scale) && (reinterpret_cast<uintptr_t>(out) & 3) == 0) {
+          *reinterpret_cast<uint32_t*>(out) = gs_code4_normal(v, scale, rcp_approx(scale));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (i < n) out[i] = (int8_t)gs_code(v[i], scale);
+        }
+        if (lane == 0) a.scales[p][tok * groups + g] = sh;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) prev[i] = cur[i];
     }
   }
 }
@@ -1500,8 +1558,8 @@ int ksd8_rosa_timemix_launch(const void* x, int x_dtype, int64_t batch, int64_t 
   a.scales[0] = reinterpret_cast<__half*>(qs);
   a.scales[1] = reinterpret_cast<__half*>(ks);
   a.scales[2] = reinterpret_cast<__half*>(vs);
-  const int64_t work = batch * t_len * ((d + 127) / 128);
-  if (work == 0) return KSD8_OK;
+  const int64_t work = (batch * t_len + TM_TOKENS - 1) / TM_TOKENS * ((d + 127) / 128);
+  if (work == 0 || d == 0) return KSD8_OK;
   int64_t blocks = (work + 7) / 8;
   if (blocks > 148 * 16) blocks = 148 * 16;
   switch (x_dtype) {

@@ -188,3 +188,35 @@ def test_rosa_mixer_training_credits():
         assert p_.grad is not None and torch.isfinite(p_.grad).all(), n
         assert torch.equal(p_.grad, pr.grad), n
     assert m.q_proj.weight.grad.abs().sum() > 0          # the credits reach the projections
+
+
+@pytest.mark.parametrize("dtype,B,T,d", [(torch.float32, 3, 37, 200), (torch.bfloat16, 2, 50, 256),
+                                         (torch.bfloat16, 1, 20, 130), (torch.float16, 2, 33, 128)])
+def test_timemix_quantize_vs_oracle(oracle, dtype, B, T, d):
+    """ksd8_rosa_timemix_quantize (_shifted, rosa.py:128-133, then the GS128
+    quantisation of each projection input) against the oracle's row quantiser
+    of the same fp32 values: codes and scales bit-exact, across runs of tokens
+    that straddle sequence starts and a partial last group."""
+    from ksdraft_b200 import _lib
+    g = torch.Generator().manual_seed(B * 100 + T + d)
+    x = (torch.randn(B, T, d, generator=g) * 3).to(dtype)
+    x[0, 5, :7] = 0
+    mixes = [torch.sigmoid(torch.randn(d, generator=g)) for _ in range(3)]
+    G = (d + 127) // 128
+    xd = x.cuda().contiguous()
+    codes = [torch.empty(B * T, d, dtype=torch.int8, device="cuda") for _ in range(3)]
+    scales = [torch.empty(B * T, G, dtype=torch.float16, device="cuda") for _ in range(3)]
+    mdev = [m.cuda().contiguous() for m in mixes]
+    _lib.check(_lib.lib().ksd8_rosa_timemix_quantize(
+        xd.data_ptr(), _lib.dtype_code(xd), B, T, d, *(m.data_ptr() for m in mdev),
+        codes[0].data_ptr(), scales[0].data_ptr(), codes[1].data_ptr(), scales[1].data_ptr(),
+        codes[2].data_ptr(), scales[2].data_ptr(), None, _lib.stream_ptr(xd.device)),
+        "rosa_timemix_quantize")
+    xf = x.float().numpy()
+    prev = np.concatenate([np.zeros((B, 1, d), np.float32), xf[:, :-1]], 1)
+    diff = torch.from_numpy(xf - prev).to(dtype).float().numpy()     # in x's dtype
+    for p in range(3):
+        xin = (prev + diff * mixes[p].numpy()).reshape(B * T, d).astype(np.float32)
+        co, so = oracle.quantize_rows_c(xin)
+        np.testing.assert_array_equal(codes[p].cpu().numpy(), co)
+        np.testing.assert_array_equal(scales[p].float().cpu().numpy(), so)
