@@ -20,24 +20,25 @@
 //                128 B) of a K group into an smem ring of STAGES slots,
 //                128-byte swizzle, no multicast.
 //   warp 1       TMEM allocation + single-thread MMA issue: 4 x
-//                tcgen05.mma.kind::i8 (K = 32 each) per group into one of two
-//                int32 accumulators in TMEM (ping-pong across groups and
-//                tiles); commits to the smem slot's "empty" barrier and to the
+//                tcgen05.mma.kind::i8 (K = 32 each) per group into one of the
+//                int32 accumulator buffers in TMEM (round robin across groups
+//                and tiles; the group's first MMA overwrites the buffer);
+//                commits to the smem slot's "empty" barrier and to the
 //                accumulator's "full" barrier.
 //   warps 2, 3   scale loaders (alternate batches of groups): fp16 sa[m0.., g]
 //                and sw[n0.., g] -> fp32 ring.
 //   warps 4..    epilogue: each thread owns one row and CPT consecutive
 //                columns of the tile.  Per group it loads the int32
-//                accumulator from TMEM (one chunk ahead), adds it into its fp32
-//                registers with packed f32x2 ops, re-arms the TMEM chunk and
-//                releases it; after the tile's last group it converts and
-//                stores the row segment while the tensor cores already work
-//                on the next tile.
-// Conversion trick: every accumulator is pre-set (tcgen05.st) to the bit
-// pattern of 1.5 * 2^23, so after the group's MMAs it holds that pattern
-// plus the int32 dot product, i.e. the fp32 number 12582912 + dot (exact for
-// |dot| < 2^22; here |dot| <= 128 * 128 * 128 = 2^21), which the first FMA of
-// the group sum consumes directly (see above).
+//                accumulator from TMEM, releases the buffer, and adds it into
+//                its fp32 registers with packed f32x2 ops; after the tile's
+//                last group it converts and stores the row segment while the
+//                tensor cores already work on the next tile.
+// Conversion trick: the int32 dot plus the bit pattern of 1.5 * 2^23 (one
+// integer add) is the fp32 number 12582912 + dot (exact for |dot| < 2^22;
+// here |dot| <= 128 * 128 * 128 = 2^21), which the first FMA of the group sum
+// consumes directly (see above).  (Pre-setting the accumulators to that
+// pattern with tcgen05.st instead, so that the MMAs add the dot to it, costs
+// a TMEM store per element per group and measured 2-6% slower.)
 #include "common.cuh"
 
 namespace ksd8 {
@@ -106,18 +107,6 @@ struct GemmSmem {
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
 };
 
-__device__ __forceinline__ void tmem_st_magic_x8(uint32_t taddr) {
-  const uint32_t m = MAGIC_BITS;
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(
-          taddr),
-      "r"(m)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
 
 __device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
   asm volatile(
@@ -134,11 +123,6 @@ __device__ __forceinline__ void tmem_ld_w(uint32_t taddr, uint32_t (&r)[W]) {
   else tmem_ld_32x32b_x32(taddr, r);
 }
 
-template <int W>
-__device__ __forceinline__ void tmem_st_magic_w(uint32_t taddr) {
-#pragma unroll
-  for (int i = 0; i < W; i += 8) tmem_st_magic_x8(taddr + i);
-}
 
 // Register splits (setmaxnreg) by block size.  12 warps (384 threads): launch
 // at 168 per thread, role warpgroup 88, the two epilogue warpgroups 208
@@ -315,14 +299,14 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
 #pragma unroll
             for (int kk = 0; kk < BK / 32; ++kk)
               mma_i8_pair(d_tmem, smem_desc_k128_sw128(a_addr + kk * 32),
-                          smem_desc_k128_sw128(b_addr + kk * 32), IDESC, 1u);
+                          smem_desc_k128_sw128(b_addr + kk * 32), IDESC, kk ? 1u : 0u);
             mma_commit_pair(&empty[s], 0x3);
             mma_commit_pair(&acc_full[buf], 0x3);
           } else {
 #pragma unroll
             for (int kk = 0; kk < BK / 32; ++kk)
               mma_i8(d_tmem, smem_desc_k128_sw128(a_addr + kk * 32),
-                     smem_desc_k128_sw128(b_addr + kk * 32), IDESC, 1u);
+                     smem_desc_k128_sw128(b_addr + kk * 32), IDESC, kk ? 1u : 0u);
             mma_commit(&empty[s]);
             mma_commit(&acc_full[buf]);
           }
@@ -395,13 +379,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
     const int col0 = chalf * CPT;          // first column within the tile
     const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16);
 
-    // Arm every accumulator buffer with the conversion offset.
-#pragma unroll
-    for (int b = 0; b < NBUF; ++b)
-#pragma unroll
-      for (int c = 0; c < NCH; ++c) tmem_st_magic_w<LDW>(t_row + b * BN + col0 + c * LDW);
-    tmem_wait_st();
-    tc_fence_before();
+    // Every accumulator buffer starts free (the group's first MMA overwrites it).
     __syncwarp();
     if (lane == 0) {
 #pragma unroll
@@ -435,16 +413,13 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
         const float* sw = sc + BM + col0;
         const uint32_t tb = t_row + buf * BN + col0;
         if constexpr (EARLY) {
-          // Whole slice in one round trip: CPT/32 loads, one wait, re-arm, and
-          // release the accumulator to the MMA before any arithmetic.
+          // Whole slice in one round trip: CPT/32 loads, one wait, and the
+          // accumulator released to the MMA before any arithmetic.
           uint32_t r[CPT];
 #pragma unroll
           for (int c = 0; c < CPT / 32; ++c)
             tmem_ld_32x32b_x32(tb + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
           tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < CPT / 8; ++c) tmem_st_magic_x8(tb + c * 8);
-          tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
@@ -459,10 +434,12 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
 #pragma unroll
               for (int j = 0; j < CPT; ++j) {
                 const int n = n0 + col0 + j;
-                if (n < args.N) o[n] = (int32_t)(r[j] - MAGIC_BITS);
+                if (n < args.N) o[n] = (int32_t)r[j];
               }
             }
           } else {
+#pragma unroll
+            for (int j = 0; j < CPT; ++j) r[j] += MAGIC_BITS;   // the fp32 number 1.5 * 2^23 + dot
 #pragma unroll
             for (int j = 0; j < CPT; j += 4) {
               const float4 w4 = *reinterpret_cast<const float4*>(sw + j);
@@ -493,7 +470,7 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
   #pragma unroll
                 for (int j = 0; j < LDW; ++j) {
                   const int n = n0 + col0 + c * LDW + j;
-                  if (n < args.N) o[n] = (int32_t)(rc[j] - MAGIC_BITS);
+                  if (n < args.N) o[n] = (int32_t)rc[j];
                 }
               }
             } else {
@@ -501,20 +478,19 @@ __global__ void __launch_bounds__((4 + EPI_WARPS) * 32, 1)
               for (int j = 0; j < LDW; j += 4) {
                 const float4 w4 = *reinterpret_cast<const float4*>(sw + c * LDW + j);
                 const int o = (c * LDW + j) / 2;
-                const float2 t0 = __ffma2_rn(
-                    make_float2(__uint_as_float(rc[j]), __uint_as_float(rc[j + 1])), sa2, ca2);
-                const float2 t1 = __ffma2_rn(
-                    make_float2(__uint_as_float(rc[j + 2]), __uint_as_float(rc[j + 3])), sa2,
-                    ca2);
+                const float2 t0 = __ffma2_rn(make_float2(__uint_as_float(rc[j] + MAGIC_BITS),
+                                                         __uint_as_float(rc[j + 1] + MAGIC_BITS)),
+                                             sa2, ca2);
+                const float2 t1 = __ffma2_rn(make_float2(__uint_as_float(rc[j + 2] + MAGIC_BITS),
+                                                         __uint_as_float(rc[j + 3] + MAGIC_BITS)),
+                                             sa2, ca2);
                 acc[o] = __ffma2_rn(t0, make_float2(w4.x, w4.y), acc[o]);
                 acc[o + 1] = __ffma2_rn(t1, make_float2(w4.z, w4.w), acc[o + 1]);
               }
             }
-            tmem_st_magic_w<LDW>(tb + c * LDW);
             if (c + 1 < NCH) tmem_wait_ld();
           }
 
-          tmem_wait_st();
           tc_fence_before();
           __syncwarp();  // one arrival per warp once all its lanes are done
           if (lane == 0) {
