@@ -676,24 +676,45 @@ __global__ void __launch_bounds__(RC_WARPS * 32) rosa_match_sorted_kernel(MatchA
       const int jhi = min(r0 - 1, t0 - 2);
       int jlo = valid ? best : 0x7fffffff;
       jlo = __reduce_min_sync(full, jlo);
-      int be = 0, bj = -1;
-      for (int j = jlo; j <= jhi; ++j) {
+      // candidates packed as (length << 8) | j, four independent running maxima
+      int pk[4] = {0, 0, 0, 0};
+      int j = jlo;
+      for (; j + 3 <= jhi; j += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint64_t x = wq ^ EW[j + u];
+          int l = x ? __clzll((long long)x) : 64;
+          l = min(l, min(cap, j + u + 1));
+          pk[u] = max(pk[u], l > 0 ? ((l << 8) | (j + u)) : 0);
+        }
+      }
+      for (; j <= jhi; ++j) {
         const uint64_t x = wq ^ EW[j];
         int l = x ? __clzll((long long)x) : 64;
         l = min(l, min(cap, j + 1));
-        if (l > 0 && l >= be) { be = l; bj = j; }
+        pk[0] = max(pk[0], l > 0 ? ((l << 8) | j) : 0);
       }
-      if (be > best) { best = be; bestj = bj; }
+      const int top = max(max(pk[0], pk[1]), max(pk[2], pk[3]));
+      if ((top >> 8) > best) { best = top >> 8; bestj = top & 0xFF; }
     }
-    // this step's own keys, j = t0 - 1 + i <= t - 1 (the latest: they win ties)
-    for (int i = 0; i < 32; ++i) {
-      const uint64_t wki = __shfl_sync(full, wk, i);
-      const int j = t0 - 1 + i;
-      if (i <= lane && j >= 0) {
+    // this step's own keys, j = t0 - 1 + i <= t - 1 (the latest: they win ties):
+    // candidates packed as (length << 8) | i, four independent running maxima
+    {
+      int pk[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint64_t wki = __shfl_sync(full, wk, i);
+        const int j = t0 - 1 + i;
         const uint64_t x = wq ^ wki;
         int l = x ? __clzll((long long)x) : 64;
         l = min(l, min(cap, j + 1));
-        if (l > 0 && l >= best) { best = l; bestj = j; }
+        const int c = (i <= lane && j >= 0 && l > 0) ? ((l << 8) | i) : 0;
+        pk[i & 3] = max(pk[i & 3], c);
+      }
+      const int top = max(max(pk[0], pk[1]), max(pk[2], pk[3]));
+      if (top && (top >> 8) >= best) {
+        best = top >> 8;
+        bestj = t0 - 1 + (top & 0xFF);
       }
     }
     if (valid) {
