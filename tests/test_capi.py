@@ -47,6 +47,15 @@ def test_host_side_validation_without_launch():
                                None, None, None) == _lib.ERR_ARG
     assert lib.ksd8_ks3_vjp(None, None, 4, 100, None, None, None, None, None, None, None, None,
                             None, None, None, None, None) == _lib.ERR_SHAPE
+    # Rosa credits: cap beyond the 64-bit window, T beyond the kernel's limit,
+    # missing buffers -- all rejected before any device call
+    assert lib.ksd8_rosa_credits(None, None, None, 1, 4, 65, None, None, None, None, None,
+                                 None) == _lib.ERR_ARG
+    assert lib.ksd8_rosa_credits(None, None, None, 1, 20000, 62, None, None, None, None, None,
+                                 None) == _lib.ERR_UNSUPPORTED
+    assert lib.ksd8_rosa_credits(None, None, None, 1, 8, 7, None, None, None, None, None,
+                                 None) == _lib.ERR_ARG
+    assert lib.ksd8_rosa_set_algorithm(5) == _lib.ERR_ARG
 
 
 def test_status_mapping_to_reference_exceptions():
