@@ -11,10 +11,12 @@ also exposes the match length and endpoint for parity checks.
 `RosaMixer` mirrors rosa.py:101-165.  With Int8Linear projections (after
 `to_int8`) its evaluation forward is the fused W8A8 pipeline: time-shift mix
 fused with the per-token quantisation of the three projection inputs, three
-GEMMs with bias writing bf16, bit packing straight from those outputs, the
-match with the payload multiply fused into its store, a transposed
-quantisation of the (B, S, T) result for the output projection, and the
-output GEMM.
+GEMMs with bias writing fp32, bit packing straight from those outputs, the
+match with the payload multiply fused into its token-major (B, T, S) store,
+the per-token quantisation of that result and the output GEMM.  In training
+mode it takes the reference's CUDA path: the hard core through HardRosaGPU
+(kernels/rosa_credit_gpu.py), whose counterfactual credits give the q / k / v
+projections their gradients.
 """
 
 from __future__ import annotations
