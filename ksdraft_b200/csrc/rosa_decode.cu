@@ -14,15 +14,17 @@
 //
 // Per stream the keys are split three ways:
 //   early keys   j < r0 = max_len - 1: their windows reach before position 0,
-//                so their length is also capped at j + 1; compared directly;
+//                so their length is also capped at j + 1; matched directly,
+//                bit-parallel over their k word (see the step kernel);
 //   main run     r0 <= j < n_main: sorted by (W(j), j) once (decode_build),
 //                static until the next rebuild -- the longest match against
 //                them is reached at the query's sorted neighbours, the latest
 //                endpoint sharing that prefix is a range maximum over ranks
 //                (max of j + 1 per block of 64 ranks plus the partial blocks);
 //   delta        n_main <= j <= t - 1: the keys appended since the last
-//                build, compared directly (the caller rebuilds the main run
-//                when the delta grows past its budget).
+//                build, matched directly and bit-parallel per k word (the
+//                caller rebuilds the main run when the delta grows past its
+//                budget).
 // All three give exact (length, latest j) candidates; the best of them is the
 // sequence matcher's answer.
 #include "common.cuh"
